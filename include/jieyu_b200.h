@@ -1,0 +1,236 @@
+/*
+ * jieyu_b200.h — C ABI of the B200 (sm_100a) decode path for jieyu.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, and
+ * returns a status code (JYC_OK == 0, negative on error; the message is in
+ * jyc_last_error()). No C++ exception crosses this boundary.
+ *
+ * Two families:
+ *   - operator entry points over DEVICE pointers on a caller stream
+ *     (jyc_matmul_q8, jyc_rmsnorm, jyc_rope_pos, jyc_attention_q8, ...): one
+ *     per reference operator, same argument meaning and order;
+ *   - the model entry points (jyc_model_create, jyc_generate, ...) that take
+ *     the reference's own host-side weight handles (WMat / LayerWeights are
+ *     binary-compatible with jyc_wmat / jyc_layer_weights), upload them to HBM
+ *     once, and run the whole token loop on the GPU.
+ *
+ * Reference paths below are relative to the jieyu source tree.
+ */
+#ifndef JIEYU_B200_H
+#define JIEYU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define JYC_API __attribute__((visibility("default")))
+#else
+#define JYC_API
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define JYC_OK               0
+#define JYC_ERR_ARG         -1   /* bad argument (reference: std::runtime_error on misuse) */
+#define JYC_ERR_CUDA        -2   /* a CUDA runtime call failed */
+#define JYC_ERR_KV_OOM      -3   /* start_pos+seq > KV capacity (reference: "KV cache 容量不足") */
+#define JYC_ERR_UNSUPPORTED -4   /* weight type / shape this build does not handle */
+#define JYC_ERR_NOMEM       -5   /* device allocation failed */
+
+/* Quantised block types, same numbering as qmat's enum (libs/matmul_libs/matmul_q.h:15). */
+enum { JYC_Q4K = 0, JYC_Q5K = 1, JYC_Q6K = 2, JYC_Q8_0 = 3 };
+
+/* Weight handle. Field order and types equal `struct WMat`
+ * (libs/date_libs/wmat.h:32-44): exactly one of f (fp32, row-major [in][out]),
+ * h (fp16, [in][out]) or q (quantised blocks, [out][in/32] x 34 B for Q8_0)
+ * is non-null. */
+typedef struct jyc_wmat {
+    const float*    f;
+    const uint16_t* h;
+    const void*     q;
+    uint8_t         qt;
+} jyc_wmat;
+
+/* Per-layer weights. Field order equals `struct LayerWeights`
+ * (libs/date_libs/date.h:75-88); bq/bk/bv may be NULL (no QKV bias). */
+typedef struct jyc_layer_weights {
+    const float* rms1_weight;
+    jyc_wmat Wq, Wk, Wv, Wo;
+    const float* bq;
+    const float* bk;
+    const float* bv;
+    const float* rms2_weight;
+    jyc_wmat W1, W2, W3;
+} jyc_layer_weights;
+
+/* Everything `generate()` receives besides the prompt (libs/model_libs/generate.h:90-104),
+ * all HOST pointers in the reference's layouts. cos/sin are RoPETable tables
+ * [max_seq][head_dim/2] (libs/date_libs/date.h:52-66). */
+typedef struct jyc_model_desc {
+    const jyc_layer_weights* layers;
+    int num_layers;
+    jyc_wmat embed;
+    jyc_wmat lm_head;
+    const float* final_rms_weight;
+    const float* cos_table;
+    const float* sin_table;
+    int max_seq;
+    int vocab_size;
+    int hidden;
+    int num_heads;
+    int num_kv_heads;
+    int head_dim;
+    int intermediate;
+} jyc_model_desc;
+
+/* Token callback, same contract as `token_cb` (libs/model_libs/generate.h:8):
+ * return non-zero to stop generation after this token. */
+typedef int (*jyc_token_cb)(int id, void* ud);
+
+/* ---- library ----------------------------------------------------------- */
+JYC_API const char* jyc_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+JYC_API const char* jyc_last_error(void);
+/* Number of device kernels this library launched so far in this process
+ * (every launch made by the library increments it). */
+JYC_API long long jyc_kernel_launches(void);
+
+/* ---- host helpers (no GPU needed) -------------------------------------- */
+/* RoPE tables exactly as RoPETable::init (libs/date_libs/date.h:52-66):
+ * freq = 1/powf(theta, 2j/hd), angle = i*freq, cosf/sinf, all in float. */
+JYC_API int jyc_rope_table(int max_seq, int head_dim, float theta,
+                           float* cos_out, float* sin_out);
+
+/* Seeded synthetic data (no reference counterpart: the reference has no
+ * quantiser, GGUF blocks are copied raw, libs/gguf_libs/gguf_convert.h:201-229).
+ * Values are an exact integer function of (seed, stream, index):
+ *   x = (u1+u2+u3+u4 - 2*65535) * scale, u_i 16-bit slices of splitmix64,
+ * i.e. a zero-mean bell-shaped variable with std = std_dev.
+ * Q8_0 quantisation: d = fp16(amax/127), q = lrintf(x / fp32(d)) clamped to
+ * [-127,127]; block = 2-byte fp16 d then 32 int8 (34 bytes). */
+JYC_API int jyc_synth_f32(uint64_t seed, uint64_t stream, float std_dev,
+                          float* out, size_t n);
+JYC_API int jyc_synth_q8_0(uint64_t seed, uint64_t stream, float std_dev,
+                           void* out_blocks, size_t rows, size_t k);
+JYC_API int jyc_synth_ids(uint64_t seed, uint64_t stream, int vocab,
+                          int* out, size_t n);
+/* fp32 -> Q8_0 blocks (same rule as jyc_synth_q8_0). k % 32 == 0. */
+JYC_API int jyc_quantize_q8_0(const float* x, void* out_blocks, size_t rows, size_t k);
+
+/* ---- operator entry points (DEVICE pointers, asynchronous on `stream`) - */
+/* Device layout of a Q8_0 matrix [n][k]: qs = n*k bytes holding q+128
+ * (row-major), d = n*(k/32) fp16 scales (row-major). Produced from the
+ * reference block layout by jyc_q8_repack. */
+JYC_API int jyc_q8_repack(const void* blocks, int n, int k,
+                          uint8_t* qs, uint16_t* d, void* stream);
+
+/* C[m][n] = A[m][k] . W^T for a Q8_0 weight W [n][k]; fp32 activations,
+ * exact fp16->fp32 scale x int8 weight products, fp32 accumulation.
+ * Replaces qmat::matmul_q(a,b,c,m,n,k,Q8_0) (libs/matmul_libs/matmul_q.h:134-162). */
+JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d,
+                          float* C, int m, int n, int k, void* stream);
+
+/* C[m][n] = A[m][k] . B with B given TRANSPOSED on the device, Bt [n][k]
+ * (jyc_f32_transpose makes it from the reference's [k][n]).
+ * Replaces matmul(m,n,k,A,B,C) (libs/matmul_libs/matmul.h:7-76). */
+JYC_API int jyc_matmul_f32(const float* A, const float* Bt, float* C,
+                           int m, int n, int k, void* stream);
+JYC_API int jyc_f32_transpose(const float* B, float* Bt, int k, int n, void* stream);
+
+/* y = x * (1/sqrtf(sum(x^2)/n + eps)) * w, for `rows` rows of n.
+ * Replaces rmsnorm(x,y,w,n,eps) (libs/model_libs/rmsnorm/rmsnorm.h:8-78). */
+JYC_API int jyc_rmsnorm(const float* x, float* y, const float* w, int rows, int n,
+                        float eps, void* stream);
+
+/* In-place interleaved-pair rotation from the tables.
+ * Replaces rope_pos(q,seq,start_pos,heads,hd,cos,sin) (libs/model_libs/rope/rope.h:108-110). */
+JYC_API int jyc_rope_pos(float* q, int seq, int start_pos, int num_heads, int head_dim,
+                         const float* cos_table, const float* sin_table, void* stream);
+
+/* Per (row, head) int8 quantisation with one fp32 scale, bit-exact with
+ * kv_pack_q8 (libs/model_libs/attention/attention_q8.h:20-37). */
+JYC_API int jyc_kv_pack_q8(const float* src, int8_t* dst, float* scale,
+                           int heads, int head_dim, int n, void* stream);
+
+/* Int8-KV GQA attention for `seq` new rows at start_pos: packs K,V into the
+ * cache, quantises Q per (row, head), int32 q.k dot, fp32 causal softmax,
+ * out = sum p*vs*v. KV cache layout equals __KVq (attention_q8.h:12-19):
+ * k,v [cap][num_kv_heads][head_dim] int8, ks,vs [cap][num_kv_heads] fp32.
+ * Replaces attention_q8 (libs/model_libs/attention/attention_q8.h:38-184). */
+JYC_API int jyc_attention_q8(const float* Q, const float* K, const float* V, float* out,
+                             int seq, int start_pos, int num_heads, int num_kv_heads,
+                             int head_dim, int8_t* kc, float* ks, int8_t* vc, float* vs,
+                             int cap, void* stream);
+
+/* y = x / (1 + e^-x), with the reference's own exp polynomial for the
+ * vector body. Replaces silu(x,y,n) (libs/model_libs/silu/silu.h:7-81). */
+JYC_API int jyc_silu(const float* x, float* y, int n, void* stream);
+
+/* First index of the maximum (strict >, ties -> lowest id) over n logits.
+ * Replaces the greedy loop of generate_cached (libs/model_libs/generate.h:57-60). */
+JYC_API int jyc_argmax(const float* logits, int n, int* out_index, void* stream);
+
+/* ---- model entry points ------------------------------------------------ */
+typedef struct jyc_model jyc_model;
+
+/* Uploads every weight once (the bind_model point, libs/model_libs/pipeline.h:63-153):
+ * Q8_0 blocks are re-laid into the device layout, fp32 [in][out] matrices are
+ * transposed, Q/K/V and gate/up are fused. Allocates a device KV cache of
+ * desc->max_seq positions. Returns NULL on error. */
+JYC_API jyc_model* jyc_model_create(const jyc_model_desc* desc);
+JYC_API void jyc_model_free(jyc_model* m);
+/* Bytes of weights one decode token streams (algorithmic, for rooflines). */
+JYC_API double jyc_model_weight_bytes_per_token(const jyc_model* m);
+/* Bytes of KV cache one decode token reads at context `ctx`. */
+JYC_API double jyc_model_kv_bytes_per_token(const jyc_model* m, int ctx);
+
+/* Full token loop, same contract as generate() (libs/model_libs/generate.h:90-112)
+ * with an internal KV cache: out_ids[0..ret) = prompt then new tokens;
+ * returns 0 if prompt_len<=0 or > max_seq, prompt_len if max_new_tokens<=0,
+ * negative on error. temperature<=0 is greedy; otherwise the reference's
+ * LCG sampler (seed 12345). */
+JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len,
+                         const int* eos_ids, int num_eos, int max_new_tokens,
+                         float temperature, int* out_ids, float repetition_penalty,
+                         jyc_token_cb cb, void* cb_ud);
+
+/* One forward pass of `seq` tokens at start_pos through the device KV cache,
+ * then the LM head on the last row: the step body of generate_cached
+ * (libs/model_libs/generate.h:40-49). logits: host fp32[vocab]
+ * (may be NULL); hidden_out: host fp32[hidden] final-norm output of the last
+ * row (may be NULL). For teacher-forced parity checks. */
+JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_pos,
+                               float* logits, float* hidden_out);
+
+/* Device KV cache contents for parity checks, copied to host in the reference
+ * layout of __KVcache (libs/date_libs/date.h:89-147) for one layer:
+ * k,v [npos][num_kv_heads][head_dim] int8, ks,vs [npos][num_kv_heads] fp32. */
+JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos,
+                              int8_t* k, float* ks, int8_t* v, float* vs);
+
+/* ---- device-resident stepping (bench / device loop) -------------------- */
+/* Prefill `prompt_len` ids (DEVICE int32 pointer) from position 0 and emit the
+ * first greedy token into the device token buffer. Asynchronous on `stream`. */
+JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prompt_len,
+                               void* stream);
+/* Run `n_steps` greedy decode steps from the current device state (each
+ * consumes the last token and appends the next). Launches replay a captured
+ * CUDA graph; asynchronous on `stream`. */
+JYC_API int jyc_decode_device(jyc_model* m, int n_steps, void* stream);
+/* Reset the device state to `len` tokens already in the buffer (and their KV
+ * entries in the cache), so decode can be replayed from the same point. */
+JYC_API int jyc_model_rewind(jyc_model* m, int len, void* stream);
+/* Kernels one decode step launches. */
+JYC_API int jyc_model_kernels_per_step(const jyc_model* m);
+/* Device pointer to the int32 token buffer [max_seq] and host read of the
+ * current length (synchronises the stream). */
+JYC_API int* jyc_model_tokens_device(jyc_model* m);
+JYC_API int jyc_model_length(jyc_model* m, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JIEYU_B200_H */

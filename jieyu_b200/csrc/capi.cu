@@ -1,0 +1,192 @@
+// capi.cu — operator-level C ABI over device pointers (one entry per reference
+// operator; see include/jieyu_b200.h for the reference function each replaces).
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "kernels.cuh"
+
+using namespace jyc;
+
+namespace {
+
+#define TRY(x)                          \
+    do {                                \
+        int _r = (x);                   \
+        if (_r != JYC_OK) return _r;    \
+    } while (0)
+
+inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Stream-ordered scratch for one op call (freed in stream order).
+struct Scratch {
+    cudaStream_t s;
+    std::vector<void*> ptrs;
+    explicit Scratch(cudaStream_t st) : s(st) {}
+    template <class T>
+    int get(T** p, size_t count) {
+        void* q = nullptr;
+        cudaError_t e = cudaMallocAsync(&q, std::max<size_t>(count, 1) * sizeof(T), s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync");
+        ptrs.push_back(q);
+        *p = static_cast<T*>(q);
+        return JYC_OK;
+    }
+    ~Scratch() {
+        for (void* q : ptrs) cudaFreeAsync(q, s);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+JYC_API int jyc_q8_repack(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d, void* stream) {
+    clear_error();
+    if (!blocks || !qs || !d) return arg_error("q8_repack: null pointer");
+    return launch_q8_repack(blocks, n, k, qs, d, 0, 1, S(stream));
+}
+
+JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d, float* C, int m,
+                          int n, int k, void* stream) {
+    clear_error();
+    if (!A || !qs || !d || !C) return arg_error("matmul_q8: null pointer");
+    if (m <= 0 || n <= 0 || k <= 0 || k % 32) return arg_error("matmul_q8: need m,n > 0 and k % 32 == 0");
+    for (int r0 = 0; r0 < m; r0 += 8) {
+        GemvArgs g{};
+        g.x = A + (size_t)r0 * k; g.ldx = k; g.m = std::min(8, m - r0); g.n = n; g.k = k;
+        g.qs = qs; g.d = d; g.y = C + (size_t)r0 * n; g.ldy = n;
+        TRY(launch_gemv(g, W_Q8, EPI_STORE, S(stream)));
+    }
+    return JYC_OK;
+}
+
+JYC_API int jyc_f32_transpose(const float* B, float* Bt, int k, int n, void* stream) {
+    clear_error();
+    if (!B || !Bt) return arg_error("f32_transpose: null pointer");
+    return launch_transpose(B, Bt, k, n, 0, 1, S(stream));
+}
+
+JYC_API int jyc_matmul_f32(const float* A, const float* Bt, float* C, int m, int n, int k,
+                           void* stream) {
+    clear_error();
+    if (!A || !Bt || !C) return arg_error("matmul_f32: null pointer");
+    if (m <= 0 || n <= 0 || k <= 0) return arg_error("matmul_f32: empty shape");
+    if (k % 8 == 0 && m <= 8) {
+        GemvArgs g{};
+        g.x = A; g.ldx = k; g.m = m; g.n = n; g.k = k; g.wt = Bt; g.y = C; g.ldy = n;
+        return launch_gemv(g, W_F32, EPI_STORE, S(stream));
+    }
+    return launch_matmul_f32_generic(A, Bt, C, m, n, k, S(stream));
+}
+
+JYC_API int jyc_rmsnorm(const float* x, float* y, const float* w, int rows, int n, float eps,
+                        void* stream) {
+    clear_error();
+    if (!x || !y || !w) return arg_error("rmsnorm: null pointer");
+    return launch_rmsnorm(x, y, w, rows, n, eps, S(stream));
+}
+
+JYC_API int jyc_rope_pos(float* q, int seq, int start_pos, int num_heads, int head_dim,
+                         const float* cos_table, const float* sin_table, void* stream) {
+    clear_error();
+    if (!q || !cos_table || !sin_table) return arg_error("rope_pos: null pointer");
+    if (seq < 0 || start_pos < 0 || num_heads <= 0 || head_dim <= 0) return arg_error("rope_pos: bad shape");
+    return launch_rope(q, seq, start_pos, num_heads, head_dim, cos_table, sin_table, S(stream));
+}
+
+JYC_API int jyc_kv_pack_q8(const float* src, int8_t* dst, float* scale, int heads, int head_dim,
+                           int n, void* stream) {
+    clear_error();
+    if (!src || !dst || !scale) return arg_error("kv_pack_q8: null pointer");
+    if (heads <= 0 || head_dim <= 0 || n < 0) return arg_error("kv_pack_q8: bad shape");
+    return launch_kv_pack(src, dst, scale, heads, head_dim, n, S(stream));
+}
+
+JYC_API int jyc_attention_q8(const float* Q, const float* K, const float* V, float* out, int seq,
+                             int start_pos, int num_heads, int num_kv_heads, int head_dim,
+                             int8_t* kc, float* ks, int8_t* vc, float* vs, int cap, void* stream) {
+    clear_error();
+    // argument checks of attention/x86/x86_classic.txt:2-8
+    if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0)
+        return arg_error("attention_q8: num_heads must be a multiple of num_kv_heads");
+    if (seq <= 0) return arg_error("attention_q8: seq must be positive");
+    if (start_pos < 0) return arg_error("attention_q8: start_pos must not be negative");
+    if (!kc || !ks || !vc || !vs || cap <= 0) return arg_error("attention_q8: KV cache pointers incomplete");
+    if ((long long)start_pos + seq > cap) {
+        set_error("attention_q8: KV cache capacity exceeded");
+        return JYC_ERR_KV_OOM;
+    }
+    if (!Q || !K || !V || !out) return arg_error("attention_q8: null pointer");
+    if (head_dim % 4 || head_dim > 256) return arg_error("attention_q8: head_dim must be a multiple of 4, <= 256");
+    cudaStream_t s = S(stream);
+    const int rows_max = 8;
+    if (attn_smem_bytes(rows_max, num_heads, num_kv_heads, head_dim) > 200 * 1024)
+        return arg_error("attention_q8: query-head group too large");
+    KVView kv{kc, ks, vc, vs, (long long)num_kv_heads * head_dim, head_dim, num_kv_heads, 1, cap};
+    const int maxpos = start_pos + seq;
+    const int target = std::max(1, 296 / num_kv_heads);
+    int chunk = (maxpos + target - 1) / target;
+    chunk = std::max(64, (chunk + 63) / 64 * 64);
+    const int nsplit = (maxpos + chunk - 1) / chunk;
+    Scratch sc(s);
+    int8_t* q8;
+    float *qsc, *po, *pml;
+    unsigned int* arrive;
+    TRY(sc.get(&q8, (size_t)rows_max * num_heads * head_dim));
+    TRY(sc.get(&qsc, (size_t)rows_max * num_heads));
+    TRY(sc.get(&po, (size_t)rows_max * num_heads * nsplit * head_dim));
+    TRY(sc.get(&pml, (size_t)rows_max * num_heads * nsplit * 2));
+    TRY(sc.get(&arrive, (size_t)num_kv_heads));
+    JYC_CUDA(cudaMemsetAsync(arrive, 0, num_kv_heads * sizeof(unsigned int), s));
+    const int qd = num_heads * head_dim, kvd = num_kv_heads * head_dim;
+    for (int r0 = 0; r0 < seq; r0 += rows_max) {
+        const int rows = std::min(rows_max, seq - r0);
+        // kv_pack_q8 of the new K,V rows into the cache + Q quantisation (inputs already roped)
+        RopeQuantArgs rq{};
+        rq.q = Q + (size_t)r0 * qd; rq.k = K + (size_t)r0 * kvd; rq.v = V + (size_t)r0 * kvd;
+        rq.ldq = 0;  // set per array below
+        rq.rows = rows; rq.H = num_heads; rq.KV = num_kv_heads; rq.hd = head_dim;
+        rq.q8 = q8; rq.qsc = qsc; rq.kv = kv; rq.pos = PosSrc{nullptr, start_pos + r0};
+        // Q, K, V have different row strides: run Q-only and K/V-only passes.
+        {
+            RopeQuantArgs a = rq;  // queries: H heads, stride qd
+            a.KV = 0; a.ldq = qd;
+            // with KV = 0 the kernel only visits query heads
+            TRY(launch_rope_quant(a, s));
+        }
+        {
+            RopeQuantArgs a = rq;  // keys and values: stride kvd, no query heads
+            a.H = 0; a.ldq = kvd;
+            a.q8 = nullptr; a.qsc = nullptr;
+            TRY(launch_rope_quant(a, s));
+        }
+        AttnArgs at{};
+        at.q8 = q8; at.qsc = qsc; at.kv = kv;
+        at.rows = rows; at.H = num_heads; at.KV = num_kv_heads; at.hd = head_dim;
+        at.chunk = chunk; at.nsplit = nsplit; at.scale = 1.0f / sqrtf((float)head_dim);
+        at.part_o = po; at.part_ml = pml; at.arrive = arrive;
+        at.out = out + (size_t)r0 * qd; at.ldo = qd; at.pos = PosSrc{nullptr, start_pos + r0};
+        TRY(launch_attention(at, s));
+    }
+    return JYC_OK;
+}
+
+JYC_API int jyc_silu(const float* x, float* y, int n, void* stream) {
+    clear_error();
+    if ((!x || !y) && n > 0) return arg_error("silu: null pointer");
+    return launch_silu(x, y, n, S(stream));
+}
+
+JYC_API int jyc_argmax(const float* logits, int n, int* out_index, void* stream) {
+    clear_error();
+    if (!logits || !out_index) return arg_error("argmax: null pointer");
+    cudaStream_t s = S(stream);
+    Scratch sc(s);
+    unsigned long long* slot;
+    TRY(sc.get(&slot, 1));
+    JYC_CUDA(cudaMemsetAsync(slot, 0, sizeof(unsigned long long), s));
+    return launch_argmax(logits, n, slot, out_index, s);
+}
+
+}  // extern "C"

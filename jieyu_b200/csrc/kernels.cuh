@@ -1,0 +1,131 @@
+// kernels.cuh — sm_100a kernels of the decode path and their launch helpers.
+//
+// Data layouts in HBM (the device copy is private, so it is laid out for the GPU):
+//   Q8_0 matrix [n][k]   qs: n*k bytes, byte = q+128, row-major (16-byte vector loads);
+//                        d : n*(k/32) fp16 scales, row-major.
+//                        34 bytes per 32 weights, the same as the reference blocks.
+//   fp32 matrix [n][k]   row-major (the reference's [k][n] transposed once at upload).
+//   KV cache (model)     k8/v8 int8 [layer][kv_head][pos][head_dim], ks/vs fp32
+//                        [layer][kv_head][pos]; the op-level entry uses the
+//                        reference's [pos][kv_head][head_dim] through strides.
+#pragma once
+#include "common.cuh"
+
+namespace jyc {
+
+enum WType { W_Q8 = 0, W_F32 = 1 };
+enum Epi { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+// Step state shared by the kernels of one decode step (device memory).
+struct DevState {
+    int len;        // tokens in the token buffer (prompt + generated)
+    int steps;      // tokens generated so far
+    int max_new;    // stop after this many new tokens
+    int max_len;    // stop when len reaches this (max_seq)
+    int active;     // 0 -> every step kernel returns immediately
+    int n_eos;
+    int eos[16];
+    unsigned long long amax;   // argmax slot (argmax_pack)
+    unsigned int head_arrive;  // last-arriver counter of the LM-head grid
+    unsigned int pad_;
+};
+
+// Where a kernel finds its first position: from the step state (decode graph,
+// pos0 = len-1, guarded by `active`) or from a host constant (prefill / ops).
+struct PosSrc {
+    const DevState* st;
+    int pos0;
+};
+__device__ __forceinline__ bool pos_inactive(const PosSrc& p) {
+    return p.st != nullptr && *(volatile const int*)&p.st->active == 0;
+}
+__device__ __forceinline__ int pos_first(const PosSrc& p) {
+    return p.st != nullptr ? (*(volatile const int*)&p.st->len) - 1 : p.pos0;
+}
+
+struct GemvArgs {
+    const float* x;        // activations [m][ldx]
+    int ldx;
+    int m, n, k;
+    const uint8_t* qs;     // Q8 weights
+    const uint16_t* d;
+    const float* wt;       // fp32 weights [n][k]
+    const float* norm_w;   // optional fused RMSNorm of x (weights [k]); nullptr = off
+    float eps;
+    float* y;              // output [m][ldy]
+    int ldy;
+    const float* bias;     // EPI_BIAS
+    DevState* st;          // EPI_ARGMAX: state updated by the last CTA; also the guard
+    const int* tokens_ro;  // unused
+    int* tokens;           // EPI_ARGMAX: token buffer
+};
+
+struct KVView {
+    int8_t* k;
+    float* ks;
+    int8_t* v;
+    float* vs;
+    long long pos_stride;    // elements between positions (int8 arrays)
+    long long head_stride;   // elements between kv heads (int8 arrays)
+    long long spos_stride;   // scale arrays
+    long long shead_stride;
+    int cap;
+};
+
+struct RopeQuantArgs {
+    const float* q;        // [rows][ldq] query heads
+    const float* k;        // [rows][ldq] key heads
+    const float* v;        // [rows][ldq] value heads
+    int ldq;               // row stride of q/k/v (floats)
+    int rows, H, KV, hd;
+    const float* cos_t;    // nullptr: inputs are already rotated (quantise only)
+    const float* sin_t;
+    int8_t* q8;            // [rows][H][hd]
+    float* qsc;            // [rows][H]
+    float* q_roped;        // optional fp32 roped Q [rows][H*hd] (op-level parity), may be null
+    float* k_roped;        // optional fp32 roped K [rows][KV*hd]
+    KVView kv;
+    PosSrc pos;
+};
+
+struct AttnArgs {
+    const int8_t* q8;
+    const float* qsc;
+    KVView kv;
+    int rows, H, KV, hd;
+    int chunk;             // positions per split (multiple of 64)
+    int nsplit;
+    float scale;           // 1/sqrtf(hd)
+    float* part_o;         // [rows][H][nsplit][hd]
+    float* part_ml;        // [rows][H][nsplit][2]
+    unsigned int* arrive;  // [KV] last-arriver counters (zero between launches)
+    float* out;            // [rows][ldo]
+    int ldo;
+    PosSrc pos;
+};
+
+// ---- launchers (kernels.cu) ----------------------------------------------
+int launch_gemv(const GemvArgs& a, int wtype, int epi, cudaStream_t s);
+int launch_rmsnorm(const float* x, float* y, const float* w, int rows, int n, float eps,
+                   cudaStream_t s);
+int launch_rope_quant(const RopeQuantArgs& a, cudaStream_t s);
+int launch_rope(float* q, int seq, int start_pos, int heads, int hd, const float* cos_t,
+                const float* sin_t, cudaStream_t s);
+int attn_smem_bytes(int rows, int H, int KV, int hd);
+int launch_attention(const AttnArgs& a, cudaStream_t s);
+int launch_embed(const int* tokens, PosSrc pos, int rows, const float* ef, const uint8_t* eqs,
+                 const uint16_t* ed, int hidden, float* X, cudaStream_t s);
+int launch_q8_repack(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d, int row_off,
+                     int row_stride, cudaStream_t s);
+int launch_transpose(const float* B, float* Bt, int k, int n, int row_off, int row_stride,
+                     cudaStream_t s);
+int launch_silu(const float* x, float* y, int n, cudaStream_t s);
+int launch_kv_pack(const float* src, int8_t* dst, float* sc, int heads, int hd, int n,
+                   cudaStream_t s);
+int launch_argmax(const float* v, int n, unsigned long long* slot, int* out, cudaStream_t s);
+int launch_matmul_f32_generic(const float* A, const float* Bt, float* C, int m, int n, int k,
+                              cudaStream_t s);
+int launch_set_state(DevState* st, int len, int max_new, int max_len, const int* eos, int n_eos,
+                     cudaStream_t s);
+
+}  // namespace jyc

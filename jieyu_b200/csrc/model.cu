@@ -1,0 +1,571 @@
+// model.cu — the device-resident token loop behind jyc_model_* / jyc_generate.
+//
+// Mirrors the reference call stack
+//   generate (generate.h:90-112) -> generate_cached (generate.h:9-89)
+//     -> forward_cached (forward.h:47-96) -> transformer_layer (transformer_layer.h:10-90)
+// with every weight uploaded once (the bind_model point, pipeline.h:63-153), a
+// device KV cache, and one decode step = one CUDA-graph replay. Token ids stay
+// on the device; the step's last kernel (LM head + argmax) appends the next id
+// and clears `active` when the reference loop would stop (EOS, max_new, max_seq).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+
+using namespace jyc;
+
+namespace {
+
+constexpr int kMT = 8;  // activation rows per prefill chunk
+
+struct DevMat {          // one weight matrix on the device, [n][k]
+    uint8_t* qs = nullptr;
+    uint16_t* d = nullptr;
+    float* f = nullptr;
+    int n = 0, k = 0;
+    double bytes() const { return f ? 4.0 * n * k : (double)n * k * 34.0 / 32.0; }
+};
+
+struct DevLayer {
+    float* rms1 = nullptr;
+    float* rms2 = nullptr;
+    float* bias = nullptr;  // fused q|k|v bias, or null
+    DevMat qkv, o, gateup, down;
+};
+
+}  // namespace
+
+struct jyc_model {
+    int L = 0, D = 0, H = 0, KV = 0, hd = 0, F = 0, V = 0, max_seq = 0;
+    int q_dim = 0, kv_dim = 0, nqkv = 0;
+    int wtype = W_Q8;
+    std::vector<DevLayer> layers;
+    DevMat head;
+    float* embed_f = nullptr;    // fp32 embedding [V][D], or
+    DevMat embed_q;              // Q8 embedding in device layout (may alias head)
+    float* final_norm = nullptr;
+    float *cos_t = nullptr, *sin_t = nullptr;
+    // KV cache [L][KV][max_seq][hd] int8, scales [L][KV][max_seq]
+    int8_t *k8 = nullptr, *v8 = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    // activations / scratch
+    float *X = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
+    float* tmp = nullptr;
+    int8_t* q8 = nullptr;
+    float* qsc = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    unsigned int* arrive = nullptr;
+    int chunk = 64, nsplit = 1;
+    DevState* st = nullptr;
+    int* tokens = nullptr;       // [max_seq + 1]
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t step_exec = nullptr;
+    std::vector<void*> allocs;
+    double weight_bytes = 0.0;
+
+    template <class T>
+    int alloc(T** p, size_t count) {
+        void* q = nullptr;
+        if (count == 0) count = 1;
+        cudaError_t e = cudaMalloc(&q, count * sizeof(T));
+        if (e != cudaSuccess) {
+            set_error(std::string("cudaMalloc: ") + cudaGetErrorString(e));
+            return JYC_ERR_NOMEM;
+        }
+        allocs.push_back(q);
+        *p = static_cast<T*>(q);
+        return JYC_OK;
+    }
+    ~jyc_model() {
+        if (step_exec) cudaGraphExecDestroy(step_exec);
+        for (void* p : allocs) cudaFree(p);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    KVView kv_layer(int l) const {
+        KVView v;
+        const size_t lay = (size_t)KV * max_seq;
+        v.k = k8 + (size_t)l * lay * hd;
+        v.v = v8 + (size_t)l * lay * hd;
+        v.ks = ks + (size_t)l * lay;
+        v.vs = vs + (size_t)l * lay;
+        v.pos_stride = hd;
+        v.head_stride = (long long)max_seq * hd;
+        v.spos_stride = 1;
+        v.shead_stride = max_seq;
+        v.cap = max_seq;
+        return v;
+    }
+};
+
+namespace {
+
+#define TRY(x)                          \
+    do {                                \
+        int _r = (x);                   \
+        if (_r != JYC_OK) return _r;    \
+    } while (0)
+
+// Uploads one reference weight (host, reference layout) into rows
+// [row_off + r*row_stride] of `dst` (device layout, n_total rows x k).
+int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int n_total,
+                int row_off, int row_stride, void* staging, size_t staging_bytes) {
+    if (w.h != nullptr && w.f == nullptr && w.q == nullptr) {
+        set_error("fp16 weights are not supported by the B200 path");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    const bool q8 = w.q != nullptr;
+    if (q8 && w.qt != JYC_Q8_0) {
+        set_error("only Q8_0 quantised weights are supported by the B200 path (got type " +
+                  std::to_string((int)w.qt) + ")");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    if (!q8 && w.f == nullptr) {
+        set_error("missing weight tensor");
+        return JYC_ERR_ARG;
+    }
+    if ((q8 ? W_Q8 : W_F32) != m->wtype) {
+        set_error("mixed Q8_0 / fp32 linear weights are not supported");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    if (dst.n == 0) {  // first piece: allocate the whole (fused) matrix
+        dst.n = n_total;
+        dst.k = k;
+        if (q8) {
+            TRY(m->alloc(&dst.qs, (size_t)n_total * k));
+            TRY(m->alloc(&dst.d, (size_t)n_total * (k / 32)));
+        } else {
+            TRY(m->alloc(&dst.f, (size_t)n_total * k));
+        }
+    }
+    const size_t bytes = q8 ? (size_t)n * (k / 32) * 34 : (size_t)n * k * 4;
+    if (bytes > staging_bytes) {
+        set_error("internal: staging buffer too small");
+        return JYC_ERR_ARG;
+    }
+    JYC_CUDA(cudaMemcpyAsync(staging, q8 ? w.q : (const void*)w.f, bytes, cudaMemcpyHostToDevice,
+                             m->stream));
+    if (q8) TRY(launch_q8_repack(staging, n, k, dst.qs, dst.d, row_off, row_stride, m->stream));
+    else TRY(launch_transpose(static_cast<const float*>(staging), dst.f, k, n, row_off, row_stride,
+                              m->stream));
+    // the staging buffer is reused by the next upload: wait for this one
+    JYC_CUDA(cudaStreamSynchronize(m->stream));
+    return JYC_OK;
+}
+
+int upload_f32(jyc_model* m, const float* src, size_t n, float** dst) {
+    TRY(m->alloc(dst, n));
+    JYC_CUDA(cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice));
+    return JYC_OK;
+}
+
+int build_model(jyc_model* m, const jyc_model_desc* d) {
+    if (!d || !d->layers || d->num_layers <= 0) return arg_error("model: no layers");
+    if (d->hidden <= 0 || d->num_heads <= 0 || d->num_kv_heads <= 0 || d->head_dim <= 0 ||
+        d->intermediate <= 0 || d->vocab_size <= 0 || d->max_seq <= 0)
+        return arg_error("model: non-positive hyper-parameter");
+    if (d->num_heads % d->num_kv_heads) return arg_error("model: num_heads % num_kv_heads != 0");
+    if (d->head_dim % 4 || d->head_dim > 256) return arg_error("model: head_dim must be a multiple of 4, <= 256");
+    if (!d->final_rms_weight || !d->cos_table || !d->sin_table)
+        return arg_error("model: missing final norm or RoPE tables");
+    m->L = d->num_layers; m->D = d->hidden; m->H = d->num_heads; m->KV = d->num_kv_heads;
+    m->hd = d->head_dim; m->F = d->intermediate; m->V = d->vocab_size; m->max_seq = d->max_seq;
+    m->q_dim = m->H * m->hd; m->kv_dim = m->KV * m->hd; m->nqkv = m->q_dim + 2 * m->kv_dim;
+    m->wtype = d->layers[0].Wq.q != nullptr ? W_Q8 : W_F32;
+    const int kq = m->wtype == W_Q8 ? 32 : 8;
+    if (m->D % kq || m->q_dim % kq || m->F % kq)
+        return arg_error("model: hidden, heads*head_dim and intermediate must be multiples of " +
+                         std::to_string(kq));
+    if (attn_smem_bytes(kMT, m->H, m->KV, m->hd) > 200 * 1024)
+        return arg_error("model: query-head group too large for the attention kernel");
+
+    JYC_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+
+    // staging for uploads: the largest single host tensor
+    size_t stage = 0;
+    auto tb = [&](int n, int k) {
+        return m->wtype == W_Q8 ? (size_t)n * (k / 32) * 34 : (size_t)n * k * 4;
+    };
+    stage = std::max({tb(m->q_dim, m->D), tb(m->kv_dim, m->D), tb(m->D, m->q_dim), tb(m->F, m->D),
+                      tb(m->D, m->F)});
+    const bool head_q8 = d->lm_head.q != nullptr;
+    const size_t head_bytes = head_q8 ? (size_t)m->V * (m->D / 32) * 34 : (size_t)m->V * m->D * 4;
+    stage = std::max(stage, head_bytes);
+    void* staging = nullptr;
+    JYC_CUDA(cudaMalloc(&staging, stage));
+    std::unique_ptr<void, void (*)(void*)> stage_guard(staging, [](void* p) { cudaFree(p); });
+
+    m->layers.resize(m->L);
+    for (int l = 0; l < m->L; l++) {
+        const jyc_layer_weights& w = d->layers[l];
+        DevLayer& dl = m->layers[l];
+        if (!w.rms1_weight || !w.rms2_weight) return arg_error("model: missing RMSNorm weight in layer " + std::to_string(l));
+        TRY(upload_f32(m, w.rms1_weight, m->D, &dl.rms1));
+        TRY(upload_f32(m, w.rms2_weight, m->D, &dl.rms2));
+        TRY(upload_wmat(m, w.Wq, m->q_dim, m->D, dl.qkv, m->nqkv, 0, 1, staging, stage));
+        TRY(upload_wmat(m, w.Wk, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim, 1, staging, stage));
+        TRY(upload_wmat(m, w.Wv, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim + m->kv_dim, 1, staging, stage));
+        TRY(upload_wmat(m, w.Wo, m->D, m->q_dim, dl.o, m->D, 0, 1, staging, stage));
+        TRY(upload_wmat(m, w.W1, m->F, m->D, dl.gateup, 2 * m->F, 0, 2, staging, stage));
+        TRY(upload_wmat(m, w.W3, m->F, m->D, dl.gateup, 2 * m->F, 1, 2, staging, stage));
+        TRY(upload_wmat(m, w.W2, m->D, m->F, dl.down, m->D, 0, 1, staging, stage));
+        if (w.bq || w.bk || w.bv) {
+            std::vector<float> b(m->nqkv, 0.0f);
+            if (w.bq) std::memcpy(b.data(), w.bq, m->q_dim * 4);
+            if (w.bk) std::memcpy(b.data() + m->q_dim, w.bk, m->kv_dim * 4);
+            if (w.bv) std::memcpy(b.data() + m->q_dim + m->kv_dim, w.bv, m->kv_dim * 4);
+            TRY(upload_f32(m, b.data(), b.size(), &dl.bias));
+        }
+        m->weight_bytes += dl.qkv.bytes() + dl.o.bytes() + dl.gateup.bytes() + dl.down.bytes() +
+                           2.0 * m->D * 4 + (dl.bias ? m->nqkv * 4.0 : 0.0);
+    }
+    // LM head (Q8 [V][D] blocks, or fp32 [D][V]) and embedding
+    {
+        const int saved = m->wtype;
+        m->wtype = head_q8 ? W_Q8 : W_F32;
+        TRY(upload_wmat(m, d->lm_head, m->V, m->D, m->head, m->V, 0, 1, staging, stage));
+        m->wtype = saved;
+        m->weight_bytes += m->head.bytes();
+    }
+    if (d->embed.f != nullptr) {
+        TRY(upload_f32(m, d->embed.f, (size_t)m->V * m->D, &m->embed_f));
+    } else if (d->embed.q != nullptr && d->embed.qt == JYC_Q8_0) {
+        if (d->embed.q == d->lm_head.q) {
+            m->embed_q = m->head;  // tied: one device copy
+        } else {
+            const int saved = m->wtype;
+            m->wtype = W_Q8;
+            TRY(upload_wmat(m, d->embed, m->V, m->D, m->embed_q, m->V, 0, 1, staging, stage));
+            m->wtype = saved;
+        }
+    } else {
+        set_error("embedding must be fp32 or Q8_0");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    m->weight_bytes += (m->embed_f ? 4.0 * m->D : m->D * 34.0 / 32.0) + 4.0 * m->D;  // row + final norm
+    TRY(upload_f32(m, d->final_rms_weight, m->D, &m->final_norm));
+    const size_t half = (size_t)m->max_seq * (m->hd / 2);
+    TRY(upload_f32(m, d->cos_table, half, &m->cos_t));
+    TRY(upload_f32(m, d->sin_table, half, &m->sin_t));
+
+    // KV cache and scratch
+    const size_t kvn = (size_t)m->L * m->KV * m->max_seq;
+    TRY(m->alloc(&m->k8, kvn * m->hd));
+    TRY(m->alloc(&m->v8, kvn * m->hd));
+    TRY(m->alloc(&m->ks, kvn));
+    TRY(m->alloc(&m->vs, kvn));
+    JYC_CUDA(cudaMemsetAsync(m->k8, 0, kvn * m->hd, m->stream));
+    JYC_CUDA(cudaMemsetAsync(m->v8, 0, kvn * m->hd, m->stream));
+    JYC_CUDA(cudaMemsetAsync(m->ks, 0, kvn * 4, m->stream));
+    JYC_CUDA(cudaMemsetAsync(m->vs, 0, kvn * 4, m->stream));
+    TRY(m->alloc(&m->X, (size_t)kMT * m->D));
+    TRY(m->alloc(&m->qkv, (size_t)kMT * m->nqkv));
+    TRY(m->alloc(&m->attn, (size_t)kMT * m->q_dim));
+    TRY(m->alloc(&m->h, (size_t)kMT * m->F));
+    TRY(m->alloc(&m->logits, (size_t)m->V));
+    TRY(m->alloc(&m->tmp, (size_t)m->D));
+    TRY(m->alloc(&m->q8, (size_t)kMT * m->q_dim));
+    TRY(m->alloc(&m->qsc, (size_t)kMT * m->H));
+    // split-K plan: ~2 CTAs per SM over the kv heads, chunks of >= 64 positions
+    const int target = std::max(1, 296 / m->KV);
+    int chunk = (m->max_seq + target - 1) / target;
+    chunk = std::max(64, (chunk + 63) / 64 * 64);
+    m->chunk = chunk;
+    m->nsplit = (m->max_seq + chunk - 1) / chunk;
+    TRY(m->alloc(&m->part_o, (size_t)kMT * m->H * m->nsplit * m->hd));
+    TRY(m->alloc(&m->part_ml, (size_t)kMT * m->H * m->nsplit * 2));
+    TRY(m->alloc(&m->arrive, (size_t)m->KV));
+    JYC_CUDA(cudaMemsetAsync(m->arrive, 0, m->KV * sizeof(unsigned int), m->stream));
+    TRY(m->alloc(&m->st, 1));
+    JYC_CUDA(cudaMemsetAsync(m->st, 0, sizeof(DevState), m->stream));
+    TRY(m->alloc(&m->tokens, (size_t)m->max_seq + 1));
+    JYC_CUDA(cudaStreamSynchronize(m->stream));
+    return JYC_OK;
+}
+
+// One transformer stack pass over `rows` (<= kMT) tokens at pos (host constant
+// or device state), then nothing else. Layer order = transformer_layer.
+int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
+    DevState* guard = pos.st ? m->st : nullptr;
+    TRY(launch_embed(m->tokens, pos, rows, m->embed_f, m->embed_q.qs, m->embed_q.d, m->D, m->X, s));
+    for (int l = 0; l < m->L; l++) {
+        const DevLayer& ly = m->layers[l];
+        GemvArgs g{};
+        g.m = rows; g.eps = 1e-5f; g.st = guard;
+        // RMSNorm -> fused Q|K|V GEMV (+ bias)
+        g.x = m->X; g.ldx = m->D; g.n = m->nqkv; g.k = m->D;
+        g.qs = ly.qkv.qs; g.d = ly.qkv.d; g.wt = ly.qkv.f; g.norm_w = ly.rms1;
+        g.y = m->qkv; g.ldy = m->nqkv; g.bias = ly.bias;
+        TRY(launch_gemv(g, m->wtype, ly.bias ? EPI_BIAS : EPI_STORE, s));
+        // RoPE(Q,K) + int8 quantisation of Q, K, V; K/V appended to the cache
+        RopeQuantArgs rq{};
+        rq.q = m->qkv; rq.k = m->qkv + m->q_dim; rq.v = m->qkv + m->q_dim + m->kv_dim;
+        rq.ldq = m->nqkv; rq.rows = rows; rq.H = m->H; rq.KV = m->KV; rq.hd = m->hd;
+        rq.cos_t = m->cos_t; rq.sin_t = m->sin_t; rq.q8 = m->q8; rq.qsc = m->qsc;
+        rq.kv = m->kv_layer(l); rq.pos = pos;
+        TRY(launch_rope_quant(rq, s));
+        // int8-KV attention (split-K flash decoding)
+        AttnArgs at{};
+        at.q8 = m->q8; at.qsc = m->qsc; at.kv = m->kv_layer(l);
+        at.rows = rows; at.H = m->H; at.KV = m->KV; at.hd = m->hd;
+        at.chunk = m->chunk; at.nsplit = m->nsplit;
+        at.scale = 1.0f / sqrtf((float)m->hd);
+        at.part_o = m->part_o; at.part_ml = m->part_ml; at.arrive = m->arrive;
+        at.out = m->attn; at.ldo = m->q_dim; at.pos = pos;
+        TRY(launch_attention(at, s));
+        // O projection + residual
+        g = GemvArgs{};
+        g.m = rows; g.eps = 1e-5f; g.st = guard;
+        g.x = m->attn; g.ldx = m->q_dim; g.n = m->D; g.k = m->q_dim;
+        g.qs = ly.o.qs; g.d = ly.o.d; g.wt = ly.o.f; g.y = m->X; g.ldy = m->D;
+        TRY(launch_gemv(g, m->wtype, EPI_RESID, s));
+        // RMSNorm -> gate|up GEMV -> SwiGLU
+        g = GemvArgs{};
+        g.m = rows; g.eps = 1e-5f; g.st = guard;
+        g.x = m->X; g.ldx = m->D; g.n = 2 * m->F; g.k = m->D;
+        g.qs = ly.gateup.qs; g.d = ly.gateup.d; g.wt = ly.gateup.f; g.norm_w = ly.rms2;
+        g.y = m->h; g.ldy = m->F;
+        TRY(launch_gemv(g, m->wtype, EPI_SWIGLU, s));
+        // down projection + residual
+        g = GemvArgs{};
+        g.m = rows; g.eps = 1e-5f; g.st = guard;
+        g.x = m->h; g.ldx = m->F; g.n = m->D; g.k = m->F;
+        g.qs = ly.down.qs; g.d = ly.down.d; g.wt = ly.down.f; g.y = m->X; g.ldy = m->D;
+        TRY(launch_gemv(g, m->wtype, EPI_RESID, s));
+    }
+    return JYC_OK;
+}
+
+// Final RMSNorm of row `row` + LM head GEMV + argmax; the last CTA appends the
+// token to the device buffer and advances the state.
+int run_head(jyc_model* m, int row, cudaStream_t s) {
+    GemvArgs g{};
+    g.m = 1; g.eps = 1e-5f; g.st = m->st; g.tokens = m->tokens;
+    g.x = m->X + (size_t)row * m->D; g.ldx = m->D; g.n = m->V; g.k = m->D;
+    g.qs = m->head.qs; g.d = m->head.d; g.wt = m->head.f; g.norm_w = m->final_norm;
+    g.y = m->logits; g.ldy = m->V;
+    return launch_gemv(g, m->head.f ? W_F32 : W_Q8, EPI_ARGMAX, s);
+}
+
+// Forward of n tokens already in m->tokens[start..start+n) in chunks of kMT,
+// then the head on the last row (state must hold len == start+n).
+int run_prefill(jyc_model* m, int start, int n, cudaStream_t s) {
+    int last_rows = 0;
+    for (int c = 0; c < n; c += kMT) {
+        const int rows = std::min(kMT, n - c);
+        TRY(run_layers(m, rows, PosSrc{nullptr, start + c}, s));
+        last_rows = rows;
+    }
+    return run_head(m, last_rows - 1, s);
+}
+
+int ensure_step_graph(jyc_model* m) {
+    if (m->step_exec) return JYC_OK;
+    cudaGraph_t graph = nullptr;
+    JYC_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int r = run_layers(m, 1, PosSrc{m->st, 0}, m->stream);
+    if (r == JYC_OK) r = run_head(m, 0, m->stream);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+    if (r != JYC_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return r;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&m->step_exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    return JYC_OK;
+}
+
+int kernels_per_step(const jyc_model* m) { return 1 + m->L * 6 + 1; }
+
+}  // namespace
+
+extern "C" {
+
+JYC_API jyc_model* jyc_model_create(const jyc_model_desc* desc) {
+    clear_error();
+    jyc_model* m = new (std::nothrow) jyc_model();
+    if (!m) {
+        set_error("out of host memory");
+        return nullptr;
+    }
+    if (build_model(m, desc) != JYC_OK) {
+        delete m;
+        return nullptr;
+    }
+    return m;
+}
+
+JYC_API void jyc_model_free(jyc_model* m) { delete m; }
+
+JYC_API double jyc_model_weight_bytes_per_token(const jyc_model* m) { return m ? m->weight_bytes : 0.0; }
+
+JYC_API double jyc_model_kv_bytes_per_token(const jyc_model* m, int ctx) {
+    if (!m) return 0.0;
+    // int8 K and V rows + one fp32 scale each, per layer, kv head and position
+    return (double)m->L * m->KV * ctx * (2.0 * m->hd + 8.0);
+}
+
+JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_pos, float* logits,
+                               float* hidden_out) {
+    clear_error();
+    if (!m || !ids || seq <= 0 || start_pos < 0) return arg_error("forward_logits: bad arguments");
+    if ((long long)start_pos + seq > m->max_seq) {
+        set_error("forward: KV cache capacity exceeded");
+        return JYC_ERR_KV_OOM;
+    }
+    for (int i = 0; i < seq; i++)
+        if (ids[i] < 0 || ids[i] >= m->V) return arg_error("forward_logits: token id out of range");
+    cudaStream_t s = m->stream;
+    JYC_CUDA(cudaMemcpyAsync(m->tokens + start_pos, ids, seq * sizeof(int), cudaMemcpyHostToDevice, s));
+    TRY(launch_set_state(m->st, start_pos + seq, 1 << 30, m->max_seq + 1, nullptr, 0, s));
+    TRY(run_prefill(m, start_pos, seq, s));
+    if (hidden_out) {
+        const int last = (seq - 1) % kMT;
+        TRY(launch_rmsnorm(m->X + (size_t)last * m->D, m->tmp, m->final_norm, 1, m->D, 1e-5f, s));
+        JYC_CUDA(cudaMemcpyAsync(hidden_out, m->tmp, m->D * sizeof(float), cudaMemcpyDeviceToHost, s));
+    }
+    if (logits)
+        JYC_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)m->V * sizeof(float), cudaMemcpyDeviceToHost, s));
+    JYC_CUDA(cudaStreamSynchronize(s));
+    return JYC_OK;
+}
+
+JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos, int8_t* k, float* ks, int8_t* v,
+                              float* vs) {
+    clear_error();
+    if (!m || layer < 0 || layer >= m->L || npos < 0 || npos > m->max_seq)
+        return arg_error("read_kv: bad arguments");
+    const KVView kv = m->kv_layer(layer);
+    std::vector<int8_t> kb((size_t)m->KV * m->max_seq * m->hd), vb(kb.size());
+    std::vector<float> ksb((size_t)m->KV * m->max_seq), vsb(ksb.size());
+    JYC_CUDA(cudaMemcpy(kb.data(), kv.k, kb.size(), cudaMemcpyDeviceToHost));
+    JYC_CUDA(cudaMemcpy(vb.data(), kv.v, vb.size(), cudaMemcpyDeviceToHost));
+    JYC_CUDA(cudaMemcpy(ksb.data(), kv.ks, ksb.size() * 4, cudaMemcpyDeviceToHost));
+    JYC_CUDA(cudaMemcpy(vsb.data(), kv.vs, vsb.size() * 4, cudaMemcpyDeviceToHost));
+    for (int p = 0; p < npos; p++)
+        for (int h = 0; h < m->KV; h++) {
+            const size_t src = ((size_t)h * m->max_seq + p);
+            const size_t dst = (size_t)p * m->KV + h;
+            std::memcpy(k + dst * m->hd, kb.data() + src * m->hd, m->hd);
+            std::memcpy(v + dst * m->hd, vb.data() + src * m->hd, m->hd);
+            ks[dst] = ksb[src];
+            vs[dst] = vsb[src];
+        }
+    return JYC_OK;
+}
+
+JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, const int* eos_ids,
+                         int num_eos, int max_new_tokens, float temperature, int* out_ids,
+                         float repetition_penalty, jyc_token_cb cb, void* cb_ud) {
+    clear_error();
+    if (!m || !out_ids) return arg_error("generate: null model or output");
+    if (prompt_len <= 0 || prompt_len > m->max_seq || !prompt_ids) return 0;
+    for (int i = 0; i < prompt_len; i++) out_ids[i] = prompt_ids[i];
+    if (max_new_tokens <= 0) return prompt_len;
+    if (temperature > 0.0f || repetition_penalty != 1.0f) {
+        set_error("generate: sampling (temperature > 0) and repetition_penalty != 1 are not built yet on the B200 path");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    if (num_eos < 0 || num_eos > 8 || (num_eos > 0 && !eos_ids)) return arg_error("generate: at most 8 EOS ids");
+    for (int i = 0; i < prompt_len; i++)
+        if (prompt_ids[i] < 0 || prompt_ids[i] >= m->V) return arg_error("generate: prompt id out of range");
+    if (prompt_len >= m->max_seq) return prompt_len;  // the loop condition len < max_seq fails at once
+    cudaStream_t s = m->stream;
+    TRY(ensure_step_graph(m));
+    JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids, prompt_len * sizeof(int), cudaMemcpyHostToDevice, s));
+    TRY(launch_set_state(m->st, prompt_len, max_new_tokens, m->max_seq, eos_ids, num_eos, s));
+    TRY(run_prefill(m, 0, prompt_len, s));
+    // decode: one graph replay per step; the state guard turns surplus steps into no-ops
+    const int max_steps = std::min(max_new_tokens, m->max_seq - prompt_len) - 1;
+    int len = prompt_len;
+    if (!cb) {
+        for (int i = 0; i < max_steps; i++) {
+            JYC_CUDA(cudaGraphLaunch(m->step_exec, s));
+            count_launch(kernels_per_step(m));
+        }
+        DevState hs;
+        JYC_CUDA(cudaMemcpyAsync(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
+        JYC_CUDA(cudaStreamSynchronize(s));
+        len = hs.len;
+        JYC_CUDA(cudaMemcpy(out_ids + prompt_len, m->tokens + prompt_len,
+                            (size_t)(len - prompt_len) * sizeof(int), cudaMemcpyDeviceToHost));
+        return len;
+    }
+    // with a callback: run blocks of steps, hand each new token to cb in order,
+    // stop (and drop any tokens computed past it) when cb asks to.
+    int done_steps = 0;
+    int block = 1;
+    while (true) {
+        DevState hs;
+        JYC_CUDA(cudaMemcpyAsync(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
+        JYC_CUDA(cudaStreamSynchronize(s));
+        JYC_CUDA(cudaMemcpy(out_ids + len, m->tokens + len, (size_t)(hs.len - len) * sizeof(int),
+                            cudaMemcpyDeviceToHost));
+        for (int i = len; i < hs.len; i++) {
+            if (cb(out_ids[i], cb_ud)) return i + 1;
+            bool stop = false;
+            for (int e = 0; e < num_eos; e++)
+                if (out_ids[i] == eos_ids[e]) stop = true;
+            if (stop) return i + 1;
+        }
+        len = hs.len;
+        if (!hs.active || done_steps >= max_steps) return len;
+        const int n = std::min(block, max_steps - done_steps);
+        for (int i = 0; i < n; i++) {
+            JYC_CUDA(cudaGraphLaunch(m->step_exec, s));
+            count_launch(kernels_per_step(m));
+        }
+        done_steps += n;
+        block = std::min(block * 2, 32);
+    }
+}
+
+JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prompt_len, void* stream) {
+    clear_error();
+    if (!m || !prompt_ids_dev || prompt_len <= 0 || prompt_len >= m->max_seq)
+        return arg_error("prefill_device: bad arguments");
+    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids_dev, prompt_len * sizeof(int), cudaMemcpyDeviceToDevice, s));
+    TRY(launch_set_state(m->st, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s));
+    return run_prefill(m, 0, prompt_len, s);
+}
+
+JYC_API int jyc_model_rewind(jyc_model* m, int len, void* stream) {
+    clear_error();
+    if (!m || len <= 0 || len >= m->max_seq) return arg_error("rewind: bad length");
+    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    return launch_set_state(m->st, len, 1 << 30, m->max_seq, nullptr, 0, s);
+}
+
+JYC_API int jyc_decode_device(jyc_model* m, int n_steps, void* stream) {
+    clear_error();
+    if (!m || n_steps < 0) return arg_error("decode_device: bad arguments");
+    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    TRY(ensure_step_graph(m));
+    for (int i = 0; i < n_steps; i++) {
+        JYC_CUDA(cudaGraphLaunch(m->step_exec, s));
+        count_launch(kernels_per_step(m));
+    }
+    return JYC_OK;
+}
+
+JYC_API int jyc_model_kernels_per_step(const jyc_model* m) { return m ? kernels_per_step(m) : 0; }
+
+JYC_API int* jyc_model_tokens_device(jyc_model* m) { return m ? m->tokens : nullptr; }
+
+JYC_API int jyc_model_length(jyc_model* m, void* stream) {
+    if (!m) return arg_error("model_length: null model");
+    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    DevState hs;
+    JYC_CUDA(cudaMemcpyAsync(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
+    JYC_CUDA(cudaStreamSynchronize(s));
+    return hs.len;
+}
+
+}  // extern "C"

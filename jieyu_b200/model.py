@@ -1,0 +1,352 @@
+"""Host-side mirror of the reference's model objects, backed by libjieyu_b200.
+
+* ``Config``      — hyper-parameters (the reference's ModelInfo / ModelRefs fields).
+* ``HostWeights`` — host buffers in the reference's own layouts (Q8_0 blocks
+  [out][in/32]x34 B, fp32 [in][out], fp32 norms/biases) plus the
+  ``LayerWeights`` / ``jyc_model_desc`` structs that point at them, i.e. what
+  ``bind_model`` produces (libs/model_libs/pipeline.h:63-153).
+* ``DeviceModel`` — the uploaded model: ``generate`` mirrors ``generate()``
+  (libs/model_libs/generate.h:90-112) and runs entirely on the GPU.
+
+Synthetic weights are a pure integer function of (seed, stream, index)
+(``jyc_synth_*``), so every process — and the CPU checker — sees the same bytes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, replace
+from typing import Callable, Optional
+
+import numpy as np
+
+from . import _capi
+from ._capi import JYC_Q8_0, LayerWeights, ModelDesc, WMat, check
+
+
+@dataclass(frozen=True)
+class Config:
+    name: str
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    inter: int
+    vocab: int
+    theta: float
+    wtype: str = "q8"          # linear weights: "q8" (Q8_0) or "f32"
+    embed: str = "f32"         # "f32", "q8" (separate) or "tied" (Q8_0, = LM head)
+    qkv_bias: bool = False
+    max_seq: int = 512
+    prompt_len: int = 32
+    new_tokens: int = 128
+    std: float = 0.02
+
+    @property
+    def q_dim(self) -> int:
+        return self.heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.kv_heads * self.head_dim
+
+
+# BASELINE.json configs (shapes as stated there).
+CONFIGS = {
+    # tiny Llama-style, Q8_0 linears, fp32 embedding/norms, max context 512
+    "c0": Config("c0_tiny", 512, 8, 8, 4, 64, 1376, 32000, 1e4, "q8", "f32", False, 512, 32, 128),
+    # Qwen2.5-0.5B shape, tied Q8_0 embedding, QKV bias, theta 1e6
+    "c1": Config("c1_qwen2.5_0.5b", 896, 24, 14, 2, 64, 4864, 151936, 1e6, "q8", "tied", True,
+                 1024, 512, 256),
+    # Llama-3.2-1B shape (Q8_0 and fp32 variants)
+    "c2": Config("c2_llama3.2_1b", 2048, 16, 32, 8, 64, 8192, 128256, 5e5, "q8", "q8", False,
+                 4352, 2048, 128),
+    "c2f": Config("c2_llama3.2_1b_f32", 2048, 16, 32, 8, 64, 8192, 128256, 5e5, "f32", "f32",
+                  False, 4352, 2048, 128),
+    # Llama-3-8B shape
+    "c3": Config("c3_llama3_8b", 4096, 32, 32, 8, 128, 14336, 128256, 5e5, "q8", "q8", False,
+                 4352, 4096, 128),
+}
+
+# Stream ids of the synthetic generator (one per tensor).
+_SLOTS = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6, "bq": 7, "bk": 8, "bv": 9}
+STREAM_EMBED = 1 << 20
+STREAM_HEAD = (1 << 20) + 1
+STREAM_PROMPT = 1 << 21
+
+
+def _stream(layer: int, slot: str) -> int:
+    return layer * 16 + _SLOTS[slot]
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def synth_q8(seed: int, stream: int, rows: int, k: int, std: float = 0.02) -> np.ndarray:
+    out = np.empty(rows * (k // 32) * 34, dtype=np.uint8)
+    check(_capi.load().jyc_synth_q8_0(seed, stream, std, _ptr(out), rows, k))
+    return out
+
+
+def synth_f32(seed: int, stream: int, n: int, std: float = 0.02) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    check(_capi.load().jyc_synth_f32(seed, stream, std, _ptr(out), n))
+    return out
+
+
+def synth_ids(seed: int, stream: int, vocab: int, n: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.int32)
+    check(_capi.load().jyc_synth_ids(seed, stream, vocab, _ptr(out), n))
+    return out
+
+
+def quantize_q8(x: np.ndarray, rows: int, k: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(rows * (k // 32) * 34, dtype=np.uint8)
+    check(_capi.load().jyc_quantize_q8_0(_ptr(x), _ptr(out), rows, k))
+    return out
+
+
+def rope_table(max_seq: int, head_dim: int, theta: float):
+    """cos/sin tables exactly as RoPETable::init (libs/date_libs/date.h:52-66)."""
+    half = head_dim // 2
+    c = np.empty(max_seq * half, dtype=np.float32)
+    s = np.empty(max_seq * half, dtype=np.float32)
+    check(_capi.load().jyc_rope_table(max_seq, head_dim, theta, _ptr(c), _ptr(s)))
+    return c, s
+
+
+def prompt_ids(cfg: Config, seed: int = 1234, index: int = 0, n: Optional[int] = None) -> np.ndarray:
+    """Uniform-random prompt ids in [0, vocab) (seeded)."""
+    return synth_ids(seed, STREAM_PROMPT + index, cfg.vocab, cfg.prompt_len if n is None else n)
+
+
+class HostWeights:
+    """Host tensors in the reference layouts + the descriptor pointing at them."""
+
+    def __init__(self, cfg: Config, tensors: dict, cos: np.ndarray, sin: np.ndarray):
+        self.cfg = cfg
+        self.t = tensors          # keeps every buffer alive
+        self.cos, self.sin = cos, sin
+        self._build_desc()
+
+    # -- constructors -------------------------------------------------------
+    @classmethod
+    def synthetic(cls, cfg: Config, seed: int = 1234) -> "HostWeights":
+        D, F, L = cfg.hidden, cfg.inter, cfg.layers
+        t: dict = {}
+        ones = np.ones(D, dtype=np.float32)
+        for l in range(L):
+            t[f"rms1.{l}"] = ones
+            t[f"rms2.{l}"] = ones
+            shapes = {"q": (cfg.q_dim, D), "k": (cfg.kv_dim, D), "v": (cfg.kv_dim, D),
+                      "o": (D, cfg.q_dim), "gate": (F, D), "up": (F, D), "down": (D, F)}
+            for name, (out, inn) in shapes.items():
+                if cfg.wtype == "q8":
+                    t[f"{name}.{l}"] = synth_q8(seed, _stream(l, name), out, inn, cfg.std)
+                else:  # fp32 [in][out]
+                    t[f"{name}.{l}"] = synth_f32(seed, _stream(l, name), inn * out, cfg.std)
+            if cfg.qkv_bias:
+                t[f"bq.{l}"] = synth_f32(seed, _stream(l, "bq"), cfg.q_dim, cfg.std)
+                t[f"bk.{l}"] = synth_f32(seed, _stream(l, "bk"), cfg.kv_dim, cfg.std)
+                t[f"bv.{l}"] = synth_f32(seed, _stream(l, "bv"), cfg.kv_dim, cfg.std)
+        V = cfg.vocab
+        if cfg.embed == "tied":
+            t["head"] = synth_q8(seed, STREAM_HEAD, V, D, cfg.std)
+        else:
+            if cfg.wtype == "q8":
+                t["head"] = synth_q8(seed, STREAM_HEAD, V, D, cfg.std)
+            else:
+                t["head"] = synth_f32(seed, STREAM_HEAD, D * V, cfg.std)  # [hidden][vocab]
+            if cfg.embed == "q8":
+                t["embed"] = synth_q8(seed, STREAM_EMBED, V, D, cfg.std)
+            else:
+                t["embed"] = synth_f32(seed, STREAM_EMBED, V * D, cfg.std)
+        t["final_norm"] = ones
+        cos, sin = rope_table(cfg.max_seq, cfg.head_dim, cfg.theta)
+        return cls(cfg, t, cos, sin)
+
+    @classmethod
+    def bind_test_kat(cls) -> "HostWeights":
+        """The fp32 model of the reference's check_bind_weights
+        (libs/text/text.h:485-541 gen_weights::build with make_weights' lm_head,
+        text.h:604-610): pseudo(i) = ((i*37)%19-9)/8, RoPE from bind_model's
+        RoPETable::init with theta 10000."""
+        cfg = Config("kat_bind", 8, 2, 2, 1, 4, 16, 24, 10000.0, "f32", "f32", False, 8, 3, 3)
+
+        def pseudo(n: int, off: int, mul: float) -> np.ndarray:
+            i = np.arange(n, dtype=np.int64) + off
+            return (((i * 37) % 19 - 9).astype(np.float32) / np.float32(8.0)) * np.float32(mul)
+
+        D, qd, kvd, F, V = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.inter, cfg.vocab
+        t = {}
+        for l in range(cfg.layers):
+            t[f"rms1.{l}"] = np.float32(1.0) + pseudo(D, 3 * l, 0.25)
+            t[f"rms2.{l}"] = np.float32(1.0) + pseudo(D, 5 * l, 0.25)
+            t[f"q.{l}"] = pseudo(D * qd, 7 * l, 0.5)
+            t[f"k.{l}"] = pseudo(D * kvd, 11 * l, 0.5)
+            t[f"v.{l}"] = pseudo(D * kvd, 13 * l, 0.5)
+            t[f"o.{l}"] = pseudo(qd * D, 17 * l, 0.5)
+            t[f"gate.{l}"] = pseudo(D * F, 19 * l, 0.5)
+            t[f"down.{l}"] = pseudo(F * D, 23 * l, 0.5)
+            t[f"up.{l}"] = pseudo(D * F, 29 * l, 0.5)
+        t["embed"] = pseudo(V * D, 101, 0.5)
+        t["head"] = pseudo(D * V, 211, 2.0)
+        t["final_norm"] = np.float32(1.0) + pseudo(D, 307, 0.25)
+        cos, sin = rope_table(cfg.max_seq, cfg.head_dim, cfg.theta)
+        return cls(cfg, t, cos, sin)
+
+    @classmethod
+    def shift_demo_kat(cls) -> "HostWeights":
+        """The converter's demo model used by check_pipeline
+        (libs/model_libs/converter.h:422-503): identity embedding for byte ids,
+        zero attention/FFN, lm_head[v][v-1] = 1 (stored [in][out] after
+        conversion), so greedy decoding emits id+1. max_seq = 1024 as the
+        C ABI derives it from max_position_embeddings (main.hpp:64-67)."""
+        cfg = Config("kat_shift", 256, 2, 8, 2, 32, 64, 259, 10000.0, "f32", "f32", False, 1024, 8, 16)
+        D, qd, kvd, F, V = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.inter, cfg.vocab
+        t = {}
+        ones = np.ones(D, dtype=np.float32)
+        for l in range(cfg.layers):
+            t[f"rms1.{l}"] = ones
+            t[f"rms2.{l}"] = ones
+            for name, n in (("q", D * qd), ("k", D * kvd), ("v", D * kvd), ("o", qd * D),
+                            ("gate", D * F), ("up", D * F), ("down", F * D)):
+                t[f"{name}.{l}"] = np.zeros(n, dtype=np.float32)
+        emb = np.zeros((V, D), dtype=np.float32)
+        for v in range(256):
+            emb[v, v] = 1.0
+        head = np.zeros((D, V), dtype=np.float32)  # [in][out]
+        for v in range(1, 256):
+            head[v - 1, v] = 1.0
+        t["embed"] = emb.reshape(-1)
+        t["head"] = head.reshape(-1)
+        t["final_norm"] = ones
+        cos, sin = rope_table(cfg.max_seq, cfg.head_dim, cfg.theta)
+        return cls(cfg, t, cos, sin)
+
+    # -- descriptor ---------------------------------------------------------
+    def _wmat(self, key: str) -> WMat:
+        a = self.t[key]
+        if a.dtype == np.uint8:
+            return WMat(None, None, _ptr(a), JYC_Q8_0)
+        return WMat(_ptr(a), None, None, 0)
+
+    def _build_desc(self) -> None:
+        cfg = self.cfg
+        L = cfg.layers
+        self.layer_arr = (LayerWeights * L)()
+        for l in range(L):
+            lw = self.layer_arr[l]
+            lw.rms1_weight = _ptr(self.t[f"rms1.{l}"])
+            lw.rms2_weight = _ptr(self.t[f"rms2.{l}"])
+            lw.Wq, lw.Wk, lw.Wv, lw.Wo = (self._wmat(f"{n}.{l}") for n in ("q", "k", "v", "o"))
+            lw.W1, lw.W2, lw.W3 = (self._wmat(f"{n}.{l}") for n in ("gate", "down", "up"))
+            for b in ("bq", "bk", "bv"):
+                setattr(lw, b, _ptr(self.t[f"{b}.{l}"]) if f"{b}.{l}" in self.t else None)
+        d = ModelDesc()
+        d.layers = self.layer_arr
+        d.num_layers = L
+        d.lm_head = self._wmat("head")
+        d.embed = self._wmat("head") if cfg.embed == "tied" else self._wmat("embed")
+        d.final_rms_weight = _ptr(self.t["final_norm"])
+        d.cos_table = _ptr(self.cos)
+        d.sin_table = _ptr(self.sin)
+        d.max_seq = cfg.max_seq
+        d.vocab_size = cfg.vocab
+        d.hidden = cfg.hidden
+        d.num_heads = cfg.heads
+        d.num_kv_heads = cfg.kv_heads
+        d.head_dim = cfg.head_dim
+        d.intermediate = cfg.inter
+        self.desc = d
+
+    def weight_bytes_per_token(self) -> float:
+        """Algorithmic weight bytes one decode token reads (Q8_0: 34 B / 32)."""
+        cfg = self.cfg
+        D, F = cfg.hidden, cfg.inter
+        per = 34.0 / 32.0 if cfg.wtype == "q8" else 4.0
+        lin = (cfg.q_dim + 2 * cfg.kv_dim) * D + D * cfg.q_dim + 3 * F * D
+        b = cfg.layers * (lin * per + 2 * D * 4 + (cfg.q_dim + 2 * cfg.kv_dim) * 4 * cfg.qkv_bias)
+        head_per = 34.0 / 32.0 if self.t["head"].dtype == np.uint8 else 4.0
+        b += cfg.vocab * D * head_per + 4 * D
+        b += D * (34.0 / 32.0 if cfg.embed in ("q8", "tied") else 4.0)
+        return b
+
+
+class DeviceModel:
+    """A model resident in HBM (jyc_model_create uploads once)."""
+
+    def __init__(self, hw: HostWeights):
+        self.hw = hw
+        self.cfg = hw.cfg
+        self.lib = _capi.load()
+        h = self.lib.jyc_model_create(C.byref(hw.desc))
+        if not h:
+            raise _capi.JycError(-1, _capi.last_error())
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.jyc_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def generate(self, prompt: np.ndarray, max_new: int, eos: Optional[list] = None,
+                 temperature: float = 0.0, repetition_penalty: float = 1.0,
+                 cb: Optional[Callable[[int], bool]] = None) -> np.ndarray:
+        """generate() contract: returns out_ids[:len] (prompt + new tokens)."""
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(self.cfg.max_seq + 1, dtype=np.int32)
+        e = np.ascontiguousarray(eos if eos else [0], dtype=np.int32)
+        ccb = _capi.TOKEN_CB(lambda i, ud: 1 if cb(i) else 0) if cb else _capi.TOKEN_CB()
+        n = check(self.lib.jyc_generate(self.h, _ptr(prompt), len(prompt), _ptr(e),
+                                        len(eos) if eos else 0, max_new, temperature, _ptr(out),
+                                        repetition_penalty, ccb, None))
+        return out[:n].copy()
+
+    def forward_logits(self, ids: np.ndarray, start_pos: int, want_hidden: bool = False):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        logits = np.empty(self.cfg.vocab, dtype=np.float32)
+        hid = np.empty(self.cfg.hidden, dtype=np.float32) if want_hidden else None
+        check(self.lib.jyc_forward_logits(self.h, _ptr(ids), len(ids), start_pos, _ptr(logits),
+                                          _ptr(hid) if hid is not None else None))
+        return (logits, hid) if want_hidden else logits
+
+    def read_kv(self, layer: int, npos: int):
+        cfg = self.cfg
+        k = np.empty(npos * cfg.kv_dim, dtype=np.int8)
+        v = np.empty_like(k)
+        ks = np.empty(npos * cfg.kv_heads, dtype=np.float32)
+        vs = np.empty_like(ks)
+        check(self.lib.jyc_model_read_kv(self.h, layer, npos, _ptr(k), _ptr(ks), _ptr(v), _ptr(vs)))
+        return k, ks, v, vs
+
+    # device-resident stepping (bench)
+    def prefill_device(self, ids_dev_ptr: int, n: int, stream: int) -> None:
+        check(self.lib.jyc_prefill_device(self.h, ids_dev_ptr, n, stream))
+
+    def decode_device(self, n_steps: int, stream: int) -> None:
+        check(self.lib.jyc_decode_device(self.h, n_steps, stream))
+
+    def rewind(self, length: int, stream: int) -> None:
+        check(self.lib.jyc_model_rewind(self.h, length, stream))
+
+    def length(self, stream: int) -> int:
+        return check(self.lib.jyc_model_length(self.h, stream))
+
+    def tokens_device_ptr(self) -> int:
+        return self.lib.jyc_model_tokens_device(self.h)
+
+    def kernels_per_step(self) -> int:
+        return self.lib.jyc_model_kernels_per_step(self.h)
+
+
+def with_max_seq(cfg: Config, max_seq: int) -> Config:
+    return replace(cfg, max_seq=max_seq)

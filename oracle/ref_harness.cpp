@@ -1,0 +1,222 @@
+/*
+ * ref_harness.cpp — TEST INFRASTRUCTURE ONLY (the checker, never the product).
+ *
+ * Compiles the UNMODIFIED jieyu reference headers (from the reference source
+ * tree, include path given by the Makefile) into oracle/_ref/libjyref.so and
+ * exposes its hot-path functions through a plain C ABI so tests and the CPU
+ * baseline can drive the reference's own code on in-memory weights:
+ *   qmat::matmul_q      libs/matmul_libs/matmul_q.h:134-162
+ *   matmul              libs/matmul_libs/matmul.h:7-76
+ *   rmsnorm             libs/model_libs/rmsnorm/rmsnorm.h:8-78
+ *   RoPETable::init     libs/date_libs/date.h:52-66
+ *   rope_pos            libs/model_libs/rope/rope.h:108-110
+ *   kv_pack_q8          libs/model_libs/attention/attention_q8.h:20-37
+ *   attention_q8        libs/model_libs/attention/attention_q8.h:38-184
+ *   silu                libs/model_libs/silu/silu.h:7-81
+ *   ffn                 libs/model_libs/ffn/ffn.h:7-19
+ *   forward_cached      libs/model_libs/forward.h:47-96
+ *   generate            libs/model_libs/generate.h:90-112
+ * Nothing here changes the reference's arithmetic; the harness only builds
+ * WMat / LayerWeights / __KVcache objects over caller buffers.
+ */
+#define JIEYU_HPP 1
+/* the reference relies on libs.h having pulled these in first (libs/libs.h:15-28) */
+#include <algorithm>
+#include <cmath>
+#include <math.h>
+#include <cstdint>
+#include <cstdlib>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+#include <chrono>
+#if defined(_OPENMP)
+#include <omp.h>
+#endif
+
+#include "date_libs/date.h"
+#include "date_libs/check_cpu.h"
+#include "date_libs/info.h"
+#include "matmul_libs/matmul.h"
+#include "matmul_libs/matmul_q.h"
+#include "model_libs/wmat_kernel.h"
+#include "model_libs/prefetch.h"
+#include "model_libs/silu/silu.h"
+#include "model_libs/rmsnorm/rmsnorm.h"
+#include "model_libs/rope/rope.h"
+#include "model_libs/attention/attention_q8.h"
+#include "model_libs/ffn/ffn.h"
+#include "model_libs/transformer_layer.h"
+#include "model_libs/forward.h"
+#include "model_libs/generate.h"
+
+#include "jieyu_b200.h"
+
+#include <cstddef>
+/* jyc_wmat / jyc_layer_weights must be layout-identical to WMat / LayerWeights. */
+static_assert(sizeof(jyc_wmat) == sizeof(WMat), "WMat layout");
+static_assert(offsetof(jyc_wmat, q) == offsetof(WMat, q), "WMat.q");
+static_assert(offsetof(jyc_wmat, qt) == offsetof(WMat, qt), "WMat.qt");
+static_assert(sizeof(jyc_layer_weights) == sizeof(LayerWeights), "LayerWeights layout");
+static_assert(offsetof(jyc_layer_weights, bq) == offsetof(LayerWeights, bq), "LW.bq");
+static_assert(offsetof(jyc_layer_weights, W3) == offsetof(LayerWeights, W3), "LW.W3");
+
+static thread_local std::string g_err;
+
+static WMat to_wmat(const jyc_wmat& w) {
+    WMat m;
+    m.f = w.f; m.h = w.h; m.q = w.q; m.qt = w.qt;
+    return m;
+}
+
+extern "C" {
+
+const char* jyref_last_error(void) { return g_err.c_str(); }
+
+/* Reads JIEYU_ISA (check_cpu.h:54-68) and fills cpu_can; pins the ISA path. */
+void jyref_init(const char* isa, int threads) {
+    if (isa != nullptr) setenv("JIEYU_ISA", isa, 1);
+    cpu_can.GetCpuCan();
+#if defined(_OPENMP)
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+}
+
+int jyref_threads(void) { return par_threads(); }
+
+void jyref_matmul_q8(const float* a, const void* b, float* c, int m, int n, int k) {
+    qmat::matmul_q(a, b, c, m, n, k, qmat::Q8_0);
+}
+
+void jyref_matmul_f32(int m, int n, int k, const float* A, const float* B, float* C) {
+    matmul(m, n, k, A, B, C);
+}
+
+void jyref_rmsnorm(float* x, float* y, const float* w, int n, float eps) {
+    rmsnorm(x, y, w, n, eps);
+}
+
+void jyref_rope_table(int max_seq, int head_dim, float theta, float* cos_out, float* sin_out) {
+    RoPETable t;
+    t.init(max_seq, head_dim, theta);
+    std::memcpy(cos_out, t.cos.data(), t.cos.size() * sizeof(float));
+    std::memcpy(sin_out, t.sin.data(), t.sin.size() * sizeof(float));
+}
+
+void jyref_rope_pos(float* q, int seq, int start_pos, int heads, int hd,
+                    const float* cos_t, const float* sin_t) {
+    rope_pos(q, seq, start_pos, heads, hd, cos_t, sin_t);
+}
+
+void jyref_kv_pack_q8(const float* src, int8_t* dst, float* sc, int heads, int hd, int n) {
+    kv_pack_q8(src, dst, sc, heads, hd, n);
+}
+
+int jyref_attention_q8(float* Q, float* K, float* V, float* out, int seq, int start_pos,
+                       int H, int KV, int hd, int8_t* kc, float* ks, int8_t* vc, float* vs,
+                       int cap) {
+    try {
+        attention_q8(Q, K, V, out, seq, start_pos, H, KV, hd, __KVq{kc, ks, vc, vs, cap});
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+    return 0;
+}
+
+void jyref_silu(float* x, float* y, int n) { silu(x, y, n); }
+
+void jyref_ffn(float* x, const jyc_wmat* w1, const jyc_wmat* w2, const jyc_wmat* w3,
+               float* out, int seq, int hidden, int inter) {
+    ffn(x, to_wmat(*w1), to_wmat(*w2), to_wmat(*w3), out, seq, hidden, inter);
+}
+
+/* ---- model level: a KV cache object plus teacher-forced forward ------- */
+void* jyref_cache_create(int L, int max_seq, int KV, int hd) {
+    __KVcache* c = new __KVcache();
+    c->init(L, max_seq, KV, hd);
+    return c;
+}
+void jyref_cache_free(void* c) { delete static_cast<__KVcache*>(c); }
+
+/* Reads one layer of the cache in its native layout. */
+void jyref_cache_read(void* cp, int layer, int npos, int8_t* k, float* ks, int8_t* v, float* vs) {
+    __KVcache* c = static_cast<__KVcache*>(cp);
+    const size_t row = (size_t)c->num_kv_heads * c->head_dim;
+    std::memcpy(k, c->k_ptr(layer, 0), (size_t)npos * row);
+    std::memcpy(v, c->v_ptr(layer, 0), (size_t)npos * row);
+    std::memcpy(ks, c->ks_ptr(layer, 0), (size_t)npos * c->num_kv_heads * sizeof(float));
+    std::memcpy(vs, c->vs_ptr(layer, 0), (size_t)npos * c->num_kv_heads * sizeof(float));
+}
+
+/* The step body of generate_cached (generate.h:43-49): embedding rows,
+ * forward_cached, LM head on the last row. */
+int jyref_forward_logits(const jyc_model_desc* d, void* cache, const int* ids, int seq,
+                         int start_pos, float* logits, float* hidden_out) {
+    try {
+        __KVcache& c = *static_cast<__KVcache*>(cache);
+        std::vector<float> X((size_t)seq * d->hidden);
+        const WMat embed = to_wmat(d->embed), head = to_wmat(d->lm_head);
+        for (int i = 0; i < seq; i++)
+            wmat_row(embed, (size_t)ids[i], d->hidden, X.data() + (size_t)i * d->hidden);
+        forward_cached(X.data(), reinterpret_cast<const LayerWeights*>(d->layers), d->num_layers,
+                       d->final_rms_weight, d->cos_table, d->sin_table, seq, start_pos, c,
+                       d->hidden, d->num_heads, d->num_kv_heads, d->head_dim, d->intermediate);
+        const float* last = X.data() + (size_t)(seq - 1) * d->hidden;
+        if (hidden_out) std::memcpy(hidden_out, last, (size_t)d->hidden * sizeof(float));
+        if (logits) matmul_w(head, 1, d->vocab_size, d->hidden, last, logits);
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+    return 0;
+}
+
+struct cb_timer {
+    int count = 0;
+    std::chrono::steady_clock::time_point first, last;
+};
+static bool timing_cb(int, void* ud) {
+    cb_timer* t = static_cast<cb_timer*>(ud);
+    const auto now = std::chrono::steady_clock::now();
+    if (t->count == 0) t->first = now;
+    t->last = now;
+    t->count++;
+    return false;
+}
+
+/* generate() (generate.h:90-112). times (optional, 3 doubles): seconds from
+ * call start to first token, first to last token (the -tokenspeed split,
+ * pipeline.h:356-367), whole call. */
+int jyref_generate(const jyc_model_desc* d, const int* prompt, int prompt_len,
+                   const int* eos, int num_eos, int max_new, float temperature,
+                   int* out_ids, float rep_penalty, double* times) {
+    try {
+        cb_timer t;
+        const auto t0 = std::chrono::steady_clock::now();
+        const int n = generate(prompt, prompt_len, eos, num_eos, to_wmat(d->embed),
+                               to_wmat(d->lm_head),
+                               reinterpret_cast<const LayerWeights*>(d->layers), d->num_layers,
+                               d->final_rms_weight, d->cos_table, d->sin_table, d->max_seq,
+                               max_new, temperature, d->vocab_size, d->hidden, d->num_heads,
+                               d->num_kv_heads, d->head_dim, d->intermediate, out_ids,
+                               rep_penalty, timing_cb, &t);
+        const auto t1 = std::chrono::steady_clock::now();
+        if (times) {
+            using sec = std::chrono::duration<double>;
+            times[0] = t.count ? sec(t.first - t0).count() : sec(t1 - t0).count();
+            times[1] = t.count > 1 ? sec(t.last - t.first).count() : 0.0;
+            times[2] = sec(t1 - t0).count();
+        }
+        return n;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+}  // extern "C"
