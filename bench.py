@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 decode path (driver contract: one JSON line on rank 0).
+
+Workload (Qwen2.5-0.5B shape, synthetic seeded Q8_0
+weights): a 512-token prompt is prefilled once; one bench step = 256 greedy
+batch-1 decode tokens from that context (positions 513..768), every weight
+streamed from HBM (525 MB of weights per token > 126 MB L2). Metric: decode
+tokens/s (device-timed with CUDA events), plus achieved HBM GB/s vs the
+measured peak, prefill tokens/s, the end-to-end number through the C ABI with
+host buffers, and the reference's own CPU path timed on this host.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 (torchrun): independent replicas, one per GPU (the batch-1 decode of
+configs[1] does not shard; no collective on the data path), value = all
+tokens / max-over-ranks time, "scaling": "weak".
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 decode tok/s"
+UNIT = "tok/s"
+PROMPT = 512
+DECODE = 256
+KCLASSES = ["embed", "qkv_gemv", "rope_quant", "attention", "o_proj_gemv", "gate_up_gemv",
+            "down_gemv", "lm_head_gemv_argmax"]
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev_index):
+        self.dev = dev_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def reference_decode_sample(hw, threads, new_tokens=16, prompt_len=16, reps=2):
+    """The reference's own generate() (oracle/_ref: the jieyu headers compiled
+    unmodified) on this host: decode tok/s over a bounded sample."""
+    import numpy as np
+
+    from jieyu_b200.model import prompt_ids
+    from oracle.bind import Reference
+    ref = Reference("fma", threads)
+    pr = prompt_ids(hw.cfg, n=prompt_len)
+    dec_tok, dec_s, tot_s = 0, 0.0, 0.0
+    times = np.zeros(3)
+    for _ in range(reps):
+        out = ref.generate(hw.desc, pr, new_tokens, max_seq=hw.cfg.max_seq, times=times)
+        n_new = len(out) - prompt_len
+        dec_tok += n_new - 1          # first token comes from the prefill pass
+        dec_s += times[1]
+        tot_s += times[2]
+    return dec_tok / dec_s, (reps * new_tokens) / tot_s, ref.lib.jyref_threads()
+
+
+def run_reference_arm(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    from jieyu_b200.model import CONFIGS, HostWeights
+    cfg = CONFIGS["c1"]
+    hw = HostWeights.synthetic(cfg)
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        reference_decode_sample(hw, threads, new_tokens=8, prompt_len=16, reps=1)
+    vals, e2es = [], []
+    t0 = time.time()
+    for _ in range(args.steps):
+        v, e, cores = reference_decode_sample(hw, threads, new_tokens=8, prompt_len=16, reps=1)
+        vals.append(v)
+        e2es.append(e)
+    wall = time.time() - t0
+    value = statistics.mean(vals)
+    sample = ("jieyu reference generate() (oracle/_ref, unmodified headers, JIEYU_ISA=fma, OpenMP) "
+              "on configs[1] weights: 16-token prompt + 8 greedy tokens per step; value = decode "
+              "tokens/s (first->last token, as -tokenspeed)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "configs[1] qwen2.5-0.5b shape, CPU sample",
+                                        "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args):
+    import numpy as np
+    import torch
+
+    from jieyu_b200 import _capi
+    from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    lib = _capi.load()
+    cfg = CONFIGS["c1"]
+    hw = HostWeights.synthetic(cfg)
+    m = DeviceModel(hw)
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    prompt = torch.from_numpy(prompt_ids(cfg)).cuda()
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    with torch.cuda.stream(stream):
+        # prefill once (KV of positions 0..511 stays resident), then timed prefills
+        m.prefill_device(prompt.data_ptr(), PROMPT, s)
+        stream.synchronize()
+        pf_ms = []
+        for _ in range(2):
+            a, b = ev(), ev()
+            a.record(stream)
+            m.prefill_device(prompt.data_ptr(), PROMPT, s)
+            b.record(stream)
+            stream.synchronize()
+            pf_ms.append(a.elapsed_time(b))
+        prefill_tps = PROMPT / (min(pf_ms) / 1e3)
+
+        def step():
+            m.rewind(PROMPT + 1, s)   # prompt + the prefill's token; KV 0..512 resident
+            m.decode_device(DECODE, s)
+
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        barrier()
+        sampler = ClockSampler(local)
+        sampler.start()
+        launches0 = lib.jyc_kernel_launches()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        stream.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        launches = lib.jyc_kernel_launches() - launches0
+        clocks = sampler.stop()
+        ms_local = e0.elapsed_time(e1)
+        assert m.length(s) == PROMPT + 1 + DECODE, "decode did not run every step"
+        ms = max_over_ranks(ms_local)
+        tokens = sum_over_ranks(args.steps * DECODE)
+        value = tokens / (ms / 1e3)
+        ms_per_step = ms / args.steps
+
+        # per-kernel device time of the decode step (event after every kernel)
+        m.rewind(PROMPT + 1, s)
+        kms = (C.c_double * 8)()
+        kl = (C.c_int * 8)()
+        kb = (C.c_double * 8)()
+        _capi.check(lib.jyc_model_profile_decode(m.h, 64, s, kms, kl, kb))
+        stream.synchronize()
+
+    # roofline of the dominant kernel class (HBM-bound GEMV)
+    peak, peak_kind = measured_peaks()
+    shares = {KCLASSES[i]: kms[i] for i in range(8)}
+    total_k = sum(shares.values())
+    dom = max(range(8), key=lambda i: kms[i])
+    per_launch_ms = kms[dom] / max(kl[dom], 1)
+    achieved = kb[dom] / (per_launch_ms / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic_c1_decode.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get(KCLASSES[dom])
+    weight_bytes = hw.weight_bytes_per_token()
+    kv_bytes = float(lib.jyc_model_kv_bytes_per_token(m.h, PROMPT + 1 + DECODE // 2))
+    step_gbs = (weight_bytes + kv_bytes) / (ms_per_step / DECODE / 1e3) / 1e9
+
+    # end to end through the C ABI (jyc_generate) with host buffers
+    pin_prompt = torch.from_numpy(prompt_ids(cfg)).pin_memory()
+    pin_out = torch.zeros(cfg.max_seq + 1, dtype=torch.int32).pin_memory()
+    e = np.zeros(1, np.int32)
+    cb = _capi.TOKEN_CB()
+    def gen():
+        n = lib.jyc_generate(m.h, pin_prompt.data_ptr(), PROMPT, e.ctypes.data, 0, DECODE, 0.0,
+                             pin_out.data_ptr(), 1.0, cb, None)
+        return _capi.check(n)
+    gen()
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    e2e_steps = max(1, min(args.steps, 3))
+    for _ in range(e2e_steps):
+        n = gen()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    assert n == PROMPT + DECODE
+    e2e_value = sum_over_ranks(e2e_steps * DECODE) / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        dec, _, cores = reference_decode_sample(hw, threads)
+        cpu = {"value": dec, "unit": UNIT, "cores": cores, "kind": "reference",
+               "sample": "jieyu reference generate() (oracle/_ref, unmodified headers, "
+                         "JIEYU_ISA=fma) on the configs[1] weights, 16-token prompt + 16 greedy "
+                         "tokens, x2; decode tok/s first->last token"}
+
+    m.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "configs[1] Qwen2.5-0.5B shape (Q8_0, tied embedding, QKV bias): "
+                               "256 greedy decode tokens after a 512-token prompt, batch 1",
+                   "model": cfg.name, "global_batch": world, "seq_len": PROMPT + DECODE,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (525 MB of weights per token vs 126 MB L2)"},
+        "hbm": {"gbs_per_step": step_gbs, "bytes_per_token": weight_bytes + kv_bytes,
+                "frac_of_peak": step_gbs / peak, "peak_gbs": peak, "peak_kind": peak_kind},
+        "roofline": {"bound": "hbm", "kernel": KCLASSES[dom], "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+                     "bytes_per_launch": kb[dom], "launch_ms": per_launch_ms,
+                     "peak_kind": peak_kind},
+        "kernel_ms_per_token": {k: v / 64 for k, v in shares.items()},
+        "kernel_share": {k: (v / total_k if total_k else None) for k, v in shares.items()},
+        "prefill": {"value": prefill_tps, "unit": "tok/s", "prompt": PROMPT},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": PROMPT * 4,
+                "d2h_bytes_per_step": DECODE * 4 + 96,
+                "note": "jyc_generate from pinned host ids: H2D prompt, prefill, 256 decode "
+                        "steps, D2H of the new ids; new tokens / wall time"},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

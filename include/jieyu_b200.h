@@ -212,6 +212,7 @@ JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos,
                               int8_t* k, float* ks, int8_t* v, float* vs);
 
 /* ---- device-resident stepping (bench / device loop) -------------------- */
+/* `stream` is used as given (0 = the legacy default stream). */
 /* Prefill `prompt_len` ids (DEVICE int32 pointer) from position 0 and emit the
  * first greedy token into the device token buffer. Asynchronous on `stream`. */
 JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prompt_len,
@@ -225,6 +226,26 @@ JYC_API int jyc_decode_device(jyc_model* m, int n_steps, void* stream);
 JYC_API int jyc_model_rewind(jyc_model* m, int len, void* stream);
 /* Kernels one decode step launches. */
 JYC_API int jyc_model_kernels_per_step(const jyc_model* m);
+/* 1 when the model decodes with the TMA-streamed kernels chained by
+ * programmatic dependent launch (Q8_0 weights), 0 with the generic kernels. */
+JYC_API int jyc_model_decode_path(const jyc_model* m);
+/* Error word of the device kernels: non-zero if a bounded wait gave up
+ * (reset != 0 clears it). */
+JYC_API int jyc_device_error(int reset);
+/* Tracing of the decode megakernel: phase boundaries per step and one traced
+ * step. out receives [ctas][points] SM-clock stamps; returns the CTA count.
+ * Point 0 = start; per layer l at 1+14l: QKV input ready, QKV done, barrier,
+ * attention done, barrier, O input ready, O done, barrier, gate/up input
+ * ready, gate/up done, barrier, down input ready, down done, barrier; then
+ * the LM head: input ready, done, barrier. */
+JYC_API int jyc_model_trace_points(const jyc_model* m);
+JYC_API int jyc_model_trace_decode(jyc_model* m, void* stream, long long* out, int cap);
+/* Per-kernel timing of decode: replays the step graph with an event after
+ * every kernel, n_steps times from the current state. Arrays of 8 kernel
+ * classes (embed, qkv, rope_quant, attention, o_proj, gate_up, down, head):
+ * summed device ms, launch counts, algorithmic bytes of one launch. */
+JYC_API int jyc_model_profile_decode(jyc_model* m, int n_steps, void* stream, double* ms,
+                                     int* launches, double* bytes);
 /* Device pointer to the int32 token buffer [max_seq] and host read of the
  * current length (synchronises the stream). */
 JYC_API int* jyc_model_tokens_device(jyc_model* m);

@@ -100,6 +100,11 @@ SIGNATURES = [
     ("jyc_decode_device", _I, [_P, _I, _P]),
     ("jyc_model_rewind", _I, [_P, _I, _P]),
     ("jyc_model_kernels_per_step", _I, [_P]),
+    ("jyc_model_profile_decode", _I, [_P, _I, _P, _P, _P, _P]),
+    ("jyc_model_decode_path", _I, [_P]),
+    ("jyc_device_error", _I, [_I]),
+    ("jyc_model_trace_points", _I, [_P]),
+    ("jyc_model_trace_decode", _I, [_P, _P, _P, _I]),
     ("jyc_model_tokens_device", _P, [_P]),
     ("jyc_model_length", _I, [_P, _P]),
 ]

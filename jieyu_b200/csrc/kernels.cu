@@ -609,17 +609,27 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     if (tid == 0) a.arrive[kvh] = 0u;
 }
 
+// One-time kernel attributes (called at model creation, outside any capture).
+int prepare_kernels() {
+    static bool done = false;
+    if (done) return JYC_OK;
+    JYC_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  200 * 1024));
+    done = true;
+    return JYC_OK;
+}
+#define TRY_PREPARE()                          \
+    do {                                       \
+        const int _r = prepare_kernels();      \
+        if (_r != JYC_OK) return _r;           \
+    } while (0)
+
 int launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.KV <= 0 || a.H % a.KV) return arg_error("attention: num_heads must be a multiple of num_kv_heads");
     if (a.hd % 4) return arg_error("attention: head_dim must be a multiple of 4");
     const int smem = attn_smem_bytes(a.rows, a.H, a.KV, a.hd);
     if (smem > 200 * 1024) return arg_error("attention: group too large for shared memory");
-    static bool attr_done = false;
-    if (!attr_done) {
-        JYC_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      200 * 1024));
-        attr_done = true;
-    }
+    TRY_PREPARE();
     dim3 grid(a.nsplit, a.KV);
     attention_kernel<<<grid, 128, smem, s>>>(a);
     JYC_LAUNCHED();

@@ -27,7 +27,7 @@ struct DevState {
     int eos[16];
     unsigned long long amax;   // argmax slot (argmax_pack)
     unsigned int head_arrive;  // last-arriver counter of the LM-head grid
-    unsigned int pad_;
+    unsigned int bar_base;     // grid-barrier counter value at the start of the next step
 };
 
 // Where a kernel finds its first position: from the step state (decode graph,
@@ -112,6 +112,7 @@ int launch_rope_quant(const RopeQuantArgs& a, cudaStream_t s);
 int launch_rope(float* q, int seq, int start_pos, int heads, int hd, const float* cos_t,
                 const float* sin_t, cudaStream_t s);
 int attn_smem_bytes(int rows, int H, int KV, int hd);
+int prepare_kernels();
 int launch_attention(const AttnArgs& a, cudaStream_t s);
 int launch_embed(const int* tokens, PosSrc pos, int rows, const float* ef, const uint8_t* eqs,
                  const uint16_t* ed, int hidden, float* X, cudaStream_t s);

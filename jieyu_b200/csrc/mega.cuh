@@ -1,0 +1,86 @@
+// mega.cuh — persistent decode-step kernel (one cooperative launch per token).
+#pragma once
+#include "kernels.cuh"
+
+namespace jyc {
+
+// Q8_0 weights in the tiled device layout read by the decode kernel: column
+// blocks of 512 (the last one may be narrower, width w_cb), block-major, rows
+// contiguous inside a block:
+//   qs: [cb][n][w_cb] signed int8 q, the 16-byte chunks of row r permuted
+//       within aligned groups of 8 chunks (chunk c -> c ^ (r & 7)) so that the
+//       tensor-core fragment loads of 8 consecutive rows hit distinct banks;
+//   d : [cb][n][w_cb/32] fp16 scales.
+// A run of consecutive rows of one block is one contiguous byte range, so a
+// tile (rows x one column block) arrives with two 1-D TMA bulk copies.
+constexpr int kMegaCB = 512;
+constexpr int kMegaRT = 48;       // rows per tile (multiple of 16)
+constexpr int kMegaMaxSlots = 6;  // ring depth upper bound
+constexpr int kMegaCW = 16;       // consumer warps
+constexpr int kMegaSlotBytes = kMegaRT * kMegaCB + kMegaRT * (kMegaCB / 32) * 2;
+
+struct MegaMat {
+    const uint8_t* qs;  // tiled copy (see above)
+    const uint16_t* d;
+    int n, k;
+    int rpc;  // rows per CTA (multiple of 16)
+    int rt;   // rows per tile (multiple of 16, <= kMegaRT)
+};
+
+struct MegaLayer {
+    MegaMat qkv, o, gu, dn;
+    const float* rms1;
+    const float* rms2;
+    const float* bias;  // fused q|k|v bias or null
+};
+
+struct MegaArgs {
+    const MegaLayer* layers;  // device array [L]
+    int L;
+    MegaMat head;
+    const float* final_norm;
+    const float* ef;          // fp32 embedding [V][D], or
+    const uint8_t* eqs;       // tiled Q8_0 embedding (n = V, k = D)
+    const uint16_t* ed;
+    int D, H, KV, hd, F, V;
+    const float* cos_t;
+    const float* sin_t;
+    int8_t* k8;               // KV cache [L][KV][max_seq][hd]
+    int8_t* v8;
+    float* ks;                // [L][KV][max_seq]
+    float* vs;
+    int max_seq;
+    float* X;                 // residual stream [D]
+    float* qkv;               // [q|k|v]
+    float* h;                 // SwiGLU output [F]
+    float* logits;            // [V]
+    float* part_o;            // attention split partials [H][nsplit][hd]
+    float* part_ml;           // [H][nsplit][2]
+    int chunk, nsplit;
+    float scale;              // 1/sqrtf(hd)
+    DevState* st;
+    int* tokens;
+    unsigned int* bar;        // grid-barrier counter (monotonic)
+    int* err;                 // device error word
+    int kmax;                 // largest GEMV input length (x / digit buffers)
+    int xs_bytes;             // shared bytes of the x / digits / attention union
+    int nslots;               // ring depth
+    long long* trace;         // optional: SM clock at each phase boundary, [CTA][kMegaTracePts]
+};
+
+// Phase boundaries recorded per CTA when tracing (per layer 14, then the head).
+constexpr int kMegaTraceLayer = 14;
+constexpr int kMegaTracePts = 1 + 64 * kMegaTraceLayer + 4;  // up to 64 layers
+
+int launch_q8_repack_tiled(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d, int n_total,
+                           int row_off, int row_stride, cudaStream_t s);
+int mega_plan(MegaMat& m, int nctas);
+int mega_smem_bytes(const MegaArgs& a);
+int mega_xs_bytes(int kmax, int G, int hd, int merge_weights);
+int mega_num_ctas();
+int launch_mega_step(const MegaArgs& a, cudaStream_t s);
+int prepare_mega_kernel(int smem);
+int mega_static_smem();  // -1 when the kernel image cannot be queried
+int* device_error_word();
+
+}  // namespace jyc

@@ -4,9 +4,13 @@
 //   generate (generate.h:90-112) -> generate_cached (generate.h:9-89)
 //     -> forward_cached (forward.h:47-96) -> transformer_layer (transformer_layer.h:10-90)
 // with every weight uploaded once (the bind_model point, pipeline.h:63-153), a
-// device KV cache, and one decode step = one CUDA-graph replay. Token ids stay
-// on the device; the step's last kernel (LM head + argmax) appends the next id
-// and clears `active` when the reference loop would stop (EOS, max_new, max_seq).
+// device KV cache, and token ids that stay on the device: the last phase of a
+// step (LM head + argmax) appends the next id and clears `active` when the
+// reference loop would stop (EOS, max_new, max_seq).
+//
+// Decode step: Q8_0 models run ONE persistent cooperative kernel per token
+// (mega.cu); other models (fp32 weights) run the generic kernels replayed as a
+// CUDA graph. Prompt rows go through the generic kernels in chunks of 8 rows.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -14,7 +18,7 @@
 #include <string>
 #include <vector>
 
-#include "kernels.cuh"
+#include "mega.cuh"
 
 using namespace jyc;
 
@@ -22,12 +26,40 @@ namespace {
 
 constexpr int kMT = 8;  // activation rows per prefill chunk
 
-struct DevMat {          // one weight matrix on the device, [n][k]
-    uint8_t* qs = nullptr;
+struct DevMat {  // one weight matrix on the device, [n][k]
+    uint8_t* qs = nullptr;   // Q8: row-major copy (generic kernels)
     uint16_t* d = nullptr;
+    uint8_t* tq = nullptr;   // Q8: tiled copy (decode megakernel), when `tiled`
+    uint16_t* td = nullptr;
     float* f = nullptr;
     int n = 0, k = 0;
+    bool tiled = false;
     double bytes() const { return f ? 4.0 * n * k : (double)n * k * 34.0 / 32.0; }
+};
+
+// Kernel classes of one generic decode step (for per-kernel timing).
+enum KClass { K_EMBED = 0, K_QKV, K_ROPEQ, K_ATTN, K_OPROJ, K_GATEUP, K_DOWN, K_HEAD, K_NCLASS };
+
+// Event marks recorded after each launch while a profiling graph is captured.
+struct Prof {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> cls;
+    cudaStream_t s = nullptr;
+    int mark(int c) {
+        cudaEvent_t e;
+        cudaError_t r = cudaEventCreate(&e);
+        if (r != cudaSuccess) return cuda_fail(r, "cudaEventCreate");
+        // external record: inside a stream capture this becomes an event-record
+        // node, so the event is timestamped on every graph replay
+        r = cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+        if (r != cudaSuccess) return cuda_fail(r, "cudaEventRecord");
+        ev.push_back(e);
+        cls.push_back(c);
+        return JYC_OK;
+    }
+    ~Prof() {
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
+    }
 };
 
 struct DevLayer {
@@ -43,10 +75,11 @@ struct jyc_model {
     int L = 0, D = 0, H = 0, KV = 0, hd = 0, F = 0, V = 0, max_seq = 0;
     int q_dim = 0, kv_dim = 0, nqkv = 0;
     int wtype = W_Q8;
+    bool tiled = false;  // Q8 matrices in the 512-column tiled layout (megakernel models)
     std::vector<DevLayer> layers;
     DevMat head;
-    float* embed_f = nullptr;    // fp32 embedding [V][D], or
-    DevMat embed_q;              // Q8 embedding in device layout (may alias head)
+    float* embed_f = nullptr;  // fp32 embedding [V][D], or
+    DevMat embed_q;            // Q8 embedding (may alias head)
     float* final_norm = nullptr;
     float *cos_t = nullptr, *sin_t = nullptr;
     // KV cache [L][KV][max_seq][hd] int8, scales [L][KV][max_seq]
@@ -60,10 +93,17 @@ struct jyc_model {
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* arrive = nullptr;
     int chunk = 64, nsplit = 1;
+    // megakernel decode
+    bool mega = false;
+    MegaArgs margs{};
+    MegaLayer* d_mlayers = nullptr;
     DevState* st = nullptr;
-    int* tokens = nullptr;       // [max_seq + 1]
+    int* tokens = nullptr;  // [max_seq + 1]
     cudaStream_t stream = nullptr;
     cudaGraphExec_t step_exec = nullptr;
+    cudaGraphExec_t prof_exec = nullptr;  // generic decode step with event marks
+    Prof* prof = nullptr;                 // set while capturing prof_exec
+    std::unique_ptr<Prof> prof_marks;
     std::vector<void*> allocs;
     double weight_bytes = 0.0;
 
@@ -82,6 +122,8 @@ struct jyc_model {
     }
     ~jyc_model() {
         if (step_exec) cudaGraphExecDestroy(step_exec);
+        if (prof_exec) cudaGraphExecDestroy(prof_exec);
+        prof_marks.reset();
         for (void* p : allocs) cudaFree(p);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -104,16 +146,16 @@ struct jyc_model {
 
 namespace {
 
-#define TRY(x)                          \
-    do {                                \
-        int _r = (x);                   \
-        if (_r != JYC_OK) return _r;    \
+#define TRY(x)                       \
+    do {                             \
+        int _r = (x);                \
+        if (_r != JYC_OK) return _r; \
     } while (0)
 
 // Uploads one reference weight (host, reference layout) into rows
 // [row_off + r*row_stride] of `dst` (device layout, n_total rows x k).
-int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int n_total,
-                int row_off, int row_stride, void* staging, size_t staging_bytes) {
+int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int n_total, int row_off,
+                int row_stride, void* staging, size_t staging_bytes, int expect_type) {
     if (w.h != nullptr && w.f == nullptr && w.q == nullptr) {
         set_error("fp16 weights are not supported by the B200 path");
         return JYC_ERR_UNSUPPORTED;
@@ -128,16 +170,21 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
         set_error("missing weight tensor");
         return JYC_ERR_ARG;
     }
-    if ((q8 ? W_Q8 : W_F32) != m->wtype) {
+    if ((q8 ? W_Q8 : W_F32) != expect_type) {
         set_error("mixed Q8_0 / fp32 linear weights are not supported");
         return JYC_ERR_UNSUPPORTED;
     }
     if (dst.n == 0) {  // first piece: allocate the whole (fused) matrix
         dst.n = n_total;
         dst.k = k;
+        dst.tiled = q8 && m->tiled;
         if (q8) {
             TRY(m->alloc(&dst.qs, (size_t)n_total * k));
             TRY(m->alloc(&dst.d, (size_t)n_total * (k / 32)));
+            if (dst.tiled) {
+                TRY(m->alloc(&dst.tq, (size_t)n_total * k));
+                TRY(m->alloc(&dst.td, (size_t)n_total * (k / 32)));
+            }
         } else {
             TRY(m->alloc(&dst.f, (size_t)n_total * k));
         }
@@ -147,11 +194,13 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
         set_error("internal: staging buffer too small");
         return JYC_ERR_ARG;
     }
-    JYC_CUDA(cudaMemcpyAsync(staging, q8 ? w.q : (const void*)w.f, bytes, cudaMemcpyHostToDevice,
-                             m->stream));
-    if (q8) TRY(launch_q8_repack(staging, n, k, dst.qs, dst.d, row_off, row_stride, m->stream));
-    else TRY(launch_transpose(static_cast<const float*>(staging), dst.f, k, n, row_off, row_stride,
-                              m->stream));
+    JYC_CUDA(cudaMemcpyAsync(staging, q8 ? w.q : (const void*)w.f, bytes, cudaMemcpyHostToDevice, m->stream));
+    if (q8) {
+        TRY(launch_q8_repack(staging, n, k, dst.qs, dst.d, row_off, row_stride, m->stream));
+        if (dst.tiled)
+            TRY(launch_q8_repack_tiled(staging, n, k, dst.tq, dst.td, n_total, row_off, row_stride, m->stream));
+    } else
+        TRY(launch_transpose(static_cast<const float*>(staging), dst.f, k, n, row_off, row_stride, m->stream));
     // the staging buffer is reused by the next upload: wait for this one
     JYC_CUDA(cudaStreamSynchronize(m->stream));
     return JYC_OK;
@@ -160,6 +209,88 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
 int upload_f32(jyc_model* m, const float* src, size_t n, float** dst) {
     TRY(m->alloc(dst, n));
     JYC_CUDA(cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice));
+    return JYC_OK;
+}
+
+// Q8_0 models whose shapes fit the tiled layout decode with the megakernel.
+bool mega_eligible(const jyc_model* m, const jyc_model_desc* d) {
+    if (m->wtype != W_Q8 || d->lm_head.q == nullptr || d->lm_head.qt != JYC_Q8_0) return false;
+    if (d->embed.f == nullptr && (d->embed.q == nullptr || d->embed.qt != JYC_Q8_0)) return false;
+    const int n16[] = {m->nqkv, m->D, 2 * m->F, m->V};
+    for (int n : n16)
+        if (n % 16) return false;
+    const int k32[] = {m->D, m->q_dim, m->F};
+    for (int k : k32)
+        if (k % 32) return false;
+    return m->hd % 16 == 0 && m->hd <= 256;
+}
+
+MegaMat mega_mat(const DevMat& w, int nctas) {
+    MegaMat mm{};
+    mm.qs = w.tq;
+    mm.d = w.td;
+    mm.n = w.n;
+    mm.k = w.k;
+    mega_plan(mm, nctas);
+    return mm;
+}
+
+int setup_mega(jyc_model* m) {
+    m->mega = false;
+    const int nctas = mega_num_ctas();
+    MegaArgs& a = m->margs;
+    a = MegaArgs{};
+    std::vector<MegaLayer> ml(m->L);
+    for (int l = 0; l < m->L; l++) {
+        const DevLayer& ly = m->layers[l];
+        ml[l].qkv = mega_mat(ly.qkv, nctas);
+        ml[l].o = mega_mat(ly.o, nctas);
+        ml[l].gu = mega_mat(ly.gateup, nctas);
+        ml[l].dn = mega_mat(ly.down, nctas);
+        ml[l].rms1 = ly.rms1;
+        ml[l].rms2 = ly.rms2;
+        ml[l].bias = ly.bias;
+    }
+    TRY(m->alloc(&m->d_mlayers, (size_t)m->L));
+    JYC_CUDA(cudaMemcpy(m->d_mlayers, ml.data(), sizeof(MegaLayer) * m->L, cudaMemcpyHostToDevice));
+    a.layers = m->d_mlayers;
+    a.L = m->L;
+    a.head = mega_mat(m->head, nctas);
+    a.final_norm = m->final_norm;
+    a.ef = m->embed_f;
+    a.eqs = m->embed_q.tq;
+    a.ed = m->embed_q.td;
+    a.D = m->D; a.H = m->H; a.KV = m->KV; a.hd = m->hd; a.F = m->F; a.V = m->V;
+    a.cos_t = m->cos_t;
+    a.sin_t = m->sin_t;
+    a.k8 = m->k8; a.v8 = m->v8; a.ks = m->ks; a.vs = m->vs;
+    a.max_seq = m->max_seq;
+    a.X = m->X; a.qkv = m->qkv; a.h = m->h; a.logits = m->logits;
+    // attention split plan: about one (kv head, split) item per CTA at full context
+    const int per_head = std::max(1, nctas / m->KV);
+    int chunk = (m->max_seq + per_head - 1) / per_head;
+    chunk = std::max(64, (chunk + 63) / 64 * 64);
+    a.chunk = chunk;
+    a.nsplit = (m->max_seq + chunk - 1) / chunk;
+    TRY(m->alloc(&a.part_o, (size_t)m->H * a.nsplit * m->hd));
+    TRY(m->alloc(&a.part_ml, (size_t)m->H * a.nsplit * 2));
+    a.scale = 1.0f / sqrtf((float)m->hd);
+    a.st = m->st;
+    a.tokens = m->tokens;
+    TRY(m->alloc(&a.bar, 1));
+    JYC_CUDA(cudaMemset(a.bar, 0, sizeof(unsigned int)));
+    a.err = device_error_word();
+    a.kmax = std::max({m->D, m->q_dim, m->F});
+    a.xs_bytes = mega_xs_bytes(a.kmax, m->H / m->KV, m->hd, m->H * a.nsplit);
+    // ring as deep as the shared memory allows (227 KB per CTA, at least 2 slots)
+    const int st_smem = mega_static_smem();
+    if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
+    const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
+    a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
+    if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode
+    const int smem = mega_smem_bytes(a);
+    TRY(prepare_mega_kernel(smem));
+    m->mega = true;
     return JYC_OK;
 }
 
@@ -182,16 +313,15 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
                          std::to_string(kq));
     if (attn_smem_bytes(kMT, m->H, m->KV, m->hd) > 200 * 1024)
         return arg_error("model: query-head group too large for the attention kernel");
+    m->tiled = mega_eligible(m, d);
 
     JYC_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    TRY(prepare_kernels());
 
     // staging for uploads: the largest single host tensor
-    size_t stage = 0;
-    auto tb = [&](int n, int k) {
-        return m->wtype == W_Q8 ? (size_t)n * (k / 32) * 34 : (size_t)n * k * 4;
-    };
-    stage = std::max({tb(m->q_dim, m->D), tb(m->kv_dim, m->D), tb(m->D, m->q_dim), tb(m->F, m->D),
-                      tb(m->D, m->F)});
+    auto tb = [&](int n, int k) { return m->wtype == W_Q8 ? (size_t)n * (k / 32) * 34 : (size_t)n * k * 4; };
+    size_t stage = std::max({tb(m->q_dim, m->D), tb(m->kv_dim, m->D), tb(m->D, m->q_dim), tb(m->F, m->D),
+                             tb(m->D, m->F)});
     const bool head_q8 = d->lm_head.q != nullptr;
     const size_t head_bytes = head_q8 ? (size_t)m->V * (m->D / 32) * 34 : (size_t)m->V * m->D * 4;
     stage = std::max(stage, head_bytes);
@@ -203,16 +333,18 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     for (int l = 0; l < m->L; l++) {
         const jyc_layer_weights& w = d->layers[l];
         DevLayer& dl = m->layers[l];
-        if (!w.rms1_weight || !w.rms2_weight) return arg_error("model: missing RMSNorm weight in layer " + std::to_string(l));
+        if (!w.rms1_weight || !w.rms2_weight)
+            return arg_error("model: missing RMSNorm weight in layer " + std::to_string(l));
         TRY(upload_f32(m, w.rms1_weight, m->D, &dl.rms1));
         TRY(upload_f32(m, w.rms2_weight, m->D, &dl.rms2));
-        TRY(upload_wmat(m, w.Wq, m->q_dim, m->D, dl.qkv, m->nqkv, 0, 1, staging, stage));
-        TRY(upload_wmat(m, w.Wk, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim, 1, staging, stage));
-        TRY(upload_wmat(m, w.Wv, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim + m->kv_dim, 1, staging, stage));
-        TRY(upload_wmat(m, w.Wo, m->D, m->q_dim, dl.o, m->D, 0, 1, staging, stage));
-        TRY(upload_wmat(m, w.W1, m->F, m->D, dl.gateup, 2 * m->F, 0, 2, staging, stage));
-        TRY(upload_wmat(m, w.W3, m->F, m->D, dl.gateup, 2 * m->F, 1, 2, staging, stage));
-        TRY(upload_wmat(m, w.W2, m->D, m->F, dl.down, m->D, 0, 1, staging, stage));
+        const int wt = m->wtype;
+        TRY(upload_wmat(m, w.Wq, m->q_dim, m->D, dl.qkv, m->nqkv, 0, 1, staging, stage, wt));
+        TRY(upload_wmat(m, w.Wk, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim, 1, staging, stage, wt));
+        TRY(upload_wmat(m, w.Wv, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim + m->kv_dim, 1, staging, stage, wt));
+        TRY(upload_wmat(m, w.Wo, m->D, m->q_dim, dl.o, m->D, 0, 1, staging, stage, wt));
+        TRY(upload_wmat(m, w.W1, m->F, m->D, dl.gateup, 2 * m->F, 0, 2, staging, stage, wt));
+        TRY(upload_wmat(m, w.W3, m->F, m->D, dl.gateup, 2 * m->F, 1, 2, staging, stage, wt));
+        TRY(upload_wmat(m, w.W2, m->D, m->F, dl.down, m->D, 0, 1, staging, stage, wt));
         if (w.bq || w.bk || w.bv) {
             std::vector<float> b(m->nqkv, 0.0f);
             if (w.bq) std::memcpy(b.data(), w.bq, m->q_dim * 4);
@@ -224,23 +356,15 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
                            2.0 * m->D * 4 + (dl.bias ? m->nqkv * 4.0 : 0.0);
     }
     // LM head (Q8 [V][D] blocks, or fp32 [D][V]) and embedding
-    {
-        const int saved = m->wtype;
-        m->wtype = head_q8 ? W_Q8 : W_F32;
-        TRY(upload_wmat(m, d->lm_head, m->V, m->D, m->head, m->V, 0, 1, staging, stage));
-        m->wtype = saved;
-        m->weight_bytes += m->head.bytes();
-    }
+    TRY(upload_wmat(m, d->lm_head, m->V, m->D, m->head, m->V, 0, 1, staging, stage, head_q8 ? W_Q8 : W_F32));
+    m->weight_bytes += m->head.bytes();
     if (d->embed.f != nullptr) {
         TRY(upload_f32(m, d->embed.f, (size_t)m->V * m->D, &m->embed_f));
     } else if (d->embed.q != nullptr && d->embed.qt == JYC_Q8_0) {
-        if (d->embed.q == d->lm_head.q) {
+        if (d->embed.q == d->lm_head.q && head_q8) {
             m->embed_q = m->head;  // tied: one device copy
         } else {
-            const int saved = m->wtype;
-            m->wtype = W_Q8;
-            TRY(upload_wmat(m, d->embed, m->V, m->D, m->embed_q, m->V, 0, 1, staging, stage));
-            m->wtype = saved;
+            TRY(upload_wmat(m, d->embed, m->V, m->D, m->embed_q, m->V, 0, 1, staging, stage, W_Q8));
         }
     } else {
         set_error("embedding must be fp32 or Q8_0");
@@ -270,7 +394,7 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     TRY(m->alloc(&m->tmp, (size_t)m->D));
     TRY(m->alloc(&m->q8, (size_t)kMT * m->q_dim));
     TRY(m->alloc(&m->qsc, (size_t)kMT * m->H));
-    // split-K plan: ~2 CTAs per SM over the kv heads, chunks of >= 64 positions
+    // split-K plan of the generic attention: ~2 CTAs per SM over the kv heads
     const int target = std::max(1, 296 / m->KV);
     int chunk = (m->max_seq + target - 1) / target;
     chunk = std::max(64, (chunk + 63) / 64 * 64);
@@ -283,15 +407,22 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     TRY(m->alloc(&m->st, 1));
     JYC_CUDA(cudaMemsetAsync(m->st, 0, sizeof(DevState), m->stream));
     TRY(m->alloc(&m->tokens, (size_t)m->max_seq + 1));
+    if (m->tiled) TRY(setup_mega(m));
     JYC_CUDA(cudaStreamSynchronize(m->stream));
     return JYC_OK;
 }
 
+#define MARK(c)                             \
+    do {                                    \
+        if (m->prof) TRY(m->prof->mark(c)); \
+    } while (0)
+
 // One transformer stack pass over `rows` (<= kMT) tokens at pos (host constant
-// or device state), then nothing else. Layer order = transformer_layer.
+// or device state) with the generic kernels. Layer order = transformer_layer.
 int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
     DevState* guard = pos.st ? m->st : nullptr;
     TRY(launch_embed(m->tokens, pos, rows, m->embed_f, m->embed_q.qs, m->embed_q.d, m->D, m->X, s));
+    MARK(K_EMBED);
     for (int l = 0; l < m->L; l++) {
         const DevLayer& ly = m->layers[l];
         GemvArgs g{};
@@ -301,6 +432,7 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
         g.qs = ly.qkv.qs; g.d = ly.qkv.d; g.wt = ly.qkv.f; g.norm_w = ly.rms1;
         g.y = m->qkv; g.ldy = m->nqkv; g.bias = ly.bias;
         TRY(launch_gemv(g, m->wtype, ly.bias ? EPI_BIAS : EPI_STORE, s));
+        MARK(K_QKV);
         // RoPE(Q,K) + int8 quantisation of Q, K, V; K/V appended to the cache
         RopeQuantArgs rq{};
         rq.q = m->qkv; rq.k = m->qkv + m->q_dim; rq.v = m->qkv + m->q_dim + m->kv_dim;
@@ -308,6 +440,7 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
         rq.cos_t = m->cos_t; rq.sin_t = m->sin_t; rq.q8 = m->q8; rq.qsc = m->qsc;
         rq.kv = m->kv_layer(l); rq.pos = pos;
         TRY(launch_rope_quant(rq, s));
+        MARK(K_ROPEQ);
         // int8-KV attention (split-K flash decoding)
         AttnArgs at{};
         at.q8 = m->q8; at.qsc = m->qsc; at.kv = m->kv_layer(l);
@@ -317,25 +450,29 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
         at.part_o = m->part_o; at.part_ml = m->part_ml; at.arrive = m->arrive;
         at.out = m->attn; at.ldo = m->q_dim; at.pos = pos;
         TRY(launch_attention(at, s));
+        MARK(K_ATTN);
         // O projection + residual
         g = GemvArgs{};
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         g.x = m->attn; g.ldx = m->q_dim; g.n = m->D; g.k = m->q_dim;
         g.qs = ly.o.qs; g.d = ly.o.d; g.wt = ly.o.f; g.y = m->X; g.ldy = m->D;
         TRY(launch_gemv(g, m->wtype, EPI_RESID, s));
+        MARK(K_OPROJ);
         // RMSNorm -> gate|up GEMV -> SwiGLU
         g = GemvArgs{};
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         g.x = m->X; g.ldx = m->D; g.n = 2 * m->F; g.k = m->D;
-        g.qs = ly.gateup.qs; g.d = ly.gateup.d; g.wt = ly.gateup.f; g.norm_w = ly.rms2;
-        g.y = m->h; g.ldy = m->F;
+        g.qs = ly.gateup.qs; g.d = ly.gateup.d; g.wt = ly.gateup.f;
+        g.norm_w = ly.rms2; g.y = m->h; g.ldy = m->F;
         TRY(launch_gemv(g, m->wtype, EPI_SWIGLU, s));
+        MARK(K_GATEUP);
         // down projection + residual
         g = GemvArgs{};
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         g.x = m->h; g.ldx = m->F; g.n = m->D; g.k = m->F;
         g.qs = ly.down.qs; g.d = ly.down.d; g.wt = ly.down.f; g.y = m->X; g.ldy = m->D;
         TRY(launch_gemv(g, m->wtype, EPI_RESID, s));
+        MARK(K_DOWN);
     }
     return JYC_OK;
 }
@@ -348,7 +485,9 @@ int run_head(jyc_model* m, int row, cudaStream_t s) {
     g.x = m->X + (size_t)row * m->D; g.ldx = m->D; g.n = m->V; g.k = m->D;
     g.qs = m->head.qs; g.d = m->head.d; g.wt = m->head.f; g.norm_w = m->final_norm;
     g.y = m->logits; g.ldy = m->V;
-    return launch_gemv(g, m->head.f ? W_F32 : W_Q8, EPI_ARGMAX, s);
+    TRY(launch_gemv(g, m->head.f ? W_F32 : W_Q8, EPI_ARGMAX, s));
+    MARK(K_HEAD);
+    return JYC_OK;
 }
 
 // Forward of n tokens already in m->tokens[start..start+n) in chunks of kMT,
@@ -364,7 +503,7 @@ int run_prefill(jyc_model* m, int start, int n, cudaStream_t s) {
 }
 
 int ensure_step_graph(jyc_model* m) {
-    if (m->step_exec) return JYC_OK;
+    if (m->mega || m->step_exec) return JYC_OK;
     cudaGraph_t graph = nullptr;
     JYC_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int r = run_layers(m, 1, PosSrc{m->st, 0}, m->stream);
@@ -381,7 +520,16 @@ int ensure_step_graph(jyc_model* m) {
     return JYC_OK;
 }
 
-int kernels_per_step(const jyc_model* m) { return 1 + m->L * 6 + 1; }
+int kernels_per_step(const jyc_model* m) { return m->mega ? 1 : 1 + m->L * 6 + 1; }
+
+// One decode step on stream s (token at len-1, guarded by the state).
+int decode_step(jyc_model* m, cudaStream_t s) {
+    if (m->mega) return launch_mega_step(m->margs, s);
+    TRY(ensure_step_graph(m));
+    JYC_CUDA(cudaGraphLaunch(m->step_exec, s));
+    count_launch(kernels_per_step(m));
+    return JYC_OK;
+}
 
 }  // namespace
 
@@ -424,9 +572,14 @@ JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_
     cudaStream_t s = m->stream;
     JYC_CUDA(cudaMemcpyAsync(m->tokens + start_pos, ids, seq * sizeof(int), cudaMemcpyHostToDevice, s));
     TRY(launch_set_state(m->st, start_pos + seq, 1 << 30, m->max_seq + 1, nullptr, 0, s));
-    TRY(run_prefill(m, start_pos, seq, s));
+    if (seq == 1 && m->mega) {
+        // a single token goes through the decode kernel (the path generate's steps use)
+        TRY(launch_mega_step(m->margs, s));
+    } else {
+        TRY(run_prefill(m, start_pos, seq, s));
+    }
     if (hidden_out) {
-        const int last = (seq - 1) % kMT;
+        const int last = (seq == 1 && m->mega) ? 0 : (seq - 1) % kMT;
         TRY(launch_rmsnorm(m->X + (size_t)last * m->D, m->tmp, m->final_norm, 1, m->D, 1e-5f, s));
         JYC_CUDA(cudaMemcpyAsync(hidden_out, m->tmp, m->D * sizeof(float), cudaMemcpyDeviceToHost, s));
     }
@@ -436,11 +589,10 @@ JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_
     return JYC_OK;
 }
 
-JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos, int8_t* k, float* ks, int8_t* v,
-                              float* vs) {
+JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos, int8_t* k, float* ks, int8_t* v, float* vs) {
     clear_error();
-    if (!m || layer < 0 || layer >= m->L || npos < 0 || npos > m->max_seq)
-        return arg_error("read_kv: bad arguments");
+    if (!m || layer < 0 || layer >= m->L || npos < 0 || npos > m->max_seq) return arg_error("read_kv: bad arguments");
+    JYC_CUDA(cudaStreamSynchronize(m->stream));
     const KVView kv = m->kv_layer(layer);
     std::vector<int8_t> kb((size_t)m->KV * m->max_seq * m->hd), vb(kb.size());
     std::vector<float> ksb((size_t)m->KV * m->max_seq), vsb(ksb.size());
@@ -460,16 +612,17 @@ JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos, int8_t* k, floa
     return JYC_OK;
 }
 
-JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, const int* eos_ids,
-                         int num_eos, int max_new_tokens, float temperature, int* out_ids,
-                         float repetition_penalty, jyc_token_cb cb, void* cb_ud) {
+JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, const int* eos_ids, int num_eos,
+                         int max_new_tokens, float temperature, int* out_ids, float repetition_penalty,
+                         jyc_token_cb cb, void* cb_ud) {
     clear_error();
     if (!m || !out_ids) return arg_error("generate: null model or output");
     if (prompt_len <= 0 || prompt_len > m->max_seq || !prompt_ids) return 0;
     for (int i = 0; i < prompt_len; i++) out_ids[i] = prompt_ids[i];
     if (max_new_tokens <= 0) return prompt_len;
     if (temperature > 0.0f || repetition_penalty != 1.0f) {
-        set_error("generate: sampling (temperature > 0) and repetition_penalty != 1 are not built yet on the B200 path");
+        set_error(
+            "generate: sampling (temperature > 0) and repetition_penalty != 1 are not built yet on the B200 path");
         return JYC_ERR_UNSUPPORTED;
     }
     if (num_eos < 0 || num_eos > 8 || (num_eos > 0 && !eos_ids)) return arg_error("generate: at most 8 EOS ids");
@@ -481,20 +634,17 @@ JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, co
     JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids, prompt_len * sizeof(int), cudaMemcpyHostToDevice, s));
     TRY(launch_set_state(m->st, prompt_len, max_new_tokens, m->max_seq, eos_ids, num_eos, s));
     TRY(run_prefill(m, 0, prompt_len, s));
-    // decode: one graph replay per step; the state guard turns surplus steps into no-ops
+    // decode: one step per token; the state guard turns surplus steps into no-ops
     const int max_steps = std::min(max_new_tokens, m->max_seq - prompt_len) - 1;
     int len = prompt_len;
     if (!cb) {
-        for (int i = 0; i < max_steps; i++) {
-            JYC_CUDA(cudaGraphLaunch(m->step_exec, s));
-            count_launch(kernels_per_step(m));
-        }
+        for (int i = 0; i < max_steps; i++) TRY(decode_step(m, s));
         DevState hs;
         JYC_CUDA(cudaMemcpyAsync(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
         JYC_CUDA(cudaStreamSynchronize(s));
         len = hs.len;
-        JYC_CUDA(cudaMemcpy(out_ids + prompt_len, m->tokens + prompt_len,
-                            (size_t)(len - prompt_len) * sizeof(int), cudaMemcpyDeviceToHost));
+        JYC_CUDA(cudaMemcpy(out_ids + prompt_len, m->tokens + prompt_len, (size_t)(len - prompt_len) * sizeof(int),
+                            cudaMemcpyDeviceToHost));
         return len;
     }
     // with a callback: run blocks of steps, hand each new token to cb in order,
@@ -517,10 +667,7 @@ JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, co
         len = hs.len;
         if (!hs.active || done_steps >= max_steps) return len;
         const int n = std::min(block, max_steps - done_steps);
-        for (int i = 0; i < n; i++) {
-            JYC_CUDA(cudaGraphLaunch(m->step_exec, s));
-            count_launch(kernels_per_step(m));
-        }
+        for (int i = 0; i < n; i++) TRY(decode_step(m, s));
         done_steps += n;
         block = std::min(block * 2, 32);
     }
@@ -530,7 +677,7 @@ JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prom
     clear_error();
     if (!m || !prompt_ids_dev || prompt_len <= 0 || prompt_len >= m->max_seq)
         return arg_error("prefill_device: bad arguments");
-    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    cudaStream_t s = (cudaStream_t)stream;  // as given: 0 is the legacy default stream
     JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids_dev, prompt_len * sizeof(int), cudaMemcpyDeviceToDevice, s));
     TRY(launch_set_state(m->st, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s));
     return run_prefill(m, 0, prompt_len, s);
@@ -539,29 +686,154 @@ JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prom
 JYC_API int jyc_model_rewind(jyc_model* m, int len, void* stream) {
     clear_error();
     if (!m || len <= 0 || len >= m->max_seq) return arg_error("rewind: bad length");
-    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    cudaStream_t s = (cudaStream_t)stream;  // as given: 0 is the legacy default stream
     return launch_set_state(m->st, len, 1 << 30, m->max_seq, nullptr, 0, s);
 }
 
 JYC_API int jyc_decode_device(jyc_model* m, int n_steps, void* stream) {
     clear_error();
     if (!m || n_steps < 0) return arg_error("decode_device: bad arguments");
-    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
-    TRY(ensure_step_graph(m));
-    for (int i = 0; i < n_steps; i++) {
-        JYC_CUDA(cudaGraphLaunch(m->step_exec, s));
-        count_launch(kernels_per_step(m));
-    }
+    cudaStream_t s = (cudaStream_t)stream;  // as given: 0 is the legacy default stream
+    for (int i = 0; i < n_steps; i++) TRY(decode_step(m, s));
     return JYC_OK;
 }
 
 JYC_API int jyc_model_kernels_per_step(const jyc_model* m) { return m ? kernels_per_step(m) : 0; }
 
+JYC_API int jyc_model_decode_path(const jyc_model* m) { return m ? (m->mega ? 2 : 0) : -1; }
+
+JYC_API int jyc_model_trace_points(const jyc_model* m) {
+    if (!m || !m->mega) return 0;
+    return 1 + m->L * kMegaTraceLayer + 4;
+}
+
+// One traced decode step (megakernel models): out receives, per CTA, the SM
+// clock at each phase boundary ([ctas][trace_points] int64); returns the CTA count.
+JYC_API int jyc_model_trace_decode(jyc_model* m, void* stream, long long* out, int cap) {
+    clear_error();
+    if (!m || !m->mega || !out) return arg_error("trace_decode: megakernel model and buffer required");
+    const int nct = mega_num_ctas(), npts = jyc_model_trace_points(m);
+    if (cap < nct * npts) return arg_error("trace_decode: buffer too small");
+    cudaStream_t s = (cudaStream_t)stream;
+    long long* d = nullptr;
+    JYC_CUDA(cudaMalloc(&d, sizeof(long long) * nct * kMegaTracePts));
+    JYC_CUDA(cudaMemsetAsync(d, 0, sizeof(long long) * nct * kMegaTracePts, s));
+    MegaArgs a = m->margs;
+    a.trace = d;
+    int r = launch_mega_step(a, s);
+    std::vector<long long> h((size_t)nct * kMegaTracePts);
+    if (r == JYC_OK) {
+        cudaError_t e = cudaMemcpyAsync(h.data(), d, h.size() * sizeof(long long), cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) r = cuda_fail(e, "trace readback");
+    }
+    cudaFree(d);
+    if (r != JYC_OK) return r;
+    for (int b = 0; b < nct; b++)
+        for (int i = 0; i < npts; i++) out[(size_t)b * npts + i] = h[(size_t)b * kMegaTracePts + i];
+    return nct;
+}
+
+JYC_API int jyc_device_error(int reset) {
+    int* p = device_error_word();
+    if (!p) return 0;
+    int v = 0;
+    if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (reset && v) {
+        const int z = 0;
+        cudaMemcpy(p, &z, sizeof(int), cudaMemcpyHostToDevice);
+    }
+    return v;
+}
+
+// Per-kernel timing of decode. Megakernel models: one class (the whole step)
+// timed with events around each launch. Generic models: the step graph is
+// replayed with an event after every kernel. Returns per class the summed
+// device milliseconds, the launch count and the algorithmic bytes of one
+// launch at the context the first profiled step runs at.
+JYC_API int jyc_model_profile_decode(jyc_model* m, int n_steps, void* stream, double* ms, int* launches,
+                                     double* bytes) {
+    clear_error();
+    if (!m || n_steps <= 0 || !ms || !launches || !bytes) return arg_error("profile_decode: bad arguments");
+    cudaStream_t s = (cudaStream_t)stream;
+    for (int c = 0; c < K_NCLASS; c++) {
+        ms[c] = 0.0;
+        launches[c] = 0;
+        bytes[c] = 0.0;
+    }
+    DevState hs;
+    JYC_CUDA(cudaStreamSynchronize(s));
+    JYC_CUDA(cudaMemcpy(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost));
+    const int ctx = hs.len;  // positions the first profiled step attends to
+    if (m->mega) {
+        bytes[0] = m->weight_bytes + (double)m->L * m->KV * ctx * (2.0 * m->hd + 8.0);
+        cudaEvent_t e0, e1;
+        JYC_CUDA(cudaEventCreate(&e0));
+        JYC_CUDA(cudaEventCreate(&e1));
+        for (int it = 0; it < n_steps; it++) {
+            JYC_CUDA(cudaEventRecord(e0, s));
+            TRY(launch_mega_step(m->margs, s));
+            JYC_CUDA(cudaEventRecord(e1, s));
+            JYC_CUDA(cudaEventSynchronize(e1));
+            float t = 0.0f;
+            JYC_CUDA(cudaEventElapsedTime(&t, e0, e1));
+            ms[0] += t;
+            launches[0] += 1;
+        }
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        return JYC_OK;
+    }
+    if (!m->prof_exec) {
+        m->prof_marks.reset(new Prof());
+        m->prof_marks->s = m->stream;
+        cudaGraph_t graph = nullptr;
+        JYC_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        m->prof = m->prof_marks.get();
+        int r = m->prof->mark(-1);
+        if (r == JYC_OK) r = run_layers(m, 1, PosSrc{m->st, 0}, m->stream);
+        if (r == JYC_OK) r = run_head(m, 0, m->stream);
+        m->prof = nullptr;
+        cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+        if (r != JYC_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return r;
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+        e = cudaGraphInstantiate(&m->prof_exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    }
+    const double wb = m->wtype == W_Q8 ? 34.0 / 32.0 : 4.0;
+    const double hb = m->head.f ? 4.0 : 34.0 / 32.0;
+    bytes[K_EMBED] = m->embed_f ? 4.0 * m->D : m->D * 34.0 / 32.0;
+    bytes[K_QKV] = (double)m->nqkv * m->D * wb + 4.0 * m->D;
+    bytes[K_ROPEQ] = 4.0 * m->nqkv;
+    bytes[K_ATTN] = (double)m->KV * ctx * (2.0 * m->hd + 8.0);
+    bytes[K_OPROJ] = (double)m->D * m->q_dim * wb;
+    bytes[K_GATEUP] = 2.0 * m->F * m->D * wb + 4.0 * m->D;
+    bytes[K_DOWN] = (double)m->D * m->F * wb;
+    bytes[K_HEAD] = (double)m->V * m->D * hb + 4.0 * m->D;
+    Prof* p = m->prof_marks.get();
+    for (int it = 0; it < n_steps; it++) {
+        JYC_CUDA(cudaGraphLaunch(m->prof_exec, s));
+        count_launch(kernels_per_step(m));
+        JYC_CUDA(cudaStreamSynchronize(s));
+        for (size_t i = 1; i < p->ev.size(); i++) {
+            float t = 0.0f;
+            JYC_CUDA(cudaEventElapsedTime(&t, p->ev[i - 1], p->ev[i]));
+            ms[p->cls[i]] += t;
+            launches[p->cls[i]] += 1;
+        }
+    }
+    return JYC_OK;
+}
+
 JYC_API int* jyc_model_tokens_device(jyc_model* m) { return m ? m->tokens : nullptr; }
 
 JYC_API int jyc_model_length(jyc_model* m, void* stream) {
     if (!m) return arg_error("model_length: null model");
-    cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+    cudaStream_t s = (cudaStream_t)stream;
     DevState hs;
     JYC_CUDA(cudaMemcpyAsync(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
     JYC_CUDA(cudaStreamSynchronize(s));

@@ -1,0 +1,210 @@
+"""Model-level parity of the device token loop (jyc_model_create / jyc_generate
+/ jyc_forward_logits) against the reference: golden fixtures produced by the
+reference itself (tests/golden) and the bit-identical CPU oracle.
+
+Bars (north star): greedy token ids identical; logits within
+LOGIT_TOL * max|logit|; argmax equal wherever the reference's top-2 gap
+exceeds 2 * LOGIT_TOL * max|logit| (near ties are reported, not failed).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from _util import LOGIT_TOL, golden, ptr
+from jieyu_b200 import _capi
+from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def c0(cuda):
+    hw = HostWeights.synthetic(CONFIGS["c0"])
+    m = DeviceModel(hw)
+    yield hw, m
+    m.close()
+
+
+def test_kat_bind_weights(cuda):
+    """check_bind_weights cases 6 and 9 (libs/text/text.h:817-913)."""
+    g = golden("kat.json")
+    m = DeviceModel(HostWeights.bind_test_kat())
+    assert list(m.generate(np.array([1, 2, 3]), 3)) == g["bind_123"]
+    a = m.generate(np.array([5, 6, 7]), 3)
+    b = m.generate(np.array([5, 6, 7]), 3)
+    assert list(a) == g["bind_567"] and list(a) == list(b)
+    m.close()
+
+
+def test_kat_shift_demo(cuda):
+    """check_pipeline case 6 (libs/text/text.h:993-1002): "abcdefgh" -> "ijklmnopqrstuvwx"."""
+    g = golden("kat.json")
+    m = DeviceModel(HostWeights.shift_demo_kat())
+    out = m.generate(np.arange(97, 105), 16)
+    assert list(out) == g["shift_abcdefgh"]
+    assert bytes(out[8:].astype(np.uint8)).decode() == "ijklmnopqrstuvwx"
+    m.close()
+
+
+def test_q8_models_decode_with_the_megakernel(c0):
+    hw, m = c0
+    lib = _capi.load()
+    assert lib.jyc_model_decode_path(m.h) == 2
+    assert lib.jyc_model_kernels_per_step(m.h) == 1
+    assert lib.jyc_device_error(0) == 0
+
+
+def test_c0_greedy_128_tokens_identical(c0):
+    """32-token prompt, 128 greedy tokens == the reference's."""
+    hw, m = c0
+    g = golden("c0.json")
+    prompt = np.array(g["prompt"], dtype=np.int32)
+    assert list(prompt) == list(prompt_ids(hw.cfg))
+    out = m.generate(prompt, hw.cfg.new_tokens)
+    assert len(out) == len(g["greedy"]) == 32 + 128
+    assert list(out) == g["greedy"]
+
+
+def _teacher_forced(m, hw, oracle, prompt, steps):
+    """Device and oracle fed the same tokens; yields (step, device, oracle) logits."""
+    cfg = hw.cfg
+    cache = oracle.cache_create(cfg.layers, cfg.max_seq, cfg.kv_heads, cfg.head_dim)
+    want = np.empty(cfg.vocab, np.float32)
+    tok = np.ascontiguousarray(prompt, np.int32)
+    pos = 0
+    try:
+        for s in range(steps + 1):
+            got = m.forward_logits(tok, pos)
+            assert oracle.forward_logits(C.byref(hw.desc), cache, ptr(tok), len(tok), pos,
+                                         ptr(want), None) == 0
+            yield s, got, want.copy(), cache, pos + len(tok)
+            pos += len(tok)
+            tok = np.array([int(np.argmax(want))], np.int32)
+    finally:
+        oracle.cache_free(cache)
+
+
+def _check_logits(got, want, ref_row=None):
+    amax = np.abs(want).max()
+    err = np.abs(got - want).max()
+    assert err <= LOGIT_TOL * amax, f"max|dlogit| {err} > {LOGIT_TOL} * {amax}"
+    top = np.sort(want.astype(np.float64))[-2:]
+    gap = top[1] - top[0]
+    if gap > 2 * LOGIT_TOL * amax:
+        assert int(np.argmax(got)) == int(np.argmax(want))
+    if ref_row is not None:
+        assert int(np.argmax(want)) == ref_row["argmax"]
+    return err / amax
+
+
+def test_c0_teacher_forced_logits(c0, oracle):
+    hw, m = c0
+    g = golden("c0.json")
+    rels = []
+    for s, got, want, cache, n in _teacher_forced(m, hw, oracle, g["prompt"], 16):
+        rels.append(_check_logits(got, want, g["teacher_forced"][s]))
+    assert max(rels) < LOGIT_TOL
+
+
+def test_c0_kv_cache_bytes(c0, oracle):
+    """int8 KV rows the device appended vs the oracle's (identical inputs up to
+    fp32 summation order: bytes may differ by one quantisation step at a
+    rounding tie, on a vanishing fraction of entries)."""
+    hw, m = c0
+    cfg = hw.cfg
+    g = golden("c0.json")
+    last = None
+    for s, got, want, cache, n in _teacher_forced(m, hw, oracle, g["prompt"], 3):
+        last = (cache, n)
+        if s == 3:
+            cache, n = last
+            for layer in (0, cfg.layers - 1):
+                k = np.empty(n * cfg.kv_dim, np.int8)
+                v = np.empty_like(k)
+                ks = np.empty(n * cfg.kv_heads, np.float32)
+                vs = np.empty_like(ks)
+                oracle.cache_read(cache, layer, n, ptr(k), ptr(ks), ptr(v), ptr(vs))
+                dk, dks, dv, dvs = m.read_kv(layer, n)
+                for a, b in ((dk, k), (dv, v)):
+                    diff = np.abs(a.astype(np.int32) - b.astype(np.int32))
+                    assert diff.max() <= 1 and (diff > 0).mean() < 1e-3
+                for a, b in ((dks, ks), (dvs, vs)):
+                    assert np.allclose(a, b, rtol=1e-5, atol=0)
+                if layer == 0:
+                    # layer 0 sees identical inputs (embedding rows): bit-exact
+                    assert np.array_equal(dk, k) and np.array_equal(dv, v)
+
+
+def test_c1_shape_greedy_and_logits(cuda, oracle):
+    """configs[1] shape (tied Q8_0 embedding, QKV bias, theta 1e6)."""
+    g = golden("c1.json")
+    hw = HostWeights.synthetic(CONFIGS["c1"])
+    m = DeviceModel(hw)
+    out = m.generate(np.array(g["prompt"], np.int32), 16)
+    assert list(out) == g["greedy"]
+    for s, got, want, cache, n in _teacher_forced(m, hw, oracle, g["prompt"], 4):
+        _check_logits(got, want, g["teacher_forced"][s])
+    m.close()
+
+
+@pytest.mark.parametrize("key", ["c2", "c2f"])
+def test_c2_shapes_short(cuda, oracle, key):
+    """configs[2] shape, Q8_0 and fp32 variants: 8-token prompt + 3 steps."""
+    from dataclasses import replace
+    cfg = replace(CONFIGS[key], max_seq=256)
+    hw = HostWeights.synthetic(cfg)
+    m = DeviceModel(hw)
+    pr = prompt_ids(cfg, n=8)
+    for s, got, want, cache, n in _teacher_forced(m, hw, oracle, pr, 3):
+        _check_logits(got, want)
+    m.close()
+
+
+def test_generate_contract_edges(c0):
+    hw, m = c0
+    pr = prompt_ids(hw.cfg)
+    lib = _capi.load()
+    out = np.zeros(hw.cfg.max_seq + 1, np.int32)
+    e = np.zeros(1, np.int32)
+    cb = _capi.TOKEN_CB()
+    # prompt_len <= 0 or > max_seq -> 0 (generate.h:25)
+    assert lib.jyc_generate(m.h, ptr(pr), 0, ptr(e), 0, 4, 0.0, ptr(out), 1.0, cb, None) == 0
+    big = np.zeros(hw.cfg.max_seq + 1, np.int32)
+    assert lib.jyc_generate(m.h, ptr(big), len(big), ptr(e), 0, 4, 0.0, ptr(out), 1.0, cb, None) == 0
+    # max_new <= 0 -> prompt_len (generate.h:32)
+    assert lib.jyc_generate(m.h, ptr(pr), 32, ptr(e), 0, 0, 0.0, ptr(out), 1.0, cb, None) == 32
+    # prompt fills the context: nothing generated
+    full = prompt_ids(hw.cfg, n=hw.cfg.max_seq)
+    assert len(m.generate(full, 4)) == hw.cfg.max_seq
+    # context limit: len stops at max_seq
+    near = prompt_ids(hw.cfg, n=hw.cfg.max_seq - 3)
+    assert len(m.generate(near, 50)) == hw.cfg.max_seq
+    # out-of-range id -> error
+    bad = pr.copy()
+    bad[3] = hw.cfg.vocab
+    with pytest.raises(_capi.JycError):
+        m.generate(bad, 2)
+
+
+def test_generate_eos_and_callback(c0):
+    hw, m = c0
+    g = golden("c0.json")
+    pr = np.array(g["prompt"], np.int32)
+    ref = g["greedy"]
+    # EOS = the 5th generated token: generation stops right after emitting it
+    eos_tok = ref[32 + 4]
+    first = ref[32:].index(eos_tok)
+    out = m.generate(pr, 100, eos=[eos_tok])
+    assert list(out) == ref[: 32 + first + 1]
+    # callback asks to stop after 3 tokens (generate.h:79)
+    seen = []
+    out = m.generate(pr, 100, cb=lambda t: (seen.append(t), len(seen) >= 3)[1])
+    assert seen == ref[32:35] and list(out) == ref[:35]
+
+
+def test_sampling_not_built_fails_loudly(c0):
+    hw, m = c0
+    with pytest.raises(_capi.JycError) as ei:
+        m.generate(prompt_ids(hw.cfg), 4, temperature=0.8)
+    assert ei.value.code == _capi.JYC_ERR_UNSUPPORTED

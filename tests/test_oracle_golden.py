@@ -1,0 +1,68 @@
+"""CPU: the oracle (plain-C restatement) reproduces the reference's own outputs
+recorded in tests/golden (produced by tests/golden/make_golden.py running the
+reference). These pin the checker the GPU tests trust."""
+import ctypes as C
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from _util import golden, ptr, sha
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+import make_golden  # noqa: E402
+
+from jieyu_b200.model import CONFIGS, HostWeights, prompt_ids  # noqa: E402
+
+
+def test_oracle_ops_match_reference_digests(oracle):
+    want = golden("ops.json")["ops"]
+    got = make_golden.run_ops(oracle)
+    assert set(got) == set(want)
+    bad = [k for k in want if got[k] != want[k]]
+    assert not bad, f"oracle differs from the reference on {bad}"
+
+
+def test_oracle_kats(oracle):
+    g = golden("kat.json")
+    hw = HostWeights.bind_test_kat()
+    assert list(oracle.generate(hw.desc, [1, 2, 3], 3, max_seq=8)) == g["bind_123"]
+    assert list(oracle.generate(hw.desc, [5, 6, 7], 3, max_seq=8)) == g["bind_567"]
+    hs = HostWeights.shift_demo_kat()
+    assert list(oracle.generate(hs.desc, list(range(97, 105)), 16, max_seq=1024)) == g["shift_abcdefgh"]
+
+
+def test_oracle_c0_greedy_and_logits(oracle):
+    g = golden("c0.json")
+    cfg = CONFIGS["c0"]
+    hw = HostWeights.synthetic(cfg)
+    pr = prompt_ids(cfg)
+    assert list(pr) == g["prompt"]
+    assert list(oracle.generate(hw.desc, pr, cfg.new_tokens, max_seq=cfg.max_seq)) == g["greedy"]
+    rows, kv = make_golden.teacher_forced(oracle, hw, pr, 16)
+    assert [r["sha"] for r in rows] == [r["sha"] for r in g["teacher_forced"]]
+    assert kv == g["kv_sha"]
+
+
+def test_oracle_c1_shape(oracle):
+    g = golden("c1.json")
+    cfg = CONFIGS["c1"]
+    hw = HostWeights.synthetic(cfg)
+    pr = prompt_ids(cfg, n=16)
+    assert list(pr) == g["prompt"]
+    assert list(oracle.generate(hw.desc, pr, 16, max_seq=cfg.max_seq)) == g["greedy"]
+    rows, kv = make_golden.teacher_forced(oracle, hw, pr, 4)
+    assert [r["sha"] for r in rows] == [r["sha"] for r in g["teacher_forced"]]
+    assert kv == g["kv_sha"]
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(os.path.dirname(
+    os.path.abspath(__file__))), "oracle", "_ref", "libjyref.so")), reason="reference build absent")
+def test_reference_build_still_matches_golden():
+    """The prebuilt reference harness (oracle/_ref) reproduces the fixtures on this host."""
+    from oracle.bind import Reference
+    ref = Reference("fma", 0)
+    want = golden("ops.json")["ops"]
+    got = make_golden.run_ops(ref)
+    assert got == want
