@@ -251,9 +251,13 @@ def run_b200(args):
         _capi.check(lib.jyc_model_profile_decode(m.h, 64, s, kms, kl, kb))
         stream.synchronize()
 
-    # roofline of the dominant kernel class (HBM-bound GEMV)
+    # roofline of the dominant kernel (HBM-bound): the decode megakernel (one
+    # launch per token, algorithmic bytes = weights + KV read per token), or on
+    # the generic path the largest kernel class
     peak, peak_kind = measured_peaks()
-    shares = {KCLASSES[i]: kms[i] for i in range(8)}
+    mega = lib.jyc_model_decode_path(m.h) == 2
+    classes = ["mega_step_kernel"] + [f"unused{i}" for i in range(1, 8)] if mega else KCLASSES
+    shares = {classes[i]: kms[i] for i in range(8) if kl[i] > 0}
     total_k = sum(shares.values())
     dom = max(range(8), key=lambda i: kms[i])
     per_launch_ms = kms[dom] / max(kl[dom], 1)
@@ -262,7 +266,7 @@ def run_b200(args):
     tpath = os.path.join(ROOT, "profiles", "traffic_c1_decode.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get(KCLASSES[dom])
+            traffic = json.load(f).get(classes[dom])
     weight_bytes = hw.weight_bytes_per_token()
     kv_bytes = float(lib.jyc_model_kv_bytes_per_token(m.h, PROMPT + 1 + DECODE // 2))
     step_gbs = (weight_bytes + kv_bytes) / (ms_per_step / DECODE / 1e3) / 1e9
@@ -312,7 +316,7 @@ def run_b200(args):
                    "l2": "inputs larger than L2 (525 MB of weights per token vs 126 MB L2)"},
         "hbm": {"gbs_per_step": step_gbs, "bytes_per_token": weight_bytes + kv_bytes,
                 "frac_of_peak": step_gbs / peak, "peak_gbs": peak, "peak_kind": peak_kind},
-        "roofline": {"bound": "hbm", "kernel": KCLASSES[dom], "achieved": achieved, "peak": peak,
+        "roofline": {"bound": "hbm", "kernel": classes[dom], "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "bytes_per_launch": kb[dom], "launch_ms": per_launch_ms,
                      "peak_kind": peak_kind},

@@ -47,10 +47,10 @@
 namespace jyc {
 
 constexpr int kMegaThreads = (kMegaCW + 1) * 32;
-constexpr int kASB = 128;  // attention positions per sub-block
 
 // Error word of the device kernels (non-zero: a bounded wait gave up; the
-// value tells which: 3 ring slot free, 4 ring slot full, 5 grid barrier).
+// value tells which: 3 ring slot free, 4 ring slot full, 5 grid barrier,
+// 6 attention K/V copy).
 __device__ int g_err_word;
 
 int* device_error_word() {
@@ -69,7 +69,11 @@ static __host__ __device__ __forceinline__ int swz_chunk(int c, int r, int nch) 
 }
 
 // ---------------------------------------------------------------------------
-// Tiled repack: reference blocks [n][k/32] x 34 B -> [cb][row][w_cb] layout.
+// Tiled repack: reference blocks [n][k/32] x 34 B -> [cb][row][w_cb] q layout
+// and the paired scale layout (see mega.cuh). Negative scales (no Q8_0
+// quantiser writes them: d = amax / 127) are flagged in g_neg_scale.
+__device__ int g_neg_scale;
+
 __global__ void q8_repack_tiled_kernel(const uint8_t* blocks, size_t nblocks, int nb, int k, uint8_t* qs,
                                        uint16_t* d, int n_total, int row_off, int row_stride) {
     for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < nblocks;
@@ -80,7 +84,9 @@ __global__ void q8_repack_tiled_kernel(const uint8_t* blocks, size_t nblocks, in
         const int col0 = bl * 32, cb = col0 / kMegaCB, w = min(kMegaCB, k - cb * kMegaCB);
         const int c = (col0 - cb * kMegaCB) / 16;  // even: first of the block's two chunks
         const uint8_t* src = blocks + b * 34;
-        d[(size_t)cb * n_total * (kMegaCB / 32) + R * (w / 32) + c / 2] = (uint16_t)src[0] | ((uint16_t)src[1] << 8);
+        const uint16_t dh = (uint16_t)src[0] | ((uint16_t)src[1] << 8);
+        if ((dh & 0x8000u) && (dh & 0x7fffu)) atomicOr(&g_neg_scale, 1);
+        d[(size_t)cb * n_total * (kMegaCB / 32) + mega_d_index(R, c / 2, w / 32)] = dh;
         uint8_t* row = qs + (size_t)cb * n_total * kMegaCB + R * w;
         for (int h = 0; h < 2; h++) {
             uint32_t* q = reinterpret_cast<uint32_t*>(row + 16 * swz_chunk(c + h, (int)(R & 7), w / 16));
@@ -91,6 +97,16 @@ __global__ void q8_repack_tiled_kernel(const uint8_t* blocks, size_t nblocks, in
             }
         }
     }
+}
+
+int mega_negative_scales(bool reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_neg_scale, sizeof(int)) != cudaSuccess) return -1;
+    if (reset) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(g_neg_scale, &z, sizeof(int)) != cudaSuccess) return -1;
+    }
+    return v;
 }
 
 int launch_q8_repack_tiled(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d, int n_total,
@@ -112,23 +128,101 @@ static __device__ __forceinline__ int mat_tiles(const MegaMat& M, int b) {
     return ((r1 - r0 + M.rt - 1) / M.rt) * ((M.k + kMegaCB - 1) / kMegaCB);
 }
 
-static __device__ bool produce_mat(const MegaMat& M, int b, int& t, int ns, uint64_t* full, uint64_t* empty,
-                                   unsigned char* ring, uint64_t pol, int* err) {
-    const int r_begin = b * M.rpc, r_end = min(r_begin + M.rpc, M.n);
-    const int ncb = (M.k + kMegaCB - 1) / kMegaCB;
-    for (int r0 = r_begin; r0 < r_end; r0 += M.rt) {
-        const int rows = min(M.rt, r_end - r0);
-        for (int cb = 0; cb < ncb; cb++, t++) {
-            const int s = t % ns, u = t / ns;
-            if (u > 0 && !mbar_wait_err(&empty[s], (u - 1) & 1, err, 3)) return false;
-            const int w = min(kMegaCB, M.k - cb * kMegaCB);
-            unsigned char* slot = ring + (size_t)s * kMegaSlotBytes;
-            const uint32_t qb = (uint32_t)(rows * w), db = (uint32_t)(rows * (w / 32) * 2);
-            mbar_expect_tx(&full[s], qb + db);
-            bulk_g2s(slot, M.qs + (size_t)cb * M.n * kMegaCB + (size_t)r0 * w, qb, &full[s], pol);
-            bulk_g2s(slot + kMegaRT * kMegaCB, M.d + (size_t)cb * M.n * (kMegaCB / 32) + (size_t)r0 * (w / 32),
-                     db, &full[s], pol);
+// Position in the ring: slot and the parity of its current fill.
+struct RingPos {
+    int s, ph;
+    __device__ __forceinline__ void next(int ns) {
+        if (++s == ns) {
+            s = 0;
+            ph ^= 1;
         }
+    }
+};
+
+// One weight tile (rows r0.., column block cb) into ring slot `slot`: two 1-D
+// bulk copies (q bytes, then the fp16 scales) completing on `bar`.
+static __device__ __forceinline__ void load_tile(const MegaMat& M, int r0, int rows, int cb, unsigned char* slot,
+                                                 uint64_t* bar, uint64_t pol) {
+    const int w = min(kMegaCB, M.k - cb * kMegaCB);
+    const uint32_t qb = (uint32_t)(rows * w), db = (uint32_t)(rows * (w / 32) * 2);
+    mbar_expect_tx(bar, qb + db);
+    bulk_g2s(slot, M.qs + (size_t)cb * M.n * kMegaCB + (size_t)r0 * w, qb, bar, pol);
+    bulk_g2s(slot + kMegaRT * kMegaCB, M.d + (size_t)cb * M.n * (kMegaCB / 32) + (size_t)r0 * (w / 32), db, bar,
+             pol);
+}
+
+// The same tile pulled into L2 ahead of its ring slot (no completion).
+static __device__ __forceinline__ void prefetch_tile(const MegaMat& M, int r0, int rows, int cb) {
+    const int w = min(kMegaCB, M.k - cb * kMegaCB);
+    bulk_prefetch_l2(M.qs + (size_t)cb * M.n * kMegaCB + (size_t)r0 * w, (uint32_t)(rows * w));
+    bulk_prefetch_l2(M.d + (size_t)cb * M.n * (kMegaCB / 32) + (size_t)r0 * (w / 32), (uint32_t)(rows * (w / 32) * 2));
+}
+
+// Walk over one CTA's tiles of the whole step, in consumer order: per layer
+// QKV, O, gate/up, down, then the LM head (l == L). Row tiles outer, column
+// blocks inner, as consume_mat takes them.
+struct TileCursor {
+    int l, m, r0, r_end, cb, ncb;
+    const MegaMat* M;
+};
+
+static __device__ __forceinline__ const MegaMat* cursor_mat(const MegaArgs& a, int l, int m) {
+    if (l >= a.L) return &a.head;
+    const MegaLayer& ly = a.layers[l];
+    return m == 0 ? &ly.qkv : m == 1 ? &ly.o : m == 2 ? &ly.gu : &ly.dn;
+}
+
+// positions c on the first tile of matrix (c.l, c.m) or later; false past the head
+static __device__ bool cursor_enter(const MegaArgs& a, TileCursor& c, int b) {
+    while (c.l <= a.L) {
+        c.M = cursor_mat(a, c.l, c.m);
+        c.r0 = b * c.M->rpc;
+        c.r_end = min(c.r0 + c.M->rpc, c.M->n);
+        c.cb = 0;
+        c.ncb = (c.M->k + kMegaCB - 1) / kMegaCB;
+        if (c.r0 < c.r_end) return true;
+        if (c.l == a.L || ++c.m == 4) {
+            c.m = 0;
+            c.l++;
+        }
+    }
+    return false;
+}
+
+static __device__ bool cursor_next(const MegaArgs& a, TileCursor& c, int b) {
+    if (++c.cb < c.ncb) return true;
+    c.cb = 0;
+    c.r0 += c.M->rt;
+    if (c.r0 < c.r_end) return true;
+    if (c.l == a.L || ++c.m == 4) {
+        c.m = 0;
+        c.l++;
+    }
+    return cursor_enter(a, c, b);
+}
+
+// Producer (one thread): every tile of the step into the ring, `pf` tiles of
+// L2 prefetch ahead of the ring. Returns false when a bounded wait gave up.
+static __device__ bool produce_step(const MegaArgs& a, int b, int ns, uint64_t* full, uint64_t* empty,
+                                    unsigned char* ring) {
+    const uint64_t pol = policy_evict_first();
+    TileCursor c{0, 0, 0, 0, 0, 0, nullptr}, p{0, 0, 0, 0, 0, 0, nullptr};
+    bool have = cursor_enter(a, c, b), phave = cursor_enter(a, p, b);
+    for (int i = 0; i < a.pf_tiles && phave; i++) {
+        prefetch_tile(*p.M, p.r0, min(p.M->rt, p.r_end - p.r0), p.cb);
+        phave = cursor_next(a, p, b);
+    }
+    RingPos rp{0, 0};
+    for (int t = 0; have; t++) {
+        if (t >= ns && !mbar_wait_err(&empty[rp.s], rp.ph ^ 1, a.err, 3)) return false;
+        load_tile(*c.M, c.r0, min(c.M->rt, c.r_end - c.r0), c.cb, ring + (size_t)rp.s * kMegaSlotBytes, &full[rp.s],
+                  pol);
+        rp.next(ns);
+        if (phave) {
+            prefetch_tile(*p.M, p.r0, min(p.M->rt, p.r_end - p.r0), p.cb);
+            phave = cursor_next(a, p, b);
+        }
+        have = cursor_next(a, c, b);
     }
     return true;
 }
@@ -144,58 +238,98 @@ static __device__ __forceinline__ void mma_s8(uint32_t a0, uint32_t a1, uint32_t
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// Exact float of an integer |c| < 2^22 with one integer and one float add
+// (the 1.5 * 2^23 bias puts c in the mantissa), avoiding the conversion unit.
+static __device__ __forceinline__ float small_i2f(int c) {
+    return __fadd_rn(__int_as_float(c + 0x4B400000), -12582912.0f);
+}
+
+// Scale pair (rows g, g+8 of a 16-row group, one Q8 block) -> both fp16
+// values as fp32 times 2^-112: exponent and mantissa moved to the fp32
+// position (exact, subnormals included; scales are non-negative, checked at
+// repack). The caller's factor carries the 2^112.
+static __device__ __forceinline__ float d_lo(uint32_t w) { return __int_as_float((w << 13) & 0x0FFFE000u); }
+static __device__ __forceinline__ float d_hi(uint32_t w) { return __int_as_float((w >> 3) & 0x0FFFE000u); }
+
 // y[rows of this CTA] = W . x for one matrix; x given as 3 int8 digit planes
 // xd[0..2][k] and per-32 block scales xsc[k/32].
+//
+// Fragment use of m16n8k32: B column j < 3 holds digit j of x (lanes g < 3
+// load it), columns 3..7 are zero. Lane (g, tq) receives C columns 2tq, 2tq+1
+// of rows g and g+8: lane tq=0 digit sums a, b, lane tq=1 digit sum c and a
+// zero, lanes tq=2,3 zeros. Every lane forms u = s1 * f(C0) + f(C1) (s1 = 2^7
+// on tq=0, 1 elsewhere) and accumulates u * d * sx * m (m = 2^7 on tq=0), i.e.
+// 2^14 a + 2^7 b on tq=0 and c on tq=1; the two meet once per row tile.
+// Accumulators carry a 2^-28 factor (scale products stay normal for block
+// maxima down to 2^-54 and finite up to 2^57), removed at the end.
 template <int EPI>
-static __device__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, int& t, int ns,
+static __device__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, RingPos& rp, int ns,
                                    uint64_t* full, uint64_t* empty, const unsigned char* ring, float* s_part,
                                    float* s_res, float* y, const float* bias, unsigned long long* s_best,
                                    int* err) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int g = lane >> 2, tq = lane & 3;
+    const float s1 = tq == 0 ? 128.0f : 1.0f;
+    const float km = tq == 0 ? 0x1p91f : 0x1p84f;  // 2^112 * 2^-28 * m
     const int r_begin = b * M.rpc, r_end = min(r_begin + M.rpc, M.n);
     const int ncb = (M.k + kMegaCB - 1) / kMegaCB;
+    const int wl = M.k - (ncb - 1) * kMegaCB;  // width of the last column block
+    // Warp w takes the 32-column blocks w + i * kMegaCW (i < BPW) of each tile.
+    // Per-lane A fragment offsets (rows g and g+8 of every 16-row group share
+    // the swizzled chunk since row & 7 == g) for full and last column blocks.
+    constexpr int BPW = (kMegaCB / 32) / kMegaCW;
+    int a_full[BPW], a_last[BPW];
+#pragma unroll
+    for (int i = 0; i < BPW; i++) {
+        const int bw = warp + i * kMegaCW, cf = 2 * bw + (tq >> 1), co = 8 * (tq & 1);
+        a_full[i] = g * kMegaCB + 16 * swz_chunk(cf, g, kMegaCB / 16) + co;
+        a_last[i] = g * wl + 16 * swz_chunk(cf, g, wl / 16) + co;
+    }
+    const int8_t* xb = xd + (size_t)min(g, 2) * M.k + 32 * warp + 8 * tq;
     constexpr int NRG = kMegaRT / 16;
     for (int r0 = r_begin; r0 < r_end; r0 += M.rt) {
         const int rows = min(M.rt, r_end - r0), nrg = rows >> 4;
         float acc[NRG][2];
 #pragma unroll
         for (int j = 0; j < NRG; j++) acc[j][0] = acc[j][1] = 0.0f;
-        for (int cb = 0; cb < ncb; cb++, t++) {
-            const int s = t % ns, u = t / ns;
-            if (!mbar_wait_err(&full[s], u & 1, err, 4)) return false;
-            const int w = min(kMegaCB, M.k - cb * kMegaCB), nblk = w >> 5, nch = w >> 4;
-            if (warp < nblk) {
-                const unsigned char* slot = ring + (size_t)s * kMegaSlotBytes;
-                const uint16_t* sd = reinterpret_cast<const uint16_t*>(slot + kMegaRT * kMegaCB);
-                const int col = cb * kMegaCB + 32 * warp + 8 * tq;
-                uint2 bf = make_uint2(0u, 0u);
-                if (g < 3) bf = *reinterpret_cast<const uint2*>(xd + (size_t)g * M.k + col);
-                const float sx = xsc[cb * (kMegaCB / 32) + warp];
-                const int c = 2 * warp + (tq >> 1), off = 8 * (tq & 1);
+        for (int cb = 0; cb < ncb; cb++) {
+            if (!mbar_wait_err(&full[rp.s], rp.ph, err, 4)) return false;
+            const bool lastb = cb == ncb - 1;
+            const int w = lastb ? wl : kMegaCB, nblk = w >> 5;
+            const unsigned char* slot = ring + (size_t)rp.s * kMegaSlotBytes;
 #pragma unroll
-                for (int rg = 0; rg < NRG; rg++) {
-                    if (rg < nrg) {
-                        const int ra = rg * 16 + g, rb = ra + 8;
-                        const uint2 A0 = *reinterpret_cast<const uint2*>(slot + ra * w + 16 * swz_chunk(c, ra, nch) + off);
-                        const uint2 A1 = *reinterpret_cast<const uint2*>(slot + rb * w + 16 * swz_chunk(c, rb, nch) + off);
-                        int c0, c1, c2, c3;
-                        mma_s8(A0.x, A1.x, A0.y, A1.y, bf.x, bf.y, c0, c1, c2, c3);
-                        // digit 2 (column 2) sits in the next lane of the quad
-                        const int la = __shfl_down_sync(0xffffffffu, c0, 1);
-                        const int lb = __shfl_down_sync(0xffffffffu, c2, 1);
-                        if (tq == 0) {
-                            const float da = h2f(sd[ra * nblk + warp]), db = h2f(sd[rb * nblk + warp]);
-                            const float fa = __fmaf_rn(16384.0f, (float)c0, (float)(128 * c1 + la));
-                            const float fb = __fmaf_rn(16384.0f, (float)c2, (float)(128 * c3 + lb));
-                            acc[rg][0] = __fmaf_rn(fa, __fmul_rn(sx, da), acc[rg][0]);
-                            acc[rg][1] = __fmaf_rn(fb, __fmul_rn(sx, db), acc[rg][1]);
+            for (int i = 0; i < BPW; i++) {
+                const int bw = warp + i * kMegaCW;
+                if (bw < nblk) {
+                    const uint32_t* dp = reinterpret_cast<const uint32_t*>(slot + kMegaRT * kMegaCB) + bw * 8 + g;
+                    uint2 bf = make_uint2(0u, 0u);
+                    if (g < 3) bf = *reinterpret_cast<const uint2*>(xb + cb * kMegaCB + 32 * i * kMegaCW);
+                    const float kx = __fmul_rn(xsc[cb * (kMegaCB / 32) + bw], km);
+                    const unsigned char* ap = slot + (lastb ? a_last[i] : a_full[i]);
+#pragma unroll
+                    for (int rg = 0; rg < NRG; rg++) {
+                        if (rg < nrg) {
+                            const uint2 A0 = *reinterpret_cast<const uint2*>(ap + rg * 16 * w);
+                            const uint2 A1 = *reinterpret_cast<const uint2*>(ap + (rg * 16 + 8) * w);
+                            const uint32_t dw = dp[rg * nblk * 8];
+                            int c0, c1, c2, c3;
+                            mma_s8(A0.x, A1.x, A0.y, A1.y, bf.x, bf.y, c0, c1, c2, c3);
+                            const float va = __fmaf_rn(s1, small_i2f(c0), small_i2f(c1));
+                            const float vb = __fmaf_rn(s1, small_i2f(c2), small_i2f(c3));
+                            acc[rg][0] = __fmaf_rn(va, __fmul_rn(d_lo(dw), kx), acc[rg][0]);
+                            acc[rg][1] = __fmaf_rn(vb, __fmul_rn(d_hi(dw), kx), acc[rg][1]);
                         }
                     }
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            if (lane == 0) mbar_arrive(&empty[rp.s]);
+            rp.next(ns);
+        }
+#pragma unroll
+        for (int rg = 0; rg < NRG; rg++) {
+            acc[rg][0] = __fadd_rn(acc[rg][0], __shfl_down_sync(0xffffffffu, acc[rg][0], 1));
+            acc[rg][1] = __fadd_rn(acc[rg][1], __shfl_down_sync(0xffffffffu, acc[rg][1], 1));
         }
         if (tq == 0) {
 #pragma unroll
@@ -210,7 +344,7 @@ static __device__ bool consume_mat(const MegaMat& M, const int8_t* xd, const flo
             float v = 0.0f;
 #pragma unroll
             for (int w2 = 0; w2 < kMegaCW; w2++) v = __fadd_rn(v, s_part[w2 * kMegaRT + e]);
-            s_res[e] = v;
+            s_res[e] = __fmul_rn(v, 0x1p28f);
         }
         csync();
         if (EPI == ME_SWIGLU) {
@@ -322,6 +456,10 @@ static __device__ bool grid_barrier(unsigned int* ctr, unsigned int target, int*
                     ok = 0;
                     break;
                 }
+                if (*(volatile int*)err != 0) {  // another CTA gave up: leave too
+                    ok = 0;
+                    break;
+                }
             }
         }
         *s_ok = ok;
@@ -330,9 +468,49 @@ static __device__ bool grid_barrier(unsigned int* ctr, unsigned int target, int*
     return *s_ok != 0;
 }
 
-// RoPE (reference slot order) + kv_pack_q8 quantisation of one head by one warp.
+// Shared-memory plan of one attention item (byte offsets inside the region
+// the x vector also uses): K and V sub-chunk tiles (TMA destinations; after
+// the PV loop the same bytes hold the cross-warp partial sums, and in the
+// split merge the (m, l) pairs and merge weights), scores, K/V scales, the
+// quantised query heads, the new position's K/V row, softmax state.
+struct AttnPlan {
+    int kv, sc, ks, vs, q8, row, qsc, m, l, al, total;
+};
+
+static __host__ __device__ __forceinline__ AttnPlan attn_plan(int G, int hd, int S) {
+    AttnPlan p;
+    const int red = kMegaCW * G * hd * 4;  // partial rows of the P.V reduction
+    int o = 0;
+    p.kv = o;
+    o += (max(2 * S * hd, red) + 15) / 16 * 16;
+    p.sc = o;
+    o += G * S * 4;
+    p.ks = o;
+    o += S * 4;
+    p.vs = o;
+    o += S * 4;
+    p.q8 = o;
+    o += (G * hd + 15) / 16 * 16;
+    p.row = o;
+    o += (2 * hd + 8 + 15) / 16 * 16;
+    p.qsc = o;
+    o += G * 4;
+    p.m = o;
+    o += G * 4;
+    p.l = o;
+    o += G * 4;
+    p.al = o;
+    o += G * 4;
+    p.total = (o + 127) / 128 * 128;
+    return p;
+}
+
+// RoPE (when ct; rotated pairs stored in the reference's slot order) +
+// kv_pack_q8 quantisation of one head row by a warp; the row goes
+// to dst/scale_out and, when dst2, also to dst2/scale2.
 static __device__ __forceinline__ void rq_warp(const float* src, int hd, const float* ct, const float* stb,
-                                               int8_t* dst, float* scale_out, int lane) {
+                                               int8_t* dst, float* scale_out, int lane, int8_t* dst2 = nullptr,
+                                               float* scale2 = nullptr) {
     constexpr int MAXP = 4;
     const int half = hd >> 1;
     float x0[MAXP], x1[MAXP];
@@ -358,50 +536,79 @@ static __device__ __forceinline__ void rq_warp(const float* src, int hd, const f
     }
     amax = warp_max(amax);
     const float inv = q8_inv(amax);
-    if (lane == 0) *scale_out = q8_scale(amax);
+    if (lane == 0) {
+        *scale_out = q8_scale(amax);
+        if (scale2) *scale2 = q8_scale(amax);
+    }
 #pragma unroll
     for (int tt = 0; tt < MAXP; tt++) {
         const int p = lane + 32 * tt;
         if (p < half) {
             const int o = ct ? rope_slot(p, half) : p;
-            dst[2 * o] = (int8_t)q8_round(x0[tt], inv);
-            dst[2 * o + 1] = (int8_t)q8_round(x1[tt], inv);
+            const int8_t q0 = (int8_t)q8_round(x0[tt], inv), q1 = (int8_t)q8_round(x1[tt], inv);
+            dst[2 * o] = q0;
+            dst[2 * o + 1] = q1;
+            if (dst2) {
+                dst2[2 * o] = q0;
+                dst2[2 * o + 1] = q1;
+            }
         }
     }
 }
 
-static int attn_item_smem(int G, int hd) {
-    // q8 [G][hd] | qsc, m, l, alpha [G] | o [G][hd] | w [G][ASB] | K tile [ASB][hd+4] (int8, padded) |
-    // V tile [ASB][hd] (fp32) | ks, vs [ASB]
-    return G * hd + 4 * G * 4 + G * hd * 4 + G * kASB * 4 + kASB * (hd + 4) + kASB * hd * 4 + 2 * kASB * 4;
+// P.V over one sub-chunk for a (column group of 4 dims, position lane)
+// thread: acc[g][i] += p[g][j] * v[j][4cg + i] for j = pl, pl + npl, ...
+template <int MAXG>
+static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const float* s_sc, const int8_t* s_v, int S,
+                                               int G, int hd, int cg, int pl, int npl, int n) {
+    for (int j = pl; j < n; j += npl) {
+        float f[4];
+        u8x4_to_f32(*reinterpret_cast<const uint32_t*>(s_v + j * hd + 4 * cg) ^ 0x80808080u, f);
+#pragma unroll
+        for (int gq = 0; gq < MAXG; gq++)
+            if (gq < G) {
+                const float p = s_sc[gq * S + j];
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[gq][i] = __fmaf_rn(p, f[i], acc[gq][i]);
+            }
+    }
 }
 
-// 16 signed bytes -> 16 exact floats (2^23 mantissa trick on b ^ 0x80 = b + 128)
-static __device__ __forceinline__ void s8x16_to_f32(uint4 w, float* f) {
-    u8x4_to_f32(w.x ^ 0x80808080u, f);
-    u8x4_to_f32(w.y ^ 0x80808080u, f + 4);
-    u8x4_to_f32(w.z ^ 0x80808080u, f + 8);
-    u8x4_to_f32(w.w ^ 0x80808080u, f + 12);
-}
-
-// One (layer, kv head, position split) attention item with the consumer threads.
-static __device__ void attn_item(const MegaArgs& a, int layer, int kvh, int split, int pos, unsigned char* sm) {
-    const int G = a.H / a.KV, hd = a.hd, half = hd >> 1;
+// One (layer, kv head, position split) attention item with the consumer
+// threads (reference: attention over the int8 cache, transformer_layer.h:35-70):
+// RoPE + int8 quantisation of the group's query heads, the K/V append at pos
+// (owner split), then per sub-chunk of up to S positions: a TMA bulk copy of
+// the K and V rows, int8 dot scores (dp4a, rotated word order so the 32 lanes
+// of a warp read 32 different banks of 32 different rows), online softmax,
+// P.V with V decoded once per 4 dims. Writes the split partials (o, m, l);
+// the last item of the kv head to finish merges all splits of its query
+// heads into the q rows of the qkv buffer (the O projection's input).
+template <int MAXG>
+static __device__ bool attn_item(const MegaArgs& a, int layer, int kvh, int split, int nv, int pos,
+                                 unsigned char* sm, uint64_t* abar, uint32_t& aph, int* s_flag, long long* tr) {
+    const int G = a.H / a.KV, hd = a.hd, half = hd >> 1, hw = hd >> 2, S = a.asub;
+#define ATR(k)                                      \
+    do {                                            \
+        if (tr && threadIdx.x == 0) tr[k] = clock64(); \
+    } while (0)
+    ATR(0);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nthr = kMegaCW * 32;
-    const int c0 = split * a.chunk, c1 = min(c0 + a.chunk, pos + 1);
-    int8_t* s_q8 = reinterpret_cast<int8_t*>(sm);
-    float* s_qsc = reinterpret_cast<float*>(sm + G * hd);
-    float* s_m = s_qsc + G;
-    float* s_l = s_m + G;
-    float* s_alpha = s_l + G;
-    float* s_o = s_alpha + G;
-    float* s_w = s_o + G * hd;
-    int8_t* s_k = reinterpret_cast<int8_t*>(s_w + G * kASB);
-    float* s_v = reinterpret_cast<float*>(s_k + kASB * (hd + 4));
-    float* s_ks = s_v + kASB * hd;
-    float* s_vs = s_ks + kASB;
+    const AttnPlan P = attn_plan(G, hd, S);
+    int8_t* s_k = reinterpret_cast<int8_t*>(sm + P.kv);
+    int8_t* s_v = s_k + S * hd;
+    float* s_sc = reinterpret_cast<float*>(sm + P.sc);
+    float* s_ks = reinterpret_cast<float*>(sm + P.ks);
+    float* s_vs = reinterpret_cast<float*>(sm + P.vs);
+    int8_t* s_q8 = reinterpret_cast<int8_t*>(sm + P.q8);
+    int8_t* s_row = reinterpret_cast<int8_t*>(sm + P.row);  // new K row | V row | k scale | v scale
+    float* s_rsc = reinterpret_cast<float*>(s_row + 2 * hd);
+    float* s_qsc = reinterpret_cast<float*>(sm + P.qsc);
+    float* s_m = reinterpret_cast<float*>(sm + P.m);
+    float* s_l = reinterpret_cast<float*>(sm + P.l);
+    float* s_al = reinterpret_cast<float*>(sm + P.al);
 
+    const int c0 = split * a.chunk, c1 = min(c0 + a.chunk, pos + 1);
     const size_t lh = (size_t)layer * a.KV + kvh;
     int8_t* kb = a.k8 + lh * a.max_seq * hd;
     int8_t* vb = a.v8 + lh * a.max_seq * hd;
@@ -410,146 +617,206 @@ static __device__ void attn_item(const MegaArgs& a, int layer, int kvh, int spli
     const float* ct = a.cos_t + (size_t)pos * half;
     const float* stb = a.sin_t + (size_t)pos * half;
     const int q_dim = a.H * hd, kv_dim = a.KV * hd;
+    const bool owner = pos < c1;
+
+    // TMA of the cached rows [j0, min(j0 + S, c1, pos)) of a sub-chunk; false when none
+    auto issue = [&](int j0) -> bool {
+        const int jb = min(min(j0 + S, c1), pos);
+        if (jb <= j0) return false;
+        if (tid == 0) {
+            const uint32_t bytes = (uint32_t)((jb - j0) * hd);
+            fence_proxy_async_smem();
+            mbar_expect_tx(abar, 2 * bytes);
+            const uint64_t pol = policy_evict_first();
+            bulk_g2s(s_k, kb + (size_t)j0 * hd, bytes, abar, pol);
+            bulk_g2s(s_v, vb + (size_t)j0 * hd, bytes, abar, pol);
+        }
+        return true;
+    };
+    bool pending = issue(c0);
 
     for (int gq = warp; gq < G; gq += kMegaCW)
         rq_warp(a.qkv + (size_t)(kvh * G + gq) * hd, hd, ct, stb, s_q8 + gq * hd, s_qsc + gq, lane);
-    if (pos < c1) {  // owner of the new position: append K (roped) and V
+    if (owner) {  // append K (roped) and V at pos; keep a copy for the tile
         if (warp == kMegaCW - 1)
-            rq_warp(a.qkv + q_dim + (size_t)kvh * hd, hd, ct, stb, kb + (size_t)pos * hd, ksb + pos, lane);
+            rq_warp(a.qkv + q_dim + (size_t)kvh * hd, hd, ct, stb, kb + (size_t)pos * hd, ksb + pos, lane, s_row,
+                    s_rsc);
         else if (warp == kMegaCW - 2)
             rq_warp(a.qkv + q_dim + kv_dim + (size_t)kvh * hd, hd, nullptr, nullptr, vb + (size_t)pos * hd,
-                    vsb + pos, lane);
-        __threadfence();  // the appended row is read back below through L2
+                    vsb + pos, lane, s_row + hd, s_rsc + 1);
     }
-    for (int e = tid; e < G * hd; e += nthr) s_o[e] = 0.0f;
     for (int gq = tid; gq < G; gq += nthr) {
         s_m[gq] = -INFINITY;
         s_l[gq] = 0.0f;
     }
+    ATR(1);
+    const int ncg = hd >> 2, npl = nthr / ncg;
+    const int cg = tid % ncg, pl = tid / ncg;
+    float acc[MAXG][4];
+#pragma unroll
+    for (int gq = 0; gq < MAXG; gq++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[gq][i] = 0.0f;
     csync();
-    const int hw = hd >> 2, hv = hd >> 4;
-    for (int j0 = c0; j0 < c1; j0 += kASB) {
-        const int nj = min(kASB, c1 - j0);
-        for (int e = tid; e < nj * hv; e += nthr) {
-            const int j = e / hv, vq = e - j * hv;
-            const size_t off = (size_t)(j0 + j) * hd + 16 * vq;
-            const uint4 kq = __ldcg(reinterpret_cast<const uint4*>(kb + off));
-            const uint4 vq4 = __ldcg(reinterpret_cast<const uint4*>(vb + off));
-            uint32_t* kd = reinterpret_cast<uint32_t*>(s_k + j * (hd + 4) + 16 * vq);
-            kd[0] = kq.x; kd[1] = kq.y; kd[2] = kq.z; kd[3] = kq.w;
-            float f[16];
-            s8x16_to_f32(vq4, f);
-            float4* vd = reinterpret_cast<float4*>(s_v + j * hd + 16 * vq);
-            vd[0] = make_float4(f[0], f[1], f[2], f[3]);
-            vd[1] = make_float4(f[4], f[5], f[6], f[7]);
-            vd[2] = make_float4(f[8], f[9], f[10], f[11]);
-            vd[3] = make_float4(f[12], f[13], f[14], f[15]);
+
+    for (int j0 = c0; j0 < c1; j0 += S) {
+        const int n = min(S, c1 - j0);
+        const int jb = min(j0 + n, pos);  // rows from the cache; pos (if inside) from s_row
+        if (pending) {
+            if (!mbar_wait_err(abar, aph, a.err, 6)) return false;
+            aph ^= 1;
         }
-        for (int j = tid; j < nj; j += nthr) {
-            s_ks[j] = __ldcg(ksb + j0 + j);
-            s_vs[j] = __ldcg(vsb + j0 + j);
+        for (int j = tid; j < n; j += nthr) {
+            const int jj = j0 + j;
+            s_ks[j] = jj < jb ? __ldcg(ksb + jj) : s_rsc[0];
+            s_vs[j] = jj < jb ? __ldcg(vsb + jj) : s_rsc[1];
+        }
+        if (jb < j0 + n) {  // this sub-chunk holds pos: its row from s_row
+            const int r = pos - j0;
+            for (int e = tid; e < hw; e += nthr) {
+                reinterpret_cast<uint32_t*>(s_k + r * hd)[e] = reinterpret_cast<const uint32_t*>(s_row)[e];
+                reinterpret_cast<uint32_t*>(s_v + r * hd)[e] = reinterpret_cast<const uint32_t*>(s_row + hd)[e];
+            }
         }
         csync();
-        for (int e = tid; e < G * kASB; e += nthr) {
-            const int gq = e / kASB, j = e - gq * kASB;
+        ATR(2);
+        // scores: entry (gq, j); word order rotated by j
+        for (int e = tid; e < G * S; e += nthr) {
+            const int gq = e / S, j = e - gq * S;
             float sc = -INFINITY;
-            if (j < nj) {
-                const int* qw = reinterpret_cast<const int*>(s_q8 + gq * hd);
-                const int* kw = reinterpret_cast<const int*>(s_k + j * (hd + 4));
+            if (j < n) {
+                const uint32_t* qw = reinterpret_cast<const uint32_t*>(s_q8 + gq * hd);
+                const uint32_t* kw = reinterpret_cast<const uint32_t*>(s_k + j * hd);
                 int dot = 0;
-                for (int wd = 0; wd < hw; wd++) dot = __dp4a(qw[wd], kw[wd], dot);
+                for (int w = 0; w < hw; w++) {
+                    const int i = (w + j) & (hw - 1);
+                    dot = __dp4a((int)qw[i], (int)kw[i], dot);
+                }
                 const float ksc = __fmul_rn(__fmul_rn(s_ks[j], s_qsc[gq]), a.scale);
                 sc = __fmul_rn((float)dot, ksc);
             }
-            s_w[e] = sc;
+            s_sc[e] = sc;
         }
         csync();
+        ATR(3);
         for (int gq = warp; gq < G; gq += kMegaCW) {
             float mx = -INFINITY;
-            for (int j = lane; j < kASB; j += 32) mx = fmaxf(mx, s_w[gq * kASB + j]);
+            for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_sc[gq * S + j]);
             mx = warp_max(mx);
             const float m_old = s_m[gq], m_new = fmaxf(m_old, mx);
             float sum = 0.0f;
-            for (int j = lane; j < kASB; j += 32) {
-                const float sv = s_w[gq * kASB + j];
+            for (int j = lane; j < n; j += 32) {
+                const float sv = s_sc[gq * S + j];
                 const float e = (sv == -INFINITY) ? 0.0f : expf(sv - m_new);
                 sum += e;
-                s_w[gq * kASB + j] = e * s_vs[j < nj ? j : 0];
+                s_sc[gq * S + j] = e * s_vs[j];
             }
             sum = warp_sum(sum);
             if (lane == 0) {
                 const float alpha = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
-                s_alpha[gq] = alpha;
+                s_al[gq] = alpha;
                 s_l[gq] = s_l[gq] * alpha + sum;
                 s_m[gq] = m_new;
             }
         }
         csync();
-        for (int e = tid; e < G * hd; e += nthr) {
-            const int gq = e / hd, dd = e - gq * hd;
-            float o = s_o[e] * s_alpha[gq];
-            const float* wp = s_w + gq * kASB;
-            const float* vp = s_v + dd;
-#pragma unroll 4
-            for (int j = 0; j < nj; j++) o = __fmaf_rn(wp[j], vp[j * hd], o);
-            s_o[e] = o;
-        }
+        ATR(4);
+#pragma unroll
+        for (int gq = 0; gq < MAXG; gq++)
+            if (gq < G) {
+                const float al = s_al[gq];
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[gq][i] = __fmul_rn(acc[gq][i], al);
+            }
+        attn_pv<MAXG>(acc, s_sc, s_v, S, G, hd, cg, pl, npl, n);
         csync();
+        ATR(5);
+        if (j0 + S < c1) pending = issue(j0 + S);
     }
+    // partial sums of the position lanes: inside a warp, then across warps
+    float* red = reinterpret_cast<float*>(sm + P.kv);
+    for (int off = ncg; off < 32; off <<= 1)
+#pragma unroll
+        for (int gq = 0; gq < MAXG; gq++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[gq][i] = __fadd_rn(acc[gq][i], __shfl_xor_sync(0xffffffffu, acc[gq][i], off));
+    const int nred = ncg >= 32 ? npl : kMegaCW;  // partial rows after the in-warp step
+    const int rrow = ncg >= 32 ? pl : warp;
+    if (ncg >= 32 || lane < ncg) {
+#pragma unroll
+        for (int gq = 0; gq < MAXG; gq++)
+            if (gq < G)
+                *reinterpret_cast<float4*>(red + ((size_t)rrow * G + gq) * hd + 4 * cg) =
+                    make_float4(acc[gq][0], acc[gq][1], acc[gq][2], acc[gq][3]);
+    }
+    csync();
     for (int e = tid; e < G * hd; e += nthr) {
+        float o = 0.0f;
+        for (int r = 0; r < nred; r++) o = __fadd_rn(o, red[(size_t)r * G * hd + e]);
         const int gq = e / hd, dd = e - gq * hd, h = kvh * G + gq;
-        a.part_o[((size_t)h * a.nsplit + split) * hd + dd] = s_o[e];
+        a.part_o[((size_t)h * a.nsplit + split) * hd + dd] = o;
     }
     for (int gq = tid; gq < G; gq += nthr) {
         const int h = kvh * G + gq;
         a.part_ml[((size_t)h * a.nsplit + split) * 2] = s_m[gq];
         a.part_ml[((size_t)h * a.nsplit + split) * 2 + 1] = s_l[gq];
     }
+    // last finisher of this kv head merges its splits
+    __threadfence();
     csync();
-}
-
-// x_s = merge of the attention split partials (the attention output row):
-// per (head, split) the merge weight exp(m_s - M) / L once, then every output
-// element sums its splits with independent loads. `scr` holds H*nsplit floats.
-static __device__ void x_combine(const MegaArgs& a, float* x_s, float* scr, int pos) {
-    const int H = a.H, hd = a.hd, ns = a.nsplit;
-    const int nvalid = min(pos / a.chunk + 1, ns);
-    const int tid = threadIdx.x;
-    for (int e = tid; e < H * nvalid; e += kMegaCW * 32) {
-        const int h = e / nvalid, s2 = e - h * nvalid;
-        scr[e] = __ldcg(a.part_ml + ((size_t)h * ns + s2) * 2);  // m
+    ATR(6);
+    if (tid == 0) {
+        const unsigned int old = atomicAdd(a.acnt + kvh, 1u);
+        *s_flag = old == (unsigned int)(nv - 1);
+        if (*s_flag) atomicExch(a.acnt + kvh, 0u);
     }
     csync();
-    for (int h = tid; h < H; h += kMegaCW * 32) {
+    ATR(7);
+    if (!*s_flag) return true;
+    __threadfence();
+    float* mw = reinterpret_cast<float*>(sm + P.kv);  // [G][nv] m, then weights
+    float* lw = mw + G * nv;                           // [G][nv] l
+    for (int e = tid; e < G * nv; e += nthr) {
+        const int gq = e / nv, s2 = e - gq * nv, h = kvh * G + gq;
+        mw[e] = __ldcg(a.part_ml + ((size_t)h * a.nsplit + s2) * 2);
+        lw[e] = __ldcg(a.part_ml + ((size_t)h * a.nsplit + s2) * 2 + 1);
+    }
+    csync();
+    for (int gq = tid; gq < G; gq += nthr) {
         float M = -INFINITY;
-        for (int s2 = 0; s2 < nvalid; s2++) M = fmaxf(M, scr[h * nvalid + s2]);
+        for (int s2 = 0; s2 < nv; s2++) M = fmaxf(M, mw[gq * nv + s2]);
         float L = 0.0f;
-        for (int s2 = 0; s2 < nvalid; s2++) {
-            const float ms = scr[h * nvalid + s2];
+        for (int s2 = 0; s2 < nv; s2++) {
+            const float ms = mw[gq * nv + s2];
             const float wgt = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            L = __fmaf_rn(wgt, __ldcg(a.part_ml + ((size_t)h * ns + s2) * 2 + 1), L);
-            scr[h * nvalid + s2] = wgt;
+            L = __fmaf_rn(wgt, lw[gq * nv + s2], L);
+            mw[gq * nv + s2] = wgt;
         }
         const float inv = 1.0f / L;
-        for (int s2 = 0; s2 < nvalid; s2++) scr[h * nvalid + s2] *= inv;
+        for (int s2 = 0; s2 < nv; s2++) mw[gq * nv + s2] *= inv;
     }
     csync();
-    for (int e = tid; e < H * hd; e += kMegaCW * 32) {
-        const int h = e / hd, dd = e - h * hd;
-        const float* po = a.part_o + (size_t)h * ns * hd + dd;
-        const float* wt = scr + h * nvalid;
+    for (int e = tid; e < G * hd; e += nthr) {
+        const int gq = e / hd, dd = e - gq * hd, h = kvh * G + gq;
+        const float* po = a.part_o + (size_t)h * a.nsplit * hd + dd;
+        const float* wt = mw + gq * nv;
         float O = 0.0f;
 #pragma unroll 8
-        for (int s2 = 0; s2 < nvalid; s2++) O = __fmaf_rn(wt[s2], __ldcg(po + (size_t)s2 * hd), O);
-        x_s[e] = O;
+        for (int s2 = 0; s2 < nv; s2++) O = __fmaf_rn(wt[s2], __ldcg(po + (size_t)s2 * hd), O);
+        a.qkv[(size_t)h * hd + dd] = O;
     }
     csync();
+    ATR(8);
+#undef ATR
+    return true;
 }
 
 __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + kMegaMaxSlots;
+    uint64_t* abar = empty + kMegaMaxSlots;  // attention K/V copies
+    static_assert(kMegaMaxSlots * 2 * 8 + 8 <= 128, "mbarriers exceed the shared-memory header");
     unsigned char* xs_region = sm + 128;
     float* x_s = reinterpret_cast<float*>(xs_region);
     int8_t* xd = reinterpret_cast<int8_t*>(xs_region + (size_t)a.kmax * 4);
@@ -568,31 +835,20 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kMegaCW);
         }
+        mbar_init(abar, 1);
         mbar_fence_init();
     }
     __syncthreads();
 
     if (warp == kMegaCW) {  // ---- producer: the step's weight tiles, in consumer order
-        if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            int t = 0;
-            bool ok = true;
-            for (int l = 0; l < a.L && ok; l++) {
-                const MegaLayer& ly = a.layers[l];
-                ok = produce_mat(ly.qkv, b, t, ns, full, empty, ring, pol, a.err) &&
-                     produce_mat(ly.o, b, t, ns, full, empty, ring, pol, a.err) &&
-                     produce_mat(ly.gu, b, t, ns, full, empty, ring, pol, a.err) &&
-                     produce_mat(ly.dn, b, t, ns, full, empty, ring, pol, a.err);
-            }
-            if (ok) produce_mat(a.head, b, t, ns, full, empty, ring, pol, a.err);
-        }
+        if (lane == 0) produce_step(a, b, ns, full, empty, ring);
         return;
     }
 
     // ---- consumers ---------------------------------------------------------
     DevState* st = a.st;
     const int active = *(volatile const int*)&st->active;
-    int t = 0;
+    RingPos rp{0, 0};
     if (!active) {  // disabled step: take every tile off the ring, then leave
         int n = 0;
         for (int l = 0; l < a.L; l++) {
@@ -600,11 +856,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             n += mat_tiles(ly.qkv, b) + mat_tiles(ly.o, b) + mat_tiles(ly.gu, b) + mat_tiles(ly.dn, b);
         }
         n += mat_tiles(a.head, b);
-        for (; t < n; t++) {
-            const int s = t % ns;
-            if (!mbar_wait_err(&full[s], (t / ns) & 1, a.err, 4)) return;
+        for (int t = 0; t < n; t++) {
+            if (!mbar_wait_err(&full[rp.s], rp.ph, a.err, 4)) return;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            if (lane == 0) mbar_arrive(&empty[rp.s]);
+            rp.next(ns);
         }
         return;
     }
@@ -612,6 +868,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     const unsigned int base = *(volatile const unsigned int*)&st->bar_base;
     const unsigned int nct = gridDim.x;
     int bi = 0;
+    uint32_t aph = 0;  // parity of abar's current phase
     bool ok = true;
     const int nvalid = min(pos / a.chunk + 1, a.nsplit);
 #define TRACE(idx)                                                               \
@@ -633,7 +890,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                     const int cb = i / kMegaCB, w = min(kMegaCB, a.D - cb * kMegaCB), c = i - cb * kMegaCB;
                     const uint8_t* row = a.eqs + (size_t)cb * a.V * kMegaCB + (size_t)id * w;
                     const int8_t q = (int8_t)row[16 * swz_chunk(c >> 4, id & 7, w >> 4) + (c & 15)];
-                    v = __fmul_rn((float)q, h2f(a.ed[(size_t)cb * a.V * (kMegaCB / 32) + (size_t)id * (w / 32) + c / 32]));
+                    v = __fmul_rn((float)q, h2f(a.ed[(size_t)cb * a.V * (kMegaCB / 32) + mega_d_index(id, c / 32, w / 32)]));
                 }
                 x_s[i] = v;
                 if (b == 0) a.X[i] = v;
@@ -645,25 +902,32 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         x_digitize(x_s, a.D, xd, xsc);
         const int tb = 1 + l * kMegaTraceLayer;
         TRACE(tb + 0);
-        ok = ly.bias ? consume_mat<ME_BIAS>(ly.qkv, xd, xsc, t, ns, full, empty, ring, s_part, s_res, a.qkv, ly.bias,
+        ok = ly.bias ? consume_mat<ME_BIAS>(ly.qkv, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.qkv, ly.bias,
                                            &s_best, a.err)
-                     : consume_mat<ME_STORE>(ly.qkv, xd, xsc, t, ns, full, empty, ring, s_part, s_res, a.qkv,
+                     : consume_mat<ME_STORE>(ly.qkv, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.qkv,
                                             nullptr, &s_best, a.err);
         TRACE(tb + 1);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
         TRACE(tb + 2);
         if (!ok) break;
         // attention items (kv head, split), round-robin over CTAs
-        for (int it = b; it < a.KV * nvalid; it += nct) attn_item(a, l, it / nvalid, it % nvalid, pos, xs_region);
+        for (int it = b; it < a.KV * nvalid && ok; it += nct) {
+            long long* tr = (a.trace && it == b) ? a.trace + (size_t)b * kMegaTracePts + tb + 14 : nullptr;
+            if (a.H / a.KV <= 4)
+                ok = attn_item<4>(a, l, it / nvalid, it % nvalid, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
+            else
+                ok = attn_item<8>(a, l, it / nvalid, it % nvalid, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
+        }
+        if (!ok) break;
         TRACE(tb + 3);
         ok = grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
         TRACE(tb + 4);
         if (!ok) break;
         // O projection + residual
-        x_combine(a, x_s, reinterpret_cast<float*>(xd), pos);
+        x_load(x_s, a.qkv, a.H * a.hd);  // merged attention rows (q part of qkv)
         x_digitize(x_s, a.H * a.hd, xd, xsc);
         TRACE(tb + 5);
-        ok = consume_mat<ME_RESID>(ly.o, xd, xsc, t, ns, full, empty, ring, s_part, s_res, a.X, nullptr, &s_best, a.err);
+        ok = consume_mat<ME_RESID>(ly.o, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.X, nullptr, &s_best, a.err);
         TRACE(tb + 6);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
         TRACE(tb + 7);
@@ -673,7 +937,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         x_norm(x_s, a.D, ly.rms2, 1e-5f, s_red);
         x_digitize(x_s, a.D, xd, xsc);
         TRACE(tb + 8);
-        ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, t, ns, full, empty, ring, s_part, s_res, a.h, nullptr, &s_best,
+        ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.h, nullptr, &s_best,
                                     a.err);
         TRACE(tb + 9);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
@@ -683,7 +947,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         x_load(x_s, a.h, a.F);
         x_digitize(x_s, a.F, xd, xsc);
         TRACE(tb + 11);
-        ok = consume_mat<ME_RESID>(ly.dn, xd, xsc, t, ns, full, empty, ring, s_part, s_res, a.X, nullptr, &s_best,
+        ok = consume_mat<ME_RESID>(ly.dn, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.X, nullptr, &s_best,
                                    a.err);
         TRACE(tb + 12);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
@@ -697,7 +961,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     x_norm(x_s, a.D, a.final_norm, 1e-5f, s_red);
     x_digitize(x_s, a.D, xd, xsc);
     TRACE(th + 0);
-    if (!consume_mat<ME_ARGMAX>(a.head, xd, xsc, t, ns, full, empty, ring, s_part, s_res, a.logits, nullptr, &s_best,
+    if (!consume_mat<ME_ARGMAX>(a.head, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.logits, nullptr, &s_best,
                                 a.err))
         return;
     TRACE(th + 1);
@@ -743,10 +1007,21 @@ int mega_plan(MegaMat& m, int nctas) {
 }
 
 // x (4 B) + three digit planes (3 B) + block scales (1/8 B) per element; the
-// attention item's scratch and the split merge's weights (after x) share it.
-int mega_xs_bytes(int kmax, int G, int hd, int merge_weights) {
-    const int xk = std::max(kmax * 4 + kmax * 3 + (kmax / 32) * 4, kmax * 4 + merge_weights * 4);
-    return (std::max(xk, attn_item_smem(G, hd)) + 127) / 128 * 128;
+// attention item's plan (sub-chunks of S positions) shares the region.
+int mega_xs_bytes(int kmax, int G, int hd, int S) {
+    const int xk = kmax * 4 + kmax * 3 + (kmax / 32) * 4;
+    return (std::max(xk, attn_plan(G, hd, S).total) + 127) / 128 * 128;
+}
+
+// Attention sub-chunk: the split length rounded up to a power of two, halved
+// while the item's plan would need more than max(x region, 96 KB).
+int mega_attn_sub(int kmax, int G, int hd, int chunk) {
+    const int xk = kmax * 4 + kmax * 3 + (kmax / 32) * 4;
+    const int cap = std::max(xk, 96 * 1024);
+    int S = 16;
+    while (S < chunk) S <<= 1;
+    while (S > 16 && attn_plan(G, hd, S).total > cap) S >>= 1;
+    return S;
 }
 
 int mega_smem_bytes(const MegaArgs& a) { return 128 + a.xs_bytes + a.nslots * kMegaSlotBytes; }

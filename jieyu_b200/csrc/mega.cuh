@@ -10,14 +10,21 @@ namespace jyc {
 //   qs: [cb][n][w_cb] signed int8 q, the 16-byte chunks of row r permuted
 //       within aligned groups of 8 chunks (chunk c -> c ^ (r & 7)) so that the
 //       tensor-core fragment loads of 8 consecutive rows hit distinct banks;
-//   d : [cb][n][w_cb/32] fp16 scales.
+//   d : [cb][n/16][w_cb/32][8][2] fp16 scales: per 16-row group and Q8 block,
+//       the scales of rows g and g+8 side by side (one 32-bit load gives the
+//       pair a tensor-core fragment row needs). Needs n % 16 == 0.
 // A run of consecutive rows of one block is one contiguous byte range, so a
 // tile (rows x one column block) arrives with two 1-D TMA bulk copies.
 constexpr int kMegaCB = 512;
 constexpr int kMegaRT = 48;       // rows per tile (multiple of 16)
 constexpr int kMegaMaxSlots = 6;  // ring depth upper bound
-constexpr int kMegaCW = 16;       // consumer warps
+constexpr int kMegaCW = 16;       // consumer warps (each takes 512 / 32 / kMegaCW column blocks of a tile)
 constexpr int kMegaSlotBytes = kMegaRT * kMegaCB + kMegaRT * (kMegaCB / 32) * 2;
+
+// index of row R, block j (of nblk in the column block) in the paired scale layout
+__host__ __device__ __forceinline__ size_t mega_d_index(size_t R, int j, int nblk) {
+    return (((R >> 4) * (size_t)nblk + j) * 8 + (R & 7)) * 2 + ((R >> 3) & 1);
+}
 
 struct MegaMat {
     const uint8_t* qs;  // tiled copy (see above)
@@ -57,6 +64,8 @@ struct MegaArgs {
     float* part_o;            // attention split partials [H][nsplit][hd]
     float* part_ml;           // [H][nsplit][2]
     int chunk, nsplit;
+    int asub;                 // attention sub-chunk (power of two, positions per K/V copy)
+    unsigned int* acnt;       // per kv head: finished split items of the current layer
     float scale;              // 1/sqrtf(hd)
     DevState* st;
     int* tokens;
@@ -65,22 +74,26 @@ struct MegaArgs {
     int kmax;                 // largest GEMV input length (x / digit buffers)
     int xs_bytes;             // shared bytes of the x / digits / attention union
     int nslots;               // ring depth
+    int pf_tiles;             // tiles of L2 prefetch ahead of the ring (0: none)
     long long* trace;         // optional: SM clock at each phase boundary, [CTA][kMegaTracePts]
 };
 
-// Phase boundaries recorded per CTA when tracing (per layer 14, then the head).
-constexpr int kMegaTraceLayer = 14;
+// Phase boundaries recorded per CTA when tracing: per layer 14 phase points
+// and 9 points inside the CTA's first attention item, then the head.
+constexpr int kMegaTraceLayer = 23;
 constexpr int kMegaTracePts = 1 + 64 * kMegaTraceLayer + 4;  // up to 64 layers
 
 int launch_q8_repack_tiled(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d, int n_total,
                            int row_off, int row_stride, cudaStream_t s);
 int mega_plan(MegaMat& m, int nctas);
 int mega_smem_bytes(const MegaArgs& a);
-int mega_xs_bytes(int kmax, int G, int hd, int merge_weights);
+int mega_xs_bytes(int kmax, int G, int hd, int S);
+int mega_attn_sub(int kmax, int G, int hd, int chunk);
 int mega_num_ctas();
 int launch_mega_step(const MegaArgs& a, cudaStream_t s);
 int prepare_mega_kernel(int smem);
 int mega_static_smem();  // -1 when the kernel image cannot be queried
 int* device_error_word();
+int mega_negative_scales(bool reset);  // 1 when a repacked Q8_0 scale was negative, -1 on error
 
 }  // namespace jyc

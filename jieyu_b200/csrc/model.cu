@@ -222,7 +222,9 @@ bool mega_eligible(const jyc_model* m, const jyc_model_desc* d) {
     const int k32[] = {m->D, m->q_dim, m->F};
     for (int k : k32)
         if (k % 32) return false;
-    return m->hd % 16 == 0 && m->hd <= 256;
+    // head_dim a power of two in [16, 256]; query heads per kv head <= 8
+    const int hd = m->hd;
+    return hd >= 16 && hd <= 256 && (hd & (hd - 1)) == 0 && m->H / m->KV <= 8;
 }
 
 MegaMat mega_mat(const DevMat& w, int nctas) {
@@ -281,12 +283,18 @@ int setup_mega(jyc_model* m) {
     JYC_CUDA(cudaMemset(a.bar, 0, sizeof(unsigned int)));
     a.err = device_error_word();
     a.kmax = std::max({m->D, m->q_dim, m->F});
-    a.xs_bytes = mega_xs_bytes(a.kmax, m->H / m->KV, m->hd, m->H * a.nsplit);
+    a.asub = mega_attn_sub(a.kmax, m->H / m->KV, m->hd, a.chunk);
+    a.xs_bytes = mega_xs_bytes(a.kmax, m->H / m->KV, m->hd, a.asub);
+    TRY(m->alloc(&a.acnt, (size_t)m->KV));
+    JYC_CUDA(cudaMemset(a.acnt, 0, sizeof(unsigned int) * m->KV));
     // ring as deep as the shared memory allows (227 KB per CTA, at least 2 slots)
     const int st_smem = mega_static_smem();
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
     const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
     a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
+    // L2 prefetch distance in tiles (JIEYU_MEGA_PREFETCH overrides; 0 disables)
+    a.pf_tiles = 8;
+    if (const char* e = getenv("JIEYU_MEGA_PREFETCH")) a.pf_tiles = std::max(0, atoi(e));
     if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode
     const int smem = mega_smem_bytes(a);
     TRY(prepare_mega_kernel(smem));
@@ -314,6 +322,7 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     if (attn_smem_bytes(kMT, m->H, m->KV, m->hd) > 200 * 1024)
         return arg_error("model: query-head group too large for the attention kernel");
     m->tiled = mega_eligible(m, d);
+    if (m->tiled && mega_negative_scales(true) < 0) return cuda_fail(cudaGetLastError(), "mega: scale flag");
 
     JYC_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     TRY(prepare_kernels());
@@ -407,7 +416,10 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     TRY(m->alloc(&m->st, 1));
     JYC_CUDA(cudaMemsetAsync(m->st, 0, sizeof(DevState), m->stream));
     TRY(m->alloc(&m->tokens, (size_t)m->max_seq + 1));
-    if (m->tiled) TRY(setup_mega(m));
+    JYC_CUDA(cudaStreamSynchronize(m->stream));
+    // the decode kernel reads scales as non-negative (every Q8_0 quantiser
+    // writes d = amax / 127); a model with a negative one decodes generically
+    if (m->tiled && mega_negative_scales(true) == 0) TRY(setup_mega(m));
     JYC_CUDA(cudaStreamSynchronize(m->stream));
     return JYC_OK;
 }

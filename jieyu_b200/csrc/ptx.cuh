@@ -38,8 +38,7 @@ static __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t par
 }
 // Bounded wait: gives up after 2^31 SM clock cycles (about a second) and
 // records `code` in *err instead of hanging.
-static __device__ __noinline__ bool mbar_wait_err(uint64_t* bar, uint32_t parity, int* err, int code) {
-    if (mbar_try_wait(bar, parity)) return true;
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err, int code) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (clock64() - t0 > (1LL << 31)) {
@@ -48,6 +47,9 @@ static __device__ __noinline__ bool mbar_wait_err(uint64_t* bar, uint32_t parity
         }
     }
     return true;
+}
+static __device__ __forceinline__ bool mbar_wait_err(uint64_t* bar, uint32_t parity, int* err, int code) {
+    return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, err, code);
 }
 
 static __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -63,6 +65,15 @@ static __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint
         " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+// orders this thread's earlier shared-memory accesses (generic proxy) before
+// later async-proxy (TMA) writes to shared memory
+static __device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// L2 prefetch of a global byte range (16-byte aligned address and size).
+static __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 static __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
     unsigned int v;
