@@ -50,7 +50,7 @@ constexpr int kMegaThreads = (kMegaCW + 1) * 32;
 
 // Error word of the device kernels (non-zero: a bounded wait gave up; the
 // value tells which: 3 ring slot free, 4 ring slot full, 5 grid barrier,
-// 6 attention K/V copy).
+// 6 attention K/V copy, 7 prefill digit copy).
 __device__ int g_err_word;
 
 int* device_error_word() {

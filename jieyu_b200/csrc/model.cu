@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "mega.cuh"
+#include "prefill.cuh"
 
 using namespace jyc;
 
@@ -96,6 +97,9 @@ struct jyc_model {
     // megakernel decode
     bool mega = false;
     MegaArgs margs{};
+    int pf_rows = 0;           // tokens per batched prefill pass (0: generic prefill)
+    int8_t* pf_dig = nullptr;  // token digit planes of the batched prefill
+    float* pf_sx = nullptr;
     MegaLayer* d_mlayers = nullptr;
     DevState* st = nullptr;
     int* tokens = nullptr;  // [max_seq + 1]
@@ -395,14 +399,25 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     JYC_CUDA(cudaMemsetAsync(m->v8, 0, kvn * m->hd, m->stream));
     JYC_CUDA(cudaMemsetAsync(m->ks, 0, kvn * 4, m->stream));
     JYC_CUDA(cudaMemsetAsync(m->vs, 0, kvn * 4, m->stream));
-    TRY(m->alloc(&m->X, (size_t)kMT * m->D));
-    TRY(m->alloc(&m->qkv, (size_t)kMT * m->nqkv));
-    TRY(m->alloc(&m->attn, (size_t)kMT * m->q_dim));
-    TRY(m->alloc(&m->h, (size_t)kMT * m->F));
+    // batched prefill (tensor-core token tiles) for models in the tiled layout
+    const bool pf_ok = m->tiled && m->D % kPfRows == 0 && m->nqkv % kPfRows == 0 && (2 * m->F) % kPfRows == 0 &&
+                       pf_attention_supported(m->H, m->KV, m->hd);
+    m->pf_rows = pf_ok ? std::min(kPfChunk, (m->max_seq + kPfTok - 1) / kPfTok * kPfTok) : 0;
+    const size_t arows = std::max(kMT, m->pf_rows);
+    TRY(m->alloc(&m->X, arows * m->D));
+    TRY(m->alloc(&m->qkv, arows * m->nqkv));
+    TRY(m->alloc(&m->attn, arows * m->q_dim));
+    TRY(m->alloc(&m->h, arows * m->F));
     TRY(m->alloc(&m->logits, (size_t)m->V));
     TRY(m->alloc(&m->tmp, (size_t)m->D));
-    TRY(m->alloc(&m->q8, (size_t)kMT * m->q_dim));
-    TRY(m->alloc(&m->qsc, (size_t)kMT * m->H));
+    TRY(m->alloc(&m->q8, arows * m->q_dim));
+    TRY(m->alloc(&m->qsc, arows * m->H));
+    if (m->pf_rows) {
+        const int kmax = std::max({m->D, m->q_dim, m->F});
+        TRY(m->alloc(&m->pf_dig, pf_digit_bytes(m->pf_rows, kmax)));
+        TRY(m->alloc(&m->pf_sx, pf_scale_floats(m->pf_rows, kmax)));
+        TRY(prepare_pf_kernels());
+    }
     // split-K plan of the generic attention: ~2 CTAs per SM over the kv heads
     const int target = std::max(1, 296 / m->KV);
     int chunk = (m->max_seq + target - 1) / target;
@@ -504,7 +519,52 @@ int run_head(jyc_model* m, int row, cudaStream_t s) {
 
 // Forward of n tokens already in m->tokens[start..start+n) in chunks of kMT,
 // then the head on the last row (state must hold len == start+n).
+// Batched prefill of tokens [start, start + n) in passes of pf_rows tokens:
+// per layer RMSNorm+digits -> QKV (tensor-core token tiles) -> RoPE/quant +
+// cache append -> causal attention -> O + residual -> RMSNorm+digits ->
+// gate/up + SwiGLU -> down + residual; then the LM head on the last token.
+int run_prefill_batched(jyc_model* m, int start, int n, cudaStream_t s) {
+    int last_rows = 0;
+    int* err = device_error_word();
+    for (int c = 0; c < n; c += m->pf_rows) {
+        const int rows = std::min(m->pf_rows, n - c);
+        TRY(launch_embed(m->tokens, PosSrc{nullptr, start + c}, rows, m->embed_f, m->embed_q.qs, m->embed_q.d,
+                         m->D, m->X, s));
+        auto gemm = [&](const DevMat& w, const float* x, int ldx, const float* norm, float* y, int ldy,
+                        const float* bias, int epi) -> int {
+            TRY(launch_pf_digitize(x, ldx, rows, w.k, norm, 1e-5f, m->pf_dig, m->pf_sx, s));
+            PfGemm g{};
+            g.qs = w.tq; g.d = w.td; g.n = w.n; g.k = w.k;
+            g.dig = m->pf_dig; g.sx = m->pf_sx; g.T = rows;
+            g.y = y; g.ldy = ldy; g.bias = bias; g.err = err;
+            return launch_pf_gemm(g, epi, s);
+        };
+        for (int l = 0; l < m->L; l++) {
+            const DevLayer& ly = m->layers[l];
+            TRY(gemm(ly.qkv, m->X, m->D, ly.rms1, m->qkv, m->nqkv, ly.bias, ly.bias ? PF_BIAS : PF_STORE));
+            RopeQuantArgs rq{};
+            rq.q = m->qkv; rq.k = m->qkv + m->q_dim; rq.v = m->qkv + m->q_dim + m->kv_dim;
+            rq.ldq = m->nqkv; rq.rows = rows; rq.H = m->H; rq.KV = m->KV; rq.hd = m->hd;
+            rq.cos_t = m->cos_t; rq.sin_t = m->sin_t; rq.q8 = m->q8; rq.qsc = m->qsc;
+            rq.kv = m->kv_layer(l); rq.pos = PosSrc{nullptr, start + c};
+            TRY(launch_rope_quant(rq, s));
+            const KVView kv = m->kv_layer(l);
+            PfAttn at{};
+            at.q8 = m->q8; at.qsc = m->qsc; at.k8 = kv.k; at.v8 = kv.v; at.ks = kv.ks; at.vs = kv.vs;
+            at.max_seq = m->max_seq; at.H = m->H; at.KV = m->KV; at.hd = m->hd; at.T = rows;
+            at.pos0 = start + c; at.scale = 1.0f / sqrtf((float)m->hd); at.out = m->attn;
+            TRY(launch_pf_attention(at, s));
+            TRY(gemm(ly.o, m->attn, m->q_dim, nullptr, m->X, m->D, nullptr, PF_RESID));
+            TRY(gemm(ly.gateup, m->X, m->D, ly.rms2, m->h, m->F, nullptr, PF_SWIGLU));
+            TRY(gemm(ly.down, m->h, m->F, nullptr, m->X, m->D, nullptr, PF_RESID));
+        }
+        last_rows = rows;
+    }
+    return run_head(m, last_rows - 1, s);
+}
+
 int run_prefill(jyc_model* m, int start, int n, cudaStream_t s) {
+    if (m->pf_rows) return run_prefill_batched(m, start, n, s);
     int last_rows = 0;
     for (int c = 0; c < n; c += kMT) {
         const int rows = std::min(kMT, n - c);
@@ -591,7 +651,7 @@ JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_
         TRY(run_prefill(m, start_pos, seq, s));
     }
     if (hidden_out) {
-        const int last = (seq == 1 && m->mega) ? 0 : (seq - 1) % kMT;
+        const int last = (seq == 1 && m->mega) ? 0 : (seq - 1) % (m->pf_rows ? m->pf_rows : kMT);
         TRY(launch_rmsnorm(m->X + (size_t)last * m->D, m->tmp, m->final_norm, 1, m->D, 1e-5f, s));
         JYC_CUDA(cudaMemcpyAsync(hidden_out, m->tmp, m->D * sizeof(float), cudaMemcpyDeviceToHost, s));
     }
