@@ -145,6 +145,63 @@ def teacher_forced(chk, hw, prompt, steps):
     return rows, kv
 
 
+def isa_spread(hw, prompt, steps):
+    """The reference's own scalar path against its fma path on identical
+    inputs (both fed the fma path's argmax): per step max|dlogit| / max|logit|,
+    and per layer (0, last) the fraction of int8 K/V bytes that differ. The
+    device parity tests allow max(1e-3, 1.25 x) this spread."""
+    cfg = hw.cfg
+    outs, kvs = [], []
+    toks = None
+    for isa in ("fma", "scalar"):
+        chk = Reference(isa, 0)
+        cache = chk.cache_create(cfg.layers, cfg.max_seq, cfg.kv_heads, cfg.head_dim)
+        logits = np.empty(cfg.vocab, np.float32)
+        seq = [np.ascontiguousarray(prompt, np.int32)]
+        if toks is not None:
+            seq += [np.array([t], np.int32) for t in toks]
+        got, tk = [], []
+        pos = 0
+        for s in range(steps + 1):
+            tok = seq[s] if s < len(seq) else np.array([tk[-1]], np.int32)
+            assert chk.forward_logits(C.byref(hw.desc), cache, p(tok), len(tok), pos, p(logits), None) == 0
+            pos += len(tok)
+            got.append(logits.copy())
+            tk.append(int(np.argmax(logits)))
+        if toks is None:
+            toks = tk[:steps]
+        n = pos
+        lay = {}
+        for layer in (0, cfg.layers - 1):
+            k = np.empty(n * cfg.kv_dim, np.int8)
+            v = np.empty_like(k)
+            ks = np.empty(n * cfg.kv_heads, np.float32)
+            vs = np.empty_like(ks)
+            chk.cache_read(cache, layer, n, p(k), p(ks), p(v), p(vs))
+            lay[layer] = (k.copy(), v.copy())
+        chk.cache_free(cache)
+        outs.append(got)
+        kvs.append(lay)
+    Reference("fma", 0)  # the library's ISA switch is global: leave it on fma
+    logit = [float(np.abs(a - b).max() / np.abs(a).max()) for a, b in zip(outs[0], outs[1])]
+    # the fma path stores roped K pairs in its slot order (rope_slot): bring
+    # the scalar path's rows into the same order before comparing bytes
+    half = cfg.head_dim // 2
+    perm = np.arange(cfg.head_dim)
+    for q in range(half):
+        g8, j = q >> 3, q & 7
+        if (g8 + 1) * 8 <= half:
+            j = j + 2 if j in (2, 3) else j - 2 if j in (4, 5) else j
+        o = g8 * 8 + j
+        perm[2 * o], perm[2 * o + 1] = 2 * q, 2 * q + 1
+    kvfrac = {}
+    for layer in kvs[0]:
+        (k0, v0), (k1, v1) = kvs[0][layer], kvs[1][layer]
+        k1 = k1.reshape(-1, cfg.head_dim)[:, perm].reshape(-1)
+        kvfrac[str(layer)] = float(max((k0 != k1).mean(), (v0 != v1).mean()))
+    return {"logits_rel": logit, "kv_frac": kvfrac}
+
+
 def main():
     ref = Reference("fma", 0)
     g = {"isa": "fma", "ops": run_ops(ref)}
@@ -181,7 +238,7 @@ def main():
     rows, kv = teacher_forced(ref, hw0, pr, 16)
     with open(os.path.join(OUT, "c0.json"), "w") as f:
         json.dump({"seed": 1234, "prompt": [int(x) for x in pr], "greedy": [int(x) for x in ids],
-                   "teacher_forced": rows, "kv_sha": kv}, f, indent=1)
+                   "teacher_forced": rows, "kv_sha": kv, "isa_spread": isa_spread(hw0, pr, 16)}, f, indent=1)
 
     # configs[1] shape: short prompt (the CPU prefill path is scalar), 16 tokens
     c1 = CONFIGS["c1"]
@@ -191,7 +248,17 @@ def main():
     rows1, kv1 = teacher_forced(ref, hw1, pr1, 4)
     with open(os.path.join(OUT, "c1.json"), "w") as f:
         json.dump({"seed": 1234, "prompt": [int(x) for x in pr1], "greedy": [int(x) for x in ids1],
-                   "teacher_forced": rows1, "kv_sha": kv1}, f, indent=1)
+                   "teacher_forced": rows1, "kv_sha": kv1, "isa_spread": isa_spread(hw1, pr1, 4)}, f, indent=1)
+
+    # configs[2] shape, Q8_0 and fp32 variants, max context 256: 8-token prompt + 3 steps
+    from dataclasses import replace
+    c2 = {}
+    for key in ("c2", "c2f"):
+        cfg = replace(CONFIGS[key], max_seq=256)
+        hw2 = HostWeights.synthetic(cfg)
+        c2[key] = {"isa_spread": isa_spread(hw2, prompt_ids(cfg, n=8), 3)}
+    with open(os.path.join(OUT, "c2.json"), "w") as f:
+        json.dump(c2, f, indent=1)
     print("golden fixtures written to", OUT)
 
 
