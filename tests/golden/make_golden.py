@@ -149,7 +149,7 @@ def isa_spread(hw, prompt, steps):
     """The reference's own scalar path against its fma path on identical
     inputs (both fed the fma path's argmax): per step max|dlogit| / max|logit|,
     and per layer (0, last) the fraction of int8 K/V bytes that differ. The
-    device parity tests allow max(1e-3, 1.25 x) this spread."""
+    device parity tests allow max(1e-3, 1.5 x) this spread."""
     cfg = hw.cfg
     outs, kvs = [], []
     toks = None

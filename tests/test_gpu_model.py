@@ -11,7 +11,7 @@ scalar and fma code paths, on identical inputs, differ by 0.9e-3
 to 2.2-3.8e-3 of max|logit|, and their int8 KV
 bytes at the last layer by 3-12 % (fp32 rounding differences amplified
 through the layers). The fixtures record that spread (tests/golden,
-isa_spread); the logit tolerance is max(LOGIT_TOL, 1.25 x the largest spread)
+isa_spread); the logit tolerance is max(LOGIT_TOL, 1.5 x the largest spread)
 and the last-layer KV byte mismatch may reach max(1e-3, 1.5 x the
 reference's own fraction). Layer 0 (identical inputs) stays bit-exact.
 """
@@ -95,12 +95,12 @@ def _teacher_forced(m, hw, oracle, prompt, steps):
 
 
 def _tol(spread, step):
-    """Logit tolerance: max(LOGIT_TOL, 1.25 x the reference's own scalar-vs-fma
+    """Logit tolerance: max(LOGIT_TOL, 1.5 x the reference's own scalar-vs-fma
     spread, the largest over the fixture's steps: the amplification is a
     property of the model, the per-step value a sample of it)."""
     if spread is None:
         return LOGIT_TOL
-    return max(LOGIT_TOL, 1.25 * max(spread["logits_rel"]))
+    return max(LOGIT_TOL, 1.5 * max(spread["logits_rel"]))
 
 
 def _check_logits(got, want, ref_row=None, tol=LOGIT_TOL):
