@@ -165,6 +165,25 @@ JYC_API int jyc_attention_q8(const float* Q, const float* K, const float* V, flo
                              int head_dim, int8_t* kc, float* ks, int8_t* vc, float* vs,
                              int cap, void* stream);
 
+/* jyc_attention_q8 without any allocation (no counterpart in the reference):
+ * same arguments, kernels and results, but its scratch (quantised queries,
+ * split partials, arrival counters) lives in one fixed device array of the
+ * library image instead of stream-ordered cudaMallocAsync memory, for callers
+ * that must not allocate (a caller inside a memory-pool-free region, a
+ * real-time thread). Limits: num_heads * head_dim <= 8192, num_kv_heads <= 256,
+ * and 8 * num_heads * head_dim * splits <= 1,048,576 floats of split partials
+ * (splits = ceil((start_pos + seq) / chunk), chunk as jyc_attention_q8 picks
+ * it); larger calls return JYC_ERR_ARG before launching anything. The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress with
+ * that device current): make that first call before any stream capture. The
+ * arrival counters must be zero when a call starts: they are at load and
+ * every completed call leaves them so. Calls overlapping in time (other
+ * streams, other host threads) share the array and race: serialise them. */
+JYC_API int jyc_attention_q8_noalloc(const float* Q, const float* K, const float* V, float* out,
+                                     int seq, int start_pos, int num_heads, int num_kv_heads,
+                                     int head_dim, int8_t* kc, float* ks, int8_t* vc, float* vs,
+                                     int cap, void* stream);
+
 /* y = x / (1 + e^-x), with the reference's own exp polynomial for the
  * vector body. Replaces silu(x,y,n) (libs/model_libs/silu/silu.h:7-81). */
 JYC_API int jyc_silu(const float* x, float* y, int n, void* stream);

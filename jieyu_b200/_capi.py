@@ -87,6 +87,7 @@ SIGNATURES = [
     ("jyc_rope_pos", _I, [_P, _I, _I, _I, _I, _P, _P, _P]),
     ("jyc_kv_pack_q8", _I, [_P, _P, _P, _I, _I, _I, _P]),
     ("jyc_attention_q8", _I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P]),
+    ("jyc_attention_q8_noalloc", _I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P]),
     ("jyc_silu", _I, [_P, _P, _I, _P]),
     ("jyc_argmax", _I, [_P, _I, _P, _P]),
     ("jyc_model_create", _P, [C.POINTER(ModelDesc)]),

@@ -2,6 +2,7 @@
 // operator; see include/jieyu_b200.h for the reference function each replaces).
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 #include <vector>
 
 #include "kernels.cuh"
@@ -157,6 +158,112 @@ JYC_API int jyc_attention_q8(const float* Q, const float* K, const float* V, flo
         }
         {
             RopeQuantArgs a = rq;  // keys and values: stride kvd, no query heads
+            a.H = 0; a.ldq = kvd;
+            a.q8 = nullptr; a.qsc = nullptr;
+            TRY(launch_rope_quant(a, s));
+        }
+        AttnArgs at{};
+        at.q8 = q8; at.qsc = qsc; at.kv = kv;
+        at.rows = rows; at.H = num_heads; at.KV = num_kv_heads; at.hd = head_dim;
+        at.chunk = chunk; at.nsplit = nsplit; at.scale = 1.0f / sqrtf((float)head_dim);
+        at.part_o = po; at.part_ml = pml; at.arrive = arrive;
+        at.out = out + (size_t)r0 * qd; at.ldo = qd; at.pos = PosSrc{nullptr, start_pos + r0};
+        TRY(launch_attention(at, s));
+    }
+    return JYC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// jyc_attention_q8_noalloc: the same kernels with a fixed scratch array.
+}  // extern "C"
+
+namespace {
+
+constexpr size_t kNaQ8 = 8 * 8192;        // int8 queries: 8 rows x num_heads*head_dim
+constexpr size_t kNaQsc = 8 * 1024;       // floats: 8 rows x num_heads
+constexpr size_t kNaPo = 1u << 20;        // floats: split partial outputs (4 MiB)
+constexpr size_t kNaPml = 1u << 16;       // floats: split (max, sum) pairs
+constexpr size_t kNaArrive = 256;         // uint32 arrival counters, one per kv head
+constexpr size_t kNaBytes = kNaQ8 + (kNaQsc + kNaPo + kNaPml) * 4 + kNaArrive * 4;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
+
+// address of the array on each device, resolved once with that device current
+std::mutex g_na_mu;
+std::vector<unsigned char*> g_na_addr;
+
+int noalloc_scratch(unsigned char** out) {
+    int dev = 0;
+    JYC_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_na_mu);
+    if ((int)g_na_addr.size() <= dev) g_na_addr.resize(dev + 1, nullptr);
+    if (!g_na_addr[dev]) {
+        void* p = nullptr;
+        JYC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_na_addr[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = g_na_addr[dev];
+    return JYC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+JYC_API int jyc_attention_q8_noalloc(const float* Q, const float* K, const float* V, float* out, int seq,
+                                     int start_pos, int num_heads, int num_kv_heads, int head_dim,
+                                     int8_t* kc, float* ks, int8_t* vc, float* vs, int cap, void* stream) {
+    clear_error();
+    if (num_kv_heads <= 0 || num_heads % num_kv_heads != 0)
+        return arg_error("attention_q8_noalloc: num_heads must be a multiple of num_kv_heads");
+    if (seq <= 0) return arg_error("attention_q8_noalloc: seq must be positive");
+    if (start_pos < 0) return arg_error("attention_q8_noalloc: start_pos must not be negative");
+    if (!kc || !ks || !vc || !vs || cap <= 0) return arg_error("attention_q8_noalloc: KV cache pointers incomplete");
+    if ((long long)start_pos + seq > cap) {
+        set_error("attention_q8_noalloc: KV cache capacity exceeded");
+        return JYC_ERR_KV_OOM;
+    }
+    if (!Q || !K || !V || !out) return arg_error("attention_q8_noalloc: null pointer");
+    if (head_dim % 4 || head_dim > 256)
+        return arg_error("attention_q8_noalloc: head_dim must be a multiple of 4, <= 256");
+    const int rows_max = 8;
+    if (attn_smem_bytes(rows_max, num_heads, num_kv_heads, head_dim) > 200 * 1024)
+        return arg_error("attention_q8_noalloc: query-head group too large");
+    const int maxpos = start_pos + seq;
+    const int target = std::max(1, 296 / num_kv_heads);
+    int chunk = (maxpos + target - 1) / target;
+    chunk = std::max(64, (chunk + 63) / 64 * 64);
+    const int nsplit = (maxpos + chunk - 1) / chunk;
+    const size_t need_q8 = (size_t)rows_max * num_heads * head_dim;
+    const size_t need_qsc = (size_t)rows_max * num_heads;
+    const size_t need_po = (size_t)rows_max * num_heads * nsplit * head_dim;
+    const size_t need_pml = (size_t)rows_max * num_heads * nsplit * 2;
+    if (need_q8 > kNaQ8 || need_qsc > kNaQsc || need_po > kNaPo || need_pml > kNaPml ||
+        (size_t)num_kv_heads > kNaArrive)
+        return arg_error("attention_q8_noalloc: call exceeds the fixed scratch (num_heads*head_dim <= 8192, "
+                         "num_kv_heads <= 256, 8*num_heads*head_dim*splits <= 1048576 floats)");
+    unsigned char* base = nullptr;
+    TRY(noalloc_scratch(&base));
+    int8_t* q8 = reinterpret_cast<int8_t*>(base);
+    float* qsc = reinterpret_cast<float*>(base + kNaQ8);
+    float* po = qsc + kNaQsc;
+    float* pml = po + kNaPo;
+    unsigned int* arrive = reinterpret_cast<unsigned int*>(pml + kNaPml);
+    cudaStream_t s = S(stream);
+    KVView kv{kc, ks, vc, vs, (long long)num_kv_heads * head_dim, head_dim, num_kv_heads, 1, cap};
+    const int qd = num_heads * head_dim, kvd = num_kv_heads * head_dim;
+    for (int r0 = 0; r0 < seq; r0 += rows_max) {
+        const int rows = std::min(rows_max, seq - r0);
+        RopeQuantArgs rq{};
+        rq.q = Q + (size_t)r0 * qd; rq.k = K + (size_t)r0 * kvd; rq.v = V + (size_t)r0 * kvd;
+        rq.rows = rows; rq.H = num_heads; rq.KV = num_kv_heads; rq.hd = head_dim;
+        rq.q8 = q8; rq.qsc = qsc; rq.kv = kv; rq.pos = PosSrc{nullptr, start_pos + r0};
+        {
+            RopeQuantArgs a = rq;
+            a.KV = 0; a.ldq = qd;
+            TRY(launch_rope_quant(a, s));
+        }
+        {
+            RopeQuantArgs a = rq;
             a.H = 0; a.ldq = kvd;
             a.q8 = nullptr; a.qsc = nullptr;
             TRY(launch_rope_quant(a, s));
