@@ -209,8 +209,10 @@ JYC_API double jyc_model_kv_bytes_per_token(const jyc_model* m, int ctx);
 /* Full token loop, same contract as generate() (libs/model_libs/generate.h:90-112)
  * with an internal KV cache: out_ids[0..ret) = prompt then new tokens;
  * returns 0 if prompt_len<=0 or > max_seq, prompt_len if max_new_tokens<=0,
- * negative on error. temperature<=0 is greedy; otherwise the reference's
- * LCG sampler (seed 12345). */
+ * negative on error. Greedy only: temperature > 0 or repetition_penalty != 1
+ * returns JYC_ERR_UNSUPPORTED (the reference's LCG sampler and penalty,
+ * generate.h:50-77, are not built on the device yet). cb (may be NULL) gets
+ * every new id in order; a non-zero return stops generation. */
 JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len,
                          const int* eos_ids, int num_eos, int max_new_tokens,
                          float temperature, int* out_ids, float repetition_penalty,
@@ -237,26 +239,29 @@ JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos,
 JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prompt_len,
                                void* stream);
 /* Run `n_steps` greedy decode steps from the current device state (each
- * consumes the last token and appends the next). Launches replay a captured
- * CUDA graph; asynchronous on `stream`. */
+ * consumes the last token and appends the next): one cooperative launch of
+ * the decode kernel per step on models in the tiled layout, a captured CUDA
+ * graph of the generic kernels otherwise; asynchronous on `stream`. */
 JYC_API int jyc_decode_device(jyc_model* m, int n_steps, void* stream);
 /* Reset the device state to `len` tokens already in the buffer (and their KV
  * entries in the cache), so decode can be replayed from the same point. */
 JYC_API int jyc_model_rewind(jyc_model* m, int len, void* stream);
 /* Kernels one decode step launches. */
 JYC_API int jyc_model_kernels_per_step(const jyc_model* m);
-/* 1 when the model decodes with the TMA-streamed kernels chained by
- * programmatic dependent launch (Q8_0 weights), 0 with the generic kernels. */
+/* 2 when the model decodes with the single-launch TMA-streamed decode kernel
+ * (Q8_0 weights in the tiled layout), 0 with the generic kernels. */
 JYC_API int jyc_model_decode_path(const jyc_model* m);
 /* Error word of the device kernels: non-zero if a bounded wait gave up
  * (reset != 0 clears it). */
 JYC_API int jyc_device_error(int reset);
 /* Tracing of the decode megakernel: phase boundaries per step and one traced
  * step. out receives [ctas][points] SM-clock stamps; returns the CTA count.
- * Point 0 = start; per layer l at 1+14l: QKV input ready, QKV done, barrier,
+ * Point 0 = start; per layer l at 1+23l: QKV input ready, QKV done, barrier,
  * attention done, barrier, O input ready, O done, barrier, gate/up input
- * ready, gate/up done, barrier, down input ready, down done, barrier; then
- * the LM head: input ready, done, barrier. */
+ * ready, gate/up done, barrier, down input ready, down done, barrier, then 9
+ * points inside the CTA's first attention item (start, queries ready, K/V in,
+ * scores, softmax, P.V, partials written, arrival counted, merge done; 0 when
+ * the CTA had no item); then the LM head: input ready, done, barrier. */
 JYC_API int jyc_model_trace_points(const jyc_model* m);
 JYC_API int jyc_model_trace_decode(jyc_model* m, void* stream, long long* out, int cap);
 /* Per-kernel timing of decode: replays the step graph with an event after
