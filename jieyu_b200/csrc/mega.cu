@@ -46,7 +46,7 @@
 
 namespace jyc {
 
-constexpr int kMegaThreads = (kMegaCW + 1) * 32;
+constexpr int kMegaThreads = (kMegaCW + 1) * 32;  // consumer warps + one copy-issuing warp
 
 // Error word of the device kernels (non-zero: a bounded wait gave up; the
 // value tells which: 3 ring slot free, 4 ring slot full, 5 grid barrier,
@@ -122,10 +122,27 @@ int launch_q8_repack_tiled(const void* blocks, int n, int k, uint8_t* qs, uint16
 
 // ---------------------------------------------------------------------------
 // tile sequence of one matrix for CTA b (shared by producer and consumers)
+// rows [r0, r1) and column blocks [cb0, cb1) of CTA b (empty when r1 <= r0)
+struct MatRange {
+    int r0, r1, cb0, cb1, kg;
+};
+
+static __device__ __forceinline__ MatRange mat_range(const MegaMat& M, int b) {
+    MatRange r;
+    const int rb = b / M.spl;
+    r.kg = b - rb * M.spl;
+    r.r0 = rb * M.rpc;
+    r.r1 = min(r.r0 + M.rpc, M.n);
+    r.cb0 = r.kg * M.cpg;
+    r.cb1 = min(r.cb0 + M.cpg, (M.k + kMegaCB - 1) / kMegaCB);
+    if (r.cb1 <= r.cb0) r.r1 = r.r0;
+    return r;
+}
+
 static __device__ __forceinline__ int mat_tiles(const MegaMat& M, int b) {
-    const int r0 = b * M.rpc, r1 = min(r0 + M.rpc, M.n);
-    if (r1 <= r0) return 0;
-    return ((r1 - r0 + M.rt - 1) / M.rt) * ((M.k + kMegaCB - 1) / kMegaCB);
+    const MatRange r = mat_range(M, b);
+    if (r.r1 <= r.r0) return 0;
+    return ((r.r1 - r.r0 + M.rt - 1) / M.rt) * (r.cb1 - r.cb0);
 }
 
 // Position in the ring: slot and the parity of its current fill.
@@ -151,37 +168,38 @@ static __device__ __forceinline__ void load_tile(const MegaMat& M, int r0, int r
              pol);
 }
 
-// The same tile pulled into L2 ahead of its ring slot (no completion).
-static __device__ __forceinline__ void prefetch_tile(const MegaMat& M, int r0, int rows, int cb) {
-    const int w = min(kMegaCB, M.k - cb * kMegaCB);
-    bulk_prefetch_l2(M.qs + (size_t)cb * M.n * kMegaCB + (size_t)r0 * w, (uint32_t)(rows * w));
-    bulk_prefetch_l2(M.d + (size_t)cb * M.n * (kMegaCB / 32) + (size_t)r0 * (w / 32), (uint32_t)(rows * (w / 32) * 2));
-}
-
 // Walk over one CTA's tiles of the whole step, in consumer order: per layer
 // QKV, O, gate/up, down, then the LM head (l == L). Row tiles outer, column
 // blocks inner, as consume_mat takes them.
 struct TileCursor {
-    int l, m, r0, r_end, cb, ncb;
+    int l, m, r0, r_end, cb, cb0, cb1;
     const MegaMat* M;
 };
 
-static __device__ __forceinline__ const MegaMat* cursor_mat(const MegaArgs& a, int l, int m) {
-    if (l >= a.L) return &a.head;
-    const MegaLayer& ly = a.layers[l];
+// The matrices of one step in device memory: layers[0..L) then the LM head.
+struct StepMats {
+    const MegaLayer* layers;
+    const MegaMat* head;  // device copy of the head's plan
+    int L;
+};
+
+static __device__ __forceinline__ const MegaMat* cursor_mat(const StepMats& sm, int l, int m) {
+    if (l >= sm.L) return sm.head;
+    const MegaLayer& ly = sm.layers[l];
     return m == 0 ? &ly.qkv : m == 1 ? &ly.o : m == 2 ? &ly.gu : &ly.dn;
 }
 
 // positions c on the first tile of matrix (c.l, c.m) or later; false past the head
-static __device__ bool cursor_enter(const MegaArgs& a, TileCursor& c, int b) {
-    while (c.l <= a.L) {
-        c.M = cursor_mat(a, c.l, c.m);
-        c.r0 = b * c.M->rpc;
-        c.r_end = min(c.r0 + c.M->rpc, c.M->n);
-        c.cb = 0;
-        c.ncb = (c.M->k + kMegaCB - 1) / kMegaCB;
+static __device__ bool cursor_enter(const StepMats& sm, TileCursor& c, int b) {
+    while (c.l <= sm.L) {
+        c.M = cursor_mat(sm, c.l, c.m);
+        const MatRange r = mat_range(*c.M, b);
+        c.r0 = r.r0;
+        c.r_end = r.r1;
+        c.cb = c.cb0 = r.cb0;
+        c.cb1 = r.cb1;
         if (c.r0 < c.r_end) return true;
-        if (c.l == a.L || ++c.m == 4) {
+        if (c.l == sm.L || ++c.m == 4) {
             c.m = 0;
             c.l++;
         }
@@ -189,45 +207,58 @@ static __device__ bool cursor_enter(const MegaArgs& a, TileCursor& c, int b) {
     return false;
 }
 
-static __device__ bool cursor_next(const MegaArgs& a, TileCursor& c, int b) {
-    if (++c.cb < c.ncb) return true;
-    c.cb = 0;
+static __device__ bool cursor_next(const StepMats& sm, TileCursor& c, int b) {
+    if (++c.cb < c.cb1) return true;
+    c.cb = c.cb0;
     c.r0 += c.M->rt;
     if (c.r0 < c.r_end) return true;
-    if (c.l == a.L || ++c.m == 4) {
+    if (c.l == sm.L || ++c.m == 4) {
         c.m = 0;
         c.l++;
     }
-    return cursor_enter(a, c, b);
+    return cursor_enter(sm, c, b);
 }
 
-// Producer (one thread): every tile of the step into the ring, `pf` tiles of
-// L2 prefetch ahead of the ring. Returns false when a bounded wait gave up.
-static __device__ bool produce_step(const MegaArgs& a, int b, int ns, uint64_t* full, uint64_t* empty,
-                                    unsigned char* ring) {
+// Producer (one thread): every tile of the step into the ring, in consumer
+// order, a slot refilled as soon as every consumer warp released it. It never
+// waits on activations, so weights keep streaming across the grid barriers.
+static __device__ bool produce_step(const StepMats& smats, int b, int ns, uint64_t* full, uint64_t* empty,
+                                    unsigned char* ring, int* err) {
     const uint64_t pol = policy_evict_first();
-    TileCursor c{0, 0, 0, 0, 0, 0, nullptr}, p{0, 0, 0, 0, 0, 0, nullptr};
-    bool have = cursor_enter(a, c, b), phave = cursor_enter(a, p, b);
-    for (int i = 0; i < a.pf_tiles && phave; i++) {
-        prefetch_tile(*p.M, p.r0, min(p.M->rt, p.r_end - p.r0), p.cb);
-        phave = cursor_next(a, p, b);
-    }
+    TileCursor c{0, 0, 0, 0, 0, 0, 0, nullptr};
+    bool have = cursor_enter(smats, c, b);
     RingPos rp{0, 0};
     for (int t = 0; have; t++) {
-        if (t >= ns && !mbar_wait_err(&empty[rp.s], rp.ph ^ 1, a.err, 3)) return false;
+        if (t >= ns && !mbar_wait_err(&empty[rp.s], rp.ph ^ 1, err, 3)) return false;
         load_tile(*c.M, c.r0, min(c.M->rt, c.r_end - c.r0), c.cb, ring + (size_t)rp.s * kMegaSlotBytes, &full[rp.s],
                   pol);
         rp.next(ns);
-        if (phave) {
-            prefetch_tile(*p.M, p.r0, min(p.M->rt, p.r_end - p.r0), p.cb);
-            phave = cursor_next(a, p, b);
-        }
-        have = cursor_next(a, c, b);
+        have = cursor_next(smats, c, b);
     }
     return true;
 }
 
-enum MegaEpi { ME_STORE = 0, ME_BIAS, ME_RESID, ME_SWIGLU, ME_ARGMAX };
+// Ring context of the consumer warps, handed to consume_mat.
+struct Ring {
+    uint64_t* full;
+    uint64_t* empty;
+    unsigned char* ring;
+    int ns;
+    RingPos rp;  // next tile to consume
+};
+
+static __device__ __forceinline__ bool wait_tile(Ring& r, int* err) {
+    return mbar_wait_err(&r.full[r.rp.s], r.rp.ph, err, 4);
+}
+
+// This warp is done with the current tile: release it and advance.
+static __device__ __forceinline__ void release_tile(Ring& r, int lane) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&r.empty[r.rp.s]);
+    r.rp.next(r.ns);
+}
+
+enum MegaEpi { ME_PART = 0, ME_SWIGLU, ME_ARGMAX };  // ME_PART: y[kg * n + row] (kg = column group)
 
 static __device__ __forceinline__ void mma_s8(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                               uint32_t b1, int& c0, int& c1, int& c2, int& c3) {
@@ -263,15 +294,14 @@ static __device__ __forceinline__ float d_hi(uint32_t w) { return __int_as_float
 // Accumulators carry a 2^-28 factor (scale products stay normal for block
 // maxima down to 2^-54 and finite up to 2^57), removed at the end.
 template <int EPI>
-static __device__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, RingPos& rp, int ns,
-                                   uint64_t* full, uint64_t* empty, const unsigned char* ring, float* s_part,
-                                   float* s_res, float* y, const float* bias, unsigned long long* s_best,
-                                   int* err) {
+static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, Ring& rg_, float* s_part,
+                                   float* s_res, float* y, unsigned long long* s_best, int* err) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int g = lane >> 2, tq = lane & 3;
     const float s1 = tq == 0 ? 128.0f : 1.0f;
     const float km = tq == 0 ? 0x1p91f : 0x1p84f;  // 2^112 * 2^-28 * m
-    const int r_begin = b * M.rpc, r_end = min(r_begin + M.rpc, M.n);
+    const MatRange R = mat_range(M, b);
+    const int r_begin = R.r0, r_end = R.r1;
     const int ncb = (M.k + kMegaCB - 1) / kMegaCB;
     const int wl = M.k - (ncb - 1) * kMegaCB;  // width of the last column block
     // Warp w takes the 32-column blocks w + i * kMegaCW (i < BPW) of each tile.
@@ -292,11 +322,11 @@ static __device__ bool consume_mat(const MegaMat& M, const int8_t* xd, const flo
         float acc[NRG][2];
 #pragma unroll
         for (int j = 0; j < NRG; j++) acc[j][0] = acc[j][1] = 0.0f;
-        for (int cb = 0; cb < ncb; cb++) {
-            if (!mbar_wait_err(&full[rp.s], rp.ph, err, 4)) return false;
+        for (int cb = R.cb0; cb < R.cb1; cb++) {
+            if (!wait_tile(rg_, err)) return false;
             const bool lastb = cb == ncb - 1;
             const int w = lastb ? wl : kMegaCB, nblk = w >> 5;
-            const unsigned char* slot = ring + (size_t)rp.s * kMegaSlotBytes;
+            const unsigned char* slot = rg_.ring + (size_t)rg_.rp.s * kMegaSlotBytes;
 #pragma unroll
             for (int i = 0; i < BPW; i++) {
                 const int bw = warp + i * kMegaCW;
@@ -322,9 +352,7 @@ static __device__ bool consume_mat(const MegaMat& M, const int8_t* xd, const flo
                     }
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[rp.s]);
-            rp.next(ns);
+            release_tile(rg_, lane);
         }
 #pragma unroll
         for (int rg = 0; rg < NRG; rg++) {
@@ -364,12 +392,7 @@ static __device__ bool consume_mat(const MegaMat& M, const int8_t* xd, const flo
             }
             if (lane == 0 && best) atomicMax(s_best, best);
         } else {
-            for (int e = tid; e < rows; e += kMegaCW * 32) {
-                float v = s_res[e];
-                if (EPI == ME_BIAS) v = __fadd_rn(v, __ldg(bias + r0 + e));
-                if (EPI == ME_RESID) v = __fadd_rn(__ldcg(y + r0 + e), v);
-                y[r0 + e] = v;
-            }
+            for (int e = tid; e < rows; e += kMegaCW * 32) y[(size_t)R.kg * M.n + r0 + e] = s_res[e];
         }
         csync();
     }
@@ -399,6 +422,38 @@ static __device__ void x_load(float* x_s, const float* src, int k) {
     float4* d4 = reinterpret_cast<float4*>(x_s);
 #pragma unroll 4
     for (int i = threadIdx.x; i < (k >> 2); i += kMegaCW * 32) d4[i] = __ldcg(s4 + i);
+    csync();
+}
+
+// x_s[0..k) = base + sum of np (<= kMaxParts) partial rows (stride k), in that
+// order; `out` (one CTA) also receives the sum. 16-byte loads, two partial
+// rows issued ahead of their adds.
+constexpr int kMaxParts = 8;
+static __device__ void x_resid(float* x_s, const float* base, const float* parts, int np, int k, float* out) {
+    const float4* b4 = reinterpret_cast<const float4*>(base);
+    const float4* p4 = reinterpret_cast<const float4*>(parts);
+    float4* d4 = reinterpret_cast<float4*>(x_s);
+    float4* o4 = reinterpret_cast<float4*>(out);
+    const int k4 = k >> 2;
+    for (int i = threadIdx.x; i < k4; i += kMegaCW * 32) {
+        float4 v = __ldcg(b4 + i);
+        for (int j0 = 0; j0 < np; j0 += 2) {  // two partial rows in flight
+            float4 q[2];
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+                if (j0 + j < np) q[j] = __ldcg(p4 + (size_t)(j0 + j) * k4 + i);
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+                if (j0 + j < np) {
+                    v.x = __fadd_rn(v.x, q[j].x);
+                    v.y = __fadd_rn(v.y, q[j].y);
+                    v.z = __fadd_rn(v.z, q[j].z);
+                    v.w = __fadd_rn(v.w, q[j].w);
+                }
+        }
+        d4[i] = v;
+        if (out) o4[i] = v;
+    }
     csync();
 }
 
@@ -506,11 +561,12 @@ static __host__ __device__ __forceinline__ AttnPlan attn_plan(int G, int hd, int
 }
 
 // RoPE (when ct; rotated pairs stored in the reference's slot order) +
-// kv_pack_q8 quantisation of one head row by a warp; the row goes
+// kv_pack_q8 quantisation of one head row by a warp. The row is the sum of
+// nsrc partial rows sstride apart (+ bias); it goes
 // to dst/scale_out and, when dst2, also to dst2/scale2.
-static __device__ __forceinline__ void rq_warp(const float* src, int hd, const float* ct, const float* stb,
-                                               int8_t* dst, float* scale_out, int lane, int8_t* dst2 = nullptr,
-                                               float* scale2 = nullptr) {
+static __device__ __forceinline__ void rq_warp(const float* src, int nsrc, size_t sstride, const float* bias, int hd,
+                                               const float* ct, const float* stb, int8_t* dst, float* scale_out,
+                                               int lane, int8_t* dst2 = nullptr, float* scale2 = nullptr) {
     constexpr int MAXP = 4;
     const int half = hd >> 1;
     float x0[MAXP], x1[MAXP];
@@ -521,7 +577,25 @@ static __device__ __forceinline__ void rq_warp(const float* src, int hd, const f
         x0[tt] = 0.0f;
         x1[tt] = 0.0f;
         if (p < half) {
-            float v0 = __ldcg(src + 2 * p), v1 = __ldcg(src + 2 * p + 1);
+            // the row = sum of the column groups' partials (+ bias), loaded
+            // two groups at a time ahead of the adds
+            float v0 = 0.0f, v1 = 0.0f;
+            for (int k0 = 0; k0 < nsrc; k0 += 2) {
+                float2 pv[2];
+#pragma unroll
+                for (int k = 0; k < 2; k++)
+                    if (k0 + k < nsrc) pv[k] = __ldcg(reinterpret_cast<const float2*>(src + (k0 + k) * sstride + 2 * p));
+#pragma unroll
+                for (int k = 0; k < 2; k++)
+                    if (k0 + k < nsrc) {
+                        v0 = k0 + k == 0 ? pv[k].x : __fadd_rn(v0, pv[k].x);
+                        v1 = k0 + k == 0 ? pv[k].y : __fadd_rn(v1, pv[k].y);
+                    }
+            }
+            if (bias) {
+                v0 = __fadd_rn(v0, __ldg(bias + 2 * p));
+                v1 = __fadd_rn(v1, __ldg(bias + 2 * p + 1));
+            }
             if (ct) {
                 const float c = ct[p], sn = stb[p];
                 const float r0 = __fmaf_rn(v0, c, -__fmul_rn(v1, sn));
@@ -582,9 +656,9 @@ static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const floa
 // of a warp read 32 different banks of 32 different rows), online softmax,
 // P.V with V decoded once per 4 dims. Writes the split partials (o, m, l);
 // the last item of the kv head to finish merges all splits of its query
-// heads into the q rows of the qkv buffer (the O projection's input).
+// heads into the attention rows buffer (the O projection's input).
 template <int MAXG>
-static __device__ bool attn_item(const MegaArgs& a, int layer, int kvh, int split, int nv, int pos,
+static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, int kvh, int split, int nv, int pos,
                                  unsigned char* sm, uint64_t* abar, uint32_t& aph, int* s_flag, long long* tr) {
     const int G = a.H / a.KV, hd = a.hd, half = hd >> 1, hw = hd >> 2, S = a.asub;
 #define ATR(k)                                      \
@@ -635,14 +709,21 @@ static __device__ bool attn_item(const MegaArgs& a, int layer, int kvh, int spli
     };
     bool pending = issue(c0);
 
-    for (int gq = warp; gq < G; gq += kMegaCW)
-        rq_warp(a.qkv + (size_t)(kvh * G + gq) * hd, hd, ct, stb, s_q8 + gq * hd, s_qsc + gq, lane);
+    const MegaLayer& ly = a.layers[layer];
+    const int nq = ly.qkv.spl;
+    const size_t nqkv = (size_t)ly.qkv.n;
+    const float* bq = ly.bias;
+    for (int gq = warp; gq < G; gq += kMegaCW) {
+        const size_t o = (size_t)(kvh * G + gq) * hd;
+        rq_warp(a.pq + o, nq, nqkv, bq ? bq + o : nullptr, hd, ct, stb, s_q8 + gq * hd, s_qsc + gq, lane);
+    }
     if (owner) {  // append K (roped) and V at pos; keep a copy for the tile
+        const size_t ok = (size_t)q_dim + (size_t)kvh * hd, ov = ok + kv_dim;
         if (warp == kMegaCW - 1)
-            rq_warp(a.qkv + q_dim + (size_t)kvh * hd, hd, ct, stb, kb + (size_t)pos * hd, ksb + pos, lane, s_row,
-                    s_rsc);
+            rq_warp(a.pq + ok, nq, nqkv, bq ? bq + ok : nullptr, hd, ct, stb, kb + (size_t)pos * hd, ksb + pos,
+                    lane, s_row, s_rsc);
         else if (warp == kMegaCW - 2)
-            rq_warp(a.qkv + q_dim + kv_dim + (size_t)kvh * hd, hd, nullptr, nullptr, vb + (size_t)pos * hd,
+            rq_warp(a.pq + ov, nq, nqkv, bq ? bq + ov : nullptr, hd, nullptr, nullptr, vb + (size_t)pos * hd,
                     vsb + pos, lane, s_row + hd, s_rsc + 1);
     }
     for (int gq = tid; gq < G; gq += nthr) {
@@ -803,7 +884,7 @@ static __device__ bool attn_item(const MegaArgs& a, int layer, int kvh, int spli
         float O = 0.0f;
 #pragma unroll 8
         for (int s2 = 0; s2 < nv; s2++) O = __fmaf_rn(wt[s2], __ldcg(po + (size_t)s2 * hd), O);
-        a.qkv[(size_t)h * hd + dd] = O;
+        a.attn[(size_t)h * hd + dd] = O;
     }
     csync();
     ATR(8);
@@ -840,27 +921,25 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     }
     __syncthreads();
 
-    if (warp == kMegaCW) {  // ---- producer: the step's weight tiles, in consumer order
-        if (lane == 0) produce_step(a, b, ns, full, empty, ring);
+    if (warp == kMegaCW) {  // ---- producer warp: the step's weight tiles, in consumer order
+        if (lane == 0) produce_step(StepMats{a.layers, a.head_dev, a.L}, b, ns, full, empty, ring, a.err);
         return;
     }
 
     // ---- consumers ---------------------------------------------------------
+    Ring rg{full, empty, ring, ns, RingPos{0, 0}};
     DevState* st = a.st;
     const int active = *(volatile const int*)&st->active;
-    RingPos rp{0, 0};
     if (!active) {  // disabled step: take every tile off the ring, then leave
         int n = 0;
         for (int l = 0; l < a.L; l++) {
             const MegaLayer& ly = a.layers[l];
             n += mat_tiles(ly.qkv, b) + mat_tiles(ly.o, b) + mat_tiles(ly.gu, b) + mat_tiles(ly.dn, b);
         }
-        n += mat_tiles(a.head, b);
+        n += mat_tiles(*a.head_dev, b);
         for (int t = 0; t < n; t++) {
-            if (!mbar_wait_err(&full[rp.s], rp.ph, a.err, 4)) return;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[rp.s]);
-            rp.next(ns);
+            if (!wait_tile(rg, a.err)) return;
+            release_tile(rg, lane);
         }
         return;
     }
@@ -895,17 +974,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                 x_s[i] = v;
                 if (b == 0) a.X[i] = v;
             }
-        } else {
-            x_load(x_s, a.X, a.D);
+        } else {  // X = X after O + the previous down projection's partials
+            x_resid(x_s, a.Xb, a.pd, a.layers[l - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);
         }
         x_norm(x_s, a.D, ly.rms1, 1e-5f, s_red);
         x_digitize(x_s, a.D, xd, xsc);
         const int tb = 1 + l * kMegaTraceLayer;
         TRACE(tb + 0);
-        ok = ly.bias ? consume_mat<ME_BIAS>(ly.qkv, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.qkv, ly.bias,
-                                           &s_best, a.err)
-                     : consume_mat<ME_STORE>(ly.qkv, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.qkv,
-                                            nullptr, &s_best, a.err);
+        ok = consume_mat<ME_PART>(ly.qkv, xd, xsc, rg, s_part, s_res, a.pq, &s_best,
+                                  a.err);
         TRACE(tb + 1);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
         TRACE(tb + 2);
@@ -923,21 +1000,21 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         ok = grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
         TRACE(tb + 4);
         if (!ok) break;
-        // O projection + residual
-        x_load(x_s, a.qkv, a.H * a.hd);  // merged attention rows (q part of qkv)
+        // O projection (partials; the residual add happens in the next reader)
+        x_load(x_s, a.attn, a.H * a.hd);  // merged attention rows
         x_digitize(x_s, a.H * a.hd, xd, xsc);
         TRACE(tb + 5);
-        ok = consume_mat<ME_RESID>(ly.o, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.X, nullptr, &s_best, a.err);
+        ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err);
         TRACE(tb + 6);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
         TRACE(tb + 7);
         if (!ok) break;
-        // gate/up + SwiGLU
-        x_load(x_s, a.X, a.D);
+        // gate/up + SwiGLU on RMSNorm(X + O partials); CTA 0 keeps that X in Xb
+        x_resid(x_s, a.X, a.po, ly.o.spl, a.D, b == 0 ? a.Xb : nullptr);
         x_norm(x_s, a.D, ly.rms2, 1e-5f, s_red);
         x_digitize(x_s, a.D, xd, xsc);
         TRACE(tb + 8);
-        ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.h, nullptr, &s_best,
+        ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, rg, s_part, s_res, a.h, &s_best,
                                     a.err);
         TRACE(tb + 9);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
@@ -947,8 +1024,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         x_load(x_s, a.h, a.F);
         x_digitize(x_s, a.F, xd, xsc);
         TRACE(tb + 11);
-        ok = consume_mat<ME_RESID>(ly.dn, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.X, nullptr, &s_best,
-                                   a.err);
+        ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best,
+                                  a.err);
         TRACE(tb + 12);
         ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
         TRACE(tb + 13);
@@ -956,12 +1033,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     if (!ok) return;
     // LM head + argmax
     const int th = 1 + a.L * kMegaTraceLayer;
-    x_load(x_s, a.X, a.D);
+    x_resid(x_s, a.Xb, a.pd, a.layers[a.L - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);  // final X kept in X
     if (tid == 0) s_best = 0ull;
     x_norm(x_s, a.D, a.final_norm, 1e-5f, s_red);
     x_digitize(x_s, a.D, xd, xsc);
     TRACE(th + 0);
-    if (!consume_mat<ME_ARGMAX>(a.head, xd, xsc, rp, ns, full, empty, ring, s_part, s_res, a.logits, nullptr, &s_best,
+    if (!consume_mat<ME_ARGMAX>(*a.head_dev, xd, xsc, rg, s_part, s_res, a.logits, &s_best,
                                 a.err))
         return;
     TRACE(th + 1);
@@ -997,12 +1074,36 @@ int mega_num_ctas() {
     return n;
 }
 
-int mega_plan(MegaMat& m, int nctas) {
+// Work split of a matrix: for every column-group count (split-K only when
+// `splittable`, at most kMaxParts groups) the least rows per CTA that fit the
+// CTAs, costed as the bytes one CTA streams + a hand-off cost per tile + an
+// epilogue cost per row tile + the readers' extra round trips; the cheapest
+// wins (fewer groups on ties).
+int mega_plan(MegaMat& m, int nctas, bool splittable) {
     if (m.n <= 0 || m.n % 16 || m.k % 32 || m.k <= 0) return JYC_ERR_UNSUPPORTED;
-    int rpc = (m.n + nctas - 1) / nctas;
-    rpc = (rpc + 15) / 16 * 16;
-    m.rpc = rpc;
-    m.rt = std::min(kMegaRT, rpc);
+    const int ncb = (m.k + kMegaCB - 1) / kMegaCB;
+    // readers sum the groups two at a time: every pair beyond the first costs
+    // them one more L2 round trip
+    const double kTileCost = 8192.0, kRowTileCost = 24576.0, kGroupCost = 2048.0, kTripCost = 24576.0;
+    double best = 1e300;
+    for (int cpg = ncb; cpg >= 1; cpg--) {
+        const int spl = (ncb + cpg - 1) / cpg;
+        if ((spl > 1 && !splittable) || spl > nctas || spl > kMaxParts) continue;
+        const int chunks = nctas / spl;
+        int rpc = (m.n + chunks - 1) / chunks;
+        rpc = (rpc + 15) / 16 * 16;
+        const int rt = std::min(kMegaRT, rpc);
+        const int rtiles = (rpc + rt - 1) / rt, tiles = rtiles * cpg;
+        const double cost = (double)rpc * cpg * kMegaCB + tiles * kTileCost + rtiles * kRowTileCost +
+                            (spl - 1) * kGroupCost + ((spl + 1) / 2 - 1) * kTripCost;
+        if (cost < best) {
+            best = cost;
+            m.rpc = rpc;
+            m.rt = rt;
+            m.spl = spl;
+            m.cpg = cpg;
+        }
+    }
     return JYC_OK;
 }
 

@@ -26,12 +26,17 @@ __host__ __device__ __forceinline__ size_t mega_d_index(size_t R, int j, int nbl
     return (((R >> 4) * (size_t)nblk + j) * 8 + (R & 7)) * 2 + ((R >> 3) & 1);
 }
 
+// Work split of one matrix over the CTAs: CTA b takes row chunk b / spl (rpc
+// rows) and column group b % spl (cpg column blocks). spl > 1 (split-K) writes
+// per-group partial sums that the next reader adds up.
 struct MegaMat {
     const uint8_t* qs;  // tiled copy (see above)
     const uint16_t* d;
     int n, k;
     int rpc;  // rows per CTA (multiple of 16)
     int rt;   // rows per tile (multiple of 16, <= kMegaRT)
+    int spl;  // column groups
+    int cpg;  // column blocks per group
 };
 
 struct MegaLayer {
@@ -45,6 +50,7 @@ struct MegaArgs {
     const MegaLayer* layers;  // device array [L]
     int L;
     MegaMat head;
+    const MegaMat* head_dev;  // device copy of `head` (walked by the copy issuer)
     const float* final_norm;
     const float* ef;          // fp32 embedding [V][D], or
     const uint8_t* eqs;       // tiled Q8_0 embedding (n = V, k = D)
@@ -57,7 +63,12 @@ struct MegaArgs {
     float* ks;                // [L][KV][max_seq]
     float* vs;
     int max_seq;
-    float* X;                 // residual stream [D]
+    float* X;                 // residual stream [D] after each layer's down projection (and the final one)
+    float* Xb;                // residual stream [D] after each layer's O projection
+    float* pq;                // QKV partial sums [qkv.spl][q|k|v] (bias added by the reader)
+    float* po;                // O partial sums [o.spl][D]
+    float* pd;                // down partial sums [dn.spl][D]
+    float* attn;              // merged attention rows [H * hd]
     float* qkv;               // [q|k|v]
     float* h;                 // SwiGLU output [F]
     float* logits;            // [V]
@@ -74,7 +85,6 @@ struct MegaArgs {
     int kmax;                 // largest GEMV input length (x / digit buffers)
     int xs_bytes;             // shared bytes of the x / digits / attention union
     int nslots;               // ring depth
-    int pf_tiles;             // tiles of L2 prefetch ahead of the ring (0: none)
     long long* trace;         // optional: SM clock at each phase boundary, [CTA][kMegaTracePts]
 };
 
@@ -85,7 +95,7 @@ constexpr int kMegaTracePts = 1 + 64 * kMegaTraceLayer + 4;  // up to 64 layers
 
 int launch_q8_repack_tiled(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d, int n_total,
                            int row_off, int row_stride, cudaStream_t s);
-int mega_plan(MegaMat& m, int nctas);
+int mega_plan(MegaMat& m, int nctas, bool splittable);
 int mega_smem_bytes(const MegaArgs& a);
 int mega_xs_bytes(int kmax, int G, int hd, int S);
 int mega_attn_sub(int kmax, int G, int hd, int chunk);

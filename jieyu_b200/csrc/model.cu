@@ -231,13 +231,13 @@ bool mega_eligible(const jyc_model* m, const jyc_model_desc* d) {
     return hd >= 16 && hd <= 256 && (hd & (hd - 1)) == 0 && m->H / m->KV <= 8;
 }
 
-MegaMat mega_mat(const DevMat& w, int nctas) {
+MegaMat mega_mat(const DevMat& w, int nctas, bool splittable) {
     MegaMat mm{};
     mm.qs = w.tq;
     mm.d = w.td;
     mm.n = w.n;
     mm.k = w.k;
-    mega_plan(mm, nctas);
+    mega_plan(mm, nctas, splittable);
     return mm;
 }
 
@@ -247,12 +247,18 @@ int setup_mega(jyc_model* m) {
     MegaArgs& a = m->margs;
     a = MegaArgs{};
     std::vector<MegaLayer> ml(m->L);
+    int sq = 1, so = 1, sd = 1;
     for (int l = 0; l < m->L; l++) {
         const DevLayer& ly = m->layers[l];
-        ml[l].qkv = mega_mat(ly.qkv, nctas);
-        ml[l].o = mega_mat(ly.o, nctas);
-        ml[l].gu = mega_mat(ly.gateup, nctas);
-        ml[l].dn = mega_mat(ly.down, nctas);
+        // QKV, O and down may split K (their readers sum the partials);
+        // gate/up (SwiGLU) and the LM head (argmax) need whole rows
+        ml[l].qkv = mega_mat(ly.qkv, nctas, true);
+        ml[l].o = mega_mat(ly.o, nctas, true);
+        ml[l].gu = mega_mat(ly.gateup, nctas, false);
+        ml[l].dn = mega_mat(ly.down, nctas, true);
+        sq = std::max(sq, ml[l].qkv.spl);
+        so = std::max(so, ml[l].o.spl);
+        sd = std::max(sd, ml[l].dn.spl);
         ml[l].rms1 = ly.rms1;
         ml[l].rms2 = ly.rms2;
         ml[l].bias = ly.bias;
@@ -261,7 +267,11 @@ int setup_mega(jyc_model* m) {
     JYC_CUDA(cudaMemcpy(m->d_mlayers, ml.data(), sizeof(MegaLayer) * m->L, cudaMemcpyHostToDevice));
     a.layers = m->d_mlayers;
     a.L = m->L;
-    a.head = mega_mat(m->head, nctas);
+    a.head = mega_mat(m->head, nctas, false);
+    MegaMat* hd_dev = nullptr;
+    TRY(m->alloc(&hd_dev, 1));
+    JYC_CUDA(cudaMemcpy(hd_dev, &a.head, sizeof(MegaMat), cudaMemcpyHostToDevice));
+    a.head_dev = hd_dev;
     a.final_norm = m->final_norm;
     a.ef = m->embed_f;
     a.eqs = m->embed_q.tq;
@@ -272,6 +282,11 @@ int setup_mega(jyc_model* m) {
     a.k8 = m->k8; a.v8 = m->v8; a.ks = m->ks; a.vs = m->vs;
     a.max_seq = m->max_seq;
     a.X = m->X; a.qkv = m->qkv; a.h = m->h; a.logits = m->logits;
+    TRY(m->alloc(&a.Xb, (size_t)m->D));
+    TRY(m->alloc(&a.pq, (size_t)sq * m->nqkv));
+    TRY(m->alloc(&a.po, (size_t)so * m->D));
+    TRY(m->alloc(&a.pd, (size_t)sd * m->D));
+    TRY(m->alloc(&a.attn, (size_t)m->q_dim));
     // attention split plan: about one (kv head, split) item per CTA at full context
     const int per_head = std::max(1, nctas / m->KV);
     int chunk = (m->max_seq + per_head - 1) / per_head;
@@ -296,9 +311,6 @@ int setup_mega(jyc_model* m) {
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
     const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
     a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
-    // L2 prefetch distance in tiles (JIEYU_MEGA_PREFETCH overrides; 0 disables)
-    a.pf_tiles = 8;
-    if (const char* e = getenv("JIEYU_MEGA_PREFETCH")) a.pf_tiles = std::max(0, atoi(e));
     if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode
     const int smem = mega_smem_bytes(a);
     TRY(prepare_mega_kernel(smem));
