@@ -631,17 +631,18 @@ static __device__ __forceinline__ void rq_warp(const float* src, int nsrc, size_
 }
 
 // P.V over one sub-chunk for a (column group of 4 dims, position lane)
-// thread: acc[g][i] += p[g][j] * v[j][4cg + i] for j = pl, pl + npl, ...
-template <int MAXG>
-static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const float* s_sc, const int8_t* s_v, int S,
-                                               int G, int hd, int cg, int pl, int npl, int n) {
-    for (int j = pl; j < n; j += npl) {
+// thread: acc[g][i] += p[g][j] * v[j][4cg + i] for j = pl, pl + NPL, ...
+template <int MAXG, int HD>
+static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const float* s_sc, const int8_t* s_v, int lS,
+                                               int G, int cg, int pl, int n) {
+    constexpr int NPL = kMegaCW * 32 / (HD / 4);
+    for (int j = pl; j < n; j += NPL) {
         float f[4];
-        u8x4_to_f32(*reinterpret_cast<const uint32_t*>(s_v + j * hd + 4 * cg) ^ 0x80808080u, f);
+        u8x4_to_f32(*reinterpret_cast<const uint32_t*>(s_v + j * HD + 4 * cg) ^ 0x80808080u, f);
 #pragma unroll
         for (int gq = 0; gq < MAXG; gq++)
             if (gq < G) {
-                const float p = s_sc[gq * S + j];
+                const float p = s_sc[(gq << lS) + j];
 #pragma unroll
                 for (int i = 0; i < 4; i++) acc[gq][i] = __fmaf_rn(p, f[i], acc[gq][i]);
             }
@@ -657,10 +658,11 @@ static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const floa
 // P.V with V decoded once per 4 dims. Writes the split partials (o, m, l);
 // the last item of the kv head to finish merges all splits of its query
 // heads into the attention rows buffer (the O projection's input).
-template <int MAXG>
+template <int MAXG, int HD>
 static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, int kvh, int split, int nv, int pos,
                                  unsigned char* sm, uint64_t* abar, uint32_t& aph, int* s_flag, long long* tr) {
-    const int G = a.H / a.KV, hd = a.hd, half = hd >> 1, hw = hd >> 2, S = a.asub;
+    constexpr int hd = HD, half = HD / 2, hw = HD / 4, HC = HD / 16;  // words, 16-byte chunks per row
+    const int G = a.H / a.KV, S = a.asub, lS = 31 - __clz(S);
 #define ATR(k)                                      \
     do {                                            \
         if (tr && threadIdx.x == 0) tr[k] = clock64(); \
@@ -731,7 +733,7 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
         s_l[gq] = 0.0f;
     }
     ATR(1);
-    const int ncg = hd >> 2, npl = nthr / ncg;
+    constexpr int ncg = HD / 4, npl = nthr / ncg;
     const int cg = tid % ncg, pl = tid / ncg;
     float acc[MAXG][4];
 #pragma unroll
@@ -761,17 +763,24 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
         }
         csync();
         ATR(2);
-        // scores: entry (gq, j); word order rotated by j
-        for (int e = tid; e < G * S; e += nthr) {
-            const int gq = e / S, j = e - gq * S;
+        // scores: entry (gq, j); 16-byte chunks in an order rotated with j so
+        // the 8 lanes of a shared-memory phase read 8 different bank groups
+        for (int e = tid; e < (G << lS); e += nthr) {
+            const int gq = e >> lS, j = e & (S - 1);
             float sc = -INFINITY;
             if (j < n) {
-                const uint32_t* qw = reinterpret_cast<const uint32_t*>(s_q8 + gq * hd);
-                const uint32_t* kw = reinterpret_cast<const uint32_t*>(s_k + j * hd);
+                const uint4* qc = reinterpret_cast<const uint4*>(s_q8 + gq * hd);
+                const uint4* kc = reinterpret_cast<const uint4*>(s_k + j * hd);
+                const int rot = HC >= 8 ? j : (j >> (3 - (HC == 4 ? 2 : HC == 2 ? 1 : 0)));
                 int dot = 0;
-                for (int w = 0; w < hw; w++) {
-                    const int i = (w + j) & (hw - 1);
-                    dot = __dp4a((int)qw[i], (int)kw[i], dot);
+#pragma unroll
+                for (int c = 0; c < HC; c++) {
+                    const int i = (c + rot) & (HC - 1);
+                    const uint4 qv = qc[i], kv = kc[i];
+                    dot = __dp4a((int)qv.x, (int)kv.x, dot);
+                    dot = __dp4a((int)qv.y, (int)kv.y, dot);
+                    dot = __dp4a((int)qv.z, (int)kv.z, dot);
+                    dot = __dp4a((int)qv.w, (int)kv.w, dot);
                 }
                 const float ksc = __fmul_rn(__fmul_rn(s_ks[j], s_qsc[gq]), a.scale);
                 sc = __fmul_rn((float)dot, ksc);
@@ -782,15 +791,15 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
         ATR(3);
         for (int gq = warp; gq < G; gq += kMegaCW) {
             float mx = -INFINITY;
-            for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_sc[gq * S + j]);
+            for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_sc[(gq << lS) + j]);
             mx = warp_max(mx);
             const float m_old = s_m[gq], m_new = fmaxf(m_old, mx);
             float sum = 0.0f;
             for (int j = lane; j < n; j += 32) {
-                const float sv = s_sc[gq * S + j];
+                const float sv = s_sc[(gq << lS) + j];
                 const float e = (sv == -INFINITY) ? 0.0f : expf(sv - m_new);
                 sum += e;
-                s_sc[gq * S + j] = e * s_vs[j];
+                s_sc[(gq << lS) + j] = e * s_vs[j];
             }
             sum = warp_sum(sum);
             if (lane == 0) {
@@ -809,7 +818,7 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
 #pragma unroll
                 for (int i = 0; i < 4; i++) acc[gq][i] = __fmul_rn(acc[gq][i], al);
             }
-        attn_pv<MAXG>(acc, s_sc, s_v, S, G, hd, cg, pl, npl, n);
+        attn_pv<MAXG, HD>(acc, s_sc, s_v, lS, G, cg, pl, n);
         csync();
         ATR(5);
         if (j0 + S < c1) pending = issue(j0 + S);
@@ -842,11 +851,12 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
         a.part_ml[((size_t)h * a.nsplit + split) * 2] = s_m[gq];
         a.part_ml[((size_t)h * a.nsplit + split) * 2 + 1] = s_l[gq];
     }
-    // last finisher of this kv head merges its splits
-    __threadfence();
+    // last finisher of this kv head merges its splits (the barrier orders the
+    // CTA's partial writes before thread 0's fence and arrival)
     csync();
     ATR(6);
     if (tid == 0) {
+        __threadfence();
         const unsigned int old = atomicAdd(a.acnt + kvh, 1u);
         *s_flag = old == (unsigned int)(nv - 1);
         if (*s_flag) atomicExch(a.acnt + kvh, 0u);
@@ -855,36 +865,40 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     ATR(7);
     if (!*s_flag) return true;
     __threadfence();
-    float* mw = reinterpret_cast<float*>(sm + P.kv);  // [G][nv] m, then weights
-    float* lw = mw + G * nv;                           // [G][nv] l
-    for (int e = tid; e < G * nv; e += nthr) {
-        const int gq = e / nv, s2 = e - gq * nv, h = kvh * G + gq;
-        mw[e] = __ldcg(a.part_ml + ((size_t)h * a.nsplit + s2) * 2);
-        lw[e] = __ldcg(a.part_ml + ((size_t)h * a.nsplit + s2) * 2 + 1);
-    }
-    csync();
-    for (int gq = tid; gq < G; gq += nthr) {
-        float M = -INFINITY;
-        for (int s2 = 0; s2 < nv; s2++) M = fmaxf(M, mw[gq * nv + s2]);
-        float L = 0.0f;
-        for (int s2 = 0; s2 < nv; s2++) {
-            const float ms = mw[gq * nv + s2];
-            const float wgt = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            L = __fmaf_rn(wgt, lw[gq * nv + s2], L);
-            mw[gq * nv + s2] = wgt;
-        }
-        const float inv = 1.0f / L;
-        for (int s2 = 0; s2 < nv; s2++) mw[gq * nv + s2] *= inv;
-    }
-    csync();
+    // every output element merges its splits itself: (m, l, o) of four splits
+    // per round trip, rescaled online to the running maximum
     for (int e = tid; e < G * hd; e += nthr) {
         const int gq = e / hd, dd = e - gq * hd, h = kvh * G + gq;
+        const float* ml = a.part_ml + (size_t)h * a.nsplit * 2;
         const float* po = a.part_o + (size_t)h * a.nsplit * hd + dd;
-        const float* wt = mw + gq * nv;
-        float O = 0.0f;
-#pragma unroll 8
-        for (int s2 = 0; s2 < nv; s2++) O = __fmaf_rn(wt[s2], __ldcg(po + (size_t)s2 * hd), O);
-        a.attn[(size_t)h * hd + dd] = O;
+        float M = -INFINITY, L = 0.0f, O = 0.0f;
+        for (int s0 = 0; s0 < nv; s0 += 4) {
+            float mv[4], lv[4], ov[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                mv[i] = -INFINITY;
+                lv[i] = ov[i] = 0.0f;
+                if (s0 + i < nv) {
+                    const float2 m2 = __ldcg(reinterpret_cast<const float2*>(ml) + s0 + i);
+                    mv[i] = m2.x;
+                    lv[i] = m2.y;
+                    ov[i] = __ldcg(po + (size_t)(s0 + i) * hd);
+                }
+            }
+            const float Mn = fmaxf(M, fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])));
+            if (Mn == -INFINITY) continue;
+            const float r = (M == -INFINITY) ? 0.0f : expf(M - Mn);
+            L = __fmul_rn(L, r);
+            O = __fmul_rn(O, r);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float w = (mv[i] == -INFINITY) ? 0.0f : expf(mv[i] - Mn);
+                L = __fmaf_rn(w, lv[i], L);
+                O = __fmaf_rn(w, ov[i], O);
+            }
+            M = Mn;
+        }
+        a.attn[(size_t)h * hd + dd] = __fdiv_rn(O, L);
     }
     csync();
     ATR(8);
@@ -892,6 +906,9 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     return true;
 }
 
+// One instantiation per attention shape (query heads per kv head <= MAXG,
+// head_dim HD): each kernel carries a single attention variant.
+template <int MAXG, int HD>
 __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
@@ -990,10 +1007,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         // attention items (kv head, split), round-robin over CTAs
         for (int it = b; it < a.KV * nvalid && ok; it += nct) {
             long long* tr = (a.trace && it == b) ? a.trace + (size_t)b * kMegaTracePts + tb + 14 : nullptr;
-            if (a.H / a.KV <= 4)
-                ok = attn_item<4>(a, l, it / nvalid, it % nvalid, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
-            else
-                ok = attn_item<8>(a, l, it / nvalid, it % nvalid, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
+            const int kv_h = it / nvalid, sp = it - kv_h * nvalid;
+            ok = attn_item<MAXG, HD>(a, l, kv_h, sp, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
         }
         if (!ok) break;
         TRACE(tb + 3);
@@ -1127,14 +1142,20 @@ int mega_attn_sub(int kmax, int G, int hd, int chunk) {
 
 int mega_smem_bytes(const MegaArgs& a) { return 128 + a.xs_bytes + a.nslots * kMegaSlotBytes; }
 
-int mega_static_smem() {
+// the kernel instantiation of a model's attention shape
+static const void* mega_kernel_for(int G, int hd) {
+    if (hd == 64) return G <= 4 ? (const void*)mega_step_kernel<4, 64> : (const void*)mega_step_kernel<8, 64>;
+    return G <= 4 ? (const void*)mega_step_kernel<4, 128> : (const void*)mega_step_kernel<8, 128>;
+}
+
+int mega_static_smem(int G, int hd) {
     cudaFuncAttributes fa{};
-    if (cudaFuncGetAttributes(&fa, mega_step_kernel) != cudaSuccess) return -1;
+    if (cudaFuncGetAttributes(&fa, mega_kernel_for(G, hd)) != cudaSuccess) return -1;
     return (int)fa.sharedSizeBytes;
 }
 
-int prepare_mega_kernel(int smem) {
-    JYC_CUDA(cudaFuncSetAttribute(mega_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+int prepare_mega_kernel(int smem, int G, int hd) {
+    JYC_CUDA(cudaFuncSetAttribute(mega_kernel_for(G, hd), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     return JYC_OK;
 }
 
@@ -1149,7 +1170,8 @@ int launch_mega_step(const MegaArgs& a, cudaStream_t s) {
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, mega_step_kernel, a);
+    void* args[] = {const_cast<MegaArgs*>(&a)};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, mega_kernel_for(a.H / a.KV, a.hd), args);
     if (e != cudaSuccess) return cuda_fail(e, "mega_step launch");
     count_launch();
     return JYC_OK;

@@ -101,8 +101,8 @@ int mega_xs_bytes(int kmax, int G, int hd, int S);
 int mega_attn_sub(int kmax, int G, int hd, int chunk);
 int mega_num_ctas();
 int launch_mega_step(const MegaArgs& a, cudaStream_t s);
-int prepare_mega_kernel(int smem);
-int mega_static_smem();  // -1 when the kernel image cannot be queried
+int prepare_mega_kernel(int smem, int G, int hd);
+int mega_static_smem(int G, int hd);  // -1 when the kernel image cannot be queried
 int* device_error_word();
 int mega_negative_scales(bool reset);  // 1 when a repacked Q8_0 scale was negative, -1 on error
 

@@ -226,9 +226,8 @@ bool mega_eligible(const jyc_model* m, const jyc_model_desc* d) {
     const int k32[] = {m->D, m->q_dim, m->F};
     for (int k : k32)
         if (k % 32) return false;
-    // head_dim a power of two in [16, 256]; query heads per kv head <= 8
-    const int hd = m->hd;
-    return hd >= 16 && hd <= 256 && (hd & (hd - 1)) == 0 && m->H / m->KV <= 8;
+    // head_dim 64 or 128; query heads per kv head <= 8
+    return (m->hd == 64 || m->hd == 128) && m->H / m->KV <= 8;
 }
 
 MegaMat mega_mat(const DevMat& w, int nctas, bool splittable) {
@@ -290,7 +289,7 @@ int setup_mega(jyc_model* m) {
     // attention split plan: about one (kv head, split) item per CTA at full context
     const int per_head = std::max(1, nctas / m->KV);
     int chunk = (m->max_seq + per_head - 1) / per_head;
-    chunk = std::max(64, (chunk + 63) / 64 * 64);
+    chunk = std::max(128, (chunk + 63) / 64 * 64);  // >= 128: few splits to merge at short contexts
     a.chunk = chunk;
     a.nsplit = (m->max_seq + chunk - 1) / chunk;
     TRY(m->alloc(&a.part_o, (size_t)m->H * a.nsplit * m->hd));
@@ -307,13 +306,13 @@ int setup_mega(jyc_model* m) {
     TRY(m->alloc(&a.acnt, (size_t)m->KV));
     JYC_CUDA(cudaMemset(a.acnt, 0, sizeof(unsigned int) * m->KV));
     // ring as deep as the shared memory allows (227 KB per CTA, at least 2 slots)
-    const int st_smem = mega_static_smem();
+    const int st_smem = mega_static_smem(m->H / m->KV, m->hd);
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
     const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
     a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
     if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode
     const int smem = mega_smem_bytes(a);
-    TRY(prepare_mega_kernel(smem));
+    TRY(prepare_mega_kernel(smem, m->H / m->KV, m->hd));
     m->mega = true;
     return JYC_OK;
 }
