@@ -251,6 +251,18 @@ JYC_API int jyc_model_kernels_per_step(const jyc_model* m);
 /* 2 when the model decodes with the single-launch TMA-streamed decode kernel
  * (Q8_0 weights in the tiled layout), 0 with the generic kernels. */
 JYC_API int jyc_model_decode_path(const jyc_model* m);
+/* Tensor-parallel stepping (no counterpart in the reference, which runs on
+ * one host): a model built from one rank's shard (its query and kv heads, its
+ * gate/up rows, the matching input columns of O and down; norms, embedding and
+ * LM head whole) decodes one token as a sequence of phase windows of the
+ * decode kernel: [2l, 2l+1) = QKV, attention and the O projection of layer l,
+ * [2l+1, 2l+2) = gate/up and down, [2L, 2L+1) = the LM head. O and down leave
+ * per-rank partial sums (jyc_model_partials: device pointers and float counts)
+ * that the caller all-reduces (sum over ranks) between windows; the next
+ * window adds them into the residual stream. */
+JYC_API int jyc_model_decode_window(jyc_model* m, int first, int last, void* stream);
+JYC_API int jyc_model_partials(jyc_model* m, float** o_part, int* o_count, float** d_part, int* d_count);
+
 /* Error word of the device kernels: non-zero if a bounded wait gave up
  * (reset != 0 clears it). */
 JYC_API int jyc_device_error(int reset);

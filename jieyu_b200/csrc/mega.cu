@@ -181,6 +181,7 @@ struct StepMats {
     const MegaLayer* layers;
     const MegaMat* head;  // device copy of the head's plan
     int L;
+    int ord_end;          // walk matrices with 4 l + m < ord_end (the head counts as 4 L)
 };
 
 static __device__ __forceinline__ const MegaMat* cursor_mat(const StepMats& sm, int l, int m) {
@@ -191,7 +192,7 @@ static __device__ __forceinline__ const MegaMat* cursor_mat(const StepMats& sm, 
 
 // positions c on the first tile of matrix (c.l, c.m) or later; false past the head
 static __device__ bool cursor_enter(const StepMats& sm, TileCursor& c, int b) {
-    while (c.l <= sm.L) {
+    while (c.l <= sm.L && (c.l < sm.L ? 4 * c.l + c.m : 4 * sm.L) < sm.ord_end) {
         c.M = cursor_mat(sm, c.l, c.m);
         const MatRange r = mat_range(*c.M, b);
         c.r0 = r.r0;
@@ -222,10 +223,10 @@ static __device__ bool cursor_next(const StepMats& sm, TileCursor& c, int b) {
 // Producer (one thread): every tile of the step into the ring, in consumer
 // order, a slot refilled as soon as every consumer warp released it. It never
 // waits on activations, so weights keep streaming across the grid barriers.
-static __device__ bool produce_step(const StepMats& smats, int b, int ns, uint64_t* full, uint64_t* empty,
-                                    unsigned char* ring, int* err) {
+static __device__ bool produce_step(const StepMats& smats, int l0, int m0, int b, int ns, uint64_t* full,
+                                    uint64_t* empty, unsigned char* ring, int* err) {
     const uint64_t pol = policy_evict_first();
-    TileCursor c{0, 0, 0, 0, 0, 0, 0, nullptr};
+    TileCursor c{l0, m0, 0, 0, 0, 0, 0, nullptr};
     bool have = cursor_enter(smats, c, b);
     RingPos rp{0, 0};
     for (int t = 0; have; t++) {
@@ -939,7 +940,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     __syncthreads();
 
     if (warp == kMegaCW) {  // ---- producer warp: the step's weight tiles, in consumer order
-        if (lane == 0) produce_step(StepMats{a.layers, a.head_dev, a.L}, b, ns, full, empty, ring, a.err);
+        if (lane == 0)
+            produce_step(StepMats{a.layers, a.head_dev, a.L, 2 * a.win1}, a.win0 >> 1, (a.win0 & 1) * 2, b, ns, full,
+                         empty, ring, a.err);
         return;
     }
 
@@ -949,11 +952,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     const int active = *(volatile const int*)&st->active;
     if (!active) {  // disabled step: take every tile off the ring, then leave
         int n = 0;
-        for (int l = 0; l < a.L; l++) {
-            const MegaLayer& ly = a.layers[l];
-            n += mat_tiles(ly.qkv, b) + mat_tiles(ly.o, b) + mat_tiles(ly.gu, b) + mat_tiles(ly.dn, b);
+        for (int p = a.win0; p < a.win1; p++) {
+            if (p >= 2 * a.L) {
+                n += mat_tiles(*a.head_dev, b);
+                continue;
+            }
+            const MegaLayer& ly = a.layers[p >> 1];
+            n += (p & 1) ? mat_tiles(ly.gu, b) + mat_tiles(ly.dn, b) : mat_tiles(ly.qkv, b) + mat_tiles(ly.o, b);
         }
-        n += mat_tiles(*a.head_dev, b);
         for (int t = 0; t < n; t++) {
             if (!wait_tile(rg, a.err)) return;
             release_tile(rg, lane);
@@ -973,79 +979,88 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     } while (0)
     TRACE(0);
 
-    for (int l = 0; l < a.L && ok; l++) {
+    // half-layer phases p = 2 l + h of this launch's window (h 0: QKV,
+    // attention, O; h 1: gate/up, down); p = 2 L is the LM head
+    for (int p = a.win0; p < a.win1 && p < 2 * a.L && ok; p++) {
+        const int l = p >> 1;
         const MegaLayer& ly = a.layers[l];
-        // QKV
-        if (l == 0) {
-            const int id = __ldcg(a.tokens + pos);
-            for (int i = tid; i < a.D; i += kMegaCW * 32) {
-                float v;
-                if (a.ef) {
-                    v = __ldg(a.ef + (size_t)id * a.D + i);
-                } else {
-                    const int cb = i / kMegaCB, w = min(kMegaCB, a.D - cb * kMegaCB), c = i - cb * kMegaCB;
-                    const uint8_t* row = a.eqs + (size_t)cb * a.V * kMegaCB + (size_t)id * w;
-                    const int8_t q = (int8_t)row[16 * swz_chunk(c >> 4, id & 7, w >> 4) + (c & 15)];
-                    v = __fmul_rn((float)q, h2f(a.ed[(size_t)cb * a.V * (kMegaCB / 32) + mega_d_index(id, c / 32, w / 32)]));
-                }
-                x_s[i] = v;
-                if (b == 0) a.X[i] = v;
-            }
-        } else {  // X = X after O + the previous down projection's partials
-            x_resid(x_s, a.Xb, a.pd, a.layers[l - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);
-        }
-        x_norm(x_s, a.D, ly.rms1, 1e-5f, s_red);
-        x_digitize(x_s, a.D, xd, xsc);
         const int tb = 1 + l * kMegaTraceLayer;
-        TRACE(tb + 0);
-        ok = consume_mat<ME_PART>(ly.qkv, xd, xsc, rg, s_part, s_res, a.pq, &s_best,
-                                  a.err);
-        TRACE(tb + 1);
-        ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
-        TRACE(tb + 2);
-        if (!ok) break;
-        // attention items (kv head, split), round-robin over CTAs
-        for (int it = b; it < a.KV * nvalid && ok; it += nct) {
-            long long* tr = (a.trace && it == b) ? a.trace + (size_t)b * kMegaTracePts + tb + 14 : nullptr;
-            const int kv_h = it / nvalid, sp = it - kv_h * nvalid;
-            ok = attn_item<MAXG, HD>(a, l, kv_h, sp, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
+        if ((p & 1) == 0) {
+            // QKV
+            if (l == 0) {
+                const int id = __ldcg(a.tokens + pos);
+                for (int i = tid; i < a.D; i += kMegaCW * 32) {
+                    float v;
+                    if (a.ef) {
+                        v = __ldg(a.ef + (size_t)id * a.D + i);
+                    } else {
+                        const int cb = i / kMegaCB, w = min(kMegaCB, a.D - cb * kMegaCB), c = i - cb * kMegaCB;
+                        const uint8_t* row = a.eqs + (size_t)cb * a.V * kMegaCB + (size_t)id * w;
+                        const int8_t q = (int8_t)row[16 * swz_chunk(c >> 4, id & 7, w >> 4) + (c & 15)];
+                        v = __fmul_rn((float)q, h2f(a.ed[(size_t)cb * a.V * (kMegaCB / 32) + mega_d_index(id, c / 32, w / 32)]));
+                    }
+                    x_s[i] = v;
+                    if (b == 0) a.X[i] = v;
+                }
+            } else {  // X = X after O + the previous down projection's partials
+                x_resid(x_s, a.Xb, a.pd, a.layers[l - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);
+            }
+            x_norm(x_s, a.D, ly.rms1, 1e-5f, s_red);
+            x_digitize(x_s, a.D, xd, xsc);
+            TRACE(tb + 0);
+            ok = consume_mat<ME_PART>(ly.qkv, xd, xsc, rg, s_part, s_res, a.pq, &s_best,
+                                      a.err);
+            TRACE(tb + 1);
+            ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
+            TRACE(tb + 2);
+            if (!ok) break;
+            // attention items (kv head, split), round-robin over CTAs
+            for (int it = b; it < a.KV * nvalid && ok; it += nct) {
+                long long* tr = (a.trace && it == b) ? a.trace + (size_t)b * kMegaTracePts + tb + 14 : nullptr;
+                const int kv_h = it / nvalid, sp = it - kv_h * nvalid;
+                ok = attn_item<MAXG, HD>(a, l, kv_h, sp, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
+            }
+            if (!ok) break;
+            TRACE(tb + 3);
+            ok = grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
+            TRACE(tb + 4);
+            if (!ok) break;
+            // O projection (partials; the residual add happens in the next reader)
+            x_load(x_s, a.attn, a.H * a.hd);  // merged attention rows
+            x_digitize(x_s, a.H * a.hd, xd, xsc);
+            TRACE(tb + 5);
+            ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err);
+            TRACE(tb + 6);
+            ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
+            TRACE(tb + 7);
+        } else {
+            // gate/up + SwiGLU on RMSNorm(X + O partials); CTA 0 keeps that X in Xb
+            x_resid(x_s, a.X, a.po, ly.o.spl, a.D, b == 0 ? a.Xb : nullptr);
+            x_norm(x_s, a.D, ly.rms2, 1e-5f, s_red);
+            x_digitize(x_s, a.D, xd, xsc);
+            TRACE(tb + 8);
+            ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, rg, s_part, s_res, a.h, &s_best,
+                                        a.err);
+            TRACE(tb + 9);
+            ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
+            TRACE(tb + 10);
+            if (!ok) break;
+            // down projection + residual
+            x_load(x_s, a.h, a.F);
+            x_digitize(x_s, a.F, xd, xsc);
+            TRACE(tb + 11);
+            ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best,
+                                      a.err);
+            TRACE(tb + 12);
+            ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
+            TRACE(tb + 13);
         }
-        if (!ok) break;
-        TRACE(tb + 3);
-        ok = grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
-        TRACE(tb + 4);
-        if (!ok) break;
-        // O projection (partials; the residual add happens in the next reader)
-        x_load(x_s, a.attn, a.H * a.hd);  // merged attention rows
-        x_digitize(x_s, a.H * a.hd, xd, xsc);
-        TRACE(tb + 5);
-        ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err);
-        TRACE(tb + 6);
-        ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
-        TRACE(tb + 7);
-        if (!ok) break;
-        // gate/up + SwiGLU on RMSNorm(X + O partials); CTA 0 keeps that X in Xb
-        x_resid(x_s, a.X, a.po, ly.o.spl, a.D, b == 0 ? a.Xb : nullptr);
-        x_norm(x_s, a.D, ly.rms2, 1e-5f, s_red);
-        x_digitize(x_s, a.D, xd, xsc);
-        TRACE(tb + 8);
-        ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, rg, s_part, s_res, a.h, &s_best,
-                                    a.err);
-        TRACE(tb + 9);
-        ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
-        TRACE(tb + 10);
-        if (!ok) break;
-        // down projection + residual
-        x_load(x_s, a.h, a.F);
-        x_digitize(x_s, a.F, xd, xsc);
-        TRACE(tb + 11);
-        ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best,
-                                  a.err);
-        TRACE(tb + 12);
-        ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
-        TRACE(tb + 13);
     }
     if (!ok) return;
+    if (a.win1 <= 2 * a.L) {  // window without the head: hand the barrier epoch on
+        if (b == 0 && tid == 0) st->bar_base = base + (unsigned int)bi * nct;
+        return;
+    }
     // LM head + argmax
     const int th = 1 + a.L * kMegaTraceLayer;
     x_resid(x_s, a.Xb, a.pd, a.layers[a.L - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);  // final X kept in X

@@ -85,6 +85,7 @@ struct MegaArgs {
     int kmax;                 // largest GEMV input length (x / digit buffers)
     int xs_bytes;             // shared bytes of the x / digits / attention union
     int nslots;               // ring depth
+    int win0, win1;           // phases of this launch: [win0, win1) of 2 l + h (h 0: QKV..O, 1: gate/up..down), 2 L = head
     long long* trace;         // optional: SM clock at each phase boundary, [CTA][kMegaTracePts]
 };
 

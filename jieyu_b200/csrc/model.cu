@@ -310,6 +310,8 @@ int setup_mega(jyc_model* m) {
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
     const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
     a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
+    a.win0 = 0;
+    a.win1 = 2 * m->L + 1;  // the whole step
     if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode
     const int smem = mega_smem_bytes(a);
     TRY(prepare_mega_kernel(smem, m->H / m->KV, m->hd));
@@ -784,6 +786,41 @@ JYC_API int jyc_decode_device(jyc_model* m, int n_steps, void* stream) {
 JYC_API int jyc_model_kernels_per_step(const jyc_model* m) { return m ? kernels_per_step(m) : 0; }
 
 JYC_API int jyc_model_decode_path(const jyc_model* m) { return m ? (m->mega ? 2 : 0) : -1; }
+
+JYC_API int jyc_model_decode_window(jyc_model* m, int first, int last, void* stream) {
+    clear_error();
+    if (!m) return arg_error("decode_window: null model");
+    if (!m->mega) {
+        set_error("decode_window: the model does not use the decode kernel");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    if (first < 0 || last <= first || last > 2 * m->L + 1) return arg_error("decode_window: bad phase range");
+    MegaArgs a = m->margs;
+    a.win0 = first;
+    a.win1 = last;
+    return launch_mega_step(a, static_cast<cudaStream_t>(stream));
+}
+
+JYC_API int jyc_model_partials(jyc_model* m, float** o_part, int* o_count, float** d_part, int* d_count) {
+    clear_error();
+    if (!m || !o_part || !o_count || !d_part || !d_count) return arg_error("model_partials: bad arguments");
+    if (!m->mega) {
+        set_error("model_partials: the model does not use the decode kernel");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    int so = 1, sd = 1;
+    std::vector<MegaLayer> ml(m->L);
+    JYC_CUDA(cudaMemcpy(ml.data(), m->d_mlayers, sizeof(MegaLayer) * m->L, cudaMemcpyDeviceToHost));
+    for (const MegaLayer& x : ml) {
+        so = std::max(so, x.o.spl);
+        sd = std::max(sd, x.dn.spl);
+    }
+    *o_part = m->margs.po;
+    *o_count = so * m->D;
+    *d_part = m->margs.pd;
+    *d_count = sd * m->D;
+    return JYC_OK;
+}
 
 JYC_API int jyc_model_trace_points(const jyc_model* m) {
     if (!m || !m->mega) return 0;
