@@ -336,6 +336,107 @@ def run_b200(args):
     return 0
 
 
+def run_tp(args):
+    """configs[3] (Llama-3-8B shape) batch-1 decode at context 4096,
+    tensor-parallel over the launched ranks (jieyu_b200.tp); N=1 runs the
+    whole model with the single-launch decode kernel. Not the driver's
+    headline line: `python bench.py --workload c3-tp` (under torchrun for N>1)."""
+    import numpy as np
+    import torch
+
+    from jieyu_b200 import _capi
+    from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids
+    from jieyu_b200.tp import TPDecoder
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    cfg = CONFIGS["c3"]
+    ctx = 4096
+    new = 64
+    hw = HostWeights.synthetic(cfg)
+    prompt = prompt_ids(cfg, n=ctx)
+    lib = _capi.load()
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    if world == 1:
+        m = DeviceModel(hw)
+        stream = torch.cuda.Stream()
+        s = stream.cuda_stream
+        ids = torch.from_numpy(prompt).cuda()
+        with torch.cuda.stream(stream):
+            m.prefill_device(ids.data_ptr(), ctx, s)
+            def step():
+                m.rewind(ctx + 1, s)
+                m.decode_device(new, s)
+            for _ in range(args.warmup):
+                step()
+            e0, e1 = ev(), ev()
+            e0.record(stream)
+            for _ in range(args.steps):
+                step()
+            e1.record(stream)
+            stream.synchronize()
+        ms = e0.elapsed_time(e1)
+        graphed = True
+        close = m.close
+        h = m.h
+    else:
+        tp = TPDecoder(hw, rank, world)
+        graphed = tp.capture()
+        tp.prefill_by_steps(prompt)
+        stream = tp.stream
+        s = stream.cuda_stream
+        def step():
+            _capi.check(lib.jyc_model_rewind(tp.m.h, ctx + 1, s))
+            tp.step(new)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+            stream.synchronize()
+            dist.barrier()
+            e0, e1 = ev(), ev()
+            e0.record(stream)
+            for _ in range(args.steps):
+                step()
+            e1.record(stream)
+            stream.synchronize()
+        ms = e0.elapsed_time(e1)
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        close = tp.close
+        h = tp.m.h
+    ms_tok = ms / (args.steps * new)
+    w_rank = float(lib.jyc_model_weight_bytes_per_token(h))
+    kv_rank = float(lib.jyc_model_kv_bytes_per_token(h, ctx + new // 2))
+    peak, peak_kind = measured_peaks()
+    gbs = (w_rank + kv_rank) / (ms_tok / 1e3) / 1e9
+    close()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "batch-1 decode tok/s (configs[3], tensor parallel)", "value": 1e3 / ms_tok, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_token": ms_tok,
+        "higher_is_better": True, "scaling": "strong", "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"configs[3] Llama-3-8B shape, Q8_0, context {ctx}, {new} greedy tokens per step",
+                   "parallelism": f"tp{world}" if world > 1 else "single GPU", "graphed": graphed},
+        "hbm_per_gpu": {"bytes_per_token": w_rank + kv_rank, "gbs": gbs, "frac_of_peak": gbs / peak,
+                        "peak_gbs": peak, "peak_kind": peak_kind},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -343,11 +444,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp"],
+                    help="c1: the headline decode line (default); c3-tp: configs[3] tensor parallel")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "c3-tp":
+        return run_tp(args)
     return run_b200(args)
 
 
