@@ -389,7 +389,7 @@ def run_tp(args):
         close = m.close
         h = m.h
     else:
-        tp = TPDecoder(hw, rank, world)
+        tp = TPDecoder(hw, rank, world, mode=args.tp_mode)
         graphed = tp.capture()
         tp.prefill_by_steps(prompt)
         stream = tp.stream
@@ -429,7 +429,8 @@ def run_tp(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_token": ms_tok,
         "higher_is_better": True, "scaling": "strong", "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"configs[3] Llama-3-8B shape, Q8_0, context {ctx}, {new} greedy tokens per step",
-                   "parallelism": f"tp{world}" if world > 1 else "single GPU", "graphed": graphed},
+                   "parallelism": f"tp{world}" if world > 1 else "single GPU", "graphed": graphed,
+                   "tp_mode": args.tp_mode if world > 1 else None},
         "hbm_per_gpu": {"bytes_per_token": w_rank + kv_rank, "gbs": gbs, "frac_of_peak": gbs / peak,
                         "peak_gbs": peak, "peak_kind": peak_kind},
     }
@@ -446,6 +447,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp"],
                     help="c1: the headline decode line (default); c3-tp: configs[3] tensor parallel")
+    ap.add_argument("--tp-mode", default="kernel", choices=["kernel", "nccl"],
+                    help="c3-tp: in-kernel NVLink exchange (default) or NCCL between kernel windows")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -261,6 +261,15 @@ JYC_API int jyc_model_decode_path(const jyc_model* m);
  * that the caller all-reduces (sum over ranks) between windows; the next
  * window adds them into the residual stream. */
 JYC_API int jyc_model_decode_window(jyc_model* m, int first, int last, void* stream);
+/* Tensor parallel inside the decode kernel (no NCCL in the token loop): each
+ * rank opens a receive area (jyc_model_tp_open returns its 64-byte CUDA IPC
+ * handle), the callers exchange the handles (all-gather in rank order) and
+ * connect (jyc_model_tp_connect maps every peer's area over NVLink). From
+ * then on every decode step on every rank stores its O and down partial rows
+ * into all ranks' areas and waits (bounded, error word 8) for all ranks'
+ * arrivals: the ranks must step together, on one node, one GPU each. */
+JYC_API int jyc_model_tp_open(jyc_model* m, int size, int rank, void* handle_out);
+JYC_API int jyc_model_tp_connect(jyc_model* m, const void* handles);
 JYC_API int jyc_model_partials(jyc_model* m, float** o_part, int* o_count, float** d_part, int* d_count);
 
 /* Error word of the device kernels: non-zero if a bounded wait gave up

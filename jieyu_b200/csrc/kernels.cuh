@@ -28,6 +28,7 @@ struct DevState {
     unsigned long long amax;   // argmax slot (argmax_pack)
     unsigned int head_arrive;  // last-arriver counter of the LM-head grid
     unsigned int bar_base;     // grid-barrier counter value at the start of the next step
+    unsigned int xbase;        // tensor-parallel exchanges of each kind completed (O / down, per step L each)
 };
 
 // Where a kernel finds its first position: from the step state (decode graph,

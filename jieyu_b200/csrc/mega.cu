@@ -50,7 +50,7 @@ constexpr int kMegaThreads = (kMegaCW + 1) * 32;  // consumer warps + one copy-i
 
 // Error word of the device kernels (non-zero: a bounded wait gave up; the
 // value tells which: 3 ring slot free, 4 ring slot full, 5 grid barrier,
-// 6 attention K/V copy, 7 prefill digit copy).
+// 6 attention K/V copy, 7 prefill digit copy, 8 tensor-parallel exchange).
 __device__ int g_err_word;
 
 int* device_error_word() {
@@ -294,9 +294,18 @@ static __device__ __forceinline__ float d_hi(uint32_t w) { return __int_as_float
 // 2^14 a + 2^7 b on tq=0 and c on tq=1; the two meet once per row tile.
 // Accumulators carry a 2^-28 factor (scale products stay normal for block
 // maxima down to 2^-54 and finite up to 2^57), removed at the end.
+// Peer stores of partial rows (tensor parallel): row values of column group kg
+// also go to dst[q][off + kg * n + row] for every rank q < n_dst.
+struct PeerPush {
+    float* const* dst;
+    int n_dst;
+    size_t off;
+};
+
 template <int EPI>
 static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, Ring& rg_, float* s_part,
-                                   float* s_res, float* y, unsigned long long* s_best, int* err) {
+                                   float* s_res, float* y, unsigned long long* s_best, int* err,
+                                   PeerPush push = PeerPush{nullptr, 0, 0}) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int g = lane >> 2, tq = lane & 3;
     const float s1 = tq == 0 ? 128.0f : 1.0f;
@@ -393,7 +402,11 @@ static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_
             }
             if (lane == 0 && best) atomicMax(s_best, best);
         } else {
-            for (int e = tid; e < rows; e += kMegaCW * 32) y[(size_t)R.kg * M.n + r0 + e] = s_res[e];
+            for (int e = tid; e < rows; e += kMegaCW * 32) {
+                const size_t o = (size_t)R.kg * M.n + r0 + e;
+                y[o] = s_res[e];
+                for (int q = 0; q < push.n_dst; q++) push.dst[q][push.off + o] = s_res[e];
+            }
         }
         csync();
     }
@@ -495,6 +508,49 @@ static __device__ void x_digitize(const float* x_s, int k, int8_t* xd, float* xs
         if (sub == 0) xsc[blk] = __fmul_rn(amax, 1.0f / 1048576.0f);  // exact: power of two
     }
     csync();
+}
+
+// Tensor parallel: after this CTA's partial rows went to every rank, make
+// them visible system-wide and count this CTA in every rank's counter for
+// this sender (slot kind * tp + tp_rank).
+static __device__ void xchg_arrive(const MegaArgs& a, int kind) {
+    csync();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int q = 0; q < a.tp; q++) atomicAdd_system(a.peer_xflag[q] + kind * a.tp + a.tp_rank, 1u);
+    }
+}
+
+static __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait (bounded) until every rank's CTAs delivered exchange number `target`
+// (counts nct per exchange) of this kind; error word 8 on a timeout.
+static __device__ bool xchg_wait(const MegaArgs& a, int kind, unsigned int target, int* s_ok) {
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const long long t0 = clock64();
+        for (int q = 0; q < a.tp && ok; q++) {
+            const unsigned int* f = a.xflag + kind * a.tp + q;
+            while ((int)(ld_acquire_sys(f) - target) < 0) {
+                if (clock64() - t0 > (1LL << 31)) {
+                    atomicExch(a.err, 8);
+                    ok = 0;
+                    break;
+                }
+                if (*(volatile int*)a.err != 0) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        *s_ok = ok;
+    }
+    csync();
+    return *s_ok != 0;
 }
 
 // Grid barrier over the consumer threads of every CTA (bounded spin).
@@ -908,8 +964,9 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
 }
 
 // One instantiation per attention shape (query heads per kv head <= MAXG,
-// head_dim HD): each kernel carries a single attention variant.
-template <int MAXG, int HD>
+// head_dim HD) and per exchange mode (TP: in-kernel tensor-parallel
+// exchange): each kernel carries only the code its model runs.
+template <int MAXG, int HD, bool TP>
 __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) {
     extern __shared__ __align__(128) unsigned char sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
@@ -968,6 +1025,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     }
     const int pos = (*(volatile const int*)&st->len) - 1;
     const unsigned int base = *(volatile const unsigned int*)&st->bar_base;
+    const unsigned int xb = *(volatile const unsigned int*)&st->xbase;  // tensor-parallel exchange epoch
     const unsigned int nct = gridDim.x;
     int bi = 0;
     uint32_t aph = 0;  // parity of abar's current phase
@@ -1003,7 +1061,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                     if (b == 0) a.X[i] = v;
                 }
             } else {  // X = X after O + the previous down projection's partials
-                x_resid(x_s, a.Xb, a.pd, a.layers[l - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);
+                if (TP) {  // every rank's down partials of layer l-1, in rank order
+                    ok = xchg_wait(a, 1, nct * (xb + (unsigned int)l), &s_ok);
+                    if (!ok) break;
+                    x_resid(x_s, a.Xb, a.xdn, a.tp * a.layers[l - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);
+                } else {
+                    x_resid(x_s, a.Xb, a.pd, a.layers[l - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);
+                }
             }
             x_norm(x_s, a.D, ly.rms1, 1e-5f, s_red);
             x_digitize(x_s, a.D, xd, xsc);
@@ -1029,13 +1093,25 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             x_load(x_s, a.attn, a.H * a.hd);  // merged attention rows
             x_digitize(x_s, a.H * a.hd, xd, xsc);
             TRACE(tb + 5);
-            ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err);
+            if (TP) {
+                ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err,
+                                          PeerPush{a.peer_xo, a.tp, (size_t)a.tp_rank * a.xo_stride});
+                if (ok) xchg_arrive(a, 0);
+            } else {
+                ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err);
+            }
             TRACE(tb + 6);
             ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
             TRACE(tb + 7);
         } else {
             // gate/up + SwiGLU on RMSNorm(X + O partials); CTA 0 keeps that X in Xb
-            x_resid(x_s, a.X, a.po, ly.o.spl, a.D, b == 0 ? a.Xb : nullptr);
+            if (TP) {  // every rank's O partials of layer l, in rank order
+                ok = xchg_wait(a, 0, nct * (xb + (unsigned int)l + 1), &s_ok);
+                if (!ok) break;
+                x_resid(x_s, a.X, a.xo, a.tp * ly.o.spl, a.D, b == 0 ? a.Xb : nullptr);
+            } else {
+                x_resid(x_s, a.X, a.po, ly.o.spl, a.D, b == 0 ? a.Xb : nullptr);
+            }
             x_norm(x_s, a.D, ly.rms2, 1e-5f, s_red);
             x_digitize(x_s, a.D, xd, xsc);
             TRACE(tb + 8);
@@ -1049,8 +1125,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             x_load(x_s, a.h, a.F);
             x_digitize(x_s, a.F, xd, xsc);
             TRACE(tb + 11);
-            ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best,
-                                      a.err);
+            if (TP) {
+                ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best, a.err,
+                                          PeerPush{a.peer_xdn, a.tp, (size_t)a.tp_rank * a.xdn_stride});
+                if (ok) xchg_arrive(a, 1);
+            } else {
+                ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best, a.err);
+            }
             TRACE(tb + 12);
             ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
             TRACE(tb + 13);
@@ -1063,7 +1144,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     }
     // LM head + argmax
     const int th = 1 + a.L * kMegaTraceLayer;
-    x_resid(x_s, a.Xb, a.pd, a.layers[a.L - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);  // final X kept in X
+    if (TP) {
+        if (!xchg_wait(a, 1, nct * (xb + (unsigned int)a.L), &s_ok)) return;
+        x_resid(x_s, a.Xb, a.xdn, a.tp * a.layers[a.L - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);  // final X
+    } else {
+        x_resid(x_s, a.Xb, a.pd, a.layers[a.L - 1].dn.spl, a.D, b == 0 ? a.X : nullptr);  // final X kept in X
+    }
     if (tid == 0) s_best = 0ull;
     x_norm(x_s, a.D, a.final_norm, 1e-5f, s_red);
     x_digitize(x_s, a.D, xd, xsc);
@@ -1088,6 +1174,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         st->steps = nsteps;
         st->amax = 0ull;
         st->bar_base = base + (unsigned int)bi * nct;
+        if (TP) st->xbase = xb + (unsigned int)a.L;
         if (stop) st->active = 0;
         __threadfence();
     }
@@ -1157,20 +1244,32 @@ int mega_attn_sub(int kmax, int G, int hd, int chunk) {
 
 int mega_smem_bytes(const MegaArgs& a) { return 128 + a.xs_bytes + a.nslots * kMegaSlotBytes; }
 
-// the kernel instantiation of a model's attention shape
-static const void* mega_kernel_for(int G, int hd) {
-    if (hd == 64) return G <= 4 ? (const void*)mega_step_kernel<4, 64> : (const void*)mega_step_kernel<8, 64>;
-    return G <= 4 ? (const void*)mega_step_kernel<4, 128> : (const void*)mega_step_kernel<8, 128>;
+// the kernel instantiation of a model's attention shape and exchange mode
+static const void* mega_kernel_for(int G, int hd, bool tp) {
+    if (tp) {
+        if (hd == 64)
+            return G <= 4 ? (const void*)mega_step_kernel<4, 64, true> : (const void*)mega_step_kernel<8, 64, true>;
+        return G <= 4 ? (const void*)mega_step_kernel<4, 128, true> : (const void*)mega_step_kernel<8, 128, true>;
+    }
+    if (hd == 64)
+        return G <= 4 ? (const void*)mega_step_kernel<4, 64, false> : (const void*)mega_step_kernel<8, 64, false>;
+    return G <= 4 ? (const void*)mega_step_kernel<4, 128, false> : (const void*)mega_step_kernel<8, 128, false>;
 }
 
 int mega_static_smem(int G, int hd) {
-    cudaFuncAttributes fa{};
-    if (cudaFuncGetAttributes(&fa, mega_kernel_for(G, hd)) != cudaSuccess) return -1;
-    return (int)fa.sharedSizeBytes;
+    int mx = 0;
+    for (int tp = 0; tp < 2; tp++) {
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, mega_kernel_for(G, hd, tp != 0)) != cudaSuccess) return -1;
+        mx = std::max(mx, (int)fa.sharedSizeBytes);
+    }
+    return mx;
 }
 
 int prepare_mega_kernel(int smem, int G, int hd) {
-    JYC_CUDA(cudaFuncSetAttribute(mega_kernel_for(G, hd), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    for (int tp = 0; tp < 2; tp++)
+        JYC_CUDA(cudaFuncSetAttribute(mega_kernel_for(G, hd, tp != 0), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      smem));
     return JYC_OK;
 }
 
@@ -1186,7 +1285,7 @@ int launch_mega_step(const MegaArgs& a, cudaStream_t s) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     void* args[] = {const_cast<MegaArgs*>(&a)};
-    cudaError_t e = cudaLaunchKernelExC(&cfg, mega_kernel_for(a.H / a.KV, a.hd), args);
+    cudaError_t e = cudaLaunchKernelExC(&cfg, mega_kernel_for(a.H / a.KV, a.hd, a.tp > 1), args);
     if (e != cudaSuccess) return cuda_fail(e, "mega_step launch");
     count_launch();
     return JYC_OK;

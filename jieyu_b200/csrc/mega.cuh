@@ -18,6 +18,7 @@ namespace jyc {
 constexpr int kMegaCB = 512;
 constexpr int kMegaRT = 48;       // rows per tile (multiple of 16)
 constexpr int kMegaMaxSlots = 6;  // ring depth upper bound
+constexpr int kMegaMaxTP = 8;       // most tensor-parallel ranks of the in-kernel exchange
 constexpr int kMegaCW = 16;       // consumer warps (each takes 512 / 32 / kMegaCW column blocks of a tile)
 constexpr int kMegaSlotBytes = kMegaRT * kMegaCB + kMegaRT * (kMegaCB / 32) * 2;
 
@@ -87,6 +88,17 @@ struct MegaArgs {
     int nslots;               // ring depth
     int win0, win1;           // phases of this launch: [win0, win1) of 2 l + h (h 0: QKV..O, 1: gate/up..down), 2 L = head
     long long* trace;         // optional: SM clock at each phase boundary, [CTA][kMegaTracePts]
+    // tensor parallel inside the kernel (tp > 1): every CTA stores its O / down
+    // partial rows into every rank's receive area (peer stores over NVLink) and
+    // bumps that rank's arrival counter for it; readers wait for all counters
+    int tp, tp_rank;
+    float* xo;                       // this rank's receive area of O partials [tp][o.spl][D]
+    float* xdn;                      // ... of down partials [tp][dn.spl][D]
+    unsigned int* xflag;             // [2][tp] arrival counters (O, down) per sender
+    int xo_stride, xdn_stride;       // floats per sender slot (spl * D)
+    float* peer_xo[kMegaMaxTP];      // every rank's xo (own included), mapped into this process
+    float* peer_xdn[kMegaMaxTP];
+    unsigned int* peer_xflag[kMegaMaxTP];
 };
 
 // Phase boundaries recorded per CTA when tracing: per layer 14 phase points

@@ -98,6 +98,11 @@ struct jyc_model {
     bool mega = false;
     MegaArgs margs{};
     int pf_rows = 0;           // tokens per batched prefill pass (0: generic prefill)
+    // tensor parallel inside the decode kernel: this rank's receive area and
+    // the peers' areas mapped through CUDA IPC
+    unsigned char* tp_region = nullptr;
+    int tp_size = 0, tp_rank = 0, tp_so = 1, tp_sd = 1;
+    std::vector<void*> tp_mapped;
     int8_t* pf_dig = nullptr;  // token digit planes of the batched prefill
     float* pf_sx = nullptr;
     MegaLayer* d_mlayers = nullptr;
@@ -125,6 +130,7 @@ struct jyc_model {
         return JYC_OK;
     }
     ~jyc_model() {
+        for (void* p : tp_mapped) cudaIpcCloseMemHandle(p);
         if (step_exec) cudaGraphExecDestroy(step_exec);
         if (prof_exec) cudaGraphExecDestroy(prof_exec);
         prof_marks.reset();
@@ -799,6 +805,68 @@ JYC_API int jyc_model_decode_window(jyc_model* m, int first, int last, void* str
     a.win0 = first;
     a.win1 = last;
     return launch_mega_step(a, static_cast<cudaStream_t>(stream));
+}
+
+JYC_API int jyc_model_tp_open(jyc_model* m, int size, int rank, void* handle_out) {
+    clear_error();
+    if (!m || !handle_out || size < 2 || size > kMegaMaxTP || rank < 0 || rank >= size)
+        return arg_error("tp_open: bad arguments (2 <= size <= 8, 0 <= rank < size)");
+    if (!m->mega) {
+        set_error("tp_open: the model does not use the decode kernel");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    if (m->tp_region) return arg_error("tp_open: already open");
+    std::vector<MegaLayer> ml(m->L);
+    JYC_CUDA(cudaMemcpy(ml.data(), m->d_mlayers, sizeof(MegaLayer) * m->L, cudaMemcpyDeviceToHost));
+    for (const MegaLayer& x : ml) {
+        m->tp_so = std::max(m->tp_so, x.o.spl);
+        m->tp_sd = std::max(m->tp_sd, x.dn.spl);
+    }
+    for (const MegaLayer& x : ml)  // readers take the senders' groups as one contiguous list
+        if (x.o.spl != m->tp_so || x.dn.spl != m->tp_sd) {
+            set_error("tp_open: layers with different split plans are not supported");
+            return JYC_ERR_UNSUPPORTED;
+        }
+    const size_t floats = (size_t)size * (m->tp_so + m->tp_sd) * m->D;
+    const size_t bytes = floats * 4 + (size_t)2 * size * sizeof(unsigned int);
+    TRY(m->alloc(&m->tp_region, bytes));
+    JYC_CUDA(cudaMemset(m->tp_region, 0, bytes));
+    JYC_CUDA(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), m->tp_region));
+    m->tp_size = size;
+    m->tp_rank = rank;
+    return JYC_OK;
+}
+
+JYC_API int jyc_model_tp_connect(jyc_model* m, const void* handles) {
+    clear_error();
+    if (!m || !handles || !m->tp_region) return arg_error("tp_connect: call tp_open first");
+    MegaArgs& a = m->margs;
+    const int t = m->tp_size;
+    const size_t xo_f = (size_t)t * m->tp_so * m->D, xd_f = (size_t)t * m->tp_sd * m->D;
+    for (int q = 0; q < t; q++) {
+        unsigned char* base = m->tp_region;
+        if (q != m->tp_rank) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const unsigned char*>(handles) + (size_t)q * sizeof(h), sizeof(h));
+            void* p = nullptr;
+            JYC_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+            m->tp_mapped.push_back(p);
+            base = static_cast<unsigned char*>(p);
+        }
+        float* f = reinterpret_cast<float*>(base);
+        a.peer_xo[q] = f;
+        a.peer_xdn[q] = f + xo_f;
+        a.peer_xflag[q] = reinterpret_cast<unsigned int*>(f + xo_f + xd_f);
+    }
+    float* own = reinterpret_cast<float*>(m->tp_region);
+    a.xo = own;
+    a.xdn = own + xo_f;
+    a.xflag = reinterpret_cast<unsigned int*>(own + xo_f + xd_f);
+    a.xo_stride = m->tp_so * m->D;
+    a.xdn_stride = m->tp_sd * m->D;
+    a.tp = t;
+    a.tp_rank = m->tp_rank;
+    return JYC_OK;
 }
 
 JYC_API int jyc_model_partials(jyc_model* m, float** o_part, int* o_count, float** d_part, int* d_count) {

@@ -9,10 +9,13 @@ rank. A rank's shard is an ordinary smaller model for the C ABI; the only
 cross-rank step is the sum of the O and down projections' partial outputs,
 two all-reduces of [hidden] per layer.
 
-A decode token is one CUDA graph: per layer the decode kernel's window
-[2l, 2l+1) (QKV, attention, O partials), all-reduce(O partials), window
-[2l+1, 2l+2) (gate/up, down partials), all-reduce(down partials); then the LM
-head window. The residual stream stays identical on every rank (same sums in
+A decode token is one launch of the decode kernel per rank: after its O and
+down projections every CTA stores its partial rows into every rank's receive
+area (peer stores over NVLink into CUDA-IPC-mapped memory) and counts itself
+in that rank's arrival counter; the next phase waits (bounded) for all
+ranks and adds their partials in rank order. (The "nccl" mode instead runs
+half-layer windows of the kernel with NCCL all-reduces between them, in one
+CUDA graph.) The residual stream stays identical on every rank (same sums in
 the same order), so every rank emits the same token.
 
 The reference (libs/model_libs/transformer_layer.h:10-90) runs the same math
@@ -92,26 +95,41 @@ class _DevBuf:
 
 
 class TPDecoder:
-    """One rank of a tensor-parallel decode (call collectively on every rank)."""
+    """One rank of a tensor-parallel decode (call collectively on every rank).
 
-    def __init__(self, hw_full: HostWeights, rank: int, size: int, group=None):
+    mode "kernel" (default): one decode-kernel launch per token; the kernel
+    exchanges the O and down partials with the other ranks itself (peer
+    stores over NVLink into CUDA-IPC-mapped receive areas, bounded waits).
+    mode "nccl": half-layer windows of the decode kernel with NCCL
+    all-reduces of the partials between them, captured in a CUDA graph."""
+
+    def __init__(self, hw_full: HostWeights, rank: int, size: int, group=None, mode: str = "kernel"):
         import torch
         import torch.distributed as dist
 
         self.torch, self.dist, self.group = torch, dist, group
-        self.rank, self.size = rank, size
+        self.rank, self.size, self.mode = rank, size, mode
         self.cfg = hw_full.cfg
         self.shard = shard_weights(hw_full, rank, size)
         self.m = DeviceModel(self.shard)
         self.lib = _capi.load()
         if self.lib.jyc_model_decode_path(self.m.h) != 2:
             raise RuntimeError("tensor-parallel decode needs the decode kernel (Q8_0 tiled layout)")
+        self.stream = torch.cuda.Stream()
+        self.graph = None
+        if mode == "kernel":
+            handle = (C.c_ubyte * 64)()
+            check(self.lib.jyc_model_tp_open(self.m.h, size, rank, handle))
+            handles = [None] * size
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            allh = (C.c_ubyte * (64 * size)).from_buffer_copy(b"".join(handles))
+            check(self.lib.jyc_model_tp_connect(self.m.h, allh))
+            dist.barrier(group=group)
+            return
         po, npo, pd, npd = C.c_void_p(), C.c_int(), C.c_void_p(), C.c_int()
         check(self.lib.jyc_model_partials(self.m.h, C.byref(po), C.byref(npo), C.byref(pd), C.byref(npd)))
         self.po = torch.as_tensor(_DevBuf(po.value, npo.value), device="cuda")
         self.pd = torch.as_tensor(_DevBuf(pd.value, npd.value), device="cuda")
-        self.stream = torch.cuda.Stream()
-        self.graph = None
 
     def _window(self, first: int, last: int) -> None:
         check(self.lib.jyc_model_decode_window(self.m.h, first, last, self.stream.cuda_stream))
@@ -126,9 +144,12 @@ class TPDecoder:
         self._window(2 * L, 2 * L + 1)
 
     def capture(self) -> bool:
-        """Records one token step (kernels + all-reduces) into a CUDA graph;
-        False (and eager steps) if the capture is refused."""
+        """nccl mode: records one token step (kernels + all-reduces) into a
+        CUDA graph; False (and eager steps) if the capture is refused or in
+        kernel mode (one launch per token needs no graph)."""
         torch = self.torch
+        if self.mode == "kernel":
+            return False
         with torch.cuda.stream(self.stream):
             self._step()  # warm-up outside capture (NCCL communicator setup)
         self.stream.synchronize()
@@ -143,8 +164,11 @@ class TPDecoder:
         return True
 
     def step(self, n: int = 1) -> None:
-        """n decode tokens (graph replays when captured) on self.stream."""
+        """n decode tokens on self.stream."""
         torch = self.torch
+        if self.mode == "kernel":
+            check(self.lib.jyc_decode_device(self.m.h, n, self.stream.cuda_stream))
+            return
         with torch.cuda.stream(self.stream):
             for _ in range(n):
                 if self.graph is not None:

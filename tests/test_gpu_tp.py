@@ -1,5 +1,6 @@
 """Tensor-parallel decode on 2 GPUs (skipped with fewer): the sharded
-decode's greedy tokens equal the single-GPU decode's (tests/tp_worker.py)."""
+decode's greedy tokens equal the single-GPU decode's (tests/tp_worker.py),
+with the in-kernel NVLink exchange and with NCCL between kernel windows."""
 import os
 import socket
 import subprocess
@@ -17,11 +18,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_tp2_decode_matches_single_gpu(cuda):
+@pytest.mark.parametrize("mode", ["kernel", "nccl"])
+def test_tp2_decode_matches_single_gpu(cuda, mode):
     torch = cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", JIEYU_TP_MODE=mode)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(HERE, "tp_worker.py")]

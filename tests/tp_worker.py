@@ -33,7 +33,8 @@ def main() -> int:
     hw = HostWeights.synthetic(cfg)
     prompt = prompt_ids(cfg, n=8)
     new = 16
-    tp = TPDecoder(hw, rank, world)
+    mode = os.environ.get("JIEYU_TP_MODE", "kernel")
+    tp = TPDecoder(hw, rank, world, mode=mode)
     graphed = tp.capture()
     tp.prefill_by_steps(prompt)      # KV of the prompt + the first new token
     torch.cuda.synchronize()
@@ -46,7 +47,7 @@ def main() -> int:
     tp.close()
     dist.barrier()
     ok = True
-    res = {"world": world, "graphed": graphed, "tp_ms_per_token": dt * 1e3 / (new - 1)}
+    res = {"world": world, "mode": mode, "graphed": graphed, "tp_ms_per_token": dt * 1e3 / (new - 1)}
     if rank == 0:
         ref = DeviceModel(hw).generate(prompt, new)
         res["tp"] = [int(x) for x in got]
