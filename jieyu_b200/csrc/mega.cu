@@ -1101,7 +1101,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                 ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err);
             }
             TRACE(tb + 6);
-            ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
+            // (tensor parallel: the readers' wait on every rank's arrival counts
+            // this rank's CTAs too, which stands in for the grid barrier)
+            if (!TP) ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
             TRACE(tb + 7);
         } else {
             // gate/up + SwiGLU on RMSNorm(X + O partials); CTA 0 keeps that X in Xb
@@ -1133,7 +1135,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                 ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best, a.err);
             }
             TRACE(tb + 12);
-            ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
+            if (!TP) ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
             TRACE(tb + 13);
         }
     }
