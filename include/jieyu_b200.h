@@ -84,6 +84,11 @@ typedef struct jyc_model_desc {
     int num_kv_heads;
     int head_dim;
     int intermediate;
+    /* Vocabulary-sharded LM head (tensor parallel; 0/0 otherwise): the
+     * embedding has embed_rows rows (0: vocab_size) and the head's row i is
+     * token vocab_offset + i. */
+    int embed_rows;
+    int vocab_offset;
 } jyc_model_desc;
 
 /* Token callback, same contract as `token_cb` (libs/model_libs/generate.h:8):

@@ -63,6 +63,8 @@ class ModelDesc(C.Structure):
         ("num_kv_heads", C.c_int),
         ("head_dim", C.c_int),
         ("intermediate", C.c_int),
+        ("embed_rows", C.c_int),
+        ("vocab_offset", C.c_int),
     ]
 
 

@@ -305,7 +305,7 @@ struct PeerPush {
 template <int EPI>
 static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, Ring& rg_, float* s_part,
                                    float* s_res, float* y, unsigned long long* s_best, int* err,
-                                   PeerPush push = PeerPush{nullptr, 0, 0}) {
+                                   PeerPush push = PeerPush{nullptr, 0, 0}, int idx_off = 0) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int g = lane >> 2, tq = lane & 3;
     const float s1 = tq == 0 ? 128.0f : 1.0f;
@@ -392,7 +392,7 @@ static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_
             unsigned long long best = 0ull;
             for (int e = tid; e < rows; e += kMegaCW * 32) {
                 y[r0 + e] = s_res[e];
-                const unsigned long long p = argmax_pack(s_res[e], r0 + e);
+                const unsigned long long p = argmax_pack(s_res[e], idx_off + r0 + e);
                 best = p > best ? p : best;
             }
 #pragma unroll
@@ -1053,9 +1053,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                         v = __ldg(a.ef + (size_t)id * a.D + i);
                     } else {
                         const int cb = i / kMegaCB, w = min(kMegaCB, a.D - cb * kMegaCB), c = i - cb * kMegaCB;
-                        const uint8_t* row = a.eqs + (size_t)cb * a.V * kMegaCB + (size_t)id * w;
+                        const uint8_t* row = a.eqs + (size_t)cb * a.Ve * kMegaCB + (size_t)id * w;
                         const int8_t q = (int8_t)row[16 * swz_chunk(c >> 4, id & 7, w >> 4) + (c & 15)];
-                        v = __fmul_rn((float)q, h2f(a.ed[(size_t)cb * a.V * (kMegaCB / 32) + mega_d_index(id, c / 32, w / 32)]));
+                        v = __fmul_rn((float)q, h2f(a.ed[(size_t)cb * a.Ve * (kMegaCB / 32) + mega_d_index(id, c / 32, w / 32)]));
                     }
                     x_s[i] = v;
                     if (b == 0) a.X[i] = v;
@@ -1157,14 +1157,31 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     x_digitize(x_s, a.D, xd, xsc);
     TRACE(th + 0);
     if (!consume_mat<ME_ARGMAX>(*a.head_dev, xd, xsc, rg, s_part, s_res, a.logits, &s_best,
-                                a.err))
+                                a.err, PeerPush{nullptr, 0, 0}, a.vocab_off))
         return;
     TRACE(th + 1);
     if (tid == 0 && s_best) atomicMax(&st->amax, s_best);
     if (!grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok)) return;
     TRACE(th + 2);
     if (b == 0 && tid == 0) {
-        const unsigned long long packed = atomicAdd(&st->amax, 0ull);
+        unsigned long long packed = atomicAdd(&st->amax, 0ull);
+        if (TP) {  // every rank's argmax of its vocabulary slice -> the largest
+            for (int q = 0; q < a.tp; q++) a.peer_xam[q][a.tp_rank] = packed;
+            __threadfence_system();
+            for (int q = 0; q < a.tp; q++) atomicAdd_system(a.peer_xflag[q] + 2 * a.tp + a.tp_rank, 1u);
+            const unsigned int target = xb / (unsigned int)a.L + 1u;
+            const long long t0 = clock64();
+            for (int q = 0; q < a.tp; q++) {
+                while ((int)(ld_acquire_sys(a.xflag + 2 * a.tp + q) - target) < 0) {
+                    if (clock64() - t0 > (1LL << 31)) {
+                        atomicExch(a.err, 8);
+                        return;
+                    }
+                }
+                const unsigned long long v = *(volatile unsigned long long*)(a.xam + q);
+                packed = v > packed ? v : packed;
+            }
+        }
         const int next = argmax_index(packed);
         const int len = st->len;
         a.tokens[len] = next;

@@ -57,6 +57,8 @@ struct MegaArgs {
     const uint8_t* eqs;       // tiled Q8_0 embedding (n = V, k = D)
     const uint16_t* ed;
     int D, H, KV, hd, F, V;
+    int Ve;                   // embedding rows (the head may hold a vocabulary slice)
+    int vocab_off;            // token id of the head's row 0
     const float* cos_t;
     const float* sin_t;
     int8_t* k8;               // KV cache [L][KV][max_seq][hd]
@@ -94,11 +96,13 @@ struct MegaArgs {
     int tp, tp_rank;
     float* xo;                       // this rank's receive area of O partials [tp][o.spl][D]
     float* xdn;                      // ... of down partials [tp][dn.spl][D]
-    unsigned int* xflag;             // [2][tp] arrival counters (O, down) per sender
+    unsigned int* xflag;             // [3][tp] arrival counters (O, down, LM-head argmax) per sender
+    unsigned long long* xam;         // [tp] packed argmax of each rank's vocabulary slice
     int xo_stride, xdn_stride;       // floats per sender slot (spl * D)
     float* peer_xo[kMegaMaxTP];      // every rank's xo (own included), mapped into this process
     float* peer_xdn[kMegaMaxTP];
     unsigned int* peer_xflag[kMegaMaxTP];
+    unsigned long long* peer_xam[kMegaMaxTP];
 };
 
 // Phase boundaries recorded per CTA when tracing: per layer 14 phase points

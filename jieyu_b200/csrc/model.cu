@@ -74,6 +74,8 @@ struct DevLayer {
 
 struct jyc_model {
     int L = 0, D = 0, H = 0, KV = 0, hd = 0, F = 0, V = 0, max_seq = 0;
+    int Ve = 0;          // embedding rows (token ids); V = LM-head rows
+    int vocab_off = 0;   // token id of LM-head row 0 (vocabulary-sharded head)
     int q_dim = 0, kv_dim = 0, nqkv = 0;
     int wtype = W_Q8;
     bool tiled = false;  // Q8 matrices in the 512-column tiled layout (megakernel models)
@@ -226,7 +228,7 @@ int upload_f32(jyc_model* m, const float* src, size_t n, float** dst) {
 bool mega_eligible(const jyc_model* m, const jyc_model_desc* d) {
     if (m->wtype != W_Q8 || d->lm_head.q == nullptr || d->lm_head.qt != JYC_Q8_0) return false;
     if (d->embed.f == nullptr && (d->embed.q == nullptr || d->embed.qt != JYC_Q8_0)) return false;
-    const int n16[] = {m->nqkv, m->D, 2 * m->F, m->V};
+    const int n16[] = {m->nqkv, m->D, 2 * m->F, m->V, m->Ve};
     for (int n : n16)
         if (n % 16) return false;
     const int k32[] = {m->D, m->q_dim, m->F};
@@ -282,6 +284,7 @@ int setup_mega(jyc_model* m) {
     a.eqs = m->embed_q.tq;
     a.ed = m->embed_q.td;
     a.D = m->D; a.H = m->H; a.KV = m->KV; a.hd = m->hd; a.F = m->F; a.V = m->V;
+    a.Ve = m->Ve; a.vocab_off = m->vocab_off;
     a.cos_t = m->cos_t;
     a.sin_t = m->sin_t;
     a.k8 = m->k8; a.v8 = m->v8; a.ks = m->ks; a.vs = m->vs;
@@ -336,6 +339,10 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
         return arg_error("model: missing final norm or RoPE tables");
     m->L = d->num_layers; m->D = d->hidden; m->H = d->num_heads; m->KV = d->num_kv_heads;
     m->hd = d->head_dim; m->F = d->intermediate; m->V = d->vocab_size; m->max_seq = d->max_seq;
+    m->Ve = d->embed_rows > 0 ? d->embed_rows : d->vocab_size;
+    m->vocab_off = d->vocab_offset;
+    if (m->vocab_off < 0 || (long long)m->vocab_off + m->V > m->Ve)
+        return arg_error("model: LM-head rows must be a slice of the embedding's vocabulary");
     m->q_dim = m->H * m->hd; m->kv_dim = m->KV * m->hd; m->nqkv = m->q_dim + 2 * m->kv_dim;
     m->wtype = d->layers[0].Wq.q != nullptr ? W_Q8 : W_F32;
     const int kq = m->wtype == W_Q8 ? 32 : 8;
@@ -355,7 +362,8 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     size_t stage = std::max({tb(m->q_dim, m->D), tb(m->kv_dim, m->D), tb(m->D, m->q_dim), tb(m->F, m->D),
                              tb(m->D, m->F)});
     const bool head_q8 = d->lm_head.q != nullptr;
-    const size_t head_bytes = head_q8 ? (size_t)m->V * (m->D / 32) * 34 : (size_t)m->V * m->D * 4;
+    const size_t head_bytes = head_q8 ? (size_t)std::max(m->V, m->Ve) * (m->D / 32) * 34
+                                      : (size_t)std::max(m->V, m->Ve) * m->D * 4;
     stage = std::max(stage, head_bytes);
     void* staging = nullptr;
     JYC_CUDA(cudaMalloc(&staging, stage));
@@ -391,12 +399,12 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     TRY(upload_wmat(m, d->lm_head, m->V, m->D, m->head, m->V, 0, 1, staging, stage, head_q8 ? W_Q8 : W_F32));
     m->weight_bytes += m->head.bytes();
     if (d->embed.f != nullptr) {
-        TRY(upload_f32(m, d->embed.f, (size_t)m->V * m->D, &m->embed_f));
+        TRY(upload_f32(m, d->embed.f, (size_t)m->Ve * m->D, &m->embed_f));
     } else if (d->embed.q != nullptr && d->embed.qt == JYC_Q8_0) {
-        if (d->embed.q == d->lm_head.q && head_q8) {
+        if (d->embed.q == d->lm_head.q && head_q8 && m->Ve == m->V) {
             m->embed_q = m->head;  // tied: one device copy
         } else {
-            TRY(upload_wmat(m, d->embed, m->V, m->D, m->embed_q, m->V, 0, 1, staging, stage, W_Q8));
+            TRY(upload_wmat(m, d->embed, m->Ve, m->D, m->embed_q, m->Ve, 0, 1, staging, stage, W_Q8));
         }
     } else {
         set_error("embedding must be fp32 or Q8_0");
@@ -659,7 +667,7 @@ JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_
         return JYC_ERR_KV_OOM;
     }
     for (int i = 0; i < seq; i++)
-        if (ids[i] < 0 || ids[i] >= m->V) return arg_error("forward_logits: token id out of range");
+        if (ids[i] < 0 || ids[i] >= m->Ve) return arg_error("forward_logits: token id out of range");
     cudaStream_t s = m->stream;
     JYC_CUDA(cudaMemcpyAsync(m->tokens + start_pos, ids, seq * sizeof(int), cudaMemcpyHostToDevice, s));
     TRY(launch_set_state(m->st, start_pos + seq, 1 << 30, m->max_seq + 1, nullptr, 0, s));
@@ -718,7 +726,7 @@ JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, co
     }
     if (num_eos < 0 || num_eos > 8 || (num_eos > 0 && !eos_ids)) return arg_error("generate: at most 8 EOS ids");
     for (int i = 0; i < prompt_len; i++)
-        if (prompt_ids[i] < 0 || prompt_ids[i] >= m->V) return arg_error("generate: prompt id out of range");
+        if (prompt_ids[i] < 0 || prompt_ids[i] >= m->Ve) return arg_error("generate: prompt id out of range");
     if (prompt_len >= m->max_seq) return prompt_len;  // the loop condition len < max_seq fails at once
     cudaStream_t s = m->stream;
     TRY(ensure_step_graph(m));
@@ -828,7 +836,7 @@ JYC_API int jyc_model_tp_open(jyc_model* m, int size, int rank, void* handle_out
             return JYC_ERR_UNSUPPORTED;
         }
     const size_t floats = (size_t)size * (m->tp_so + m->tp_sd) * m->D;
-    const size_t bytes = floats * 4 + (size_t)2 * size * sizeof(unsigned int);
+    const size_t bytes = floats * 4 + (size_t)4 * size * sizeof(unsigned int) + (size_t)size * 8;
     TRY(m->alloc(&m->tp_region, bytes));
     JYC_CUDA(cudaMemset(m->tp_region, 0, bytes));
     JYC_CUDA(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), m->tp_region));
@@ -853,15 +861,18 @@ JYC_API int jyc_model_tp_connect(jyc_model* m, const void* handles) {
             m->tp_mapped.push_back(p);
             base = static_cast<unsigned char*>(p);
         }
+        // layout: xo [t][so][D] | xdn [t][sd][D] | flags [3][t] (+1 pad) | xam [t] (8-byte aligned)
         float* f = reinterpret_cast<float*>(base);
         a.peer_xo[q] = f;
         a.peer_xdn[q] = f + xo_f;
         a.peer_xflag[q] = reinterpret_cast<unsigned int*>(f + xo_f + xd_f);
+        a.peer_xam[q] = reinterpret_cast<unsigned long long*>(a.peer_xflag[q] + 4 * t);
     }
     float* own = reinterpret_cast<float*>(m->tp_region);
     a.xo = own;
     a.xdn = own + xo_f;
     a.xflag = reinterpret_cast<unsigned int*>(own + xo_f + xd_f);
+    a.xam = reinterpret_cast<unsigned long long*>(a.xflag + 4 * t);
     a.xo_stride = m->tp_so * m->D;
     a.xdn_stride = m->tp_sd * m->D;
     a.tp = t;

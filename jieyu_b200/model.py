@@ -41,6 +41,8 @@ class Config:
     prompt_len: int = 32
     new_tokens: int = 128
     std: float = 0.02
+    embed_rows: int = 0        # embedding rows when the LM head holds a vocabulary slice (0: vocab)
+    vocab_offset: int = 0      # token id of the LM head's first row
 
     @property
     def q_dim(self) -> int:
@@ -260,6 +262,8 @@ class HostWeights:
         d.num_kv_heads = cfg.kv_heads
         d.head_dim = cfg.head_dim
         d.intermediate = cfg.inter
+        d.embed_rows = cfg.embed_rows
+        d.vocab_offset = cfg.vocab_offset
         self.desc = d
 
     def weight_bytes_per_token(self) -> float:

@@ -4,10 +4,11 @@ Sharding (one process per GPU, torch.distributed over NCCL for the plumbing):
 rank r of t holds query heads [r H/t, (r+1) H/t) and kv heads
 [r KV/t, (r+1) KV/t) (Q, K, V rows and biases), gate/up rows [r F/t, ..), and
 the matching INPUT columns of O (q_dim/t) and down (F/t), so attention and the
-int8 KV cache are rank-local; norms, embedding and LM head are whole on every
-rank. A rank's shard is an ordinary smaller model for the C ABI; the only
-cross-rank step is the sum of the O and down projections' partial outputs,
-two all-reduces of [hidden] per layer.
+int8 KV cache are rank-local; the LM head keeps rows [r V/t, (r+1) V/t) of
+the vocabulary; norms and the embedding are whole on every rank. A rank's
+shard is an ordinary smaller model for the C ABI; the cross-rank steps are
+the sums of the O and down projections' partial outputs (two per layer) and
+the largest of the ranks' argmaxes over their vocabulary slices.
 
 A decode token is one launch of the decode kernel per rank: after its O and
 down projections every CTA stores its partial rows into every rank's receive
@@ -56,8 +57,10 @@ def shard_config(cfg: Config, size: int) -> Config:
                    name=f"{cfg.name}_tp{size}")
 
 
-def shard_weights(hw: HostWeights, rank: int, size: int) -> HostWeights:
-    """Rank `rank`'s shard of Q8_0 host weights (see the module docstring)."""
+def shard_weights(hw: HostWeights, rank: int, size: int, shard_head: bool = True) -> HostWeights:
+    """Rank `rank`'s shard of Q8_0 host weights (see the module docstring);
+    shard_head=False keeps the whole LM head (the "nccl" mode, whose head
+    window picks the token from the rank's own logits)."""
     cfg = hw.cfg
     if cfg.wtype != "q8":
         raise ValueError("tensor parallelism is built for Q8_0 weights")
@@ -81,9 +84,20 @@ def shard_weights(hw: HostWeights, rank: int, size: int) -> HostWeights:
             t[f"bq.{l}"] = np.ascontiguousarray(hw.t[f"bq.{l}"][q0:q1])
             t[f"bk.{l}"] = np.ascontiguousarray(hw.t[f"bk.{l}"][k0:k1])
             t[f"bv.{l}"] = np.ascontiguousarray(hw.t[f"bv.{l}"][k0:k1])
-    for key in ("head", "embed", "final_norm"):
-        if key in hw.t:
-            t[key] = hw.t[key]
+    # LM head: rank r keeps vocabulary rows [r V/t, (r+1) V/t); the embedding
+    # stays whole (a tied embedding becomes a separate whole Q8_0 copy)
+    V = cfg.vocab
+    if shard_head and V % size == 0 and (V // size) % 16 == 0:
+        v0, v1 = rank * V // size, (rank + 1) * V // size
+        t["head"] = _q8_rows(hw.t["head"], D, v0, v1)
+        t["embed"] = hw.t["head"] if cfg.embed == "tied" else hw.t["embed"]
+        sc = replace(sc, vocab=v1 - v0, embed_rows=V, vocab_offset=v0,
+                     embed="q8" if cfg.embed == "tied" else cfg.embed)
+    else:
+        t["head"] = hw.t["head"]
+        if "embed" in hw.t:
+            t["embed"] = hw.t["embed"]
+    t["final_norm"] = hw.t["final_norm"]
     return HostWeights(sc, t, hw.cos, hw.sin)
 
 
@@ -110,7 +124,7 @@ class TPDecoder:
         self.torch, self.dist, self.group = torch, dist, group
         self.rank, self.size, self.mode = rank, size, mode
         self.cfg = hw_full.cfg
-        self.shard = shard_weights(hw_full, rank, size)
+        self.shard = shard_weights(hw_full, rank, size, shard_head=(mode == "kernel"))
         self.m = DeviceModel(self.shard)
         self.lib = _capi.load()
         if self.lib.jyc_model_decode_path(self.m.h) != 2:

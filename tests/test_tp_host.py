@@ -10,7 +10,7 @@ import pytest
 from jieyu_b200.model import Config, HostWeights, synth_f32
 from jieyu_b200.tp import shard_config, shard_weights
 
-CFG = Config("tp_small", 256, 2, 8, 4, 64, 512, 1000, 1e4, "q8", "f32", False, 64, 4, 4)
+CFG = Config("tp_small", 256, 2, 8, 4, 64, 512, 1024, 1e4, "q8", "f32", False, 64, 4, 4)
 
 
 def _blocks(blob, rows, k):
@@ -31,7 +31,13 @@ def test_shards_reassemble_the_model(size):
             assert np.array_equal(whole, _blocks(hw.t[f"{name}.{l}"], D, k)), name
     sc = shards[0].cfg
     assert (sc.heads, sc.kv_heads, sc.inter) == (CFG.heads // size, CFG.kv_heads // size, CFG.inter // size)
-    assert shards[0].t["head"] is hw.t["head"]
+    # vocabulary-sharded LM head: the slices re-assemble it, the embedding stays whole
+    if CFG.vocab % size == 0 and (CFG.vocab // size) % 16 == 0:
+        assert np.array_equal(np.concatenate([s.t["head"] for s in shards]), hw.t["head"])
+        assert [s.cfg.vocab_offset for s in shards] == [r * CFG.vocab // size for r in range(size)]
+        assert all(s.cfg.embed_rows == CFG.vocab for s in shards)
+    else:
+        assert shards[0].t["head"] is hw.t["head"]
 
 
 def test_shard_config_rejects_uneven_splits():
