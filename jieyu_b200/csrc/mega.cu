@@ -557,8 +557,9 @@ static __device__ bool xchg_wait(const MegaArgs& a, int kind, unsigned int targe
 static __device__ bool grid_barrier(unsigned int* ctr, unsigned int target, int* err, int* s_ok) {
     csync();
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ctr, 1u);
+        // arrive with a release reduction (no return trip to wait for); the
+        // CTA barrier above orders every thread's writes before it
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(ctr), "r"(1u) : "memory");
         int ok = 1;
         if ((int)(ld_acquire_gpu(ctr) - target) < 0) {
             const long long t0 = clock64();
