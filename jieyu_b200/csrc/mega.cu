@@ -717,10 +717,12 @@ static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const floa
 // the last item of the kv head to finish merges all splits of its query
 // heads into the attention rows buffer (the O projection's input).
 template <int MAXG, int HD>
-static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, int kvh, int split, int nv, int pos,
-                                 unsigned char* sm, uint64_t* abar, uint32_t& aph, int* s_flag, long long* tr) {
+static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, int kvh, int grp, int split, int nv,
+                                                 int pos, unsigned char* sm, uint64_t* abar, uint32_t& aph,
+                                                 int* s_flag, long long* tr) {
     constexpr int hd = HD, half = HD / 2, hw = HD / 4, HC = HD / 16;  // words, 16-byte chunks per row
-    const int G = a.H / a.KV, S = a.asub, lS = 31 - __clz(S);
+    const int GA = a.H / a.KV, S = a.asub, lS = 31 - __clz(S);
+    const int G = a.gsz, g0 = grp * G;  // this item's query heads: kvh * GA + g0 .. + G
 #define ATR(k)                                      \
     do {                                            \
         if (tr && threadIdx.x == 0) tr[k] = clock64(); \
@@ -728,7 +730,7 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     ATR(0);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nthr = kMegaCW * 32;
-    const AttnPlan P = attn_plan(G, hd, S);
+    const AttnPlan P = attn_plan(GA, hd, S);
     int8_t* s_k = reinterpret_cast<int8_t*>(sm + P.kv);
     int8_t* s_v = s_k + S * hd;
     float* s_sc = reinterpret_cast<float*>(sm + P.sc);
@@ -774,17 +776,19 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     const size_t nqkv = (size_t)ly.qkv.n;
     const float* bq = ly.bias;
     for (int gq = warp; gq < G; gq += kMegaCW) {
-        const size_t o = (size_t)(kvh * G + gq) * hd;
+        const size_t o = (size_t)(kvh * GA + g0 + gq) * hd;
         rq_warp(a.pq + o, nq, nqkv, bq ? bq + o : nullptr, hd, ct, stb, s_q8 + gq * hd, s_qsc + gq, lane);
     }
-    if (owner) {  // append K (roped) and V at pos; keep a copy for the tile
+    if (owner) {  // K (roped) and V at pos into the tile; the head group 0 item appends them to the cache
         const size_t ok = (size_t)q_dim + (size_t)kvh * hd, ov = ok + kv_dim;
+        const bool app = g0 == 0;
         if (warp == kMegaCW - 1)
-            rq_warp(a.pq + ok, nq, nqkv, bq ? bq + ok : nullptr, hd, ct, stb, kb + (size_t)pos * hd, ksb + pos,
-                    lane, s_row, s_rsc);
+            rq_warp(a.pq + ok, nq, nqkv, bq ? bq + ok : nullptr, hd, ct, stb, app ? kb + (size_t)pos * hd : s_row,
+                    app ? ksb + pos : s_rsc, lane, app ? s_row : nullptr, app ? s_rsc : nullptr);
         else if (warp == kMegaCW - 2)
-            rq_warp(a.pq + ov, nq, nqkv, bq ? bq + ov : nullptr, hd, nullptr, nullptr, vb + (size_t)pos * hd,
-                    vsb + pos, lane, s_row + hd, s_rsc + 1);
+            rq_warp(a.pq + ov, nq, nqkv, bq ? bq + ov : nullptr, hd, nullptr, nullptr,
+                    app ? vb + (size_t)pos * hd : s_row + hd, app ? vsb + pos : s_rsc + 1, lane,
+                    app ? s_row + hd : nullptr, app ? s_rsc + 1 : nullptr);
     }
     for (int gq = tid; gq < G; gq += nthr) {
         s_m[gq] = -INFINITY;
@@ -901,11 +905,11 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     for (int e = tid; e < G * hd; e += nthr) {
         float o = 0.0f;
         for (int r = 0; r < nred; r++) o = __fadd_rn(o, red[(size_t)r * G * hd + e]);
-        const int gq = e / hd, dd = e - gq * hd, h = kvh * G + gq;
+        const int gq = e / hd, dd = e - gq * hd, h = kvh * GA + g0 + gq;
         a.part_o[((size_t)h * a.nsplit + split) * hd + dd] = o;
     }
     for (int gq = tid; gq < G; gq += nthr) {
-        const int h = kvh * G + gq;
+        const int h = kvh * GA + g0 + gq;
         a.part_ml[((size_t)h * a.nsplit + split) * 2] = s_m[gq];
         a.part_ml[((size_t)h * a.nsplit + split) * 2 + 1] = s_l[gq];
     }
@@ -915,9 +919,10 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     ATR(6);
     if (tid == 0) {
         __threadfence();
-        const unsigned int old = atomicAdd(a.acnt + kvh, 1u);
+        unsigned int* cnt = a.acnt + kvh * (GA / G) + grp;
+        const unsigned int old = atomicAdd(cnt, 1u);
         *s_flag = old == (unsigned int)(nv - 1);
-        if (*s_flag) atomicExch(a.acnt + kvh, 0u);
+        if (*s_flag) atomicExch(cnt, 0u);
     }
     csync();
     ATR(7);
@@ -926,7 +931,7 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     // every output element merges its splits itself: (m, l, o) of four splits
     // per round trip, rescaled online to the running maximum
     for (int e = tid; e < G * hd; e += nthr) {
-        const int gq = e / hd, dd = e - gq * hd, h = kvh * G + gq;
+        const int gq = e / hd, dd = e - gq * hd, h = kvh * GA + g0 + gq;
         const float* ml = a.part_ml + (size_t)h * a.nsplit * 2;
         const float* po = a.part_o + (size_t)h * a.nsplit * hd + dd;
         float M = -INFINITY, L = 0.0f, O = 0.0f;
@@ -1080,10 +1085,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             TRACE(tb + 2);
             if (!ok) break;
             // attention items (kv head, split), round-robin over CTAs
-            for (int it = b; it < a.KV * nvalid && ok; it += nct) {
+            const int ngrp = a.H / a.KV / a.gsz;  // query-head groups per kv head
+            for (int it = b; it < a.KV * ngrp * nvalid && ok; it += nct) {
                 long long* tr = (a.trace && it == b) ? a.trace + (size_t)b * kMegaTracePts + tb + 14 : nullptr;
-                const int kv_h = it / nvalid, sp = it - kv_h * nvalid;
-                ok = attn_item<MAXG, HD>(a, l, kv_h, sp, nvalid, pos, xs_region, abar, aph, &s_ok, tr);
+                const int kv_h = it / (ngrp * nvalid), rem = it - kv_h * ngrp * nvalid, gr = rem / nvalid;
+                ok = attn_item<MAXG, HD>(a, l, kv_h, gr, rem - gr * nvalid, nvalid, pos, xs_region, abar, aph,
+                                         &s_ok, tr);
             }
             if (!ok) break;
             TRACE(tb + 3);
@@ -1264,16 +1271,21 @@ int mega_attn_sub(int kmax, int G, int hd, int chunk) {
 
 int mega_smem_bytes(const MegaArgs& a) { return 128 + a.xs_bytes + a.nslots * kMegaSlotBytes; }
 
-// the kernel instantiation of a model's attention shape and exchange mode
-static const void* mega_kernel_for(int G, int hd, bool tp) {
-    if (tp) {
-        if (hd == 64)
-            return G <= 4 ? (const void*)mega_step_kernel<4, 64, true> : (const void*)mega_step_kernel<8, 64, true>;
-        return G <= 4 ? (const void*)mega_step_kernel<4, 128, true> : (const void*)mega_step_kernel<8, 128, true>;
-    }
+// the kernel instantiation of a model's attention shape (query heads per
+// attention item G, head_dim) and exchange mode
+template <bool TP>
+static const void* mega_kernel_tp(int G, int hd) {
     if (hd == 64)
-        return G <= 4 ? (const void*)mega_step_kernel<4, 64, false> : (const void*)mega_step_kernel<8, 64, false>;
-    return G <= 4 ? (const void*)mega_step_kernel<4, 128, false> : (const void*)mega_step_kernel<8, 128, false>;
+        return G <= 1   ? (const void*)mega_step_kernel<1, 64, TP>
+               : G <= 4 ? (const void*)mega_step_kernel<4, 64, TP>
+                        : (const void*)mega_step_kernel<8, 64, TP>;
+    return G <= 1   ? (const void*)mega_step_kernel<1, 128, TP>
+           : G <= 4 ? (const void*)mega_step_kernel<4, 128, TP>
+                    : (const void*)mega_step_kernel<8, 128, TP>;
+}
+
+static const void* mega_kernel_for(int G, int hd, bool tp) {
+    return tp ? mega_kernel_tp<true>(G, hd) : mega_kernel_tp<false>(G, hd);
 }
 
 int mega_static_smem(int G, int hd) {
@@ -1305,7 +1317,7 @@ int launch_mega_step(const MegaArgs& a, cudaStream_t s) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     void* args[] = {const_cast<MegaArgs*>(&a)};
-    cudaError_t e = cudaLaunchKernelExC(&cfg, mega_kernel_for(a.H / a.KV, a.hd, a.tp > 1), args);
+    cudaError_t e = cudaLaunchKernelExC(&cfg, mega_kernel_for(a.gsz, a.hd, a.tp > 1), args);
     if (e != cudaSuccess) return cuda_fail(e, "mega_step launch");
     count_launch();
     return JYC_OK;

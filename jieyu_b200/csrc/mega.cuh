@@ -79,6 +79,7 @@ struct MegaArgs {
     float* part_ml;           // [H][nsplit][2]
     int chunk, nsplit;
     int asub;                 // attention sub-chunk (power of two, positions per K/V copy)
+    int gsz;                  // query heads per attention item (a divisor of H / KV)
     unsigned int* acnt;       // per kv head: finished split items of the current layer
     float scale;              // 1/sqrtf(hd)
     DevState* st;

@@ -310,12 +310,16 @@ int setup_mega(jyc_model* m) {
     JYC_CUDA(cudaMemset(a.bar, 0, sizeof(unsigned int)));
     a.err = device_error_word();
     a.kmax = std::max({m->D, m->q_dim, m->F});
+    // attention items: one per (kv head, split) at long contexts; one per
+    // (query head, split) when those fit the CTAs at full context (short
+    // contexts: more parallelism, fewer splits to merge per item)
+    a.gsz = (m->KV * (m->H / m->KV) * a.nsplit <= nctas) ? 1 : m->H / m->KV;
     a.asub = mega_attn_sub(a.kmax, m->H / m->KV, m->hd, a.chunk);
     a.xs_bytes = mega_xs_bytes(a.kmax, m->H / m->KV, m->hd, a.asub);
-    TRY(m->alloc(&a.acnt, (size_t)m->KV));
-    JYC_CUDA(cudaMemset(a.acnt, 0, sizeof(unsigned int) * m->KV));
+    TRY(m->alloc(&a.acnt, (size_t)m->H));  // one per (kv head, query-head group)
+    JYC_CUDA(cudaMemset(a.acnt, 0, sizeof(unsigned int) * m->H));
     // ring as deep as the shared memory allows (227 KB per CTA, at least 2 slots)
-    const int st_smem = mega_static_smem(m->H / m->KV, m->hd);
+    const int st_smem = mega_static_smem(a.gsz, m->hd);
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
     const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
     a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
@@ -323,7 +327,7 @@ int setup_mega(jyc_model* m) {
     a.win1 = 2 * m->L + 1;  // the whole step
     if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode
     const int smem = mega_smem_bytes(a);
-    TRY(prepare_mega_kernel(smem, m->H / m->KV, m->hd));
+    TRY(prepare_mega_kernel(smem, a.gsz, m->hd));
     m->mega = true;
     return JYC_OK;
 }
