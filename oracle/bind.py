@@ -68,6 +68,8 @@ class Oracle(_Checker):
         self.lib.jyo_set_threads.argtypes = [_I]
         self.lib.jyo_generate.restype = _I
         self.lib.jyo_generate.argtypes = [_P, _P, _I, _P, _I, _I, _F, _P, _F]
+        self.lib.jyo_sample.restype = _I
+        self.lib.jyo_sample.argtypes = [_P, _I, _F, _F, _P, _I, _I, C.POINTER(C.c_uint)]
         if threads:
             self.lib.jyo_set_threads(threads)
 

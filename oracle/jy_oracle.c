@@ -441,6 +441,48 @@ int jyo_forward_logits(const jyc_model_desc* d, void* cache, const int* ids, int
     return r ? -1 : 0;
 }
 
+/* The token pick of one generate step (generate.h:50-77): repetition penalty
+ * over the ids generated so far (out_ids[prompt_len..len)), then greedy
+ * (first index of the maximum) or, with temperature > 0, the reference's
+ * sampler: expf((l - max) / T) written back, summed in double, one LCG step
+ * (rng = rng * 1664525 + 1013904223), r = (rng >> 8) / 2^24 * sum, the first
+ * v whose running r -= p_v reaches <= 0 (V - 1 if none). logits is modified
+ * in place as in the reference. */
+int jyo_sample(float* logits, int V, float temperature, float rep_penalty, const int* out_ids,
+               int prompt_len, int len, unsigned* rng) {
+    if (rep_penalty != 1.0f)
+        for (int i = prompt_len; i < len; i++) {
+            const int id = out_ids[i];
+            if (id >= 0 && id < V)
+                logits[id] = (logits[id] > 0.0f) ? logits[id] / rep_penalty : logits[id] * rep_penalty;
+        }
+    int next = 0;
+    if (temperature <= 0.0f) {
+        for (int v = 1; v < V; v++)
+            if (logits[v] > logits[next]) next = v;
+        return next;
+    }
+    float mx = logits[0];
+    for (int v = 1; v < V; v++)
+        if (logits[v] > mx) mx = logits[v];
+    double sum = 0.0;
+    for (int v = 0; v < V; v++) {
+        logits[v] = expf((logits[v] - mx) / temperature);
+        sum += logits[v];
+    }
+    *rng = *rng * 1664525u + 1013904223u;
+    double rr = (double)(*rng >> 8) / 16777216.0 * sum;
+    next = V - 1;
+    for (int v = 0; v < V; v++) {
+        rr -= logits[v];
+        if (rr <= 0.0) {
+            next = v;
+            break;
+        }
+    }
+    return next;
+}
+
 /* generate + generate_cached (generate.h:9-112). */
 int jyo_generate(const jyc_model_desc* d, const int* prompt, int prompt_len, const int* eos,
                  int num_eos, int max_new, float temperature, int* out_ids, float rep_penalty) {
@@ -460,33 +502,7 @@ int jyo_generate(const jyc_model_desc* d, const int* prompt, int prompt_len, con
         const float* last = X + (size_t)(seq - 1) * D;
         err |= matmul_w(&d->lm_head, 1, V, D, last, logits);
         if (err) break;
-        if (rep_penalty != 1.0f)
-            for (int i = prompt_len; i < len; i++) {
-                const int id = out_ids[i];
-                if (id >= 0 && id < V)
-                    logits[id] = (logits[id] > 0.0f) ? logits[id] / rep_penalty : logits[id] * rep_penalty;
-            }
-        int next = 0;
-        if (temperature <= 0.0f) {
-            for (int v = 1; v < V; v++)
-                if (logits[v] > logits[next]) next = v;
-        } else {
-            float mx = logits[0];
-            for (int v = 1; v < V; v++)
-                if (logits[v] > mx) mx = logits[v];
-            double sum = 0.0;
-            for (int v = 0; v < V; v++) {
-                logits[v] = expf((logits[v] - mx) / temperature);
-                sum += logits[v];
-            }
-            rng = rng * 1664525u + 1013904223u;
-            double rr = (double)(rng >> 8) / 16777216.0 * sum;
-            next = V - 1;
-            for (int v = 0; v < V; v++) {
-                rr -= logits[v];
-                if (rr <= 0.0) { next = v; break; }
-            }
-        }
+        const int next = jyo_sample(logits, V, temperature, rep_penalty, out_ids, prompt_len, len, &rng);
         out_ids[len++] = next;
         seq = 1;
         int stop = 0;

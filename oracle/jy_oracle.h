@@ -47,6 +47,8 @@ void jyo_cache_read(void* c, int layer, int npos, int8_t* k, float* ks, int8_t* 
 int jyo_forward_logits(const jyc_model_desc* d, void* cache, const int* ids, int seq,
                        int start_pos, float* logits, float* hidden_out);
 /* generate (generate.h:90-112), greedy or LCG sampling, repetition penalty. */
+int jyo_sample(float* logits, int V, float temperature, float rep_penalty, const int* out_ids,
+               int prompt_len, int len, unsigned* rng);
 int jyo_generate(const jyc_model_desc* d, const int* prompt, int prompt_len, const int* eos,
                  int num_eos, int max_new, float temperature, int* out_ids, float rep_penalty);
 

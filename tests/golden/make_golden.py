@@ -236,8 +236,13 @@ def main():
     pr = prompt_ids(c0)
     ids = ref.generate(hw0.desc, pr, c0.new_tokens, max_seq=c0.max_seq)
     rows, kv = teacher_forced(ref, hw0, pr, 16)
+    # the reference's sampler and repetition penalty (generate.h:50-77)
+    sampled = ref.generate(hw0.desc, pr, 64, temperature=0.8, rep=1.3, max_seq=c0.max_seq)
+    penalized = ref.generate(hw0.desc, pr, 64, temperature=0.0, rep=1.3, max_seq=c0.max_seq)
     with open(os.path.join(OUT, "c0.json"), "w") as f:
         json.dump({"seed": 1234, "prompt": [int(x) for x in pr], "greedy": [int(x) for x in ids],
+                   "sampled_t0.8_p1.3": [int(x) for x in sampled],
+                   "greedy_p1.3": [int(x) for x in penalized],
                    "teacher_forced": rows, "kv_sha": kv, "isa_spread": isa_spread(hw0, pr, 16)}, f, indent=1)
 
     # configs[1] shape: short prompt (the CPU prefill path is scalar), 16 tokens

@@ -45,6 +45,19 @@ def test_oracle_c0_greedy_and_logits(oracle):
     assert kv == g["kv_sha"]
 
 
+def test_oracle_sampler_and_penalty_match_reference(oracle):
+    """jyo_sample (the generate.h:50-77 restatement) reproduces the reference's
+    sampled (T 0.8) and repetition-penalised (1.3) sequences on configs[0]."""
+    g = golden("c0.json")
+    cfg = CONFIGS["c0"]
+    hw = HostWeights.synthetic(cfg)
+    pr = prompt_ids(cfg)
+    got = oracle.generate(hw.desc, pr, 64, temperature=0.8, rep=1.3, max_seq=cfg.max_seq)
+    assert list(got) == g["sampled_t0.8_p1.3"]
+    got = oracle.generate(hw.desc, pr, 64, temperature=0.0, rep=1.3, max_seq=cfg.max_seq)
+    assert list(got) == g["greedy_p1.3"]
+
+
 def test_oracle_c1_shape(oracle):
     g = golden("c1.json")
     cfg = CONFIGS["c1"]
