@@ -197,6 +197,21 @@ JYC_API int jyc_silu(const float* x, float* y, int n, void* stream);
  * Replaces the greedy loop of generate_cached (libs/model_libs/generate.h:57-60). */
 JYC_API int jyc_argmax(const float* logits, int n, int* out_index, void* stream);
 
+/* The token pick of one generate step, on the device (all pointers device
+ * memory; one CTA). Replaces the pick of generate_cached
+ * (libs/model_libs/generate.h:50-77): for every out_ids[i], i in
+ * [prompt_len, len), a positive logits[id] is divided by repetition_penalty
+ * and a non-positive one multiplied (once per occurrence, in order); then
+ * temperature <= 0 takes the first index of the maximum, else logits[v]
+ * becomes expf((logits[v] - max) / temperature), *rng advances one LCG step
+ * (rng * 1664525 + 1013904223) and the pick is the first v where
+ * (rng >> 8) / 2^24 * sum minus the running sum reaches <= 0 (vocab_size - 1
+ * if none). logits is modified in place, as in the reference. The sum runs in
+ * double over 512 contiguous chunks (the reference: one running sum), and
+ * expf is CUDA's (within its 2-ulp bound of the reference's libm). */
+JYC_API int jyc_sample(float* logits, int vocab_size, float temperature, float repetition_penalty,
+                       const int* out_ids, int prompt_len, int len, unsigned int* rng, int* next, void* stream);
+
 /* ---- model entry points ------------------------------------------------ */
 typedef struct jyc_model jyc_model;
 
@@ -214,10 +229,11 @@ JYC_API double jyc_model_kv_bytes_per_token(const jyc_model* m, int ctx);
 /* Full token loop, same contract as generate() (libs/model_libs/generate.h:90-112)
  * with an internal KV cache: out_ids[0..ret) = prompt then new tokens;
  * returns 0 if prompt_len<=0 or > max_seq, prompt_len if max_new_tokens<=0,
- * negative on error. Greedy only: temperature > 0 or repetition_penalty != 1
- * returns JYC_ERR_UNSUPPORTED (the reference's LCG sampler and penalty,
- * generate.h:50-77, are not built on the device yet). cb (may be NULL) gets
- * every new id in order; a non-zero return stops generation. */
+ * negative on error. temperature > 0 samples and repetition_penalty != 1
+ * penalises as jyc_sample describes (the reference's LCG, seeded 12345 per
+ * call, generate.h:36 and 50-77), on the device; a tensor-parallel shard
+ * (vocabulary-sliced head) returns JYC_ERR_UNSUPPORTED for them. cb (may be
+ * NULL) gets every new id in order; a non-zero return stops generation. */
 JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len,
                          const int* eos_ids, int num_eos, int max_new_tokens,
                          float temperature, int* out_ids, float repetition_penalty,

@@ -92,6 +92,7 @@ SIGNATURES = [
     ("jyc_attention_q8_noalloc", _I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P]),
     ("jyc_silu", _I, [_P, _P, _I, _P]),
     ("jyc_argmax", _I, [_P, _I, _P, _P]),
+    ("jyc_sample", _I, [_P, _I, C.c_float, C.c_float, _P, _I, _I, _P, _P, _P]),
     ("jyc_model_create", _P, [C.POINTER(ModelDesc)]),
     ("jyc_model_free", None, [_P]),
     ("jyc_model_weight_bytes_per_token", C.c_double, [_P]),

@@ -296,4 +296,14 @@ JYC_API int jyc_argmax(const float* logits, int n, int* out_index, void* stream)
     return launch_argmax(logits, n, slot, out_index, s);
 }
 
+JYC_API int jyc_sample(float* logits, int vocab_size, float temperature, float repetition_penalty,
+                       const int* out_ids, int prompt_len, int len, unsigned int* rng, int* next, void* stream) {
+    clear_error();
+    if (!logits || !rng || !next || vocab_size <= 0) return arg_error("sample: bad arguments");
+    if (repetition_penalty != 1.0f && (!out_ids || prompt_len < 0 || len < prompt_len))
+        return arg_error("sample: penalty needs out_ids[prompt_len..len)");
+    return launch_sample(logits, vocab_size, temperature, repetition_penalty, out_ids, prompt_len, len, rng, next,
+                         S(stream));
+}
+
 }  // extern "C"

@@ -10,6 +10,7 @@
 //   argmax epilogue  greedy loop                        libs/model_libs/generate.h:57-60
 //   embed            wmat_row                           libs/model_libs/wmat_kernel.h:18-29
 #include "kernels.cuh"
+#include "sample.cuh"
 
 #include <algorithm>
 
@@ -226,6 +227,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a) {
                 st->steps = nsteps;
                 st->amax = 0ull;
                 st->head_arrive = 0u;
+                st->fresh = 1;
                 if (stop) st->active = 0;
                 __threadfence();
             }
@@ -835,7 +837,72 @@ __global__ void set_state_kernel(DevState* st, int len, int max_new, int max_len
     for (int i = 0; i < 8; i++) st->eos[i] = e[i];
     st->amax = 0ull;
     st->head_arrive = 0u;
+    st->fresh = 0;
+    st->temperature = 0.0f;  // greedy until generate asks for its sampler
+    st->penalty = 1.0f;
+    st->rng = 12345u;
+    st->prompt_len = len;
 }
+__global__ void set_sampling_kernel(DevState* st, float temperature, float penalty, unsigned int rng,
+                                    int prompt_len) {
+    st->temperature = temperature;
+    st->penalty = penalty;
+    st->rng = rng;
+    st->prompt_len = prompt_len;
+}
+int launch_set_sampling(DevState* st, float temperature, float penalty, unsigned int rng, int prompt_len,
+                        cudaStream_t s) {
+    set_sampling_kernel<<<1, 1, 0, s>>>(st, temperature, penalty, rng, prompt_len);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+
+// Sampling on a path whose head picked greedily (prefill, the per-op decode
+// step): pick the appended token again from the same logits (in place) with
+// the step's sampler and redo the stop test (generate.h:78-86).
+__global__ void __launch_bounds__(kSampleThreads) resample_last_kernel(DevState* st, float* logits,
+                                                                       unsigned int* stag, int V, int* tokens) {
+    __shared__ double scratch[kSampleThreads + 1];
+    if (!st->fresh) return;  // the step appended no token
+    const int len = st->len;  // the new token sits at len - 1
+    unsigned int rng = st->rng;
+    const int next = sample_block(logits, V, st->temperature, st->penalty, tokens, st->prompt_len, len - 1, &rng,
+                                  scratch, stag);
+    if (threadIdx.x == 0) {
+        tokens[len - 1] = next;
+        st->rng = rng;
+        bool stop = len >= st->max_len || st->steps >= st->max_new;
+        for (int e = 0; e < st->n_eos; e++)
+            if (next == st->eos[e]) stop = true;
+        st->active = stop ? 0 : 1;
+        st->fresh = 0;
+    }
+}
+int launch_resample_last(DevState* st, float* logits, unsigned int* stag, int V, int* tokens, cudaStream_t s) {
+    resample_last_kernel<<<1, kSampleThreads, 0, s>>>(st, logits, stag, V, tokens);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(float* logits, int V, float temperature,
+                                                                float penalty, const int* ids, int prompt_len,
+                                                                int len, unsigned int* rng, int* out) {
+    __shared__ double scratch[kSampleThreads + 1];
+    unsigned int r = *rng;
+    const int next = sample_block(logits, V, temperature, penalty, ids, prompt_len, len, &r, scratch, nullptr);
+    if (threadIdx.x == 0) {
+        *out = next;
+        *rng = r;
+    }
+}
+int launch_sample(float* logits, int V, float temperature, float penalty, const int* ids, int prompt_len, int len,
+                  unsigned int* rng_dev, int* out_dev, cudaStream_t s) {
+    sample_kernel<<<1, kSampleThreads, 0, s>>>(logits, V, temperature, penalty, ids, prompt_len, len, rng_dev,
+                                               out_dev);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+
 int launch_set_state(DevState* st, int len, int max_new, int max_len, const int* eos, int n_eos,
                      cudaStream_t s) {
     if (n_eos > 8) return arg_error("generate: at most 8 EOS ids are supported");

@@ -29,6 +29,11 @@ struct DevState {
     unsigned int head_arrive;  // last-arriver counter of the LM-head grid
     unsigned int bar_base;     // grid-barrier counter value at the start of the next step
     unsigned int xbase;        // tensor-parallel exchanges of each kind completed (O / down, per step L each)
+    float temperature;         // > 0: sample (the reference's sampler), else greedy
+    float penalty;             // repetition penalty over the generated ids (1: none)
+    unsigned int rng;          // the sampler's LCG state
+    int prompt_len;            // generated ids start here (penalty range)
+    int fresh;                 // the last head appended a token not yet re-picked by the sampler
 };
 
 // Where a kernel finds its first position: from the step state (decode graph,
@@ -127,6 +132,11 @@ int launch_kv_pack(const float* src, int8_t* dst, float* sc, int heads, int hd, 
 int launch_argmax(const float* v, int n, unsigned long long* slot, int* out, cudaStream_t s);
 int launch_matmul_f32_generic(const float* A, const float* Bt, float* C, int m, int n, int k,
                               cudaStream_t s);
+int launch_set_sampling(DevState* st, float temperature, float penalty, unsigned int rng, int prompt_len,
+                        cudaStream_t s);
+int launch_resample_last(DevState* st, float* logits, unsigned int* stag, int V, int* tokens, cudaStream_t s);
+int launch_sample(float* logits, int V, float temperature, float penalty, const int* ids, int prompt_len, int len,
+                  unsigned int* rng_dev, int* out_dev, cudaStream_t s);
 int launch_set_state(DevState* st, int len, int max_new, int max_len, const int* eos, int n_eos,
                      cudaStream_t s);
 

@@ -42,6 +42,7 @@
 #include <cmath>
 
 #include "mega.cuh"
+#include "sample.cuh"
 #include "ptx.cuh"
 
 namespace jyc {
@@ -1171,7 +1172,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     if (tid == 0 && s_best) atomicMax(&st->amax, s_best);
     if (!grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok)) return;
     TRACE(th + 2);
-    if (b == 0 && tid == 0) {
+    if (b != 0) return;
+    int next;
+    if (!TP && (st->temperature > 0.0f || st->penalty != 1.0f)) {
+        // sampler / repetition penalty over the whole logits row (CTA 0's consumers)
+        unsigned int rng = st->rng;
+        next = sample_block(a.logits, a.V, st->temperature, st->penalty, a.tokens, st->prompt_len, st->len, &rng,
+                            reinterpret_cast<double*>(x_s), a.stag);
+        if (tid == 0) st->rng = rng;
+    } else {
+        if (tid != 0) return;
         unsigned long long packed = atomicAdd(&st->amax, 0ull);
         if (TP) {  // every rank's argmax of its vocabulary slice -> the largest
             for (int q = 0; q < a.tp; q++) a.peer_xam[q][a.tp_rank] = packed;
@@ -1190,7 +1200,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                 packed = v > packed ? v : packed;
             }
         }
-        const int next = argmax_index(packed);
+        next = argmax_index(packed);
+    }
+    if (tid == 0) {
         const int len = st->len;
         a.tokens[len] = next;
         const int nlen = len + 1, nsteps = st->steps + 1;
@@ -1202,6 +1214,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         st->amax = 0ull;
         st->bar_base = base + (unsigned int)bi * nct;
         if (TP) st->xbase = xb + (unsigned int)a.L;
+        st->fresh = 0;
         if (stop) st->active = 0;
         __threadfence();
     }
@@ -1255,7 +1268,8 @@ int mega_plan(MegaMat& m, int nctas, bool splittable) {
 // attention item's plan (sub-chunks of S positions) shares the region.
 int mega_xs_bytes(int kmax, int G, int hd, int S) {
     const int xk = kmax * 4 + kmax * 3 + (kmax / 32) * 4;
-    return (std::max(xk, attn_plan(G, hd, S).total) + 127) / 128 * 128;
+    const int samp = (kSampleThreads + 1) * (int)sizeof(double);  // the sampler's scratch (head phase)
+    return (std::max(std::max(xk, samp), attn_plan(G, hd, S).total) + 127) / 128 * 128;
 }
 
 // Attention sub-chunk: the split length rounded up to a power of two, halved

@@ -75,6 +75,7 @@ struct MegaArgs {
     float* qkv;               // [q|k|v]
     float* h;                 // SwiGLU output [F]
     float* logits;            // [V]
+    unsigned int* stag;       // the sampler's penalty tags [2 V]
     float* part_o;            // attention split partials [H][nsplit][hd]
     float* part_ml;           // [H][nsplit][2]
     int chunk, nsplit;

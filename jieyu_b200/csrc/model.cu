@@ -90,6 +90,7 @@ struct jyc_model {
     float *ks = nullptr, *vs = nullptr;
     // activations / scratch
     float *X = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
+    unsigned int* stag = nullptr;  // the sampler's penalty tags: first index [V], counts [V]
     float* tmp = nullptr;
     int8_t* q8 = nullptr;
     float* qsc = nullptr;
@@ -289,7 +290,7 @@ int setup_mega(jyc_model* m) {
     a.sin_t = m->sin_t;
     a.k8 = m->k8; a.v8 = m->v8; a.ks = m->ks; a.vs = m->vs;
     a.max_seq = m->max_seq;
-    a.X = m->X; a.qkv = m->qkv; a.h = m->h; a.logits = m->logits;
+    a.X = m->X; a.qkv = m->qkv; a.h = m->h; a.logits = m->logits; a.stag = m->stag;
     TRY(m->alloc(&a.Xb, (size_t)m->D));
     TRY(m->alloc(&a.pq, (size_t)sq * m->nqkv));
     TRY(m->alloc(&a.po, (size_t)so * m->D));
@@ -440,6 +441,7 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     TRY(m->alloc(&m->attn, arows * m->q_dim));
     TRY(m->alloc(&m->h, arows * m->F));
     TRY(m->alloc(&m->logits, (size_t)m->V));
+    TRY(m->alloc(&m->stag, 2 * (size_t)m->V));
     TRY(m->alloc(&m->tmp, (size_t)m->D));
     TRY(m->alloc(&m->q8, arows * m->q_dim));
     TRY(m->alloc(&m->qsc, arows * m->H));
@@ -723,9 +725,9 @@ JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, co
     if (prompt_len <= 0 || prompt_len > m->max_seq || !prompt_ids) return 0;
     for (int i = 0; i < prompt_len; i++) out_ids[i] = prompt_ids[i];
     if (max_new_tokens <= 0) return prompt_len;
-    if (temperature > 0.0f || repetition_penalty != 1.0f) {
-        set_error(
-            "generate: sampling (temperature > 0) and repetition_penalty != 1 are not built yet on the B200 path");
+    const bool sampling = temperature > 0.0f || repetition_penalty != 1.0f;
+    if (sampling && m->margs.tp > 1) {
+        set_error("generate: sampling over a vocabulary-sliced (tensor-parallel) head is not built");
         return JYC_ERR_UNSUPPORTED;
     }
     if (num_eos < 0 || num_eos > 8 || (num_eos > 0 && !eos_ids)) return arg_error("generate: at most 8 EOS ids");
@@ -736,12 +738,25 @@ JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, co
     TRY(ensure_step_graph(m));
     JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids, prompt_len * sizeof(int), cudaMemcpyHostToDevice, s));
     TRY(launch_set_state(m->st, prompt_len, max_new_tokens, m->max_seq, eos_ids, num_eos, s));
+    // the reference's sampler state: LCG seed 12345 per call (generate.h:36)
+    if (sampling) {
+        TRY(launch_set_sampling(m->st, temperature, repetition_penalty, 12345u, prompt_len, s));
+        JYC_CUDA(cudaMemsetAsync(m->stag, 0xFF, (size_t)m->V * sizeof(unsigned int), s));
+        JYC_CUDA(cudaMemsetAsync(m->stag + m->V, 0, (size_t)m->V * sizeof(unsigned int), s));
+    }
     TRY(run_prefill(m, 0, prompt_len, s));
+    if (sampling) TRY(launch_resample_last(m->st, m->logits, m->stag, m->V, m->tokens, s));
     // decode: one step per token; the state guard turns surplus steps into no-ops
+    // (the decode kernel samples in its head phase; the per-op step re-picks)
+    auto step = [&]() -> int {
+        TRY(decode_step(m, s));
+        if (sampling && !m->mega) TRY(launch_resample_last(m->st, m->logits, m->stag, m->V, m->tokens, s));
+        return JYC_OK;
+    };
     const int max_steps = std::min(max_new_tokens, m->max_seq - prompt_len) - 1;
     int len = prompt_len;
     if (!cb) {
-        for (int i = 0; i < max_steps; i++) TRY(decode_step(m, s));
+        for (int i = 0; i < max_steps; i++) TRY(step());
         DevState hs;
         JYC_CUDA(cudaMemcpyAsync(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
         JYC_CUDA(cudaStreamSynchronize(s));
@@ -770,7 +785,7 @@ JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, co
         len = hs.len;
         if (!hs.active || done_steps >= max_steps) return len;
         const int n = std::min(block, max_steps - done_steps);
-        for (int i = 0; i < n; i++) TRY(decode_step(m, s));
+        for (int i = 0; i < n; i++) TRY(step());
         done_steps += n;
         block = std::min(block * 2, 32);
     }

@@ -235,3 +235,61 @@ def test_argmax_ties_and_specials(cuda):
     v2d = dev(torch, v2)
     _capi.check(lib.jyc_argmax(v2d.data_ptr(), 17, out.data_ptr(), stream(torch)))
     assert int(host(out)[0]) == 0
+
+
+# (vocabulary, temperature, repetition penalty)
+SAMPLE_CASES = [
+    (17, 0.8, 1.0),        # fewer logits than sampler threads
+    (1000, 0.0, 1.3),      # penalty + greedy
+    (32000, 0.8, 1.3),     # configs[0] vocabulary
+    (151936, 0.8, 1.3),    # configs[1] vocabulary
+    (151936, 1.7, 1.0),    # flatter distribution
+    (128256, 0.3, 2.0),    # configs[3] vocabulary, peaked
+]
+
+
+@pytest.mark.parametrize("V,T,pen", SAMPLE_CASES)
+def test_sample_matches_oracle(cuda, oracle, V, T, pen):
+    """jyc_sample == jyo_sample (generate.h:50-77) over 12 consecutive draws
+    sharing one LCG state: same picks, same rng, the penalised logits bit-exact
+    and the probabilities written back within 4e-7 relative (CUDA's expf is
+    within 2 ulp, the host libm's within 1) above the smallest normal."""
+    torch = cuda
+    lib = _lib()
+    rs = np.random.default_rng(V * 7 + int(T * 10) + int(pen * 10))
+    p0 = 6
+    gen = rs.integers(0, min(V, 64), 40)                    # repeats on purpose
+    ids = np.concatenate([rs.integers(0, V, p0), gen, [-1, V]]).astype(np.int32)  # two ids outside [0, V)
+    ids_d = dev(torch, ids)
+    rng_h = C.c_uint(12345)
+    rng_d = torch.tensor([12345], dtype=torch.int32, device="cuda")
+    out_d = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for draw in range(12):
+        logits = (rs.standard_normal(V) * 4.0).astype(np.float32)
+        logits[rs.integers(0, V)] = 0.0                     # a zero logit: multiplied, stays 0
+        want = logits.copy()
+        n = len(ids) - (draw % 3)                           # growing / shrinking penalty ranges
+        pick = oracle.lib.jyo_sample(want.ctypes.data, V, T, pen, ids.ctypes.data, p0, n, C.byref(rng_h))
+        ld = dev(torch, logits)
+        _capi.check(lib.jyc_sample(ld.data_ptr(), V, T, pen, ids_d.data_ptr(), p0, n, rng_d.data_ptr(),
+                                   out_d.data_ptr(), stream(torch)))
+        assert int(host(out_d)[0]) == pick, f"draw {draw}"
+        assert int(host(rng_d).view(np.uint32)[0]) == rng_h.value
+        got = host(ld)
+        if T <= 0.0:
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        else:
+            # (+ the smallest normal: denormal results carry no relative
+            # accuracy; the sum they join is >= 1, the maximum's own term)
+            assert np.all(np.abs(got - want) <= 4e-7 * np.abs(want) + np.float32(2.0 ** -126))
+
+
+def test_sample_argument_errors(cuda):
+    torch = cuda
+    lib = _lib()
+    buf = torch.zeros(64, dtype=torch.float32, device="cuda")
+    p = buf.data_ptr()
+    s = stream(torch)
+    assert lib.jyc_sample(p, 0, f32(0.8), f32(1.0), None, 0, 0, p, p, s) == _capi.JYC_ERR_ARG
+    assert lib.jyc_sample(p, 16, f32(0.8), f32(1.3), None, 0, 4, p, p, s) == _capi.JYC_ERR_ARG
+    assert lib.jyc_sample(p, 16, f32(0.8), f32(1.3), p, 5, 4, p, p, s) == _capi.JYC_ERR_ARG
