@@ -6,6 +6,8 @@
 #include <vector>
 
 #include "kernels.cuh"
+#include "mega.cuh"
+#include "tcgemm.cuh"
 
 using namespace jyc;
 
@@ -53,6 +55,28 @@ JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d, 
     clear_error();
     if (!A || !qs || !d || !C) return arg_error("matmul_q8: null pointer");
     if (m <= 0 || n <= 0 || k <= 0 || k % 32) return arg_error("matmul_q8: need m,n > 0 and k % 32 == 0");
+    if (m >= kTcMinRows) {
+        // a real contraction: tcgen05 tiles of 128 weight rows x up to 128 rows of A
+        cudaStream_t s = S(stream);
+        const int N = tc_token_tile(m);
+        Scratch sc(s);
+        __half* xs = nullptr;
+        int* xe = nullptr;
+        TRY(sc.get(&xs, tc_split_halves(m, N, k)));
+        TRY(sc.get(&xe, (size_t)tc_padded_tokens(m, N)));
+        TRY(launch_tc_split(A, k, m, k, nullptr, 0.0f, N, xs, xe, s));
+        TcGemm g{};
+        g.qs = qs; g.d = d; g.n = n; g.k = k; g.xs = xs; g.xe = xe; g.T = m; g.N = N;
+        g.y = C; g.ldy = n; g.err = device_error_word();
+        g.splits = tc_plan_splits(n, k, m, N, 16);
+        if (g.splits > 1) {
+            const size_t tiles = (size_t)((n + kTcRows - 1) / kTcRows) * ((m + N - 1) / N);
+            TRY(sc.get(&g.part, (size_t)g.splits * m * n));
+            TRY(sc.get(&g.cnt, tiles));
+            JYC_CUDA(cudaMemsetAsync(g.cnt, 0, tiles * sizeof(unsigned int), s));
+        }
+        return launch_tc_gemm(g, TC_STORE, s);
+    }
     for (int r0 = 0; r0 < m; r0 += 8) {
         GemvArgs g{};
         g.x = A + (size_t)r0 * k; g.ldx = k; g.m = std::min(8, m - r0); g.n = n; g.k = k;
