@@ -58,17 +58,21 @@ JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d, 
     if (m >= kTcMinRows) {
         // a real contraction: tcgen05 tiles of 128 weight rows x up to 128 rows of A
         cudaStream_t s = S(stream);
-        const int N = tc_token_tile(m);
+        int N = 0, splits = 1;
+        tc_plan(n, k, m, kTcMaxSplits, &N, &splits);
         Scratch sc(s);
         __half* xs = nullptr;
         int* xe = nullptr;
         TRY(sc.get(&xs, tc_split_halves(m, N, k)));
         TRY(sc.get(&xe, (size_t)tc_padded_tokens(m, N)));
+        uint8_t* rexp = nullptr;
+        TRY(sc.get(&rexp, (size_t)n));
+        TRY(launch_tc_rowexp(d, n, k, rexp, s));
         TRY(launch_tc_split(A, k, m, k, nullptr, 0.0f, N, xs, xe, s));
         TcGemm g{};
-        g.qs = qs; g.d = d; g.n = n; g.k = k; g.xs = xs; g.xe = xe; g.T = m; g.N = N;
+        g.qs = qs; g.d = d; g.rexp = rexp; g.n = n; g.k = k; g.xs = xs; g.xe = xe; g.T = m; g.N = N;
         g.y = C; g.ldy = n; g.err = device_error_word();
-        g.splits = tc_plan_splits(n, k, m, N, 16);
+        g.splits = splits;
         if (g.splits > 1) {
             const size_t tiles = (size_t)((n + kTcRows - 1) / kTcRows) * ((m + N - 1) / N);
             TRY(sc.get(&g.part, (size_t)g.splits * m * n));

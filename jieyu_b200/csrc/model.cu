@@ -20,6 +20,7 @@
 
 #include "mega.cuh"
 #include "prefill.cuh"
+#include "tcgemm.cuh"
 
 using namespace jyc;
 
@@ -32,6 +33,7 @@ struct DevMat {  // one weight matrix on the device, [n][k]
     uint16_t* d = nullptr;
     uint8_t* tq = nullptr;   // Q8: tiled copy (decode megakernel), when `tiled`
     uint16_t* td = nullptr;
+    uint8_t* rexp = nullptr; // Q8: per-row exponent of the largest scale (tensor-core path)
     float* f = nullptr;
     int n = 0, k = 0;
     bool tiled = false;
@@ -106,8 +108,13 @@ struct jyc_model {
     unsigned char* tp_region = nullptr;
     int tp_size = 0, tp_rank = 0, tp_so = 1, tp_sd = 1;
     std::vector<void*> tp_mapped;
-    int8_t* pf_dig = nullptr;  // token digit planes of the batched prefill
-    float* pf_sx = nullptr;
+    // batched prefill on the tensor cores: split activations, per-token
+    // exponents, split-K partial sums and their arrival counters
+    __half* tc_xs = nullptr;
+    int* tc_xe = nullptr;
+    float* tc_part = nullptr;
+    size_t tc_part_floats = 0;
+    unsigned int* tc_cnt = nullptr;
     MegaLayer* d_mlayers = nullptr;
     DevState* st = nullptr;
     int* tokens = nullptr;  // [max_seq + 1]
@@ -431,10 +438,9 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     JYC_CUDA(cudaMemsetAsync(m->v8, 0, kvn * m->hd, m->stream));
     JYC_CUDA(cudaMemsetAsync(m->ks, 0, kvn * 4, m->stream));
     JYC_CUDA(cudaMemsetAsync(m->vs, 0, kvn * 4, m->stream));
-    // batched prefill (tensor-core token tiles) for models in the tiled layout
-    const bool pf_ok = m->tiled && m->D % kPfRows == 0 && m->nqkv % kPfRows == 0 && (2 * m->F) % kPfRows == 0 &&
-                       pf_attention_supported(m->H, m->KV, m->hd);
-    m->pf_rows = pf_ok ? std::min(kPfChunk, (m->max_seq + kPfTok - 1) / kPfTok * kPfTok) : 0;
+    // batched prefill (tcgen05 token tiles) for Q8_0 models
+    const bool pf_ok = m->wtype == W_Q8 && pf_attention_supported(m->H, m->KV, m->hd);
+    m->pf_rows = pf_ok ? std::min(kPfChunk, m->max_seq) : 0;
     const size_t arows = std::max(kMT, m->pf_rows);
     TRY(m->alloc(&m->X, arows * m->D));
     TRY(m->alloc(&m->qkv, arows * m->nqkv));
@@ -447,9 +453,28 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     TRY(m->alloc(&m->qsc, arows * m->H));
     if (m->pf_rows) {
         const int kmax = std::max({m->D, m->q_dim, m->F});
-        TRY(m->alloc(&m->pf_dig, pf_digit_bytes(m->pf_rows, kmax)));
-        TRY(m->alloc(&m->pf_sx, pf_scale_floats(m->pf_rows, kmax)));
+        const int nmax = std::max({m->nqkv, m->D, 2 * m->F, m->V});
+        const int N = tc_token_tile(m->pf_rows);
+        TRY(m->alloc(&m->tc_xs, tc_split_halves(m->pf_rows, N, kmax)));
+        TRY(m->alloc(&m->tc_xe, (size_t)tc_padded_tokens(m->pf_rows, N)));
+        m->tc_part_floats = (size_t)kTcMaxSplits * m->pf_rows * std::max({m->nqkv, m->D});
+        TRY(m->alloc(&m->tc_part, m->tc_part_floats));
+        const size_t tiles = (size_t)((nmax + kTcRows - 1) / kTcRows) * ((m->pf_rows + 15) / 16);
+        TRY(m->alloc(&m->tc_cnt, tiles));
+        JYC_CUDA(cudaMemsetAsync(m->tc_cnt, 0, tiles * sizeof(unsigned int), m->stream));
         TRY(prepare_pf_kernels());
+        TRY(prepare_tc_kernels());
+        // per-row scale exponents of every matrix the tensor-core path reads
+        auto rowexp = [&](DevMat& w) -> int {
+            TRY(m->alloc(&w.rexp, (size_t)w.n));
+            return launch_tc_rowexp(w.d, w.n, w.k, w.rexp, m->stream);
+        };
+        for (DevLayer& ly : m->layers) {
+            TRY(rowexp(ly.qkv));
+            TRY(rowexp(ly.o));
+            TRY(rowexp(ly.gateup));
+            TRY(rowexp(ly.down));
+        }
     }
     // split-K plan of the generic attention: ~2 CTAs per SM over the kv heads
     const int target = std::max(1, 296 / m->KV);
@@ -550,6 +575,24 @@ int run_head(jyc_model* m, int row, cudaStream_t s) {
     return JYC_OK;
 }
 
+// Y = X . W^T over `rows` tokens on the tensor cores (split-K when the tiles
+// alone do not fill the GPU): RMSNorm (norm != null) + fp16 hi/lo split of X,
+// then the tcgen05 GEMM with the epilogue `epi`.
+int run_tc_gemm(jyc_model* m, const DevMat& w, const float* x, int ldx, int rows, const float* norm, float* y,
+                int ldy, const float* bias, int epi, int* err, cudaStream_t s) {
+    const int cap = (int)std::min<size_t>(kTcMaxSplits, m->tc_part_floats / ((size_t)rows * w.n));
+    int N = 0, splits = 1;
+    tc_plan(w.n, w.k, rows, std::max(1, cap), &N, &splits);
+    TRY(launch_tc_split(x, ldx, rows, w.k, norm, 1e-5f, N, m->tc_xs, m->tc_xe, s));
+    TcGemm g{};
+    g.qs = w.qs; g.d = w.d; g.rexp = w.rexp; g.n = w.n; g.k = w.k;
+    g.xs = m->tc_xs; g.xe = m->tc_xe; g.T = rows; g.N = N;
+    g.y = y; g.ldy = ldy; g.bias = bias; g.err = err;
+    g.splits = splits;
+    g.part = m->tc_part; g.cnt = m->tc_cnt;
+    return launch_tc_gemm(g, epi, s);
+}
+
 // Forward of n tokens already in m->tokens[start..start+n) in chunks of kMT,
 // then the head on the last row (state must hold len == start+n).
 // Batched prefill of tokens [start, start + n) in passes of pf_rows tokens:
@@ -565,16 +608,11 @@ int run_prefill_batched(jyc_model* m, int start, int n, cudaStream_t s) {
                          m->D, m->X, s));
         auto gemm = [&](const DevMat& w, const float* x, int ldx, const float* norm, float* y, int ldy,
                         const float* bias, int epi) -> int {
-            TRY(launch_pf_digitize(x, ldx, rows, w.k, norm, 1e-5f, m->pf_dig, m->pf_sx, s));
-            PfGemm g{};
-            g.qs = w.tq; g.d = w.td; g.n = w.n; g.k = w.k;
-            g.dig = m->pf_dig; g.sx = m->pf_sx; g.T = rows;
-            g.y = y; g.ldy = ldy; g.bias = bias; g.err = err;
-            return launch_pf_gemm(g, epi, s);
+            return run_tc_gemm(m, w, x, ldx, rows, norm, y, ldy, bias, epi, err, s);
         };
         for (int l = 0; l < m->L; l++) {
             const DevLayer& ly = m->layers[l];
-            TRY(gemm(ly.qkv, m->X, m->D, ly.rms1, m->qkv, m->nqkv, ly.bias, ly.bias ? PF_BIAS : PF_STORE));
+            TRY(gemm(ly.qkv, m->X, m->D, ly.rms1, m->qkv, m->nqkv, ly.bias, ly.bias ? TC_BIAS : TC_STORE));
             RopeQuantArgs rq{};
             rq.q = m->qkv; rq.k = m->qkv + m->q_dim; rq.v = m->qkv + m->q_dim + m->kv_dim;
             rq.ldq = m->nqkv; rq.rows = rows; rq.H = m->H; rq.KV = m->KV; rq.hd = m->hd;
@@ -587,9 +625,9 @@ int run_prefill_batched(jyc_model* m, int start, int n, cudaStream_t s) {
             at.max_seq = m->max_seq; at.H = m->H; at.KV = m->KV; at.hd = m->hd; at.T = rows;
             at.pos0 = start + c; at.scale = 1.0f / sqrtf((float)m->hd); at.out = m->attn;
             TRY(launch_pf_attention(at, s));
-            TRY(gemm(ly.o, m->attn, m->q_dim, nullptr, m->X, m->D, nullptr, PF_RESID));
-            TRY(gemm(ly.gateup, m->X, m->D, ly.rms2, m->h, m->F, nullptr, PF_SWIGLU));
-            TRY(gemm(ly.down, m->h, m->F, nullptr, m->X, m->D, nullptr, PF_RESID));
+            TRY(gemm(ly.o, m->attn, m->q_dim, nullptr, m->X, m->D, nullptr, TC_RESID));
+            TRY(gemm(ly.gateup, m->X, m->D, ly.rms2, m->h, m->F, nullptr, TC_SWIGLU));
+            TRY(gemm(ly.down, m->h, m->F, nullptr, m->X, m->D, nullptr, TC_RESID));
         }
         last_rows = rows;
     }

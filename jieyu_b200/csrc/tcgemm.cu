@@ -7,17 +7,21 @@
 //              K chunk brings its hi and lo planes, already in the 128-byte
 //              swizzled K-major layout the MMA reads;
 //   warp 1     one thread issues the MMAs: per 16-wide K step
-//              D += Whi.Xhi + Whi.Xlo + Wlo.Xhi (tcgen05.mma kind::f16, fp32
-//              accumulate, M=128, N tokens), then tcgen05.commit frees the
-//              stage; the last commit signals the accumulator;
+//              [D | E] += Whi.[Xhi | Xlo] (one MMA of width 2N) and
+//              E += Wlo.Xhi (tcgen05.mma kind::f16, fp32 accumulators in
+//              tensor memory, M=128) into the accumulator set of the chunk's
+//              group, then tcgen05.commit frees the stage and, after the
+//              group's last chunk, signals the set;
 //   warps 2-9  converters: each thread dequantises one 32-weight block of one
 //              row per chunk (q * d * 2^S exactly in fp32, split into fp16 hi
 //              and lo), stores both into the swizzled A planes of the stage
 //              and arrives on the stage's barrier; loads run 3 chunks ahead
-//              in registers. After the K loop they are the epilogue: lanes of
-//              tensor memory = weight rows, columns = tokens (tcgen05.ld),
-//              unscaled by 2^-S_row 2^-s_token, then stored (+ bias, residual
-//              or SwiGLU of interleaved gate/up rows). With K split over CTAs
+//              in registers. They also drain every finished chunk's
+//              accumulator set (tcgen05.ld: lanes = weight rows, columns =
+//              tokens) into fp32 registers, and after the K loop run the
+//              epilogue: unscale by 2^-S_row 2^-s_token, then store (+ bias,
+//              residual or SwiGLU of interleaved gate/up rows) through a
+//              shared-memory tile in coalesced rows. With K split over CTAs
 //              each writes its partial tile and the last to arrive sums the
 //              partials in split order (deterministic) and runs the epilogue.
 // Every wait is bounded and reports error word 9.
@@ -35,15 +39,19 @@ constexpr int kThreads = 320;
 constexpr int kPlaneA = kTcRows * 128;  // one A plane (hi or lo) of a chunk: 128 rows x 128 bytes
 constexpr int kSmemBudget = 200 * 1024;
 constexpr int kErrTc = 9;
+constexpr int kGroup = 2;  // K chunks accumulated per tensor-memory set before the drain
 
 template <int N>
 struct TcCfg {
     static constexpr int kPlaneB = N * 128;
     static constexpr int kStage = 2 * kPlaneA + 2 * kPlaneB;
     static constexpr int kStages = (kSmemBudget / kStage) > 4 ? 4 : (kSmemBudget / kStage);
-    static constexpr int kCols = N < 32 ? 32 : N;  // tensor-memory columns: a power of two >= 32
-    // alignment slack + stages + barriers + tmem slot/flag + row maxima
-    static constexpr int kSmem = 1024 + kStages * kStage + 8 * (3 * kStages + 1) + 16 + 4 * kTcRows;
+    // tensor-memory columns (a power of two >= 32): two accumulator sets of
+    // [N hi.hi columns | N hi.lo + lo.hi columns]; the corrections accumulate
+    // apart so the large accumulator takes one rounding per K step, not three
+    static constexpr int kCols = 4 * N < 32 ? 32 : 4 * N;
+    // alignment slack + stages + barriers + tmem slot/flags
+    static constexpr int kSmem = 1024 + kStages * kStage + 8 * (3 * kStages + 4) + 16;
 };
 
 // ---- tcgen05 / tensor-memory helpers ---------------------------------------
@@ -85,6 +93,26 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
     v[0] = __uint_as_float(r0); v[1] = __uint_as_float(r1); v[2] = __uint_as_float(r2); v[3] = __uint_as_float(r3);
     v[4] = __uint_as_float(r4); v[5] = __uint_as_float(r5); v[6] = __uint_as_float(r6); v[7] = __uint_as_float(r7);
 }
+// 16 columns at ta and 16 at tb of this warp's 32 lanes, one wait for both
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* a, float* b) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, "
+        "[%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(ta), "r"(tb)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        a[i] = __uint_as_float(r[i]);
+        b[i] = __uint_as_float(r[16 + i]);
+    }
+}
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (stride byte offset), sm_100 descriptor version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -101,6 +129,7 @@ __device__ __forceinline__ void named_sync_conv() { asm volatile("bar.sync 1, 25
 // 2^e for e in [-126, 127], exactly
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 // copy without an L2 hint (the token planes are re-read by every row tile)
 __device__ __forceinline__ void bulk_g2s_keep(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -108,15 +137,25 @@ __device__ __forceinline__ void bulk_g2s_keep(void* dst, const void* src, uint32
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-// 8 fp32 values (already scaled) -> 16 bytes of fp16 hi and 16 bytes of lo
+// 8 fp32 values (already scaled below 2^15) -> 16 bytes of fp16 hi and 16
+// bytes of lo. Veltkamp's split (c = f (2^13 + 1), hi = c - (c - f)) rounds f
+// to its leading 11 bits in fp32, so hi converts to fp16 exactly and
+// lo = f - hi is exact in fp32 (the fp16 conversion of lo keeps 11 of its at
+// most 13 bits: all of them for the 18-bit weight products).
 __device__ __forceinline__ void split8(const float* f, uint4& hi, uint4& lo) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const __half2 hh = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-        const float2 hf = __half22float2(hh);
-        h[i] = h2u(hh);
-        l[i] = h2u(__floats2half2_rn(__fsub_rn(f[2 * i], hf.x), __fsub_rn(f[2 * i + 1], hf.y)));
+        float hv[2], lv[2];
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const float x = f[2 * i + e];
+            const float c = __fmul_rn(x, 8193.0f);
+            hv[e] = __fsub_rn(c, __fsub_rn(c, x));
+            lv[e] = __fsub_rn(x, hv[e]);
+        }
+        h[i] = h2u(__floats2half2_rn(hv[0], hv[1]));
+        l[i] = h2u(__floats2half2_rn(lv[0], lv[1]));
     }
     hi = make_uint4(h[0], h[1], h[2], h[3]);
     lo = make_uint4(l[0], l[1], l[2], l[3]);
@@ -125,22 +164,31 @@ __device__ __forceinline__ void split8(const float* f, uint4& hi, uint4& lo) {
 template <int N, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
     using C = TcCfg<N>;
+    constexpr int CH = N / 2;  // accumulator columns (tokens) per converter thread
     extern __shared__ unsigned char tc_smraw[];
     // the 128-byte swizzle is a function of the address bits: 1024-byte aligned tiles
     unsigned char* sm = tc_smraw + ((1024u - (smem_u32(tc_smraw) & 1023u)) & 1023u);
     uint64_t* afull = reinterpret_cast<uint64_t*>(sm + C::kStages * C::kStage);  // converters done (256 arrivals)
     uint64_t* bfull = afull + C::kStages;                                         // token planes landed (tx)
     uint64_t* empty = bfull + C::kStages;                                         // MMAs of the stage done
-    uint64_t* accf = empty + C::kStages;                                          // accumulator complete
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accf + 1);
+    uint64_t* accf = empty + C::kStages;   // [2] accumulator set b holds a finished chunk (MMA commit)
+    uint64_t* accfree = accf + 2;          // [2] accumulator set b drained (256 arrivals)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accfree + 2);
     unsigned int* s_flag = s_tmem + 1;
-    unsigned int* s_rmax = s_tmem + 4;  // [128] max |d| (fp16 magnitude bits) per row
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 2);  // a bounded wait gave up
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x, tt = blockIdx.y, z = blockIdx.z;
     const int nkc = (p.k + kTcKC - 1) / kTcKC;
     const int per = (nkc + p.splits - 1) / p.splits;
     const int c0 = z * per, nch = min(nkc, c0 + per) - c0;  // the host plan leaves no split empty
+    // bounded wait; after any give-up in this CTA every later wait is skipped
+    auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (*s_abort) return false;
+        if (mbar_wait_err(bar, parity, p.err, kErrTc)) return true;
+        *s_abort = 1;
+        return false;
+    };
 
     if (tid == 0) {
         for (int s = 0; s < C::kStages; s++) {
@@ -148,10 +196,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
             mbar_init(&bfull[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accf, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&accfree[b], 256);
+        }
+        *s_abort = 0;
         mbar_fence_init();
     }
-    if (tid >= 64 && tid < 64 + kTcRows) s_rmax[tid - 64] = 0u;
     if (warp == 0) {
         __syncwarp();
         tmem_alloc(s_tmem, C::kCols);
@@ -168,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
             int issued = 0;
             for (int j = 0; j < nch; j++) {
                 const int s = j % C::kStages;
-                if (j >= C::kStages && !mbar_wait_err(&empty[s], ((j / C::kStages) - 1) & 1, p.err, kErrTc)) break;
+                if (j >= C::kStages && !wait(&empty[s], ((j / C::kStages) - 1) & 1)) break;
                 mbar_expect_tx(&bfull[s], 2 * C::kPlaneB);
                 bulk_g2s_keep(sm + s * C::kStage + 2 * kPlaneA, src + (size_t)j * 2 * C::kPlaneB, 2 * C::kPlaneB,
                               &bfull[s]);
@@ -180,26 +231,31 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            // B hi and lo planes are adjacent rows of one K-major tile: a single
+            // MMA of width 2N gives Whi.Xhi (columns [0, N)) and Whi.Xlo
+            // (columns [N, 2N)); Wlo.Xhi then accumulates into [N, 2N)
+            constexpr uint32_t idesc2 = idesc_f16<2 * N>();
             constexpr uint32_t idesc = idesc_f16<N>();
             for (int j = 0; j < nch; j++) {
-                const int s = j % C::kStages;
+                const int s = j % C::kStages, g = j / kGroup, b = g & 1;
+                const bool first = j % kGroup == 0;  // the group's first chunk overwrites the set
                 const uint32_t ph = (j / C::kStages) & 1;
-                if (!mbar_wait_err(&afull[s], ph, p.err, kErrTc) || !mbar_wait_err(&bfull[s], ph, p.err, kErrTc))
-                    break;
+                if (first && g >= 2 && !wait(&accfree[b], ((g >> 1) - 1) & 1)) break;
+                if (!wait(&afull[s], ph) || !wait(&bfull[s], ph)) break;
                 tc_fence_after();
                 const uint32_t st = smem_u32(sm + s * C::kStage);
                 const uint64_t ah = sw128_desc(st), al = sw128_desc(st + kPlaneA);
-                const uint64_t bh = sw128_desc(st + 2 * kPlaneA), bl = sw128_desc(st + 2 * kPlaneA + C::kPlaneB);
+                const uint64_t bh = sw128_desc(st + 2 * kPlaneA);
+                const uint32_t dm = tmem + (uint32_t)(2 * N * b), dc = dm + N;
 #pragma unroll
                 for (int ks = 0; ks < kTcKC / 16; ks++) {
                     const uint64_t o = 2 * ks;  // 32 bytes further along K, in 16-byte units
-                    tc_mma_f16(tmem, ah + o, bh + o, idesc, (j | ks) != 0);
-                    tc_mma_f16(tmem, ah + o, bl + o, idesc, 1u);
-                    tc_mma_f16(tmem, al + o, bh + o, idesc, 1u);
+                    tc_mma_f16(dm, ah + o, bh + o, idesc2, !first || ks != 0);
+                    tc_mma_f16(dc, al + o, bh + o, idesc, 1u);
                 }
                 tc_commit(&empty[s]);
+                if (j % kGroup == kGroup - 1 || j == nch - 1) tc_commit(&accf[b]);
             }
-            tc_commit(accf);  // also after an error: the epilogue waits on it
         }
     } else {
         // ---------------- converters ----------------
@@ -210,17 +266,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
         const int nb = p.k >> 5;
         const uint8_t* qrow = p.qs + (size_t)(rv ? R : 0) * p.k;
         const uint16_t* drow = p.d + (size_t)(rv ? R : 0) * nb;
-        {
-            unsigned int mx = 0u;
-            if (rv) {
-                const int bend = min(nb, 2 * (c0 + nch));
-                for (int b = 2 * c0 + h; b < bend; b += 2) mx = max(mx, (unsigned int)(__ldg(drow + b) & 0x7FFFu));
-            }
-            atomicMax(&s_rmax[r], mx);
-        }
-        named_sync_conv();
         // rows scaled by 2^S with S = 22 - exponent field of max |d|: 127 max|d| 2^S < 2^15
-        const float rup = exp2i(22 - (int)(s_rmax[r] >> 10));
+        const float rup = exp2i(22 - (rv ? (int)__ldg(p.rexp + R) : 0));
         uint4 qa[4][2];
         uint16_t dd[4];
         auto load = [&](int j, uint4* q, uint16_t& dv) {
@@ -235,33 +282,76 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
                 dv = 0;
             }
         };
-        bool ok = true;
         auto convert = [&](int j, const uint4* q, uint16_t dv) {
             const int s = j % C::kStages;
-            if (j >= C::kStages && ok && !mbar_wait_err(&empty[s], ((j / C::kStages) - 1) & 1, p.err, kErrTc))
-                ok = false;
+            if (j >= C::kStages) wait(&empty[s], ((j / C::kStages) - 1) & 1);
             unsigned char* ah = sm + s * C::kStage + r * 128;
-            const float ds = __fmul_rn(h2f(dv), rup);
+            // packed half2 arithmetic, two weights per instruction:
+            // q = (0x6400 | u) - 1152 exactly (fp16 1024 + u, u = q + 128);
+            // hi = fp16(q d_s) rounded to nearest; lo = fma(q, d_s, -hi) is the
+            // exact residual (q d_s has at most 18 significant bits)
+            const __half2 ds2 = __float2half2_rn(__fmul_rn(h2f(dv), rup));
+            const __half2 off = __float2half2_rn(1152.0f);
             const uint32_t* w = reinterpret_cast<const uint32_t*>(q);
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                float f[8];
-                u8x4_to_f32(w[2 * c], f);
-                u8x4_to_f32(w[2 * c + 1], f + 4);
+                uint32_t hw[4], lw[4];
 #pragma unroll
-                for (int i = 0; i < 8; i++) f[i] = __fmul_rn(f[i], ds);
-                uint4 hi, lo;
-                split8(f, hi, lo);
+                for (int i = 0; i < 4; i++) {
+                    const uint32_t pk = __byte_perm(w[2 * c + (i >> 1)], 0x64646464u, (i & 1) ? 0x4342u : 0x4140u);
+                    const __half2 q2 = __hsub2(u2h(pk), off);
+                    const __half2 h2 = __hmul2_rn(q2, ds2);
+                    hw[i] = h2u(h2);
+                    lw[i] = h2u(__hfma2(q2, ds2, __hneg2(h2)));
+                }
                 const int pos = ((4 * h + c) ^ (r & 7)) * 16;
-                *reinterpret_cast<uint4*>(ah + pos) = hi;
-                *reinterpret_cast<uint4*>(ah + kPlaneA + pos) = lo;
+                *reinterpret_cast<uint4*>(ah + pos) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4*>(ah + kPlaneA + pos) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
             }
             fence_proxy_async_smem();
             mbar_arrive(&afull[s]);
         };
+        // The tensor cores accumulate in fp32 with truncation; over a long K
+        // that biases sums toward zero. Each group of kGroup chunks therefore
+        // lands in one of two accumulator sets, and these threads add it into
+        // fp32 registers (round to nearest) one group later, while the MMAs
+        // fill the other set.
+        const int q4 = warp & 3, half = (warp - 2) >> 2;  // lane quadrant, column half
+        const int re = 32 * q4 + lane;
+        const uint32_t tq = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)(half * CH);
+        float acc[CH];
+#pragma unroll
+        for (int c = 0; c < CH; c++) acc[c] = 0.0f;
+        auto drain = [&](int g) {
+            const int b = g & 1;
+            wait(&accf[b], (g >> 1) & 1);
+            tc_fence_after();
+            const uint32_t ta = tq + (uint32_t)(2 * N * b);
+            if (CH % 16 == 0) {
+#pragma unroll
+                for (int c = 0; c < CH; c += 16) {
+                    float mv[16], cv[16];
+                    tmem_ld16x2(ta + (uint32_t)c, ta + (uint32_t)(N + c), mv, cv);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc[c + i] = __fadd_rn(acc[c + i], __fadd_rn(mv[i], cv[i]));
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < CH; c += 8) {
+                    float mv[8], cv[8];
+                    tmem_ld8(ta + (uint32_t)c, mv);
+                    tmem_ld8(ta + (uint32_t)(N + c), cv);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) acc[c + i] = __fadd_rn(acc[c + i], __fadd_rn(mv[i], cv[i]));
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&accfree[b]);
+        };
         if (nch > 0) load(0, qa[0], dd[0]);
         if (nch > 1) load(1, qa[1], dd[1]);
         if (nch > 2) load(2, qa[2], dd[2]);
+        int drained = 0;  // next group to drain
         for (int j0 = 0; j0 < nch; j0 += 4) {
 #pragma unroll
             for (int u = 0; u < 4; u++) {
@@ -269,60 +359,89 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
                 if (j < nch) {
                     if (j + 3 < nch) load(j + 3, qa[(u + 3) & 3], dd[(u + 3) & 3]);
                     convert(j, qa[u], dd[u]);
+                    // a group's chunks are converted: drain the group before it
+                    if (j % kGroup == kGroup - 1 && j >= kGroup) drain(drained++);
                 }
             }
         }
+        while (drained * kGroup < nch) drain(drained++);
 
         // ---------------- epilogue ----------------
-        mbar_wait_err(accf, 0, p.err, kErrTc);
-        tc_fence_after();
-        constexpr int CH = N / 2;  // columns (tokens) per warp: two warps share a lane quadrant
-        const int q4 = warp & 3, half = (warp - 2) >> 2;
-        const int re = 32 * q4 + lane, Re = mt * kTcRows + re;
-        const bool rev = Re < p.n;
-        const float rdown = exp2i((int)(s_rmax[re] >> 10) - 22);
-        const int t0 = tt * N + half * CH;
-        const uint32_t tq = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)(half * CH);
-        // final values of 8 columns -> output (bias / residual / SwiGLU)
-        auto store8 = [&](int c, const float* v) {
+        // 1. register accumulators (thread = row re, tokens of its column half)
+        //    -> scaled fp32 tile [N tokens][128 rows] in the idle stage memory
+        //    (every MMA has completed: the last drain waited for it)
+        float* stile = reinterpret_cast<float*>(sm);
+        {
+            const int Re = mt * kTcRows + re;
+            const float rdown = exp2i((Re < p.n ? (int)__ldg(p.rexp + Re) : 0) - 22);
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int t = t0 + c + i;
-                const bool ok_t = t < p.T;
-                if (EPI == TC_SWIGLU) {
-                    // rows 2j (gate) and 2j+1 (up) sit in adjacent lanes
-                    const float upv = __shfl_down_sync(0xffffffffu, v[i], 1);
-                    if ((lane & 1) == 0 && rev && ok_t)
-                        p.y[(size_t)t * p.ldy + (Re >> 1)] = __fmul_rn(silu_ref(v[i]), upv);
-                } else if (rev && ok_t) {
-                    float* yp = p.y + (size_t)t * p.ldy + Re;
-                    if (EPI == TC_STORE) *yp = v[i];
-                    if (EPI == TC_BIAS) *yp = __fadd_rn(v[i], __ldg(p.bias + Re));
-                    if (EPI == TC_RESID) *yp = __fadd_rn(*yp, v[i]);
+            for (int c = 0; c < CH; c++) {
+                const int tl = half * CH + c;
+                stile[tl * kTcRows + re] = __fmul_rn(__fmul_rn(acc[c], rdown), exp2i(-__ldg(p.xe + tt * N + tl)));
+            }
+        }
+        named_sync_conv();
+        // 2. coalesced row-major passes: element e = ct + 256 i is (token e / 128,
+        //    row e % 128); groups of 16 keep 16 loads in flight per thread
+        constexpr int kPer = N * kTcRows / 256, kG = kPer < 16 ? kPer : 16;
+        const int rl = ct & (kTcRows - 1), Rg = mt * kTcRows + rl;
+        const bool rok = Rg < p.n;
+        auto tok_of = [&](int i) { return tt * N + ((ct + 256 * i) >> 7); };
+        auto epilogue = [&](int i0, const float* v) {
+            if (EPI == TC_RESID) {
+                float old[kG];
+#pragma unroll
+                for (int u = 0; u < kG; u++) {
+                    const int t = tok_of(i0 + u);
+                    old[u] = (rok && t < p.T) ? p.y[(size_t)t * p.ldy + Rg] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < kG; u++) {
+                    const int t = tok_of(i0 + u);
+                    if (rok && t < p.T) p.y[(size_t)t * p.ldy + Rg] = __fadd_rn(old[u], v[u]);
+                }
+            } else {
+                const float b = (EPI == TC_BIAS && rok) ? __ldg(p.bias + Rg) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < kG; u++) {
+                    const int t = tok_of(i0 + u);
+                    const bool ok_t = t < p.T;
+                    if (EPI == TC_SWIGLU) {
+                        // rows 2j (gate) and 2j+1 (up) sit in adjacent lanes
+                        const float upv = __shfl_down_sync(0xffffffffu, v[u], 1);
+                        if ((lane & 1) == 0 && rok && ok_t)
+                            p.y[(size_t)t * p.ldy + (Rg >> 1)] = __fmul_rn(silu_ref(v[u]), upv);
+                    } else if (rok && ok_t) {
+                        p.y[(size_t)t * p.ldy + Rg] = EPI == TC_BIAS ? __fadd_rn(v[u], b) : v[u];
+                    }
                 }
             }
         };
-        // accumulator columns c..c+7, unscaled by 2^-S_row 2^-s_token
-        auto load8 = [&](int c, float* v) {
-            tmem_ld8(tq + (uint32_t)c, v);
-#pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], rdown), exp2i(-__ldg(p.xe + t0 + c + i)));
-        };
-        if (p.splits == 1) {
+        if (p.splits == 1 && EPI == TC_SWIGLU) {
+            // thread = one (gate, up) row pair of tokens ct / 64 + 4 i: one silu per pair
+            const int pr = ct & 63, R2 = mt * (kTcRows / 2) + pr;
+            const bool pok = 2 * R2 < p.n;
+#pragma unroll 4
+            for (int tl = ct >> 6; tl < N; tl += 4) {
+                const int t = tt * N + tl;
+                const float2 gu = *reinterpret_cast<const float2*>(stile + tl * kTcRows + 2 * pr);
+                if (pok && t < p.T) p.y[(size_t)t * p.ldy + R2] = __fmul_rn(silu_ref(gu.x), gu.y);
+            }
+        } else if (p.splits == 1) {
 #pragma unroll 1
-            for (int c = 0; c < CH; c += 8) {
-                float v[8];
-                load8(c, v);
-                store8(c, v);
+            for (int i0 = 0; i0 < kPer; i0 += kG) {
+                float v[kG];
+#pragma unroll
+                for (int u = 0; u < kG; u++) v[u] = stile[ct + 256 * (i0 + u)];
+                epilogue(i0, v);
             }
         } else {
+            // partial tile of this K range; the last CTA of the tile to arrive
+            // sums all of them in split order and runs the epilogue
 #pragma unroll 1
-            for (int c = 0; c < CH; c += 8) {
-                float v[8];
-                load8(c, v);
-#pragma unroll
-                for (int i = 0; i < 8; i++)
-                    if (rev && t0 + c + i < p.T) p.part[((size_t)z * p.T + t0 + c + i) * p.n + Re] = v[i];
+            for (int i = 0; i < kPer; i++) {
+                const int t = tok_of(i);
+                if (rok && t < p.T) p.part[((size_t)z * p.T + t) * p.n + Rg] = stile[ct + 256 * i];
             }
             __threadfence();
             named_sync_conv();
@@ -331,20 +450,36 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
                 *s_flag = (old == (unsigned int)(p.splits - 1)) ? 1u : 0u;
             }
             named_sync_conv();
-            if (*s_flag != 0u) {  // last of the tile's splits: sum them in split order
+            if (*s_flag != 0u) {
                 __threadfence();
 #pragma unroll 1
-                for (int c = 0; c < CH; c += 8) {
-                    float v[8];
+                for (int i0 = 0; i0 < kPer; i0 += kG) {
+                    float v[kG];
 #pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float sum = 0.0f;
-                        if (rev && t0 + c + i < p.T)
-                            for (int zz = 0; zz < p.splits; zz++)
-                                sum = __fadd_rn(sum, __ldcg(p.part + ((size_t)zz * p.T + t0 + c + i) * p.n + Re));
-                        v[i] = sum;
+                    for (int u = 0; u < kG; u++) v[u] = 0.0f;
+                    // per 8 elements: four splits' loads in flight before their in-order adds
+#pragma unroll
+                    for (int g0 = 0; g0 < kG; g0 += 8) {
+                        constexpr int kR = kG < 8 ? kG : 8;
+                        for (int z0 = 0; z0 < p.splits; z0 += 4) {
+                            float ld[4][kR];
+#pragma unroll
+                            for (int zi = 0; zi < 4; zi++)
+#pragma unroll
+                                for (int u = 0; u < kR; u++) {
+                                    const int t = tok_of(i0 + g0 + u);
+                                    ld[zi][u] = (rok && t < p.T && z0 + zi < p.splits)
+                                                    ? __ldcg(p.part + ((size_t)(z0 + zi) * p.T + t) * p.n + Rg)
+                                                    : 0.0f;
+                                }
+#pragma unroll
+                            for (int zi = 0; zi < 4; zi++)
+#pragma unroll
+                                for (int u = 0; u < kR; u++)
+                                    if (z0 + zi < p.splits) v[g0 + u] = __fadd_rn(v[g0 + u], ld[zi][u]);
+                        }
                     }
-                    store8(c, v);
+                    epilogue(i0, v);
                 }
                 if (ct == 0) p.cnt[mt * gridDim.y + tt] = 0u;
             }
@@ -432,6 +567,18 @@ __global__ void __launch_bounds__(256) tc_split_kernel(const float* x, int ldx, 
     }
 }
 
+// Per weight row: the fp16 exponent field of max |d| over its scales (one
+// warp per row).
+__global__ void __launch_bounds__(256) tc_rowexp_kernel(const uint16_t* d, int n, int nb, uint8_t* rexp) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= n) return;
+    unsigned int mx = 0u;
+    for (int b = lane; b < nb; b += 32) mx = max(mx, (unsigned int)(__ldg(d + (size_t)row * nb + b) & 0x7FFFu));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) rexp[row] = (uint8_t)(mx >> 10);
+}
+
 template <int N>
 int set_smem() {
     using C = TcCfg<N>;
@@ -469,25 +616,39 @@ size_t tc_split_halves(int T, int N, int k) {
     return (size_t)tc_padded_tokens(T, N) * nkc * 2 * kTcKC;
 }
 
-int tc_plan_splits(int n, int k, int T, int N, int max_splits) {
-    const int tiles = ((n + kTcRows - 1) / kTcRows) * ((T + N - 1) / N);
-    const int nkc = (k + kTcKC - 1) / kTcKC;
+void tc_plan(int n, int k, int T, int max_splits, int* N_out, int* splits_out) {
+    // Cost model in microseconds at ~1.9 GHz: a CTA pays a fixed ~3 us (tensor
+    // memory, barriers, pipeline fill, epilogue) plus per 64-wide K chunk the
+    // slower of its weight conversion + accumulator drain (~250 + 2.4 N
+    // cycles) and its 12 MMAs (128 x N x 16 each, ~6.35 N cycles); K splits
+    // add a partial-sum pass.
+    const int nkc = (k + kTcKC - 1) / kTcKC, mtiles = (n + kTcRows - 1) / kTcRows;
     const int sms = mega_num_ctas();
-    int best = 1;
-    double best_cost = 1e30;
-    for (int s = 1; s <= std::min(max_splits, nkc); s++) {
-        const int per = (nkc + s - 1) / s;
-        const int eff = (nkc + per - 1) / per;  // no empty split
-        if (eff != s) continue;
-        const int waves = (tiles * s + sms - 1) / sms;
-        // chunks of the slowest SM + a per-CTA fixed cost (~2 chunks) + the partial-sum pass
-        const double cost = (double)waves * (per + 2) + (s > 1 ? 1.0 + 0.1 * s : 0.0);
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
-            best = s;
+    double best = 1e30;
+    *N_out = tc_token_tile(T);
+    *splits_out = 1;
+    for (int N = 16; N <= tc_token_tile(T); N *= 2) {
+        const double chunk_us = std::max(250.0 + 2.4 * N, 6.35 * N) / 1900.0;
+        const int tiles = mtiles * ((T + N - 1) / N);
+        for (int s = 1; s <= std::min(max_splits, nkc); s++) {
+            const int per = (nkc + s - 1) / s;
+            if ((nkc + per - 1) / per != s) continue;  // no empty split
+            const int waves = (tiles * s + sms - 1) / sms;
+            const double cost = waves * (3.0 + per * chunk_us) + (s > 1 ? 2.0 + 0.2 * s : 0.0);
+            if (cost < best - 1e-9) {
+                best = cost;
+                *N_out = N;
+                *splits_out = s;
+            }
         }
     }
-    return best;
+}
+
+int launch_tc_rowexp(const uint16_t* d, int n, int k, uint8_t* rexp, cudaStream_t s) {
+    if (n <= 0 || k <= 0 || k % 32) return arg_error("tc_rowexp: n > 0, k % 32 == 0");
+    tc_rowexp_kernel<<<(n + 7) / 8, 256, 0, s>>>(d, n, k / 32, rexp);
+    JYC_LAUNCHED();
+    return JYC_OK;
 }
 
 int launch_tc_split(const float* x, int ldx, int T, int k, const float* norm_w, float eps, int N, __half* xs,
@@ -518,6 +679,7 @@ int launch_tc_gemm(const TcGemm& p, int epi, cudaStream_t s) {
     const int per = (nkc + p.splits - 1) / p.splits;
     if ((nkc + per - 1) / per != p.splits) return arg_error("tc_gemm: a K split would be empty");
     if (p.splits > 1 && (!p.part || !p.cnt)) return arg_error("tc_gemm: split-K needs partial buffers");
+    if (!p.rexp) return arg_error("tc_gemm: row exponents missing");
     const int pr = prepare_tc_kernels();
     if (pr != JYC_OK) return pr;
     switch (p.N) {

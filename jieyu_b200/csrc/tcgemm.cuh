@@ -23,6 +23,7 @@ enum TcEpi { TC_STORE = 0, TC_BIAS, TC_RESID, TC_SWIGLU };
 struct TcGemm {
     const uint8_t* qs;   // Q8_0 weights [n][k], byte = q + 128 (row-major device copy)
     const uint16_t* d;   // fp16 scales [n][k/32]
+    const uint8_t* rexp; // [n] fp16 exponent field of each row's max |d| (launch_tc_rowexp)
     int n, k;
     const __half* xs;    // split activations in the tc_split layout for token tile N
     const int* xe;       // per-token power-of-two exponents [token tiles * N]
@@ -38,6 +39,7 @@ struct TcGemm {
 
 constexpr int kTcRows = 128;  // weight rows per CTA tile (UMMA M)
 constexpr int kTcKC = 64;     // K elements per pipeline chunk
+constexpr int kTcMaxSplits = 16; // K splits at most
 constexpr int kTcMinRows = 16;  // activation rows from which a matmul runs on the tensor cores
 
 // Token tile width used for T tokens.
@@ -46,14 +48,18 @@ int tc_token_tile(int T);
 size_t tc_split_halves(int T, int N, int k);
 // Token rows (T padded to the tile) = entries of the exponent array.
 int tc_padded_tokens(int T, int N);
-// K splits that fill the GPU for this shape (1 = none), at most max_splits.
-int tc_plan_splits(int n, int k, int T, int N, int max_splits);
+// Token tile N and K splits (1 = none, at most max_splits) for an n x k
+// weight over T tokens: the pair with the least modelled time.
+void tc_plan(int n, int k, int T, int max_splits, int* N, int* splits);
 
 // x [T][ldx] (optionally RMSNorm'd with weights norm_w) -> fp16 hi/lo planes
 // in the swizzled tile layout the GEMM copies with one bulk copy per chunk.
 int launch_tc_split(const float* x, int ldx, int T, int k, const float* norm_w, float eps, int N, __half* xs,
                     int* xe, cudaStream_t s);
 int launch_tc_gemm(const TcGemm& p, int epi, cudaStream_t s);
+// rexp[r] = exponent field of max_b |d[r][b]| (the GEMM scales row r by
+// 2^(22 - rexp[r]) before splitting it into fp16 hi/lo).
+int launch_tc_rowexp(const uint16_t* d, int n, int k, uint8_t* rexp, cudaStream_t s);
 int prepare_tc_kernels();
 
 }  // namespace jyc
