@@ -293,6 +293,37 @@ JYC_API int jyc_model_tp_open(jyc_model* m, int size, int rank, void* handle_out
 JYC_API int jyc_model_tp_connect(jyc_model* m, const void* handles);
 JYC_API int jyc_model_partials(jyc_model* m, float** o_part, int* o_count, float** d_part, int* d_count);
 
+/* ---- batched decode (configs[4]; no counterpart in the reference, whose
+ * generate_cached runs one sequence, libs/model_libs/generate.h:9-89) ------- */
+/* num_seqs independent sequences over one model, each with its own int8 KV
+ * cache slot of the model's max_seq positions (the layout of the model's own
+ * cache) and its own token buffer; every step appends one greedy token to
+ * every sequence, with the same arithmetic per sequence as jyc_generate's
+ * greedy steps. The matmuls of a step run over all num_seqs rows together:
+ * GEMV kernels below 16 sequences, tcgen05 token tiles from 16 on. Needs a
+ * Q8_0 model with the batched prefill; at most min(512, max_seq, 256)
+ * sequences. While a batch runs, the model must not decode on its own (they
+ * share the model's activation buffers). */
+typedef struct jyc_batch jyc_batch;
+JYC_API jyc_batch* jyc_batch_create(jyc_model* m, int num_seqs);
+JYC_API void jyc_batch_free(jyc_batch* b);
+/* Prefill sequence `seq` with prompt_ids (HOST int32[prompt_len]) from
+ * position 0 and append its first greedy token (synchronous). */
+JYC_API int jyc_batch_prefill(jyc_batch* b, int seq, const int* prompt_ids, int prompt_len);
+/* n_steps batched greedy steps on `stream` (one captured CUDA graph per
+ * step); a sequence whose buffer is full stops growing. */
+JYC_API int jyc_batch_decode(jyc_batch* b, int n_steps, void* stream);
+/* Every sequence back to `len` tokens (its cache entries before len kept). */
+JYC_API int jyc_batch_rewind(jyc_batch* b, int len, void* stream);
+/* Copies up to cap ids of sequence `seq` (prompt + generated) to out_ids
+ * (host); returns its length. Synchronises the device. */
+JYC_API int jyc_batch_tokens(jyc_batch* b, int seq, int* out_ids, int cap);
+/* 2: matmuls on the tcgen05 tiles, 1: GEMV kernels. */
+JYC_API int jyc_batch_path(const jyc_batch* b);
+JYC_API int jyc_batch_kernels_per_step(const jyc_batch* b);
+/* KV-cache bytes one batched step reads with every sequence at context ctx. */
+JYC_API double jyc_batch_kv_bytes_per_step(const jyc_batch* b, int ctx);
+
 /* Error word of the device kernels: non-zero if a bounded wait gave up
  * (reset != 0 clears it). */
 JYC_API int jyc_device_error(int reset);

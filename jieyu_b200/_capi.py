@@ -115,6 +115,15 @@ SIGNATURES = [
     ("jyc_model_trace_decode", _I, [_P, _P, _P, _I]),
     ("jyc_model_tokens_device", _P, [_P]),
     ("jyc_model_length", _I, [_P, _P]),
+    ("jyc_batch_create", _P, [_P, _I]),
+    ("jyc_batch_free", None, [_P]),
+    ("jyc_batch_prefill", _I, [_P, _I, _P, _I]),
+    ("jyc_batch_decode", _I, [_P, _I, _P]),
+    ("jyc_batch_rewind", _I, [_P, _I, _P]),
+    ("jyc_batch_tokens", _I, [_P, _I, _P, _I]),
+    ("jyc_batch_path", _I, [_P]),
+    ("jyc_batch_kernels_per_step", _I, [_P]),
+    ("jyc_batch_kv_bytes_per_step", C.c_double, [_P, _I]),
 ]
 
 _lib = None

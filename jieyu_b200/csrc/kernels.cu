@@ -318,7 +318,7 @@ __global__ void rope_quant_kernel(RopeQuantArgs a) {
     const int nh = a.H + 2 * a.KV;
     if (unit >= a.rows * nh) return;
     const int i = unit / nh, h = unit % nh;
-    const int pos = pos_first(a.pos) + i;
+    const int pos = a.row_len ? a.row_len[i] - 1 : pos_first(a.pos) + i;
     const int hd = a.hd, half = hd >> 1;
     const bool is_q = h < a.H, is_k = !is_q && h < a.H + a.KV;
     const float* src = is_q ? a.q + (size_t)i * a.ldq + (size_t)h * hd
@@ -364,8 +364,8 @@ __global__ void rope_quant_kernel(RopeQuantArgs a) {
     } else {
         const int kvh = is_k ? h - a.H : h - a.H - a.KV;
         if (pos >= a.kv.cap) return;  // host checks capacity; never write past the cache
-        int8_t* base = is_k ? a.kv.k : a.kv.v;
-        float* sbase = is_k ? a.kv.ks : a.kv.vs;
+        int8_t* base = (is_k ? a.kv.k : a.kv.v) + (a.row_len ? (size_t)i * a.kv_row_stride : 0);
+        float* sbase = (is_k ? a.kv.ks : a.kv.vs) + (a.row_len ? (size_t)i * a.skv_row_stride : 0);
         dst = base + (size_t)pos * a.kv.pos_stride + (size_t)kvh * a.kv.head_stride;
         if (lane == 0) sbase[(size_t)pos * a.kv.spos_stride + (size_t)kvh * a.kv.shead_stride] = sc;
         if (is_k && a.k_roped) {
@@ -463,8 +463,19 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     if (pos_inactive(a.pos)) return;
     extern __shared__ __align__(16) unsigned char smem[];
     const int G = a.H / a.KV, P = a.rows * G, hd = a.hd;
-    const int kvh = blockIdx.y, split = blockIdx.x;
-    const int pos0 = pos_first(a.pos);
+    const int kvh = blockIdx.y, split = blockIdx.x, b = blockIdx.z;
+    const int pos0 = a.row_len ? a.row_len[b] - 1 : pos_first(a.pos);
+    // sequence b of a batch: its query rows, cache, partials and counters
+    const int8_t* q8 = a.q8 + (size_t)b * a.rows * a.H * hd;
+    const float* qsc = a.qsc + (size_t)b * a.rows * a.H;
+    const int8_t* kbase = a.kv.k + (size_t)b * a.kv_row_stride;
+    const int8_t* vbase = a.kv.v + (size_t)b * a.kv_row_stride;
+    const float* ksbase = a.kv.ks + (size_t)b * a.skv_row_stride;
+    const float* vsbase = a.kv.vs + (size_t)b * a.skv_row_stride;
+    float* part_o = a.part_o + (size_t)b * a.rows * a.H * a.nsplit * hd;
+    float* part_ml = a.part_ml + (size_t)b * a.rows * a.H * a.nsplit * 2;
+    unsigned int* arrive = a.arrive + (size_t)b * a.KV;
+    float* out = a.out + (size_t)b * a.rows * a.ldo;
     const int pos_last = pos0 + a.rows - 1;
     const int c0 = split * a.chunk;
     const int c1 = min(c0 + a.chunk, pos_last + 1);
@@ -486,21 +497,21 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
         // pair p = (row i, group head g) -> query head h = kvh*G + g
         for (int e = tid; e < P * hd; e += nthr) {
             const int p = e / hd, dd = e % hd, i = p / G, g = p % G;
-            s_q8[e] = a.q8[((size_t)i * a.H + kvh * G + g) * hd + dd];
+            s_q8[e] = q8[((size_t)i * a.H + kvh * G + g) * hd + dd];
             s_o[e] = 0.0f;
         }
         for (int p = tid; p < P; p += nthr) {
             const int i = p / G, g = p % G;
-            s_qsc[p] = a.qsc[(size_t)i * a.H + kvh * G + g];
+            s_qsc[p] = qsc[(size_t)i * a.H + kvh * G + g];
             s_m[p] = -INFINITY;
             s_l[p] = 0.0f;
         }
         __syncthreads();
 
-        const int8_t* kb = a.kv.k + (size_t)kvh * a.kv.head_stride;
-        const int8_t* vb = a.kv.v + (size_t)kvh * a.kv.head_stride;
-        const float* ksb = a.kv.ks + (size_t)kvh * a.kv.shead_stride;
-        const float* vsb = a.kv.vs + (size_t)kvh * a.kv.shead_stride;
+        const int8_t* kb = kbase + (size_t)kvh * a.kv.head_stride;
+        const int8_t* vb = vbase + (size_t)kvh * a.kv.head_stride;
+        const float* ksb = ksbase + (size_t)kvh * a.kv.shead_stride;
+        const float* vsb = vsbase + (size_t)kvh * a.kv.shead_stride;
         const int hw = hd >> 2;  // 32-bit words per head row
 
         for (int j0 = c0; j0 < c1; j0 += SB) {
@@ -571,11 +582,11 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
         for (int e = tid; e < P * hd; e += nthr) {
             const int p = e / hd, dd = e % hd, i = p / G, g = p % G;
             const int h = kvh * G + g;
-            a.part_o[(((size_t)i * a.H + h) * a.nsplit + split) * hd + dd] = s_o[e];
+            part_o[(((size_t)i * a.H + h) * a.nsplit + split) * hd + dd] = s_o[e];
         }
         for (int p = tid; p < P; p += nthr) {
             const int i = p / G, g = p % G, h = kvh * G + g;
-            float* ml = a.part_ml + (((size_t)i * a.H + h) * a.nsplit + split) * 2;
+            float* ml = part_ml + (((size_t)i * a.H + h) * a.nsplit + split) * 2;
             ml[0] = s_m[p];
             ml[1] = s_l[p];
         }
@@ -586,7 +597,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     __threadfence();
     __syncthreads();
     if (tid == 0) {
-        const unsigned int prev = atomicAdd(&a.arrive[kvh], 1u);
+        const unsigned int prev = atomicAdd(&arrive[kvh], 1u);
         s_last = (prev == gridDim.x - 1) ? 1u : 0u;
     }
     __syncthreads();
@@ -597,18 +608,18 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
         const int p = e / hd, dd = e % hd, i = p / G, g = p % G, h = kvh * G + g;
         const size_t base = ((size_t)i * a.H + h) * a.nsplit;
         float M = -INFINITY;
-        for (int s2 = 0; s2 < nvalid; s2++) M = fmaxf(M, __ldcg(a.part_ml + (base + s2) * 2));
+        for (int s2 = 0; s2 < nvalid; s2++) M = fmaxf(M, __ldcg(part_ml + (base + s2) * 2));
         float L = 0.0f, O = 0.0f;
         for (int s2 = 0; s2 < nvalid; s2++) {
-            const float ms = __ldcg(a.part_ml + (base + s2) * 2);
+            const float ms = __ldcg(part_ml + (base + s2) * 2);
             if (ms == -INFINITY) continue;
             const float wgt = expf(ms - M);
-            L = __fmaf_rn(wgt, __ldcg(a.part_ml + (base + s2) * 2 + 1), L);
-            O = __fmaf_rn(wgt, __ldcg(a.part_o + (base + s2) * hd + dd), O);
+            L = __fmaf_rn(wgt, __ldcg(part_ml + (base + s2) * 2 + 1), L);
+            O = __fmaf_rn(wgt, __ldcg(part_o + (base + s2) * hd + dd), O);
         }
-        a.out[(size_t)i * a.ldo + (size_t)h * hd + dd] = O / L;
+        out[(size_t)i * a.ldo + (size_t)h * hd + dd] = O / L;
     }
-    if (tid == 0) a.arrive[kvh] = 0u;
+    if (tid == 0) arrive[kvh] = 0u;
 }
 
 // One-time kernel attributes (called at model creation, outside any capture).
@@ -632,7 +643,8 @@ int launch_attention(const AttnArgs& a, cudaStream_t s) {
     const int smem = attn_smem_bytes(a.rows, a.H, a.KV, a.hd);
     if (smem > 200 * 1024) return arg_error("attention: group too large for shared memory");
     TRY_PREPARE();
-    dim3 grid(a.nsplit, a.KV);
+    if (a.row_len && a.rows != 1) return arg_error("attention: batched decode takes one row per sequence");
+    dim3 grid(a.nsplit, a.KV, a.row_len ? a.nseq : 1);
     attention_kernel<<<grid, 128, smem, s>>>(a);
     JYC_LAUNCHED();
     return JYC_OK;

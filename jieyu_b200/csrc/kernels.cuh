@@ -92,6 +92,11 @@ struct RopeQuantArgs {
     float* k_roped;        // optional fp32 roped K [rows][KV*hd]
     KVView kv;
     PosSrc pos;
+    // batched decode (row_len != null): row i is the last token of sequence i,
+    // at position row_len[i] - 1, with its cache at kv + i * kv_row_stride
+    const int* row_len;
+    long long kv_row_stride;   // int8 elements between sequences' caches
+    long long skv_row_stride;  // scale elements between sequences' caches
 };
 
 struct AttnArgs {
@@ -108,6 +113,14 @@ struct AttnArgs {
     float* out;            // [rows][ldo]
     int ldo;
     PosSrc pos;
+    // batched decode (row_len != null, rows == 1, grid z = sequences):
+    // sequence b's query row b at position row_len[b] - 1 over its own cache
+    // (kv + b * kv_row_stride); partials, arrival counters and output rows
+    // are per sequence
+    const int* row_len;
+    int nseq;
+    long long kv_row_stride;
+    long long skv_row_stride;
 };
 
 // ---- launchers (kernels.cu) ----------------------------------------------

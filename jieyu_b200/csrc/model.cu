@@ -21,12 +21,14 @@
 #include "mega.cuh"
 #include "prefill.cuh"
 #include "tcgemm.cuh"
+#include "batch.cuh"
 
 using namespace jyc;
 
 namespace {
 
 constexpr int kMT = 8;  // activation rows per prefill chunk
+constexpr int kMaxBatchSeqs = 256;  // sequences of one batched decode
 
 struct DevMat {  // one weight matrix on the device, [n][k]
     uint8_t* qs = nullptr;   // Q8: row-major copy (generic kernels)
@@ -648,10 +650,12 @@ int run_prefill(jyc_model* m, int start, int n, cudaStream_t s) {
 int ensure_step_graph(jyc_model* m) {
     if (m->mega || m->step_exec) return JYC_OK;
     cudaGraph_t graph = nullptr;
+    const long long counted = jyc_kernel_launches();
     JYC_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int r = run_layers(m, 1, PosSrc{m->st, 0}, m->stream);
     if (r == JYC_OK) r = run_head(m, 0, m->stream);
     cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+    count_launch((int)(counted - jyc_kernel_launches()));  // captured, not launched
     if (r != JYC_OK) {
         if (graph) cudaGraphDestroy(graph);
         return r;
@@ -1094,6 +1098,286 @@ JYC_API int jyc_model_length(jyc_model* m, void* stream) {
     JYC_CUDA(cudaMemcpyAsync(&hs, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, s));
     JYC_CUDA(cudaStreamSynchronize(s));
     return hs.len;
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Batched decode: B independent sequences over one model, each with its own
+// int8 KV cache slot (the model's cache layout, [slot][layer][kv head][pos][hd])
+// and length; one step appends one greedy token to every sequence. The
+// matmuls run over the B rows together: generic GEMV kernels below
+// kTcMinRows sequences, tcgen05 token tiles from there on.
+// ===========================================================================
+struct jyc_batch {
+    jyc_model* m = nullptr;
+    int B = 0, cap = 0;
+    int8_t *k8 = nullptr, *v8 = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    long long slot_q = 0, slot_s = 0;  // int8 / scale elements per slot
+    int* tokens = nullptr;             // [B][cap + 1]
+    int* lens = nullptr;               // [B]
+    float* logits = nullptr;           // [B][V]
+    unsigned long long* slots = nullptr;
+    float *part_o = nullptr, *part_ml = nullptr;
+    unsigned int* arrive = nullptr;
+    int chunk = 64, nsplit = 1;
+    bool tc = false;
+    cudaGraphExec_t step_exec = nullptr;
+    std::vector<void*> allocs;
+
+    template <class T>
+    int alloc(T** p, size_t count) {
+        void* q = nullptr;
+        cudaError_t e = cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T));
+        if (e != cudaSuccess) {
+            set_error(std::string("cudaMalloc: ") + cudaGetErrorString(e));
+            return JYC_ERR_NOMEM;
+        }
+        allocs.push_back(q);
+        *p = static_cast<T*>(q);
+        return JYC_OK;
+    }
+    ~jyc_batch() {
+        if (step_exec) cudaGraphExecDestroy(step_exec);
+        for (void* p : allocs) cudaFree(p);
+    }
+    KVView kv_layer(int l) const {
+        KVView v = m->kv_layer(l);
+        const size_t lay = (size_t)m->KV * m->max_seq;
+        v.k = k8 + (size_t)l * lay * m->hd;
+        v.v = v8 + (size_t)l * lay * m->hd;
+        v.ks = ks + (size_t)l * lay;
+        v.vs = vs + (size_t)l * lay;
+        return v;
+    }
+};
+
+namespace {
+
+// Y[rows] = X[rows] . W^T (+ epilogue) over the batch's rows
+int batch_gemm(jyc_batch* bt, const DevMat& w, const float* x, int ldx, const float* norm, float* y, int ldy,
+               const float* bias, int epi, cudaStream_t s) {
+    jyc_model* m = bt->m;
+    if (bt->tc) {
+        const int tepi = epi == EPI_BIAS ? TC_BIAS : epi == EPI_RESID ? TC_RESID : epi == EPI_SWIGLU ? TC_SWIGLU : TC_STORE;
+        return run_tc_gemm(m, w, x, ldx, bt->B, norm, y, ldy, bias, tepi, device_error_word(), s);
+    }
+    for (int r0 = 0; r0 < bt->B; r0 += kMT) {
+        GemvArgs g{};
+        g.m = std::min(kMT, bt->B - r0); g.eps = 1e-5f;
+        g.x = x + (size_t)r0 * ldx; g.ldx = ldx; g.n = w.n; g.k = w.k;
+        g.qs = w.qs; g.d = w.d; g.wt = w.f; g.norm_w = norm;
+        g.y = y + (size_t)r0 * ldy; g.ldy = ldy; g.bias = bias;
+        TRY(launch_gemv(g, w.f ? W_F32 : W_Q8, epi, s));
+    }
+    return JYC_OK;
+}
+
+// One batched step: every sequence's last token through the stack, LM head,
+// greedy pick appended (lengths advance on the device).
+int batch_step(jyc_batch* bt, cudaStream_t s) {
+    jyc_model* m = bt->m;
+    const int B = bt->B;
+    TRY(launch_bd_embed(bt->tokens, bt->cap + 1, bt->lens, B, m->embed_f, m->embed_q.qs, m->embed_q.d, m->D, m->X,
+                        s));
+    for (int l = 0; l < m->L; l++) {
+        const DevLayer& ly = m->layers[l];
+        TRY(batch_gemm(bt, ly.qkv, m->X, m->D, ly.rms1, m->qkv, m->nqkv, ly.bias, ly.bias ? EPI_BIAS : EPI_STORE, s));
+        const KVView kv = bt->kv_layer(l);
+        RopeQuantArgs rq{};
+        rq.q = m->qkv; rq.k = m->qkv + m->q_dim; rq.v = m->qkv + m->q_dim + m->kv_dim;
+        rq.ldq = m->nqkv; rq.rows = B; rq.H = m->H; rq.KV = m->KV; rq.hd = m->hd;
+        rq.cos_t = m->cos_t; rq.sin_t = m->sin_t; rq.q8 = m->q8; rq.qsc = m->qsc;
+        rq.kv = kv; rq.pos = PosSrc{nullptr, 0};
+        rq.row_len = bt->lens; rq.kv_row_stride = bt->slot_q; rq.skv_row_stride = bt->slot_s;
+        TRY(launch_rope_quant(rq, s));
+        AttnArgs at{};
+        at.q8 = m->q8; at.qsc = m->qsc; at.kv = kv;
+        at.rows = 1; at.H = m->H; at.KV = m->KV; at.hd = m->hd;
+        at.chunk = bt->chunk; at.nsplit = bt->nsplit;
+        at.scale = 1.0f / sqrtf((float)m->hd);
+        at.part_o = bt->part_o; at.part_ml = bt->part_ml; at.arrive = bt->arrive;
+        at.out = m->attn; at.ldo = m->q_dim; at.pos = PosSrc{nullptr, 0};
+        at.row_len = bt->lens; at.nseq = B; at.kv_row_stride = bt->slot_q; at.skv_row_stride = bt->slot_s;
+        TRY(launch_attention(at, s));
+        TRY(batch_gemm(bt, ly.o, m->attn, m->q_dim, nullptr, m->X, m->D, nullptr, EPI_RESID, s));
+        TRY(batch_gemm(bt, ly.gateup, m->X, m->D, ly.rms2, m->h, m->F, nullptr, EPI_SWIGLU, s));
+        TRY(batch_gemm(bt, ly.down, m->h, m->F, nullptr, m->X, m->D, nullptr, EPI_RESID, s));
+    }
+    TRY(batch_gemm(bt, m->head, m->X, m->D, m->final_norm, bt->logits, m->V, nullptr, EPI_STORE, s));
+    return launch_bd_argmax(bt->logits, m->V, B, bt->slots, bt->tokens, bt->cap + 1, bt->lens, bt->cap, s);
+}
+
+int ensure_batch_graph(jyc_batch* bt) {
+    if (bt->step_exec) return JYC_OK;
+    cudaStream_t cs = bt->m->stream;
+    cudaGraph_t graph = nullptr;
+    const long long counted = jyc_kernel_launches();
+    JYC_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    const int r = batch_step(bt, cs);
+    cudaError_t e = cudaStreamEndCapture(cs, &graph);
+    count_launch((int)(counted - jyc_kernel_launches()));  // captured, not launched
+    if (r != JYC_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return r;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&bt->step_exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    return JYC_OK;
+}
+
+int kernels_per_batch_step(const jyc_batch* bt) {
+    const jyc_model* m = bt->m;
+    const int per_gemm = bt->tc ? 2 : (bt->B + kMT - 1) / kMT;  // split + GEMM, or GEMV row chunks
+    return 1 + m->L * (4 * per_gemm + 2) + per_gemm + 2;
+}
+
+}  // namespace
+
+extern "C" {
+
+JYC_API jyc_batch* jyc_batch_create(jyc_model* m, int num_seqs) {
+    clear_error();
+    if (!m || num_seqs <= 0) {
+        set_error("batch_create: bad arguments");
+        return nullptr;
+    }
+    if (m->wtype != W_Q8 || !m->pf_rows || m->head.f) {
+        set_error("batch_create: batched decode needs a Q8_0 model (layers and LM head) with the batched prefill");
+        return nullptr;
+    }
+    if (num_seqs > m->pf_rows || num_seqs > kMaxBatchSeqs) {
+        set_error("batch_create: at most " + std::to_string(std::min(m->pf_rows, kMaxBatchSeqs)) + " sequences");
+        return nullptr;
+    }
+    jyc_batch* bt = new (std::nothrow) jyc_batch();
+    if (!bt) {
+        set_error("out of host memory");
+        return nullptr;
+    }
+    bt->m = m;
+    bt->B = num_seqs;
+    bt->cap = m->max_seq;
+    bt->tc = num_seqs >= kTcMinRows;
+    auto fail = [&](int) -> jyc_batch* {
+        delete bt;
+        return nullptr;
+    };
+    cudaStream_t s = m->stream;
+    const size_t lay = (size_t)m->L * m->KV * m->max_seq;
+    bt->slot_q = (long long)(lay * m->hd);
+    bt->slot_s = (long long)lay;
+    int r = JYC_OK;
+    if (r == JYC_OK) r = bt->alloc(&bt->k8, (size_t)num_seqs * bt->slot_q);
+    if (r == JYC_OK) r = bt->alloc(&bt->v8, (size_t)num_seqs * bt->slot_q);
+    if (r == JYC_OK) r = bt->alloc(&bt->ks, (size_t)num_seqs * bt->slot_s);
+    if (r == JYC_OK) r = bt->alloc(&bt->vs, (size_t)num_seqs * bt->slot_s);
+    if (r == JYC_OK) r = bt->alloc(&bt->tokens, (size_t)num_seqs * (bt->cap + 1));
+    if (r == JYC_OK) r = bt->alloc(&bt->lens, (size_t)num_seqs);
+    if (r == JYC_OK) r = bt->alloc(&bt->logits, (size_t)num_seqs * m->V);
+    if (r == JYC_OK) r = bt->alloc(&bt->slots, (size_t)num_seqs);
+    // attention split plan: about two CTAs per SM over (sequence, kv head, split)
+    if (r == JYC_OK) {
+        const long long target = 2LL * mega_num_ctas();
+        int chunk = (int)(((long long)m->max_seq * num_seqs * m->KV + target - 1) / target);
+        bt->chunk = std::max(64, (chunk + 63) / 64 * 64);
+        bt->nsplit = (m->max_seq + bt->chunk - 1) / bt->chunk;
+        if (attn_smem_bytes(1, m->H, m->KV, m->hd) > 200 * 1024) r = arg_error("batch_create: query-head group too large");
+    }
+    if (r == JYC_OK) r = bt->alloc(&bt->part_o, (size_t)num_seqs * m->H * bt->nsplit * m->hd);
+    if (r == JYC_OK) r = bt->alloc(&bt->part_ml, (size_t)num_seqs * m->H * bt->nsplit * 2);
+    if (r == JYC_OK) r = bt->alloc(&bt->arrive, (size_t)num_seqs * m->KV);
+    if (r == JYC_OK && bt->tc && !m->head.rexp) {  // the LM head on the tensor cores
+        r = m->alloc(&m->head.rexp, (size_t)m->head.n);
+        if (r == JYC_OK) r = launch_tc_rowexp(m->head.d, m->head.n, m->head.k, m->head.rexp, s);
+    }
+    if (r != JYC_OK) return fail(r);
+    auto zero = [&](void* p, size_t bytes) -> int {
+        const cudaError_t e = cudaMemsetAsync(p, 0, bytes, s);
+        return e == cudaSuccess ? JYC_OK : cuda_fail(e, "cudaMemsetAsync");
+    };
+    if (r == JYC_OK) r = zero(bt->k8, (size_t)num_seqs * bt->slot_q);
+    if (r == JYC_OK) r = zero(bt->v8, (size_t)num_seqs * bt->slot_q);
+    if (r == JYC_OK) r = zero(bt->ks, (size_t)num_seqs * bt->slot_s * 4);
+    if (r == JYC_OK) r = zero(bt->vs, (size_t)num_seqs * bt->slot_s * 4);
+    if (r == JYC_OK) r = zero(bt->lens, (size_t)num_seqs * 4);
+    if (r == JYC_OK) r = zero(bt->slots, (size_t)num_seqs * 8);
+    if (r == JYC_OK) r = zero(bt->arrive, (size_t)num_seqs * m->KV * 4);
+    if (r == JYC_OK) {
+        const cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) r = cuda_fail(e, "cudaStreamSynchronize");
+    }
+    if (r != JYC_OK) return fail(r);
+    return bt;
+}
+
+JYC_API void jyc_batch_free(jyc_batch* bt) { delete bt; }
+
+JYC_API int jyc_batch_prefill(jyc_batch* bt, int seq, const int* prompt_ids, int prompt_len) {
+    clear_error();
+    if (!bt || seq < 0 || seq >= bt->B || !prompt_ids || prompt_len <= 0 || prompt_len >= bt->cap)
+        return arg_error("batch_prefill: bad arguments");
+    jyc_model* m = bt->m;
+    cudaStream_t s = m->stream;
+    int* tok = bt->tokens + (size_t)seq * (bt->cap + 1);
+    JYC_CUDA(cudaMemcpyAsync(tok, prompt_ids, (size_t)prompt_len * sizeof(int), cudaMemcpyHostToDevice, s));
+    // the model's own prefill, pointed at this sequence's cache slot and token
+    // buffer (kernels take the pointers at launch; the model's are restored)
+    int8_t* k8 = m->k8; int8_t* v8 = m->v8; float* ks = m->ks; float* vs = m->vs; int* tokens = m->tokens;
+    m->k8 = bt->k8 + (size_t)seq * bt->slot_q;
+    m->v8 = bt->v8 + (size_t)seq * bt->slot_q;
+    m->ks = bt->ks + (size_t)seq * bt->slot_s;
+    m->vs = bt->vs + (size_t)seq * bt->slot_s;
+    m->tokens = tok;
+    int r = launch_set_state(m->st, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s);
+    if (r == JYC_OK) r = run_prefill(m, 0, prompt_len, s);
+    m->k8 = k8; m->v8 = v8; m->ks = ks; m->vs = vs; m->tokens = tokens;
+    TRY(r);
+    TRY(launch_bd_take_len(m->st, bt->lens, seq, s));
+    JYC_CUDA(cudaStreamSynchronize(s));
+    return JYC_OK;
+}
+
+JYC_API int jyc_batch_decode(jyc_batch* bt, int n_steps, void* stream) {
+    clear_error();
+    if (!bt || n_steps < 0) return arg_error("batch_decode: bad arguments");
+    TRY(ensure_batch_graph(bt));
+    cudaStream_t s = (cudaStream_t)stream;  // as given: 0 is the legacy default stream
+    for (int i = 0; i < n_steps; i++) {
+        JYC_CUDA(cudaGraphLaunch(bt->step_exec, s));
+        count_launch(kernels_per_batch_step(bt));
+    }
+    return JYC_OK;
+}
+
+JYC_API int jyc_batch_rewind(jyc_batch* bt, int len, void* stream) {
+    clear_error();
+    if (!bt || len <= 0 || len >= bt->cap) return arg_error("batch_rewind: bad length");
+    return launch_bd_set_lens(bt->lens, bt->B, len, (cudaStream_t)stream);
+}
+
+JYC_API int jyc_batch_tokens(jyc_batch* bt, int seq, int* out_ids, int cap) {
+    clear_error();
+    if (!bt || seq < 0 || seq >= bt->B || !out_ids || cap <= 0) return arg_error("batch_tokens: bad arguments");
+    int len = 0;
+    JYC_CUDA(cudaStreamSynchronize(bt->m->stream));
+    JYC_CUDA(cudaDeviceSynchronize());
+    JYC_CUDA(cudaMemcpy(&len, bt->lens + seq, sizeof(int), cudaMemcpyDeviceToHost));
+    const int n = std::min(len, cap);
+    JYC_CUDA(cudaMemcpy(out_ids, bt->tokens + (size_t)seq * (bt->cap + 1), (size_t)n * sizeof(int),
+                        cudaMemcpyDeviceToHost));
+    return len;
+}
+
+JYC_API int jyc_batch_path(const jyc_batch* bt) { return bt ? (bt->tc ? 2 : 1) : -1; }
+
+JYC_API int jyc_batch_kernels_per_step(const jyc_batch* bt) { return bt ? kernels_per_batch_step(bt) : 0; }
+
+JYC_API double jyc_batch_kv_bytes_per_step(const jyc_batch* bt, int ctx) {
+    return bt ? bt->B * jyc_model_kv_bytes_per_token(bt->m, ctx) : 0.0;
 }
 
 }  // extern "C"

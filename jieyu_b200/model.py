@@ -68,6 +68,10 @@ CONFIGS = {
     # Llama-3-8B shape
     "c3": Config("c3_llama3_8b", 4096, 32, 32, 8, 128, 14336, 128256, 5e5, "q8", "q8", False,
                  4352, 4096, 128),
+    # batched decode sweep on the Llama-3.2-1B shape (Q8_0), every
+    # sequence at context 2048 + 128 greedy tokens
+    "c4": Config("c4_llama3.2_1b_batched", 2048, 16, 32, 8, 64, 8192, 128256, 5e5, "q8", "q8", False,
+                 2304, 2048, 128),
 }
 
 # Stream ids of the synthetic generator (one per tensor).
@@ -350,6 +354,52 @@ class DeviceModel:
 
     def kernels_per_step(self) -> int:
         return self.lib.jyc_model_kernels_per_step(self.h)
+
+
+class BatchDecoder:
+    """B independent sequences decoded together on one DeviceModel
+    (jyc_batch_*): per-sequence prefill, then batched greedy steps."""
+
+    def __init__(self, model: "DeviceModel", num_seqs: int):
+        self.model = model
+        self.lib = model.lib
+        self.n = num_seqs
+        h = self.lib.jyc_batch_create(model.h, num_seqs)
+        if not h:
+            raise _capi.JycError(-1, _capi.last_error())
+        self.h = h
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.lib.jyc_batch_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prefill(self, seq: int, prompt: np.ndarray) -> None:
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        check(self.lib.jyc_batch_prefill(self.h, seq, _ptr(prompt), len(prompt)))
+
+    def decode(self, n_steps: int, stream: int = 0) -> None:
+        check(self.lib.jyc_batch_decode(self.h, n_steps, stream))
+
+    def rewind(self, length: int, stream: int = 0) -> None:
+        check(self.lib.jyc_batch_rewind(self.h, length, stream))
+
+    def tokens(self, seq: int) -> np.ndarray:
+        out = np.zeros(self.model.cfg.max_seq + 1, dtype=np.int32)
+        n = check(self.lib.jyc_batch_tokens(self.h, seq, _ptr(out), len(out)))
+        return out[:n].copy()
+
+    def path(self) -> int:
+        return self.lib.jyc_batch_path(self.h)
+
+    def kernels_per_step(self) -> int:
+        return self.lib.jyc_batch_kernels_per_step(self.h)
 
 
 def with_max_seq(cfg: Config, max_seq: int) -> Config:
