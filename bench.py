@@ -438,6 +438,111 @@ def run_tp(args):
     return 0
 
 
+def run_c4(args):
+    """batched decode sweep on the Llama-3.2-1B shape (Q8_0), one
+    GPU. B = 1, 4, 16, 32, 64 sequences, each prefilled with its own
+    2048-token random prompt; one step = rewind every sequence to context
+    2049 and decode 128 greedy tokens per sequence. B = 1 runs the
+    single-sequence decode kernel, B = 4 the batched GEMV path, B >= 16 the
+    tcgen05 tiles. Also times the 2048-token prefill (configs[2]'s prefill)."""
+    import numpy as np
+    import torch
+
+    from jieyu_b200 import _capi
+    from jieyu_b200.model import CONFIGS, BatchDecoder, DeviceModel, HostWeights, synth_ids
+
+    if env_int("RANK", 0) != 0:
+        return 0
+    torch.cuda.set_device(env_int("LOCAL_RANK", 0))
+    cfg = CONFIGS["c4"]
+    ctx, new = 2048, 128
+    hw = HostWeights.synthetic(cfg)
+    m = DeviceModel(hw)
+    lib = _capi.load()
+    peak, peak_kind = measured_peaks()
+    tpeak = 1590.0  # the fallback burst bf16 figure when the driver's file is absent
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        with open(pp) as f:
+            tpeak = float(json.load(f).get("bf16_tflops", tpeak))
+    w_bytes = float(lib.jyc_model_weight_bytes_per_token(m.h))
+    # multiply-adds per token of the matmuls (Q, K, V, O, gate, up, down; LM head)
+    D, F, qd, kvd = cfg.hidden, cfg.inter, cfg.q_dim, cfg.kv_dim
+    macs = cfg.layers * (D * (qd + 2 * kvd) + qd * D + 2 * D * F + F * D) + cfg.vocab * D
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    prompts = [synth_ids(2026, 4000 + b, cfg.vocab, ctx) for b in range(64)]
+    sweep = []
+    prefill_tps = None
+    clocks = ClockSampler(env_int("LOCAL_RANK", 0))
+    clocks.start()
+    for B in (1, 4, 16, 32, 64):
+        bt = None
+        if B == 1:
+            ids = torch.from_numpy(prompts[0]).cuda()
+            with torch.cuda.stream(stream):
+                e0, e1 = ev(), ev()
+                m.prefill_device(ids.data_ptr(), ctx, s)  # warm
+                e0.record(stream)
+                m.prefill_device(ids.data_ptr(), ctx, s)
+                e1.record(stream)
+                stream.synchronize()
+                prefill_tps = ctx / (e0.elapsed_time(e1) / 1e3)
+
+            def step():
+                m.rewind(ctx + 1, s)
+                m.decode_device(new, s)
+            path = "single-sequence decode kernel"
+        else:
+            bt = BatchDecoder(m, B)
+            for b in range(B):
+                bt.prefill(b, prompts[b])
+
+            def step(bt=bt):
+                bt.rewind(ctx + 1, s)
+                bt.decode(new, s)
+            path = "tcgen05 tiles" if bt.path() == 2 else "batched GEMV"
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+            stream.synchronize()
+            e0, e1 = ev(), ev()
+            e0.record(stream)
+            for _ in range(args.steps):
+                step()
+            e1.record(stream)
+            stream.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps / new  # per batched step
+        kv = B * float(lib.jyc_model_kv_bytes_per_token(m.h, ctx + new // 2))
+        gbs = (w_bytes + kv) / (ms / 1e3) / 1e9
+        tflops = 2.0 * macs * B / (ms / 1e3) / 1e12
+        sweep.append({"seqs": B, "tok_s": B / (ms / 1e3), "ms_per_step": ms, "path": path,
+                      "hbm_gbs": gbs, "hbm_frac": gbs / peak, "bytes_per_step": w_bytes + kv,
+                      "tensor_tflops": tflops, "tensor_frac": tflops / tpeak})
+        assert lib.jyc_device_error(1) == 0
+        if bt is not None:
+            bt.close()
+    clk = clocks.stop()
+    m.close()
+    best = max(sweep, key=lambda r: r["tok_s"])
+    line = {
+        "metric": "batched decode aggregate tok/s (configs[4])", "value": sweep[-1]["tok_s"], "unit": "tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"configs[4] Llama-3.2-1B shape, Q8_0, {ctx}-token context per sequence, "
+                               f"{new} greedy tokens per sequence per step",
+                   "l2": "inputs larger than L2 (1.3 GB of weights per step)"},
+        "sweep": sweep, "best": {"seqs": best["seqs"], "tok_s": best["tok_s"]},
+        "prefill": {"value": prefill_tps, "unit": "tok/s", "prompt": ctx, "model": "configs[2] shape (Q8_0)"},
+        "peaks": {"hbm_gbs": peak, "hbm_kind": peak_kind, "bf16_tflops": tpeak,
+                  "note": "tensor_tflops counts 2*params*seqs per step (the fp16 hi/lo split does 3x that)"},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -445,8 +550,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp"],
-                    help="c1: the headline decode line (default); c3-tp: configs[3] tensor parallel")
+    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp", "c4"],
+                    help="c1: the headline decode line (default); c3-tp: configs[3] tensor parallel; "
+                         "c4: configs[4] batched decode sweep")
     ap.add_argument("--tp-mode", default="kernel", choices=["kernel", "nccl"],
                     help="c3-tp: in-kernel NVLink exchange (default) or NCCL between kernel windows")
     args = ap.parse_args()
@@ -456,6 +562,8 @@ def main():
         return run_reference_arm(args)
     if args.workload == "c3-tp":
         return run_tp(args)
+    if args.workload == "c4":
+        return run_c4(args)
     return run_b200(args)
 
 

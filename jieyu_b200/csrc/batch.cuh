@@ -20,4 +20,28 @@ int launch_bd_take_len(const DevState* st, int* lens, int b, cudaStream_t s);
 // lens[b] = len for every b.
 int launch_bd_set_lens(int* lens, int nseq, int len, cudaStream_t s);
 
+// Attention of one new row per sequence over its own int8 KV cache slot.
+struct BdAttn {
+    const int8_t* q8;     // [nseq][H][hd] roped, quantised queries
+    const float* qsc;     // [nseq][H]
+    const int8_t* k8;     // this layer's cache in slot 0: [KV][cap][hd]
+    const int8_t* v8;
+    const float* ks;      // [KV][cap]
+    const float* vs;
+    long long slot_q;     // int8 elements between sequences' caches
+    long long slot_s;     // scale elements between sequences' caches
+    int cap, H, KV, hd;
+    int chunk, nsplit;    // positions per split (multiple of 128), splits
+    const int* lens;      // [nseq]: the new row sits at lens[b] - 1
+    float scale;          // 1/sqrtf(hd)
+    float* part_o;        // [nseq][H][nsplit][hd]
+    float* part_ml;       // [nseq][H][nsplit][2]
+    unsigned int* arrive; // [nseq][KV], zero at rest
+    float* out;           // [nseq][ldo]
+    int ldo;
+};
+bool bd_attention_supported(int H, int KV, int hd);
+int bd_attention_chunk(int cap, int nseq, int KV);
+int launch_bd_attention(const BdAttn& a, int nseq, cudaStream_t s);
+
 }  // namespace jyc

@@ -463,19 +463,18 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
     if (pos_inactive(a.pos)) return;
     extern __shared__ __align__(16) unsigned char smem[];
     const int G = a.H / a.KV, P = a.rows * G, hd = a.hd;
-    const int kvh = blockIdx.y, split = blockIdx.x, b = blockIdx.z;
-    const int pos0 = a.row_len ? a.row_len[b] - 1 : pos_first(a.pos);
-    // sequence b of a batch: its query rows, cache, partials and counters
-    const int8_t* q8 = a.q8 + (size_t)b * a.rows * a.H * hd;
-    const float* qsc = a.qsc + (size_t)b * a.rows * a.H;
-    const int8_t* kbase = a.kv.k + (size_t)b * a.kv_row_stride;
-    const int8_t* vbase = a.kv.v + (size_t)b * a.kv_row_stride;
-    const float* ksbase = a.kv.ks + (size_t)b * a.skv_row_stride;
-    const float* vsbase = a.kv.vs + (size_t)b * a.skv_row_stride;
-    float* part_o = a.part_o + (size_t)b * a.rows * a.H * a.nsplit * hd;
-    float* part_ml = a.part_ml + (size_t)b * a.rows * a.H * a.nsplit * 2;
-    unsigned int* arrive = a.arrive + (size_t)b * a.KV;
-    float* out = a.out + (size_t)b * a.rows * a.ldo;
+    const int kvh = blockIdx.y, split = blockIdx.x;
+    const int pos0 = pos_first(a.pos);
+    const int8_t* q8 = a.q8;
+    const float* qsc = a.qsc;
+    const int8_t* kbase = a.kv.k;
+    const int8_t* vbase = a.kv.v;
+    const float* ksbase = a.kv.ks;
+    const float* vsbase = a.kv.vs;
+    float* part_o = a.part_o;
+    float* part_ml = a.part_ml;
+    unsigned int* arrive = a.arrive;
+    float* out = a.out;
     const int pos_last = pos0 + a.rows - 1;
     const int c0 = split * a.chunk;
     const int c1 = min(c0 + a.chunk, pos_last + 1);
@@ -643,8 +642,7 @@ int launch_attention(const AttnArgs& a, cudaStream_t s) {
     const int smem = attn_smem_bytes(a.rows, a.H, a.KV, a.hd);
     if (smem > 200 * 1024) return arg_error("attention: group too large for shared memory");
     TRY_PREPARE();
-    if (a.row_len && a.rows != 1) return arg_error("attention: batched decode takes one row per sequence");
-    dim3 grid(a.nsplit, a.KV, a.row_len ? a.nseq : 1);
+    dim3 grid(a.nsplit, a.KV);
     attention_kernel<<<grid, 128, smem, s>>>(a);
     JYC_LAUNCHED();
     return JYC_OK;

@@ -113,14 +113,6 @@ struct AttnArgs {
     float* out;            // [rows][ldo]
     int ldo;
     PosSrc pos;
-    // batched decode (row_len != null, rows == 1, grid z = sequences):
-    // sequence b's query row b at position row_len[b] - 1 over its own cache
-    // (kv + b * kv_row_stride); partials, arrival counters and output rows
-    // are per sequence
-    const int* row_len;
-    int nseq;
-    long long kv_row_stride;
-    long long skv_row_stride;
 };
 
 // ---- launchers (kernels.cu) ----------------------------------------------

@@ -1192,15 +1192,16 @@ int batch_step(jyc_batch* bt, cudaStream_t s) {
         rq.kv = kv; rq.pos = PosSrc{nullptr, 0};
         rq.row_len = bt->lens; rq.kv_row_stride = bt->slot_q; rq.skv_row_stride = bt->slot_s;
         TRY(launch_rope_quant(rq, s));
-        AttnArgs at{};
-        at.q8 = m->q8; at.qsc = m->qsc; at.kv = kv;
-        at.rows = 1; at.H = m->H; at.KV = m->KV; at.hd = m->hd;
-        at.chunk = bt->chunk; at.nsplit = bt->nsplit;
+        BdAttn at{};
+        at.q8 = m->q8; at.qsc = m->qsc;
+        at.k8 = kv.k; at.v8 = kv.v; at.ks = kv.ks; at.vs = kv.vs;
+        at.slot_q = bt->slot_q; at.slot_s = bt->slot_s;
+        at.cap = m->max_seq; at.H = m->H; at.KV = m->KV; at.hd = m->hd;
+        at.chunk = bt->chunk; at.nsplit = bt->nsplit; at.lens = bt->lens;
         at.scale = 1.0f / sqrtf((float)m->hd);
         at.part_o = bt->part_o; at.part_ml = bt->part_ml; at.arrive = bt->arrive;
-        at.out = m->attn; at.ldo = m->q_dim; at.pos = PosSrc{nullptr, 0};
-        at.row_len = bt->lens; at.nseq = B; at.kv_row_stride = bt->slot_q; at.skv_row_stride = bt->slot_s;
-        TRY(launch_attention(at, s));
+        at.out = m->attn; at.ldo = m->q_dim;
+        TRY(launch_bd_attention(at, B, s));
         TRY(batch_gemm(bt, ly.o, m->attn, m->q_dim, nullptr, m->X, m->D, nullptr, EPI_RESID, s));
         TRY(batch_gemm(bt, ly.gateup, m->X, m->D, ly.rms2, m->h, m->F, nullptr, EPI_SWIGLU, s));
         TRY(batch_gemm(bt, ly.down, m->h, m->F, nullptr, m->X, m->D, nullptr, EPI_RESID, s));
@@ -1232,6 +1233,7 @@ int ensure_batch_graph(jyc_batch* bt) {
 int kernels_per_batch_step(const jyc_batch* bt) {
     const jyc_model* m = bt->m;
     const int per_gemm = bt->tc ? 2 : (bt->B + kMT - 1) / kMT;  // split + GEMM, or GEMV row chunks
+    // embed; per layer 4 matmuls + RoPE/KV append + attention; LM head; argmax + append
     return 1 + m->L * (4 * per_gemm + 2) + per_gemm + 2;
 }
 
@@ -1279,13 +1281,12 @@ JYC_API jyc_batch* jyc_batch_create(jyc_model* m, int num_seqs) {
     if (r == JYC_OK) r = bt->alloc(&bt->lens, (size_t)num_seqs);
     if (r == JYC_OK) r = bt->alloc(&bt->logits, (size_t)num_seqs * m->V);
     if (r == JYC_OK) r = bt->alloc(&bt->slots, (size_t)num_seqs);
-    // attention split plan: about two CTAs per SM over (sequence, kv head, split)
+    // attention split plan: about three CTAs per SM over (sequence, kv head, split)
     if (r == JYC_OK) {
-        const long long target = 2LL * mega_num_ctas();
-        int chunk = (int)(((long long)m->max_seq * num_seqs * m->KV + target - 1) / target);
-        bt->chunk = std::max(64, (chunk + 63) / 64 * 64);
+        if (!bd_attention_supported(m->H, m->KV, m->hd))
+            r = arg_error("batch_create: head_dim 64 or 128 and at most 8 query heads per kv head");
+        bt->chunk = bd_attention_chunk(m->max_seq, num_seqs, m->KV);
         bt->nsplit = (m->max_seq + bt->chunk - 1) / bt->chunk;
-        if (attn_smem_bytes(1, m->H, m->KV, m->hd) > 200 * 1024) r = arg_error("batch_create: query-head group too large");
     }
     if (r == JYC_OK) r = bt->alloc(&bt->part_o, (size_t)num_seqs * m->H * bt->nsplit * m->hd);
     if (r == JYC_OK) r = bt->alloc(&bt->part_ml, (size_t)num_seqs * m->H * bt->nsplit * 2);
