@@ -108,18 +108,18 @@ int launch_bd_set_lens(int* lens, int nseq, int len, cudaStream_t s) {
 // transformer_layer for one new row per sequence, libs/model_libs/attention/
 // attention_q8.h:38-184, with the reference's score scaling
 // dot * ((ks * qs) * 1/sqrt(hd)), fp32 online softmax and the V scale folded
-// into the weights). CTA = (position split, kv head, sequence), 256 threads.
-// Per block of 128 positions: K and V rows arrive with 16-byte cp.async into
-// a double buffer (16-byte chunks rotated per row so that row-parallel reads
-// are free of bank conflicts); each thread scores one position against up to
-// half the query heads (dp4a); one warp per head runs the online softmax; P.V
-// gives each thread 4 output dims of one head over a share of the positions.
-// Partials (m, l, o) per split; the last CTA of (sequence, kv head) merges.
+// into the weights). CTA = (position split, kv head, sequence), 8 warps; each
+// warp owns a contiguous run of the split's positions and keeps its own
+// online-softmax state, so the loop has no CTA-wide barrier. Per tile of 32
+// positions: lane j's K and V rows arrive with 16-byte cp.async into the
+// warp's double buffer (chunks rotated per row: conflict-free row reads);
+// lane j scores position j against every query head of the kv head (dp4a);
+// the weights go through shared memory and each lane accumulates P.V for its
+// HD/32 dims of every head. The warps merge at the end; partials (m, l, o)
+// per split, and the last CTA of (sequence, kv head) merges the splits.
 namespace jyc {
 namespace {
 
-constexpr int kBdKB = 128;    // positions per block
-constexpr int kBdStages = 3;  // blocks in the cp.async ring (two in flight while one is used)
 
 template <int HD>
 __device__ __forceinline__ int bd_rot(int j) {
@@ -138,147 +138,183 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Per-warp shared memory: K and V tiles [2 buffers][32 rows][HD] (16-byte
+// chunks rotated by bd_rot) and the tile's weights [32][8 heads].
 template <int HD>
-__global__ void __launch_bounds__(256) bd_attention_kernel(BdAttn a) {
-    constexpr int KB = kBdKB, NCH = HD / 16;
+constexpr int bd_warp_bytes() {
+    return 4 * 32 * HD + 32 * 8 * 4;
+}
+
+template <int HD, int NW>
+__global__ void __launch_bounds__(NW * 32) bd_attention_kernel(BdAttn a) {
+    constexpr int NCH = HD / 16, DPL = HD / 32, MAXG = 8;
     extern __shared__ __align__(16) unsigned char bd_sm[];
     const int G = a.H / a.KV;
-    int8_t* sk = reinterpret_cast<int8_t*>(bd_sm);                    // [kBdStages][KB][HD]
-    int8_t* sv = sk + kBdStages * KB * HD;                              // [kBdStages][KB][HD]
-    float* sks = reinterpret_cast<float*>(sv + kBdStages * KB * HD);    // [kBdStages][KB]
-    float* svs = sks + kBdStages * KB;                                  // [kBdStages][KB]
-    float* sp = svs + kBdStages * KB;                                   // [G][KB] scores, then weights
-    float* sred = sp + G * KB;                                  // [256 / NQ][G * HD] P.V partials
-    int8_t* sq = reinterpret_cast<int8_t*>(sred + 256 * 4);     // [G][HD]
-    float* sqs = reinterpret_cast<float*>(sq + G * HD);         // [G]
-    float* s_m = sqs + G;
-    float* s_l = s_m + G;
-    float* s_al = s_l + G;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int8_t* sq = reinterpret_cast<int8_t*>(bd_sm);  // [G][HD] queries (<= 1 KB)
+    float* sqs = reinterpret_cast<float*>(bd_sm + 1024);
+    unsigned char* wb = bd_sm + 1024 + 64 + warp * bd_warp_bytes<HD>();
+    int8_t* sk = reinterpret_cast<int8_t*>(wb);                // [2][32][HD]
+    int8_t* sv = sk + 2 * 32 * HD;                             // [2][32][HD]
+    float* sp = reinterpret_cast<float*>(sv + 2 * 32 * HD);   // [32][MAXG]
 
-    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, tid = threadIdx.x, lane = tid & 31,
-              warp = tid >> 5;
+    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int pos_last = a.lens[b] - 1;
     const int c0 = split * a.chunk, c1 = min(c0 + a.chunk, pos_last + 1);
-    const int NQ = G * HD / 4, NJG = 256 / NQ;  // output quads; position groups of P.V
-    const int q = tid % NQ, jg = tid / NQ, g_pv = (4 * q) / HD, d0 = (4 * q) % HD;
-    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const size_t hq = (size_t)b * a.H + (size_t)kvh * G;  // first query head row of this CTA
 
     if (c0 <= pos_last) {
-        for (int e = tid; e < G * HD / 16; e += 256)
+        for (int e = tid; e < G * HD / 16; e += NW * 32)
             reinterpret_cast<uint4*>(sq)[e] = __ldg(reinterpret_cast<const uint4*>(a.q8 + hq * HD) + e);
-        if (tid < G) {
-            sqs[tid] = __ldg(a.qsc + hq + tid);
-            s_m[tid] = -INFINITY;
-            s_l[tid] = 0.0f;
-        }
+        if (tid < G) sqs[tid] = __ldg(a.qsc + hq + tid);
+        __syncthreads();
         const int8_t* kb = a.k8 + (size_t)b * a.slot_q + (size_t)kvh * a.cap * HD;
         const int8_t* vb = a.v8 + (size_t)b * a.slot_q + (size_t)kvh * a.cap * HD;
         const float* ksb = a.ks + (size_t)b * a.slot_s + (size_t)kvh * a.cap;
         const float* vsb = a.vs + (size_t)b * a.slot_s + (size_t)kvh * a.cap;
-        // one commit group per call (empty past the end) keeps the group count uniform
-        auto issue = [&](int j0, int buf) {
-            const int nj = j0 < c1 ? min(KB, c1 - j0) : 0;
-            for (int e = tid; e < nj * NCH; e += 256) {
-                const int j = e / NCH, c = e % NCH, ph = ((c + bd_rot<HD>(j)) & (NCH - 1)) * 16;
-                cp_async16(sk + (buf * KB + j) * HD + ph, kb + (size_t)(j0 + j) * HD + c * 16);
-                cp_async16(sv + (buf * KB + j) * HD + ph, vb + (size_t)(j0 + j) * HD + c * 16);
-            }
-            for (int j = tid; j < nj; j += 256) {
-                cp_async4(sks + buf * KB + j, ksb + j0 + j);
-                cp_async4(svs + buf * KB + j, vsb + j0 + j);
+        // this warp's positions [w0, w1)
+        const int per = a.chunk / NW, w0 = c0 + warp * per, w1 = min(w0 + per, c1);
+        const int ntile = w1 > w0 ? (w1 - w0 + 31) / 32 : 0;
+        // lane j copies row j of tile t (one commit group per call, empty past the end)
+        auto issue = [&](int t, int buf) {
+            const int j = w0 + 32 * t + lane;
+            if (t < ntile && j < w1) {
+#pragma unroll
+                for (int c = 0; c < NCH; c++) {
+                    const int ph = ((c + bd_rot<HD>(lane)) & (NCH - 1)) * 16;
+                    cp_async16(sk + (buf * 32 + lane) * HD + ph, kb + (size_t)j * HD + c * 16);
+                    cp_async16(sv + (buf * 32 + lane) * HD + ph, vb + (size_t)j * HD + c * 16);
+                }
             }
             cp_async_commit();
         };
+        float m[MAXG], l[MAXG], o[MAXG][DPL];
 #pragma unroll
-        for (int st = 0; st < kBdStages - 1; st++) issue(c0 + st * KB, st);
-        int buf = 0;
-        for (int j0 = c0; j0 < c1; j0 += KB, buf = (buf + 1) % kBdStages) {
-            const int nj = min(KB, c1 - j0);
-            issue(j0 + (kBdStages - 1) * KB, (buf + kBdStages - 1) % kBdStages);
-            cp_async_wait<kBdStages - 1>();  // block j0's group (and every older one) has landed
-            __syncthreads();  // ... for every thread
-            // scores: thread -> position j, heads hh, hh + 2, ...
-            {
-                const int j = tid & (KB - 1), hh = tid >> 7;
-                const uint4* krow = reinterpret_cast<const uint4*>(sk + (buf * KB + j) * HD);
-                for (int g = hh; g < G; g += 2) {
-                    float sc = -INFINITY;
-                    if (j < nj) {
-                        const uint4* qrow = reinterpret_cast<const uint4*>(sq + g * HD);
-                        int dot = 0;
+        for (int g = 0; g < MAXG; g++) {
+            m[g] = -INFINITY;
+            l[g] = 0.0f;
 #pragma unroll
-                        for (int c = 0; c < NCH; c++) {
-                            const uint4 kw = krow[(c + bd_rot<HD>(j)) & (NCH - 1)];
-                            const uint4 qw = qrow[c];
-                            dot = __dp4a((int)qw.x, (int)kw.x, dot);
-                            dot = __dp4a((int)qw.y, (int)kw.y, dot);
-                            dot = __dp4a((int)qw.z, (int)kw.z, dot);
-                            dot = __dp4a((int)qw.w, (int)kw.w, dot);
-                        }
-                        sc = __fmul_rn((float)dot, __fmul_rn(__fmul_rn(sks[buf * KB + j], sqs[g]), a.scale));
-                    }
-                    sp[g * KB + j] = sc;
-                }
+            for (int i = 0; i < DPL; i++) o[g][i] = 0.0f;
+        }
+        issue(0, 0);
+        float ksn = 0.0f, vsn = 0.0f;
+        if (ntile > 0 && w0 + lane < w1) {
+            ksn = __ldg(ksb + w0 + lane);
+            vsn = __ldg(vsb + w0 + lane);
+        }
+        for (int t = 0; t < ntile; t++) {
+            const int buf = t & 1, jt = w0 + 32 * t, nj = min(32, w1 - jt);
+            issue(t + 1, buf ^ 1);
+            const float ksc = ksn, vsc = vsn;
+            if (t + 1 < ntile && jt + 32 + lane < w1) {
+                ksn = __ldg(ksb + jt + 32 + lane);
+                vsn = __ldg(vsb + jt + 32 + lane);
             }
-            __syncthreads();
-            // online softmax: warp g takes head g
-            for (int g = warp; g < G; g += 8) {
-                float v[KB / 32];
-                float mx = -INFINITY;
+            cp_async_wait<1>();
+            __syncwarp();
+            // scores of position jt + lane for every head, online softmax per head
+            const uint4* krow = reinterpret_cast<const uint4*>(sk + (buf * 32 + lane) * HD);
+            uint4 kr[NCH];
 #pragma unroll
-                for (int i = 0; i < KB / 32; i++) {
-                    v[i] = sp[g * KB + 32 * i + lane];
-                    mx = fmaxf(mx, v[i]);
-                }
-                mx = warp_max(mx);
-                const float m_old = s_m[g], m_new = fmaxf(m_old, mx);
-                float sum = 0.0f;
+            for (int c = 0; c < NCH; c++) kr[c] = krow[(c + bd_rot<HD>(lane)) & (NCH - 1)];
+            float pw[MAXG];
 #pragma unroll
-                for (int i = 0; i < KB / 32; i++) {
-                    const int j = 32 * i + lane;
-                    const float e = v[i] == -INFINITY ? 0.0f : expf(v[i] - m_new);
-                    sum += e;
-                    sp[g * KB + j] = e * (j < nj ? svs[buf * KB + j] : 0.0f);
+            for (int g = 0; g < MAXG; g++) {
+                pw[g] = 0.0f;
+                if (g >= G) continue;
+                const uint4* qrow = reinterpret_cast<const uint4*>(sq + g * HD);
+                int dot = 0;
+#pragma unroll
+                for (int c = 0; c < NCH; c++) {
+                    const uint4 qw = qrow[c];
+                    dot = __dp4a((int)qw.x, (int)kr[c].x, dot);
+                    dot = __dp4a((int)qw.y, (int)kr[c].y, dot);
+                    dot = __dp4a((int)qw.z, (int)kr[c].z, dot);
+                    dot = __dp4a((int)qw.w, (int)kr[c].w, dot);
                 }
-                sum = warp_sum(sum);
-                if (lane == 0) {
-                    const float al = m_old == -INFINITY ? 0.0f : expf(m_old - m_new);
-                    s_al[g] = al;
-                    s_l[g] = s_l[g] * al + sum;
-                    s_m[g] = m_new;
-                }
+                const float sc = lane < nj ? __fmul_rn((float)dot, __fmul_rn(__fmul_rn(ksc, sqs[g]), a.scale))
+                                           : -INFINITY;
+                const float mn = fmaxf(m[g], warp_max(sc));
+                const float e = sc == -INFINITY ? 0.0f : expf(sc - mn);
+                const float al = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
+                m[g] = mn;
+                l[g] = l[g] * al + e;  // per-lane share, summed over lanes at the end
+#pragma unroll
+                for (int i = 0; i < DPL; i++) o[g][i] = __fmul_rn(o[g][i], al);
+                pw[g] = e * vsc;
             }
-            __syncthreads();
-            // P.V: 4 dims of head g_pv over positions jg, jg + NJG, ...
-            if (jg < NJG) {
-                const float al = s_al[g_pv];
-#pragma unroll
-                for (int i = 0; i < 4; i++) o[i] = __fmul_rn(o[i], al);
-                const int c = d0 >> 4, w4 = d0 & 15;
-                for (int j = jg; j < nj; j += NJG) {
-                    const int8_t* vr = sv + (buf * KB + j) * HD + ((c + bd_rot<HD>(j)) & (NCH - 1)) * 16 + w4;
-                    float f[4];
+            *reinterpret_cast<float4*>(sp + lane * MAXG) = make_float4(pw[0], pw[1], pw[2], pw[3]);
+            if (G > 4) *reinterpret_cast<float4*>(sp + lane * MAXG + 4) = make_float4(pw[4], pw[5], pw[6], pw[7]);
+            __syncwarp();
+            // P.V: lane owns dims [DPL lane, DPL lane + DPL) of every head
+            const int c = (DPL * lane) >> 4, off = (DPL * lane) & 15;
+            for (int jj = 0; jj < nj; jj++) {
+                const int8_t* vr = sv + (buf * 32 + jj) * HD + ((c + bd_rot<HD>(jj)) & (NCH - 1)) * 16 + off;
+                float f[4];
+                if (DPL == 4) {
                     u8x4_to_f32(*reinterpret_cast<const uint32_t*>(vr) ^ 0x80808080u, f);
-                    const float p = sp[g_pv * KB + j];
+                } else {
+                    u8x4_to_f32((uint32_t)(*reinterpret_cast<const uint16_t*>(vr)) ^ 0x80808080u, f);
+                }
+                const float4 p0 = *reinterpret_cast<const float4*>(sp + jj * MAXG);
+                const float pg[4] = {p0.x, p0.y, p0.z, p0.w};
 #pragma unroll
-                    for (int i = 0; i < 4; i++) o[i] = __fmaf_rn(p, f[i], o[i]);
+                for (int g = 0; g < 4; g++)
+#pragma unroll
+                    for (int i = 0; i < DPL; i++) o[g][i] = __fmaf_rn(pg[g], f[i], o[g][i]);
+                if (G > 4) {
+                    const float4 p1 = *reinterpret_cast<const float4*>(sp + jj * MAXG + 4);
+                    const float ph[4] = {p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+                    for (int g = 0; g < 4; g++)
+#pragma unroll
+                        for (int i = 0; i < DPL; i++) o[4 + g][i] = __fmaf_rn(ph[g], f[i], o[4 + g][i]);
                 }
             }
-            __syncthreads();  // buffers and weights are reused by the next block
+            __syncwarp();  // the next iteration's copies overwrite this buffer
         }
-        // sum the position groups' P.V partials
-        if (jg < NJG) *reinterpret_cast<float4*>(sred + jg * G * HD + 4 * q) = make_float4(o[0], o[1], o[2], o[3]);
+        cp_async_wait<0>();
+        // merge the warps: (m, l, o) per warp -> shared memory, then per head
+#pragma unroll
+        for (int g = 0; g < MAXG; g++) l[g] = warp_sum(l[g]);
+        __syncthreads();  // every warp is done with its tiles: reuse the area
+        float* mw = reinterpret_cast<float*>(bd_sm + 1024 + 64);  // [NW][MAXG]
+        float* lw = mw + NW * MAXG;                                // [NW][MAXG]
+        float* ow = lw + NW * MAXG;                                // [NW][G][HD]
+        if (lane < MAXG) {
+            float mv = m[0], lv = l[0];
+#pragma unroll
+            for (int g = 1; g < MAXG; g++)
+                if (lane == g) {
+                    mv = m[g];
+                    lv = l[g];
+                }
+            mw[warp * MAXG + lane] = mv;
+            lw[warp * MAXG + lane] = lv;
+        }
+#pragma unroll
+        for (int g = 0; g < MAXG; g++)
+            if (g < G)
+#pragma unroll
+                for (int i = 0; i < DPL; i++) ow[(warp * G + g) * HD + DPL * lane + i] = o[g][i];
         __syncthreads();
-        for (int e = tid; e < G * HD; e += 256) {
-            float acc = 0.0f;
-            for (int z = 0; z < NJG; z++) acc += sred[z * G * HD + e];
+        for (int e = tid; e < G * HD; e += NW * 32) {
             const int g = e / HD, d = e % HD;
-            a.part_o[((hq + g) * a.nsplit + split) * HD + d] = acc;
-        }
-        if (tid < G) {
-            a.part_ml[((hq + tid) * a.nsplit + split) * 2] = s_m[tid];
-            a.part_ml[((hq + tid) * a.nsplit + split) * 2 + 1] = s_l[tid];
+            float M = -INFINITY;
+            for (int w = 0; w < NW; w++) M = fmaxf(M, mw[w * MAXG + g]);
+            float L = 0.0f, O = 0.0f;
+            for (int w = 0; w < NW; w++) {
+                const float mv = mw[w * MAXG + g];
+                if (mv == -INFINITY) continue;
+                const float wgt = expf(mv - M);
+                L = __fmaf_rn(wgt, lw[w * MAXG + g], L);
+                O = __fmaf_rn(wgt, ow[(w * G + g) * HD + d], O);
+            }
+            a.part_o[((hq + g) * a.nsplit + split) * HD + d] = O;
+            if (d == 0) {
+                a.part_ml[((hq + g) * a.nsplit + split) * 2] = M;
+                a.part_ml[((hq + g) * a.nsplit + split) * 2 + 1] = L;
+            }
         }
     }
 
@@ -294,7 +330,7 @@ __global__ void __launch_bounds__(256) bd_attention_kernel(BdAttn a) {
     if (!s_last) return;
     __threadfence();
     const int nvalid = pos_last / a.chunk + 1;
-    for (int e = tid; e < G * HD; e += 256) {
+    for (int e = tid; e < G * HD; e += NW * 32) {
         const int g = e / HD, d = e % HD;
         const size_t base = (hq + g) * a.nsplit;
         float M = -INFINITY;
@@ -312,39 +348,45 @@ __global__ void __launch_bounds__(256) bd_attention_kernel(BdAttn a) {
     if (tid == 0) a.arrive[(size_t)b * a.KV + kvh] = 0u;
 }
 
-int bd_attn_smem(int hd, int G) {
-    return 2 * kBdStages * kBdKB * hd + 2 * kBdStages * kBdKB * 4 + G * kBdKB * 4 + 256 * 4 * 4 + G * hd + 4 * G * 4;
+constexpr int kBdWarps = 8;  // warps per CTA
+
+int bd_attn_smem(int hd) {
+    const int warps = 1024 + 64 + kBdWarps * (hd == 64 ? bd_warp_bytes<64>() : bd_warp_bytes<128>());
+    const int merge = 1024 + 64 + (2 * kBdWarps * 8 + kBdWarps * 8 * hd) * 4;
+    return warps > merge ? warps : merge;
 }
 
 }  // namespace
 
 bool bd_attention_supported(int H, int KV, int hd) {
     const int G = KV > 0 ? H / KV : 0;
-    return (hd == 64 || hd == 128) && KV > 0 && H % KV == 0 && G >= 1 && G <= 8 && (G * hd) % 64 == 0;
+    return (hd == 64 || hd == 128) && KV > 0 && H % KV == 0 && G >= 1 && G <= 8;
 }
 
 int bd_attention_chunk(int cap, int nseq, int KV) {
+    // about three CTAs per SM over (split, kv head, sequence); a chunk is a
+    // whole number of 32-position tiles for each of the kBdWarps warps
+    constexpr int q = 32 * kBdWarps;
     const long long target = 3LL * 148;
     long long chunk = ((long long)cap * nseq * KV + target - 1) / target;
-    chunk = (chunk + kBdKB - 1) / kBdKB * kBdKB;
-    return (int)std::max<long long>(kBdKB, std::min<long long>(chunk, ((long long)cap + kBdKB - 1) / kBdKB * kBdKB));
+    chunk = (chunk + q - 1) / q * q;
+    return (int)std::max<long long>(q, std::min<long long>(chunk, ((long long)cap + q - 1) / q * q));
 }
 
 int launch_bd_attention(const BdAttn& a, int nseq, cudaStream_t s) {
     if (!bd_attention_supported(a.H, a.KV, a.hd)) return arg_error("bd_attention: unsupported head shape");
-    if (a.chunk % kBdKB) return arg_error("bd_attention: chunk must be a multiple of 128");
-    const int G = a.H / a.KV, smem = bd_attn_smem(a.hd, G);
+    if (a.chunk % (32 * kBdWarps)) return arg_error("bd_attention: chunk must be a multiple of 256");
     static bool attr = false;
     if (!attr) {
-        JYC_CUDA(cudaFuncSetAttribute(bd_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      bd_attn_smem(64, 8)));
-        JYC_CUDA(cudaFuncSetAttribute(bd_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      bd_attn_smem(128, 8)));
+        JYC_CUDA(cudaFuncSetAttribute(bd_attention_kernel<64, kBdWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      bd_attn_smem(64)));
+        JYC_CUDA(cudaFuncSetAttribute(bd_attention_kernel<128, kBdWarps>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, bd_attn_smem(128)));
         attr = true;
     }
     const dim3 grid(a.nsplit, a.KV, nseq);
-    if (a.hd == 64) bd_attention_kernel<64><<<grid, 256, smem, s>>>(a);
-    else bd_attention_kernel<128><<<grid, 256, smem, s>>>(a);
+    if (a.hd == 64) bd_attention_kernel<64, kBdWarps><<<grid, kBdWarps * 32, bd_attn_smem(64), s>>>(a);
+    else bd_attention_kernel<128, kBdWarps><<<grid, kBdWarps * 32, bd_attn_smem(128), s>>>(a);
     JYC_LAUNCHED();
     return JYC_OK;
 }

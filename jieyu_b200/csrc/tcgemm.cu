@@ -39,7 +39,6 @@ constexpr int kThreads = 320;
 constexpr int kPlaneA = kTcRows * 128;  // one A plane (hi or lo) of a chunk: 128 rows x 128 bytes
 constexpr int kSmemBudget = 200 * 1024;
 constexpr int kErrTc = 9;
-constexpr int kGroup = 2;  // K chunks accumulated per tensor-memory set before the drain
 
 template <int N>
 struct TcCfg {
@@ -52,6 +51,31 @@ struct TcCfg {
     static constexpr int kCols = 4 * N < 32 ? 32 : 4 * N;
     // alignment slack + stages + barriers + tmem slot/flags
     static constexpr int kSmem = 1024 + kStages * kStage + 8 * (3 * kStages + 4) + 16;
+};
+
+// Tensor-memory A variant (token tiles up to 64): the weight planes go to
+// tensor memory (tcgen05.st), shared memory holds only the token operand.
+constexpr int kGroup = 2;         // K chunks accumulated per tensor-memory set before the drain
+constexpr int kTaStageCols = 64;  // one A stage: hi (32 columns) + lo (32 columns) of 128 rows x 64 K
+constexpr int kTaDone = 32;       // group-completion barriers in the ring (> any waiter's lag in groups)
+template <int N>
+struct TcCfgTa {
+    static constexpr int kPlaneB = N * 128;
+    static constexpr int kStage = 2 * kPlaneB;  // token hi + lo planes of a chunk
+    // A bulk copy completes about every 600 cycles whatever its size up to
+    // 32 KB, so the token planes of kCB consecutive chunks travel together
+    static constexpr int kCB = kStage >= 32768 ? 1 : 32768 / kStage;
+    static constexpr int kSlotsB = 4;                 // B slots of kCB chunks
+    static constexpr int kStagesB = kSlotsB * kCB;    // chunks of B in shared memory
+    static constexpr int kStagesA = 4;
+    static constexpr int kAccCols = 4 * N;
+    static constexpr int kCols = 512;  // 4N + 4 x 64 <= 512 for N <= 64
+    static_assert(kAccCols + kStagesA * kTaStageCols <= kCols, "tensor memory");
+    // the epilogue tile [N][128] floats reuses the token stages
+    static_assert(kStagesB * kStage >= N * kTcRows * 4, "epilogue tile");
+    static constexpr int kSmem = 1024 + kStagesB * kStage + 8 * (kStagesA + kSlotsB + kTaDone + 2) + 16;
+    static_assert(kStagesA % kGroup == 0, "A stages hold whole groups");
+    static_assert(kStagesB / kGroup + kStagesA < kTaDone, "group ring deeper than any waiter's lag");
 };
 
 // ---- tcgen05 / tensor-memory helpers ---------------------------------------
@@ -76,6 +100,26 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D[tmem] (+)= A[tmem] . B[smem]^T (A: lane = row, two fp16 of K per column)
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// this warp's 32 lanes, 16 consecutive columns from registers
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // arrives once on `bar` when every MMA this thread issued so far has completed
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -494,6 +538,337 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(TcGemm p) {
     }
 }
 
+template <int N, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_ta_kernel(TcGemm p) {
+    using C = TcCfgTa<N>;
+    constexpr int CH = N / 2;  // accumulator columns (tokens) per converter thread
+    extern __shared__ unsigned char tc_smraw[];
+    // the 128-byte swizzle is a function of the address bits: 1024-byte aligned tiles
+    unsigned char* sm = tc_smraw + ((1024u - (smem_u32(tc_smraw) & 1023u)) & 1023u);
+    // One tcgen05.commit per group of kGroup chunks (a commit costs hundreds of
+    // cycles): gdone[g % kTaDone] completes when group g's MMAs have, which
+    // frees its A and B stages and lets its accumulator set be drained.
+    uint64_t* afull = reinterpret_cast<uint64_t*>(sm + C::kStagesB * C::kStage);  // A stage written (256 arrivals)
+    uint64_t* bfull = afull + C::kStagesA;                                         // token slot landed (tx)
+    uint64_t* gdone = bfull + C::kSlotsB;                                          // [kTaDone] group MMAs done
+    uint64_t* accfree = gdone + kTaDone;   // [2] accumulator set b drained (256 arrivals)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accfree + 2);
+    unsigned int* s_flag = s_tmem + 1;
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 2);  // a bounded wait gave up
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.x, tt = blockIdx.y, z = blockIdx.z;
+    const int nkc = (p.k + kTcKC - 1) / kTcKC;
+    const int per = (nkc + p.splits - 1) / p.splits;
+    const int c0 = z * per, nch = min(nkc, c0 + per) - c0;  // the host plan leaves no split empty
+    // bounded wait; after any give-up in this CTA every later wait is skipped
+    auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (*s_abort) return false;
+        if (mbar_wait_err(bar, parity, p.err, kErrTc)) return true;
+        *s_abort = 1;
+        return false;
+    };
+
+    if (tid == 0) {
+        for (int s = 0; s < C::kStagesA; s++) mbar_init(&afull[s], 256);
+        for (int s = 0; s < C::kSlotsB; s++) mbar_init(&bfull[s], 1);
+        for (int g = 0; g < kTaDone; g++) mbar_init(&gdone[g], 1);
+        for (int b = 0; b < 2; b++) mbar_init(&accfree[b], 256);
+        *s_abort = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        __syncwarp();
+        tmem_alloc(s_tmem, C::kCols);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+    // wait until group g's MMAs are complete
+    auto wait_group = [&](int g) -> bool { return wait(&gdone[g % kTaDone], (g / kTaDone) & 1); };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const unsigned char* src =
+                reinterpret_cast<const unsigned char*>(p.xs) + ((size_t)tt * nkc + c0) * 2 * C::kPlaneB;
+            // load u brings chunks [u kCB, u kCB + kCB) into slot u % kSlotsB, once
+            // the MMAs of that slot's previous chunks are done
+            const int nload = (nch + C::kCB - 1) / C::kCB;
+            int issued = 0;
+            for (int u = 0; u < nload; u++) {
+                const int sl = u % C::kSlotsB, cj = u * C::kCB, cn = min(C::kCB, nch - cj);
+                if (u >= C::kSlotsB && !wait_group((cj - C::kSlotsB * C::kCB + C::kCB - 1) / kGroup)) break;
+                mbar_expect_tx(&bfull[sl], cn * C::kStage);
+                bulk_g2s_keep(sm + sl * C::kCB * C::kStage, src + (size_t)cj * C::kStage, cn * C::kStage, &bfull[sl]);
+                issued = u + 1;
+            }
+            // no copy may still be landing when the CTA exits (matters only after an error)
+            for (int u = max(0, issued - C::kSlotsB); u < issued; u++)
+                mbar_wait_err(&bfull[u % C::kSlotsB], (u / C::kSlotsB) & 1, p.err, kErrTc);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // B hi and lo planes are adjacent rows of one K-major tile: a single
+            // MMA of width 2N gives Whi.Xhi (columns [0, N)) and Whi.Xlo
+            // (columns [N, 2N)); Wlo.Xhi then accumulates into [N, 2N)
+            constexpr uint32_t idesc2 = idesc_f16<2 * N>();
+            constexpr uint32_t idesc = idesc_f16<N>();
+            for (int j = 0; j < nch; j++) {
+                const int sa = j % C::kStagesA, g = j / kGroup, b = g & 1;
+                const int u = j / C::kCB, sl = u % C::kSlotsB;  // the token slot holding chunk j
+                const bool first = j % kGroup == 0;  // the group's first chunk overwrites the set
+                if (first && g >= 2 && !wait(&accfree[b], ((g >> 1) - 1) & 1)) break;
+                if (!wait(&afull[sa], (j / C::kStagesA) & 1) || !wait(&bfull[sl], (u / C::kSlotsB) & 1)) break;
+                tc_fence_after();
+                const uint64_t bh = sw128_desc(smem_u32(sm + (sl * C::kCB + j % C::kCB) * C::kStage));
+                const uint32_t ah = tmem + (uint32_t)(C::kAccCols + kTaStageCols * sa), al = ah + 32;
+                const uint32_t dm = tmem + (uint32_t)(2 * N * b), dc = dm + N;
+#pragma unroll
+                for (int ks = 0; ks < kTcKC / 16; ks++) {
+                    // A: 8 columns (16 fp16 of K) per step; B: 32 bytes further along K
+                    tc_mma_f16_ts(dm, ah + 8 * ks, bh + 2 * ks, idesc2, !first || ks != 0);
+                    tc_mma_f16_ts(dc, al + 8 * ks, bh + 2 * ks, idesc, 1u);
+                }
+                if (j % kGroup == kGroup - 1 || j == nch - 1) tc_commit(&gdone[g % kTaDone]);
+            }
+        }
+    } else {
+        // ---------------- converters ----------------
+        const int ct = tid - 64, cw = ct >> 5;
+        // a warp writes only its own tensor-memory lane quadrant: rows 32 (warp & 3) + lane
+        const int r = 32 * (warp & 3) + lane, h = cw >> 2;  // tile row, which 32-block of the chunk
+        const int R = mt * kTcRows + r;
+        const bool rv = R < p.n;
+        const int nb = p.k >> 5;
+        const uint8_t* qrow = p.qs + (size_t)(rv ? R : 0) * p.k;
+        const uint16_t* drow = p.d + (size_t)(rv ? R : 0) * nb;
+        // rows scaled by 2^S with S = 22 - exponent field of max |d|: 127 max|d| 2^S < 2^15
+        const float rup = exp2i(22 - (rv ? (int)__ldg(p.rexp + R) : 0));
+        uint4 qa[4][2];
+        uint16_t dd[4];
+        auto load = [&](int j, uint4* q, uint16_t& dv) {
+            const int kb = 2 * (c0 + j) + h;
+            if (rv && kb < nb) {
+                const uint4* src = reinterpret_cast<const uint4*>(qrow + (size_t)kb * 32);
+                q[0] = __ldg(src);
+                q[1] = __ldg(src + 1);
+                dv = __ldg(drow + kb);
+            } else {
+                q[0] = q[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+                dv = 0;
+            }
+        };
+        auto convert = [&](int j, const uint4* q, uint16_t dv) {
+            const int sa = j % C::kStagesA;
+            if (j >= C::kStagesA) wait_group((j - C::kStagesA) / kGroup);
+            tc_fence_after();
+            // hi and lo planes of this row's 32 weights: 16 columns each (two
+            // fp16 of K per 32-bit column), the same exact half2 split as the
+            // shared-memory variant
+            const __half2 ds2 = __float2half2_rn(__fmul_rn(h2f(dv), rup));
+            const __half2 off = __float2half2_rn(1152.0f);
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(q);
+            uint32_t hw[16], lw[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const uint32_t pk = __byte_perm(w[i >> 1], 0x64646464u, (i & 1) ? 0x4342u : 0x4140u);
+                const __half2 q2 = __hsub2(u2h(pk), off);
+                const __half2 h2 = __hmul2_rn(q2, ds2);
+                hw[i] = h2u(h2);
+                lw[i] = h2u(__hfma2(q2, ds2, __hneg2(h2)));
+            }
+            const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) +
+                                (uint32_t)(C::kAccCols + kTaStageCols * sa + 16 * h);
+            tmem_st16(ta, hw);
+            tmem_st16(ta + 32, lw);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&afull[sa]);
+        };
+        // The tensor cores accumulate in fp32 with truncation; over a long K
+        // that biases sums toward zero. Each group of kGroup chunks therefore
+        // lands in one of two accumulator sets, and these threads add it into
+        // fp32 registers (round to nearest) one group later, while the MMAs
+        // fill the other set.
+        const int q4 = warp & 3, half = (warp - 2) >> 2;  // lane quadrant, column half
+        const int re = 32 * q4 + lane;
+        const uint32_t tq = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)(half * CH);
+        float acc[CH];
+#pragma unroll
+        for (int c = 0; c < CH; c++) acc[c] = 0.0f;
+        auto drain = [&](int g) {
+            const int b = g & 1;
+            wait_group(g);
+            tc_fence_after();
+            const uint32_t ta = tq + (uint32_t)(2 * N * b);
+            if (CH % 16 == 0) {
+#pragma unroll
+                for (int c = 0; c < CH; c += 16) {
+                    float mv[16], cv[16];
+                    tmem_ld16x2(ta + (uint32_t)c, ta + (uint32_t)(N + c), mv, cv);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc[c + i] = __fadd_rn(acc[c + i], __fadd_rn(mv[i], cv[i]));
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < CH; c += 8) {
+                    float mv[8], cv[8];
+                    tmem_ld8(ta + (uint32_t)c, mv);
+                    tmem_ld8(ta + (uint32_t)(N + c), cv);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) acc[c + i] = __fadd_rn(acc[c + i], __fadd_rn(mv[i], cv[i]));
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&accfree[b]);
+        };
+        if (nch > 0) load(0, qa[0], dd[0]);
+        if (nch > 1) load(1, qa[1], dd[1]);
+        if (nch > 2) load(2, qa[2], dd[2]);
+        int drained = 0;  // next group to drain
+        for (int j0 = 0; j0 < nch; j0 += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int j = j0 + u;
+                if (j < nch) {
+                    if (j + 3 < nch) load(j + 3, qa[(u + 3) & 3], dd[(u + 3) & 3]);
+                    convert(j, qa[u], dd[u]);
+                    // a group's chunks are converted: drain the group before it
+                    if (j % kGroup == kGroup - 1 && j >= kGroup) drain(drained++);
+                }
+            }
+        }
+        while (drained * kGroup < nch) drain(drained++);
+
+        // ---------------- epilogue ----------------
+        // 1. register accumulators (thread = row re, tokens of its column half)
+        //    -> scaled fp32 tile [N tokens][128 rows] in the idle stage memory
+        //    (every MMA has completed: the last drain waited for it)
+        float* stile = reinterpret_cast<float*>(sm);
+        {
+            const int Re = mt * kTcRows + re;
+            const float rdown = exp2i((Re < p.n ? (int)__ldg(p.rexp + Re) : 0) - 22);
+#pragma unroll
+            for (int c = 0; c < CH; c++) {
+                const int tl = half * CH + c;
+                stile[tl * kTcRows + re] = __fmul_rn(__fmul_rn(acc[c], rdown), exp2i(-__ldg(p.xe + tt * N + tl)));
+            }
+        }
+        named_sync_conv();
+        // 2. coalesced row-major passes: element e = ct + 256 i is (token e / 128,
+        //    row e % 128); groups of 16 keep 16 loads in flight per thread
+        constexpr int kPer = N * kTcRows / 256, kG = kPer < 16 ? kPer : 16;
+        const int rl = ct & (kTcRows - 1), Rg = mt * kTcRows + rl;
+        const bool rok = Rg < p.n;
+        auto tok_of = [&](int i) { return tt * N + ((ct + 256 * i) >> 7); };
+        auto epilogue = [&](int i0, const float* v) {
+            if (EPI == TC_RESID) {
+                float old[kG];
+#pragma unroll
+                for (int u = 0; u < kG; u++) {
+                    const int t = tok_of(i0 + u);
+                    old[u] = (rok && t < p.T) ? p.y[(size_t)t * p.ldy + Rg] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < kG; u++) {
+                    const int t = tok_of(i0 + u);
+                    if (rok && t < p.T) p.y[(size_t)t * p.ldy + Rg] = __fadd_rn(old[u], v[u]);
+                }
+            } else {
+                const float b = (EPI == TC_BIAS && rok) ? __ldg(p.bias + Rg) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < kG; u++) {
+                    const int t = tok_of(i0 + u);
+                    const bool ok_t = t < p.T;
+                    if (EPI == TC_SWIGLU) {
+                        // rows 2j (gate) and 2j+1 (up) sit in adjacent lanes
+                        const float upv = __shfl_down_sync(0xffffffffu, v[u], 1);
+                        if ((lane & 1) == 0 && rok && ok_t)
+                            p.y[(size_t)t * p.ldy + (Rg >> 1)] = __fmul_rn(silu_ref(v[u]), upv);
+                    } else if (rok && ok_t) {
+                        p.y[(size_t)t * p.ldy + Rg] = EPI == TC_BIAS ? __fadd_rn(v[u], b) : v[u];
+                    }
+                }
+            }
+        };
+        if (p.splits == 1 && EPI == TC_SWIGLU) {
+            // thread = one (gate, up) row pair of tokens ct / 64 + 4 i: one silu per pair
+            const int pr = ct & 63, R2 = mt * (kTcRows / 2) + pr;
+            const bool pok = 2 * R2 < p.n;
+#pragma unroll 4
+            for (int tl = ct >> 6; tl < N; tl += 4) {
+                const int t = tt * N + tl;
+                const float2 gu = *reinterpret_cast<const float2*>(stile + tl * kTcRows + 2 * pr);
+                if (pok && t < p.T) p.y[(size_t)t * p.ldy + R2] = __fmul_rn(silu_ref(gu.x), gu.y);
+            }
+        } else if (p.splits == 1) {
+#pragma unroll 1
+            for (int i0 = 0; i0 < kPer; i0 += kG) {
+                float v[kG];
+#pragma unroll
+                for (int u = 0; u < kG; u++) v[u] = stile[ct + 256 * (i0 + u)];
+                epilogue(i0, v);
+            }
+        } else {
+            // partial tile of this K range; the last CTA of the tile to arrive
+            // sums all of them in split order and runs the epilogue
+#pragma unroll 1
+            for (int i = 0; i < kPer; i++) {
+                const int t = tok_of(i);
+                if (rok && t < p.T) p.part[((size_t)z * p.T + t) * p.n + Rg] = stile[ct + 256 * i];
+            }
+            __threadfence();
+            named_sync_conv();
+            if (ct == 0) {
+                const unsigned int old = atomicAdd(&p.cnt[mt * gridDim.y + tt], 1u);
+                *s_flag = (old == (unsigned int)(p.splits - 1)) ? 1u : 0u;
+            }
+            named_sync_conv();
+            if (*s_flag != 0u) {
+                __threadfence();
+#pragma unroll 1
+                for (int i0 = 0; i0 < kPer; i0 += kG) {
+                    float v[kG];
+#pragma unroll
+                    for (int u = 0; u < kG; u++) v[u] = 0.0f;
+                    // per 8 elements: four splits' loads in flight before their in-order adds
+#pragma unroll
+                    for (int g0 = 0; g0 < kG; g0 += 8) {
+                        constexpr int kR = kG < 8 ? kG : 8;
+                        for (int z0 = 0; z0 < p.splits; z0 += 4) {
+                            float ld[4][kR];
+#pragma unroll
+                            for (int zi = 0; zi < 4; zi++)
+#pragma unroll
+                                for (int u = 0; u < kR; u++) {
+                                    const int t = tok_of(i0 + g0 + u);
+                                    ld[zi][u] = (rok && t < p.T && z0 + zi < p.splits)
+                                                    ? __ldcg(p.part + ((size_t)(z0 + zi) * p.T + t) * p.n + Rg)
+                                                    : 0.0f;
+                                }
+#pragma unroll
+                            for (int zi = 0; zi < 4; zi++)
+#pragma unroll
+                                for (int u = 0; u < kR; u++)
+                                    if (z0 + zi < p.splits) v[g0 + u] = __fadd_rn(v[g0 + u], ld[zi][u]);
+                        }
+                    }
+                    epilogue(i0, v);
+                }
+                if (ct == 0) p.cnt[mt * gridDim.y + tt] = 0u;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kCols);
+    }
+}
+
 // One token row -> optional RMSNorm -> power-of-two scale -> fp16 hi/lo in the
 // swizzled tile layout: [token tile][chunk][hi, lo][N tokens][64 halves], the
 // 16-byte chunk c of token row i stored at chunk c ^ (i & 7). Rows t >= T
@@ -579,26 +954,38 @@ __global__ void __launch_bounds__(256) tc_rowexp_kernel(const uint16_t* d, int n
     if (lane == 0) rexp[row] = (uint8_t)(mx >> 10);
 }
 
+// token tiles up to 64 take the tensor-memory-A kernel, 128 the shared-memory one
+template <int N, int EPI>
+constexpr auto tc_kernel() {
+    if constexpr (N <= 64) return tc_gemm_ta_kernel<N, EPI>;
+    else return tc_gemm_kernel<N, EPI>;
+}
+template <int N>
+constexpr int tc_smem() {
+    if constexpr (N <= 64) return TcCfgTa<N>::kSmem;
+    else return TcCfg<N>::kSmem;
+}
+
 template <int N>
 int set_smem() {
-    using C = TcCfg<N>;
-    static_assert(C::kSmem <= 227 * 1024, "tc_gemm shared memory");
-    JYC_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<N, TC_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    JYC_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<N, TC_BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    JYC_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<N, TC_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    JYC_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<N, TC_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    constexpr int smem = tc_smem<N>();
+    static_assert(smem <= 227 * 1024, "tc_gemm shared memory");
+    JYC_CUDA(cudaFuncSetAttribute(tc_kernel<N, TC_STORE>(), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    JYC_CUDA(cudaFuncSetAttribute(tc_kernel<N, TC_BIAS>(), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    JYC_CUDA(cudaFuncSetAttribute(tc_kernel<N, TC_RESID>(), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    JYC_CUDA(cudaFuncSetAttribute(tc_kernel<N, TC_SWIGLU>(), cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     return JYC_OK;
 }
 
 template <int N>
 int launch_n(const TcGemm& p, int epi, cudaStream_t s) {
     const dim3 grid((p.n + kTcRows - 1) / kTcRows, (p.T + N - 1) / N, p.splits);
-    const int smem = TcCfg<N>::kSmem;
+    constexpr int smem = tc_smem<N>();
     switch (epi) {
-        case TC_STORE: tc_gemm_kernel<N, TC_STORE><<<grid, kThreads, smem, s>>>(p); break;
-        case TC_BIAS: tc_gemm_kernel<N, TC_BIAS><<<grid, kThreads, smem, s>>>(p); break;
-        case TC_RESID: tc_gemm_kernel<N, TC_RESID><<<grid, kThreads, smem, s>>>(p); break;
-        case TC_SWIGLU: tc_gemm_kernel<N, TC_SWIGLU><<<grid, kThreads, smem, s>>>(p); break;
+        case TC_STORE: tc_kernel<N, TC_STORE>()<<<grid, kThreads, smem, s>>>(p); break;
+        case TC_BIAS: tc_kernel<N, TC_BIAS>()<<<grid, kThreads, smem, s>>>(p); break;
+        case TC_RESID: tc_kernel<N, TC_RESID>()<<<grid, kThreads, smem, s>>>(p); break;
+        case TC_SWIGLU: tc_kernel<N, TC_SWIGLU>()<<<grid, kThreads, smem, s>>>(p); break;
         default: return arg_error("tc_gemm: epilogue");
     }
     JYC_LAUNCHED();
