@@ -58,6 +58,7 @@ struct TcCfg {
 constexpr int kGroup = 2;         // K chunks accumulated per tensor-memory set before the drain
 constexpr int kTaStageCols = 64;  // one A stage: hi (32 columns) + lo (32 columns) of 128 rows x 64 K
 constexpr int kTaDone = 32;       // group-completion barriers in the ring (> any waiter's lag in groups)
+constexpr int kTaQRing = 8;       // chunks of weight bytes in flight per converter thread (cp.async)
 template <int N>
 struct TcCfgTa {
     static constexpr int kPlaneB = N * 128;
@@ -73,7 +74,8 @@ struct TcCfgTa {
     static_assert(kAccCols + kStagesA * kTaStageCols <= kCols, "tensor memory");
     // the epilogue tile [N][128] floats reuses the token stages
     static_assert(kStagesB * kStage >= N * kTcRows * 4, "epilogue tile");
-    static constexpr int kSmem = 1024 + kStagesB * kStage + 8 * (kStagesA + kSlotsB + kTaDone + 2) + 16;
+    static constexpr int kSmem =
+        1024 + kStagesB * kStage + kTaQRing * 256 * 32 + 8 * (kStagesA + kSlotsB + kTaDone + 2) + 16;
     static_assert(kStagesA % kGroup == 0, "A stages hold whole groups");
     static_assert(kStagesB / kGroup + kStagesA < kTaDone, "group ring deeper than any waiter's lag");
 };
@@ -170,6 +172,27 @@ __device__ __forceinline__ constexpr uint32_t idesc_f16() {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
 }
 __device__ __forceinline__ void named_sync_conv() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// 16-byte asynchronous global -> shared copy (L2 only) and its commit groups
+__device__ __forceinline__ void cp_async16_cg(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_groups() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// non-blocking test of an mbarrier phase (no suspension when not yet complete)
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // 2^e for e in [-126, 127], exactly
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -548,7 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_ta_kernel(TcGemm p) {
     // One tcgen05.commit per group of kGroup chunks (a commit costs hundreds of
     // cycles): gdone[g % kTaDone] completes when group g's MMAs have, which
     // frees its A and B stages and lets its accumulator set be drained.
-    uint64_t* afull = reinterpret_cast<uint64_t*>(sm + C::kStagesB * C::kStage);  // A stage written (256 arrivals)
+    // shared memory: token slots | weight-byte ring | barriers
+    uint64_t* afull = reinterpret_cast<uint64_t*>(sm + C::kStagesB * C::kStage + kTaQRing * 256 * 32);  // A stage written (256 arrivals)
     uint64_t* bfull = afull + C::kStagesA;                                         // token slot landed (tx)
     uint64_t* gdone = bfull + C::kSlotsB;                                          // [kTaDone] group MMAs done
     uint64_t* accfree = gdone + kTaDone;   // [2] accumulator set b drained (256 arrivals)
@@ -563,6 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_ta_kernel(TcGemm p) {
     const int c0 = z * per, nch = min(nkc, c0 + per) - c0;  // the host plan leaves no split empty
     // bounded wait; after any give-up in this CTA every later wait is skipped
     auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (mbar_test(bar, parity)) return true;  // already complete: no suspend round trip
         if (*s_abort) return false;
         if (mbar_wait_err(bar, parity, p.err, kErrTc)) return true;
         *s_abort = 1;
@@ -619,7 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_ta_kernel(TcGemm p) {
                 const int u = j / C::kCB, sl = u % C::kSlotsB;  // the token slot holding chunk j
                 const bool first = j % kGroup == 0;  // the group's first chunk overwrites the set
                 if (first && g >= 2 && !wait(&accfree[b], ((g >> 1) - 1) & 1)) break;
-                if (!wait(&afull[sa], (j / C::kStagesA) & 1) || !wait(&bfull[sl], (u / C::kSlotsB) & 1)) break;
+                if (!wait(&afull[sa], (j / C::kStagesA) & 1)) break;
+                if (j % C::kCB == 0 && !wait(&bfull[sl], (u / C::kSlotsB) & 1)) break;  // slot entry
                 tc_fence_after();
                 const uint64_t bh = sw128_desc(smem_u32(sm + (sl * C::kCB + j % C::kCB) * C::kStage));
                 const uint32_t ah = tmem + (uint32_t)(C::kAccCols + kTaStageCols * sa), al = ah + 32;
@@ -645,20 +671,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_ta_kernel(TcGemm p) {
         const uint16_t* drow = p.d + (size_t)(rv ? R : 0) * nb;
         // rows scaled by 2^S with S = 22 - exponent field of max |d|: 127 max|d| 2^S < 2^15
         const float rup = exp2i(22 - (rv ? (int)__ldg(p.rexp + R) : 0));
-        uint4 qa[4][2];
-        uint16_t dd[4];
-        auto load = [&](int j, uint4* q, uint16_t& dv) {
+        // weight bytes: each thread's 32 bytes per chunk land in its own slot
+        // of a kTaQRing-deep cp.async ring (64 KB in flight per SM); the fp16
+        // scales come 3 chunks ahead in registers
+        unsigned char* qring = sm + C::kStagesB * C::kStage + (size_t)ct * 32;  // + slot * 256 * 32
+        auto issue_q = [&](int j) {
             const int kb = 2 * (c0 + j) + h;
-            if (rv && kb < nb) {
-                const uint4* src = reinterpret_cast<const uint4*>(qrow + (size_t)kb * 32);
-                q[0] = __ldg(src);
-                q[1] = __ldg(src + 1);
-                dv = __ldg(drow + kb);
-            } else {
-                q[0] = q[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-                dv = 0;
+            if (j < nch && rv && kb < nb) {
+                const unsigned char* src = qrow + (size_t)kb * 32;
+                unsigned char* dst = qring + (size_t)(j % kTaQRing) * 256 * 32;
+                cp_async16_cg(dst, src);
+                cp_async16_cg(dst + 16, src + 16);
             }
+            cp_async_commit_group();
         };
+        uint16_t dd[4];
+        auto load = [&](int j, uint4*, uint16_t& dv) {
+            const int kb = 2 * (c0 + j) + h;
+            dv = (rv && kb < nb) ? __ldg(drow + kb) : (uint16_t)0;
+        };
+        uint4 qa[4][2];  // (the weight bytes of chunk j, read from the ring)
         auto convert = [&](int j, const uint4* q, uint16_t dv) {
             const int sa = j % C::kStagesA;
             if (j >= C::kStagesA) wait_group((j - C::kStagesA) / kGroup);
@@ -726,6 +758,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_ta_kernel(TcGemm p) {
         if (nch > 0) load(0, qa[0], dd[0]);
         if (nch > 1) load(1, qa[1], dd[1]);
         if (nch > 2) load(2, qa[2], dd[2]);
+#pragma unroll
+        for (int i = 0; i < kTaQRing - 1; i++) issue_q(i);
         int drained = 0;  // next group to drain
         for (int j0 = 0; j0 < nch; j0 += 4) {
 #pragma unroll
@@ -733,6 +767,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_ta_kernel(TcGemm p) {
                 const int j = j0 + u;
                 if (j < nch) {
                     if (j + 3 < nch) load(j + 3, qa[(u + 3) & 3], dd[(u + 3) & 3]);
+                    issue_q(j + kTaQRing - 1);
+                    cp_async_wait_groups<kTaQRing - 1>();  // this thread's bytes of chunk j landed
+                    {
+                        const int kb = 2 * (c0 + j) + h;
+                        if (rv && kb < nb) {
+                            const uint4* q = reinterpret_cast<const uint4*>(qring + (size_t)(j % kTaQRing) * 256 * 32);
+                            qa[u][0] = q[0];
+                            qa[u][1] = q[1];
+                        } else {
+                            qa[u][0] = qa[u][1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+                        }
+                    }
                     convert(j, qa[u], dd[u]);
                     // a group's chunks are converted: drain the group before it
                     if (j % kGroup == kGroup - 1 && j >= kGroup) drain(drained++);
