@@ -455,7 +455,7 @@ def run_c4(args):
         return 0
     torch.cuda.set_device(env_int("LOCAL_RANK", 0))
     cfg = CONFIGS["c4"]
-    ctx, new = 2048, 128
+    ctx, new = 2048, args.decode_tokens
     hw = HostWeights.synthetic(cfg)
     m = DeviceModel(hw)
     lib = _capi.load()
@@ -477,7 +477,7 @@ def run_c4(args):
     prefill_tps = None
     clocks = ClockSampler(env_int("LOCAL_RANK", 0))
     clocks.start()
-    for B in (1, 4, 16, 32, 64):
+    for B in [int(x) for x in args.seqs.split(",")]:
         bt = None
         if B == 1:
             ids = torch.from_numpy(prompts[0]).cuda()
@@ -507,12 +507,16 @@ def run_c4(args):
             for _ in range(args.warmup):
                 step()
             stream.synchronize()
+            if args.nvtx:
+                torch.cuda.nvtx.range_push("timed")
             e0, e1 = ev(), ev()
             e0.record(stream)
             for _ in range(args.steps):
                 step()
             e1.record(stream)
             stream.synchronize()
+            if args.nvtx:
+                torch.cuda.nvtx.range_pop()
         ms = e0.elapsed_time(e1) / args.steps / new  # per batched step
         kv = B * float(lib.jyc_model_kv_bytes_per_token(m.h, ctx + new // 2))
         gbs = (w_bytes + kv) / (ms / 1e3) / 1e9
@@ -543,6 +547,75 @@ def run_c4(args):
     return 0
 
 
+def run_prefill(args):
+    """Prompt prefill of one config on one GPU (the BASELINE metric's prefill
+    tok/s): configs[1] 512 tokens, configs[2] 2048, configs[3] 4096, random
+    seeded ids; one step = one whole prefill (K/V of every position written,
+    first token picked). Roofline: the tensor pipe; algorithmic FLOPs =
+    2 x matmul parameters x tokens + causal attention 4 L H hd T(T+1)/2."""
+    import numpy as np
+    import torch
+
+    from jieyu_b200 import _capi
+    from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids
+
+    if env_int("RANK", 0) != 0:
+        return 0
+    torch.cuda.set_device(env_int("LOCAL_RANK", 0))
+    cfg = CONFIGS[args.model]
+    T = cfg.prompt_len
+    hw = HostWeights.synthetic(cfg)
+    m = DeviceModel(hw)
+    lib = _capi.load()
+    D, F, qd, kvd = cfg.hidden, cfg.inter, cfg.q_dim, cfg.kv_dim
+    params = cfg.layers * (D * (qd + 2 * kvd) + qd * D + 3 * D * F)
+    flops = 2.0 * params * T + 4.0 * cfg.layers * cfg.heads * cfg.head_dim * T * (T + 1) / 2
+    tpeak = 1590.0
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        with open(pp) as f:
+            tpeak = float(json.load(f).get("bf16_tflops", tpeak))
+    ids = torch.from_numpy(prompt_ids(cfg, n=T)).cuda()
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            m.prefill_device(ids.data_ptr(), T, s)
+        stream.synchronize()
+        clocks = ClockSampler(env_int("LOCAL_RANK", 0))
+        clocks.start()
+        if args.nvtx:
+            torch.cuda.nvtx.range_push("timed")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = lib.jyc_kernel_launches()
+        e0.record(stream)
+        for _ in range(args.steps):
+            m.prefill_device(ids.data_ptr(), T, s)
+        e1.record(stream)
+        stream.synchronize()
+        if args.nvtx:
+            torch.cuda.nvtx.range_pop()
+        clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    assert lib.jyc_device_error(1) == 0
+    launches = lib.jyc_kernel_launches() - l0
+    m.close()
+    tflops = flops / (ms / 1e3) / 1e12
+    line = {
+        "metric": f"prefill tok/s ({args.model})", "value": T / (ms / 1e3), "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{cfg.name}: prefill of a {T}-token random prompt (Q8_0 weights)",
+                   "l2": "weights larger than L2 (126 MB)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tpeak, "unit": "TFLOP/s",
+                     "frac": tflops / tpeak, "flops_per_step": flops,
+                     "note": "algorithmic FLOPs; the exact fp16 hi/lo split issues 3x the matmul MMA work"},
+        "gpu_launches": int(launches), "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -550,9 +623,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp", "c4"],
+    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp", "c4", "prefill"],
                     help="c1: the headline decode line (default); c3-tp: configs[3] tensor parallel; "
-                         "c4: configs[4] batched decode sweep")
+                         "c4: configs[4] batched decode sweep; prefill: prompt prefill of --model")
+    ap.add_argument("--model", default="c1", choices=["c1", "c2", "c3"], help="prefill workload: which config")
+    ap.add_argument("--seqs", default="1,4,16,32,64", help="c4: sequence counts of the sweep")
+    ap.add_argument("--nvtx", action="store_true", help="mark the timed region as NVTX range 'timed' (profiling)")
+    ap.add_argument("--decode-tokens", type=int, default=128, help="c4: greedy tokens per sequence per step")
     ap.add_argument("--tp-mode", default="kernel", choices=["kernel", "nccl"],
                     help="c3-tp: in-kernel NVLink exchange (default) or NCCL between kernel windows")
     args = ap.parse_args()
@@ -564,6 +641,8 @@ def main():
         return run_tp(args)
     if args.workload == "c4":
         return run_c4(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
     return run_b200(args)
 
 
