@@ -548,24 +548,32 @@ def run_c4(args):
 
 
 def run_prefill(args):
-    """Prompt prefill of one config on one GPU (the BASELINE metric's prefill
-    tok/s): configs[1] 512 tokens, configs[2] 2048, configs[3] 4096, random
-    seeded ids; one step = one whole prefill (K/V of every position written,
-    first token picked). Roofline: the tensor pipe; algorithmic FLOPs =
-    2 x matmul parameters x tokens + causal attention 4 L H hd T(T+1)/2."""
-    import numpy as np
+    """Prompt prefill of one config (the BASELINE metric's prefill tok/s):
+    configs[1] 512 tokens, configs[2] 2048, configs[3] 4096, random seeded
+    ids; one step = one whole prefill (K/V of every position written, first
+    token picked). One GPU: the batched prefill. N GPUs (torchrun, configs[3]):
+    tensor parallel (jieyu_b200.tp.TPDecoder.prefill: shards' O and down
+    partials all-reduced over NCCL, one prompt per step over all ranks:
+    "scaling": "strong"), max over ranks. Roofline: the tensor pipe;
+    algorithmic FLOPs = 2 x matmul parameters x tokens + causal attention
+    4 L H hd T(T+1)/2."""
     import torch
 
     from jieyu_b200 import _capi
     from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids
 
-    if env_int("RANK", 0) != 0:
-        return 0
-    torch.cuda.set_device(env_int("LOCAL_RANK", 0))
+    world, rank, local = env_int("WORLD_SIZE", 1), env_int("RANK", 0), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
     cfg = CONFIGS[args.model]
     T = cfg.prompt_len
     hw = HostWeights.synthetic(cfg)
-    m = DeviceModel(hw)
     lib = _capi.load()
     D, F, qd, kvd = cfg.hidden, cfg.inter, cfg.q_dim, cfg.kv_dim
     params = cfg.layers * (D * (qd + 2 * kvd) + qd * D + 3 * D * F)
@@ -575,14 +583,30 @@ def run_prefill(args):
     if os.path.exists(pp):
         with open(pp) as f:
             tpeak = float(json.load(f).get("bf16_tflops", tpeak))
-    ids = torch.from_numpy(prompt_ids(cfg, n=T)).cuda()
-    stream = torch.cuda.Stream()
-    s = stream.cuda_stream
+    if world > 1:
+        from jieyu_b200.tp import TPDecoder
+        tp = TPDecoder(hw, rank, world, mode="kernel")
+        prompt = prompt_ids(cfg, n=T)
+        stream = tp.stream
+
+        def step():
+            tp.prefill(prompt)
+        close = tp.close
+    else:
+        m = DeviceModel(hw)
+        ids = torch.from_numpy(prompt_ids(cfg, n=T)).cuda()
+        stream = torch.cuda.Stream()
+
+        def step():
+            m.prefill_device(ids.data_ptr(), T, stream.cuda_stream)
+        close = m.close
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            m.prefill_device(ids.data_ptr(), T, s)
+            step()
         stream.synchronize()
-        clocks = ClockSampler(env_int("LOCAL_RANK", 0))
+        if dist is not None:
+            dist.barrier()
+        clocks = ClockSampler(local)
         clocks.start()
         if args.nvtx:
             torch.cuda.nvtx.range_push("timed")
@@ -590,26 +614,36 @@ def run_prefill(args):
         l0 = lib.jyc_kernel_launches()
         e0.record(stream)
         for _ in range(args.steps):
-            m.prefill_device(ids.data_ptr(), T, s)
+            step()
         e1.record(stream)
         stream.synchronize()
         if args.nvtx:
             torch.cuda.nvtx.range_pop()
         clk = clocks.stop()
     ms = e0.elapsed_time(e1) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     assert lib.jyc_device_error(1) == 0
     launches = lib.jyc_kernel_launches() - l0
-    m.close()
+    close()
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
     tflops = flops / (ms / 1e3) / 1e12
     line = {
-        "metric": f"prefill tok/s ({args.model})", "value": T / (ms / 1e3), "unit": "tok/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "dtype": "f32", "data": "synthetic",
+        "metric": f"prefill tok/s ({args.model})", "value": T / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{cfg.name}: prefill of a {T}-token random prompt (Q8_0 weights)",
+                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
                    "l2": "weights larger than L2 (126 MB)"},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tpeak, "unit": "TFLOP/s",
-                     "frac": tflops / tpeak, "flops_per_step": flops,
-                     "note": "algorithmic FLOPs; the exact fp16 hi/lo split issues 3x the matmul MMA work"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tpeak * world, "unit": "TFLOP/s",
+                     "frac": tflops / (tpeak * world), "flops_per_step": flops,
+                     "note": "algorithmic FLOPs over all GPUs; the exact fp16 hi/lo split issues 3x the matmul "
+                             "MMA work"},
         "gpu_launches": int(launches), "clocks": clk,
     }
     print(json.dumps(line), flush=True)

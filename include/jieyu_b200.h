@@ -296,6 +296,18 @@ JYC_API int jyc_model_decode_window(jyc_model* m, int first, int last, void* str
 JYC_API int jyc_model_tp_open(jyc_model* m, int size, int rank, void* handle_out);
 JYC_API int jyc_model_tp_connect(jyc_model* m, const void* handles);
 JYC_API int jyc_model_partials(jyc_model* m, float** o_part, int* o_count, float** d_part, int* d_count);
+/* Tensor-parallel prefill on a shard (no counterpart in the reference): runs
+ * half-layer phases [first, last) of the batched prefill for the token rows
+ * [start, start + rows) (ids already in the device token buffer; rows at most
+ * the batched prefill's pass, jyc_model_prefill_partial's max_rows): phase 2l =
+ * RMSNorm, QKV, RoPE + int8 cache append and attention of layer l, then the O
+ * projection; phase 2l+1 = RMSNorm, gate/up + SwiGLU, down projection. O and
+ * down write this shard's partial rows [rows][hidden] to the buffer that
+ * jyc_model_prefill_partial returns (no residual add); the caller sums it over
+ * the ranks (all-reduce) between windows, and the next window adds the sum to
+ * the residual stream. Phase 0 starts from the embedding. */
+JYC_API int jyc_model_prefill_window(jyc_model* m, int start, int rows, int first, int last, void* stream);
+JYC_API int jyc_model_prefill_partial(jyc_model* m, float** part, int* max_rows);
 
 /* ---- batched decode (configs[4]; no counterpart in the reference, whose
  * generate_cached runs one sequence, libs/model_libs/generate.h:9-89) ------- */

@@ -110,6 +110,8 @@ SIGNATURES = [
     ("jyc_model_tp_open", _I, [_P, _I, _I, _P]),
     ("jyc_model_tp_connect", _I, [_P, _P]),
     ("jyc_model_partials", _I, [_P, C.POINTER(_P), C.POINTER(_I), C.POINTER(_P), C.POINTER(_I)]),
+    ("jyc_model_prefill_window", _I, [_P, _I, _I, _I, _I, _P]),
+    ("jyc_model_prefill_partial", _I, [_P, C.POINTER(_P), C.POINTER(_I)]),
     ("jyc_device_error", _I, [_I]),
     ("jyc_model_trace_points", _I, [_P]),
     ("jyc_model_trace_decode", _I, [_P, _P, _P, _I]),

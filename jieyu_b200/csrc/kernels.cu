@@ -251,9 +251,17 @@ static int launch_gemv_t(const GemvArgs& a, cudaStream_t s) {
 template <int WT, int MT, int EPI>
 static int launch_gemv_rpw(const GemvArgs& a, cudaStream_t s) {
     // Enough row groups for ~2 waves of 4-warp CTAs on 148 SMs, but more rows
-    // per warp (fewer x reloads) when the matrix is tall.
-    if (EPI == EPI_SWIGLU) return launch_gemv_t<WT, MT, 2, EPI>(a, s);
-    if (MT > 1) return launch_gemv_t<WT, MT, 1, EPI>(a, s);
+    // per warp (the activation loads shared by more weight rows) when the
+    // matrix is tall; 8 activation rows keep one or two weight rows per warp
+    // (registers).
+    if (EPI == EPI_SWIGLU) {
+        if (MT <= 4 && a.n >= 148 * 4 * 4 * 2) return launch_gemv_t<WT, MT, 4, EPI>(a, s);
+        return launch_gemv_t<WT, MT, 2, EPI>(a, s);
+    }
+    if (MT == 8) {
+        if (a.n >= 148 * 4 * 2 * 2) return launch_gemv_t<WT, MT, 2, EPI>(a, s);
+        return launch_gemv_t<WT, MT, 1, EPI>(a, s);
+    }
     if (a.n >= 148 * 4 * 4 * 4) return launch_gemv_t<WT, MT, 4, EPI>(a, s);
     if (a.n >= 148 * 4 * 2 * 2) return launch_gemv_t<WT, MT, 2, EPI>(a, s);
     return launch_gemv_t<WT, MT, 1, EPI>(a, s);
@@ -262,6 +270,8 @@ static int launch_gemv_rpw(const GemvArgs& a, cudaStream_t s) {
 template <int WT, int EPI>
 static int launch_gemv_mt(const GemvArgs& a, cudaStream_t s) {
     if (a.m == 1) return launch_gemv_rpw<WT, 1, EPI>(a, s);
+    if (a.m == 2) return launch_gemv_rpw<WT, 2, EPI>(a, s);
+    if (a.m <= 4) return launch_gemv_rpw<WT, 4, EPI>(a, s);
     return launch_gemv_rpw<WT, 8, EPI>(a, s);
 }
 
@@ -288,6 +298,20 @@ int launch_gemv(const GemvArgs& a, int wtype, int epi, cudaStream_t s) {
     }
     if (a.k % 8) return arg_error("gemv: fp32 path needs k % 8 == 0");
     return launch_gemv_epi<W_F32>(a, epi, s);
+}
+
+// ---------------------------------------------------------------------------
+// x[i] += p[i] (the residual add of a partial sum computed elsewhere).
+__global__ void add_rows_kernel(float* x, const float* p, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        x[i] = __fadd_rn(x[i], p[i]);
+}
+int launch_add_rows(float* x, const float* p, size_t n, cudaStream_t s) {
+    if (n == 0) return JYC_OK;
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
+    add_rows_kernel<<<blocks, 256, 0, s>>>(x, p, n);
+    JYC_LAUNCHED();
+    return JYC_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -119,6 +119,7 @@ struct AttnArgs {
 int launch_gemv(const GemvArgs& a, int wtype, int epi, cudaStream_t s);
 int launch_rmsnorm(const float* x, float* y, const float* w, int rows, int n, float eps,
                    cudaStream_t s);
+int launch_add_rows(float* x, const float* p, size_t n, cudaStream_t s);
 int launch_rope_quant(const RopeQuantArgs& a, cudaStream_t s);
 int launch_rope(float* q, int seq, int start_pos, int heads, int hd, const float* cos_t,
                 const float* sin_t, cudaStream_t s);

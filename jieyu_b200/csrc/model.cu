@@ -112,6 +112,7 @@ struct jyc_model {
     std::vector<void*> tp_mapped;
     // batched prefill on the tensor cores: split activations, per-token
     // exponents, split-K partial sums and their arrival counters
+    float* pf_part = nullptr;  // [pf_rows][D]: a shard's O / down partial rows (tensor-parallel prefill)
     __half* tc_xs = nullptr;
     int* tc_xe = nullptr;
     float* tc_part = nullptr;
@@ -463,6 +464,7 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
         TRY(m->alloc(&m->tc_part, m->tc_part_floats));
         const size_t tiles = (size_t)((nmax + kTcRows - 1) / kTcRows) * ((m->pf_rows + 15) / 16);
         TRY(m->alloc(&m->tc_cnt, tiles));
+        TRY(m->alloc(&m->pf_part, (size_t)m->pf_rows * m->D));
         JYC_CUDA(cudaMemsetAsync(m->tc_cnt, 0, tiles * sizeof(unsigned int), m->stream));
         TRY(prepare_pf_kernels());
         TRY(prepare_tc_kernels());
@@ -634,6 +636,49 @@ int run_prefill_batched(jyc_model* m, int start, int n, cudaStream_t s) {
         last_rows = rows;
     }
     return run_head(m, last_rows - 1, s);
+}
+
+// Half-layer phases [first, last) of the batched prefill for token rows
+// [start, start + rows) of a tensor-parallel shard: phase 2l = RMSNorm + QKV +
+// RoPE/cache append + attention + O, phase 2l+1 = RMSNorm + gate/up + SwiGLU +
+// down. O and down leave this shard's partial rows in pf_part (no residual
+// add); the caller sums them over the ranks between windows and the next
+// phase adds the sum into X. Phase 0 starts from the embedding.
+int run_prefill_window(jyc_model* m, int start, int rows, int first, int last, cudaStream_t s) {
+    int* err = device_error_word();
+    for (int p = first; p < last; p++) {
+        const int l = p >> 1;
+        const DevLayer& ly = m->layers[l];
+        if (p == 0)
+            TRY(launch_embed(m->tokens, PosSrc{nullptr, start}, rows, m->embed_f, m->embed_q.qs, m->embed_q.d, m->D,
+                             m->X, s));
+        else
+            TRY(launch_add_rows(m->X, m->pf_part, (size_t)rows * m->D, s));
+        auto gemm = [&](const DevMat& w, const float* x, int ldx, const float* norm, float* y, int ldy,
+                        const float* bias, int epi) -> int {
+            return run_tc_gemm(m, w, x, ldx, rows, norm, y, ldy, bias, epi, err, s);
+        };
+        if ((p & 1) == 0) {
+            TRY(gemm(ly.qkv, m->X, m->D, ly.rms1, m->qkv, m->nqkv, ly.bias, ly.bias ? TC_BIAS : TC_STORE));
+            RopeQuantArgs rq{};
+            rq.q = m->qkv; rq.k = m->qkv + m->q_dim; rq.v = m->qkv + m->q_dim + m->kv_dim;
+            rq.ldq = m->nqkv; rq.rows = rows; rq.H = m->H; rq.KV = m->KV; rq.hd = m->hd;
+            rq.cos_t = m->cos_t; rq.sin_t = m->sin_t; rq.q8 = m->q8; rq.qsc = m->qsc;
+            rq.kv = m->kv_layer(l); rq.pos = PosSrc{nullptr, start};
+            TRY(launch_rope_quant(rq, s));
+            const KVView kv = m->kv_layer(l);
+            PfAttn at{};
+            at.q8 = m->q8; at.qsc = m->qsc; at.k8 = kv.k; at.v8 = kv.v; at.ks = kv.ks; at.vs = kv.vs;
+            at.max_seq = m->max_seq; at.H = m->H; at.KV = m->KV; at.hd = m->hd; at.T = rows;
+            at.pos0 = start; at.scale = 1.0f / sqrtf((float)m->hd); at.out = m->attn;
+            TRY(launch_pf_attention(at, s));
+            TRY(gemm(ly.o, m->attn, m->q_dim, nullptr, m->pf_part, m->D, nullptr, TC_STORE));
+        } else {
+            TRY(gemm(ly.gateup, m->X, m->D, ly.rms2, m->h, m->F, nullptr, TC_SWIGLU));
+            TRY(gemm(ly.down, m->h, m->F, nullptr, m->pf_part, m->D, nullptr, TC_STORE));
+        }
+    }
+    return JYC_OK;
 }
 
 int run_prefill(jyc_model* m, int start, int n, cudaStream_t s) {
@@ -841,6 +886,31 @@ JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prom
     JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids_dev, prompt_len * sizeof(int), cudaMemcpyDeviceToDevice, s));
     TRY(launch_set_state(m->st, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s));
     return run_prefill(m, 0, prompt_len, s);
+}
+
+JYC_API int jyc_model_prefill_window(jyc_model* m, int start, int rows, int first, int last, void* stream) {
+    clear_error();
+    if (!m) return arg_error("prefill_window: null model");
+    if (!m->pf_rows) {
+        set_error("prefill_window: the model has no batched prefill (Q8_0 weights, supported head shape)");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    if (rows <= 0 || rows > m->pf_rows || start < 0 || start + rows > m->max_seq)
+        return arg_error("prefill_window: rows must be in [1, " + std::to_string(m->pf_rows) + "] within max_seq");
+    if (first < 0 || last <= first || last > 2 * m->L) return arg_error("prefill_window: bad phase range");
+    return run_prefill_window(m, start, rows, first, last, static_cast<cudaStream_t>(stream));
+}
+
+JYC_API int jyc_model_prefill_partial(jyc_model* m, float** part, int* max_rows) {
+    clear_error();
+    if (!m || !part || !max_rows) return arg_error("prefill_partial: null argument");
+    if (!m->pf_rows) {
+        set_error("prefill_partial: the model has no batched prefill");
+        return JYC_ERR_UNSUPPORTED;
+    }
+    *part = m->pf_part;
+    *max_rows = m->pf_rows;
+    return JYC_OK;
 }
 
 JYC_API int jyc_model_rewind(jyc_model* m, int len, void* stream) {
@@ -1119,6 +1189,7 @@ struct jyc_batch {
     int* lens = nullptr;               // [B]
     float* logits = nullptr;           // [B][V]
     unsigned long long* slots = nullptr;
+    float* xn = nullptr;               // [B][hidden] normalised rows (GEMV path)
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* arrive = nullptr;
     int chunk = 64, nsplit = 1;
@@ -1163,11 +1234,17 @@ int batch_gemm(jyc_batch* bt, const DevMat& w, const float* x, int ldx, const fl
         const int tepi = epi == EPI_BIAS ? TC_BIAS : epi == EPI_RESID ? TC_RESID : epi == EPI_SWIGLU ? TC_SWIGLU : TC_STORE;
         return run_tc_gemm(m, w, x, ldx, bt->B, norm, y, ldy, bias, tepi, device_error_word(), s);
     }
+    // RMSNorm once per row (not once per weight row inside the GEMV)
+    if (norm) {
+        TRY(launch_rmsnorm(x, bt->xn, norm, bt->B, w.k, 1e-5f, s));
+        x = bt->xn;
+        ldx = w.k;
+    }
     for (int r0 = 0; r0 < bt->B; r0 += kMT) {
         GemvArgs g{};
         g.m = std::min(kMT, bt->B - r0); g.eps = 1e-5f;
         g.x = x + (size_t)r0 * ldx; g.ldx = ldx; g.n = w.n; g.k = w.k;
-        g.qs = w.qs; g.d = w.d; g.wt = w.f; g.norm_w = norm;
+        g.qs = w.qs; g.d = w.d; g.wt = w.f;
         g.y = y + (size_t)r0 * ldy; g.ldy = ldy; g.bias = bias;
         TRY(launch_gemv(g, w.f ? W_F32 : W_Q8, epi, s));
     }
@@ -1233,8 +1310,9 @@ int ensure_batch_graph(jyc_batch* bt) {
 int kernels_per_batch_step(const jyc_batch* bt) {
     const jyc_model* m = bt->m;
     const int per_gemm = bt->tc ? 2 : (bt->B + kMT - 1) / kMT;  // split + GEMM, or GEMV row chunks
-    // embed; per layer 4 matmuls + RoPE/KV append + attention; LM head; argmax + append
-    return 1 + m->L * (4 * per_gemm + 2) + per_gemm + 2;
+    const int norms = bt->tc ? 0 : 1;  // the GEMV path normalises in its own kernel (QKV, gate/up, head)
+    // embed; per layer 4 matmuls (2 normalised) + RoPE/KV append + attention; LM head; argmax + append
+    return 1 + m->L * (4 * per_gemm + 2 * norms + 2) + per_gemm + norms + 2;
 }
 
 }  // namespace
@@ -1281,6 +1359,7 @@ JYC_API jyc_batch* jyc_batch_create(jyc_model* m, int num_seqs) {
     if (r == JYC_OK) r = bt->alloc(&bt->lens, (size_t)num_seqs);
     if (r == JYC_OK) r = bt->alloc(&bt->logits, (size_t)num_seqs * m->V);
     if (r == JYC_OK) r = bt->alloc(&bt->slots, (size_t)num_seqs);
+    if (r == JYC_OK) r = bt->alloc(&bt->xn, (size_t)num_seqs * m->D);
     // attention split plan: about three CTAs per SM over (sequence, kv head, split)
     if (r == JYC_OK) {
         if (!bd_attention_supported(m->H, m->KV, m->hd))

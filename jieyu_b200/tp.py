@@ -204,6 +204,37 @@ class TPDecoder:
                 self.step(1)
         self.stream.synchronize()
 
+    def prefill(self, prompt: np.ndarray) -> None:
+        """Tensor-parallel prefill (call on every rank): the prompt's first
+        T - 1 tokens run in passes of the batched prefill, each pass as
+        half-layer windows with an NCCL all-reduce (sum) of the shards' O and
+        down partial rows between them; the last layer's MLP half is skipped
+        (no KV entry depends on it). The last prompt token then goes through
+        one tensor-parallel decode step, which writes its KV entries and
+        appends the first new token (the LM head's argmax over the ranks'
+        vocabulary slices)."""
+        torch, dist = self.torch, self.dist
+        T = len(prompt)
+        ids = torch.from_numpy(np.ascontiguousarray(prompt, dtype=np.int32)).cuda()
+        tok_ptr = self.lib.jyc_model_tokens_device(self.m.h)
+        toks = torch.as_tensor(_DevBuf(tok_ptr, self.cfg.max_seq + 1, "<i4"), device="cuda")
+        part, cap = C.c_void_p(), C.c_int()
+        check(self.lib.jyc_model_prefill_partial(self.m.h, C.byref(part), C.byref(cap)))
+        D, L = self.cfg.hidden, self.cfg.layers
+        pbuf = torch.as_tensor(_DevBuf(part.value, cap.value * D), device="cuda")
+        s = self.stream.cuda_stream
+        with torch.cuda.stream(self.stream):
+            toks[:T].copy_(ids)
+            n = T - 1
+            for start in range(0, n, cap.value):
+                rows = min(cap.value, n - start)
+                for p in range(2 * L - 1):
+                    check(self.lib.jyc_model_prefill_window(self.m.h, start, rows, p, p + 1, s))
+                    if p + 1 < 2 * L - 1:
+                        dist.all_reduce(pbuf[: rows * D], group=self.group)
+            check(self.lib.jyc_model_rewind(self.m.h, T, s))
+            self.step(1)
+
     def tokens(self, n: int) -> np.ndarray:
         torch = self.torch
         self.stream.synchronize()

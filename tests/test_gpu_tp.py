@@ -1,6 +1,9 @@
-"""Tensor-parallel decode on 2 GPUs (skipped with fewer): the sharded
-decode's greedy tokens equal the single-GPU decode's (tests/tp_worker.py),
-with the in-kernel NVLink exchange and with NCCL between kernel windows."""
+"""Tensor-parallel decode on 2 GPUs (skipped with fewer): every greedy token
+of the sharded decode is the whole model's argmax on the same history, or a
+near tie (tests/tp_worker.py),
+with the in-kernel NVLink exchange, with NCCL between kernel windows, and
+after a tensor-parallel batched prefill (NCCL all-reduce of the shards' O and
+down partial rows, two prefill passes)."""
 import os
 import socket
 import subprocess
@@ -18,7 +21,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("mode", ["kernel", "nccl"])
+@pytest.mark.parametrize("mode", ["kernel", "nccl", "prefill"])
 def test_tp2_decode_matches_single_gpu(cuda, mode):
     torch = cuda
     if torch.cuda.device_count() < 2:
