@@ -8,6 +8,7 @@
 #include "kernels.cuh"
 #include "mega.cuh"
 #include "tcgemm.cuh"
+#include "skinny.cuh"
 
 using namespace jyc;
 
@@ -80,6 +81,23 @@ JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d, 
             JYC_CUDA(cudaMemsetAsync(g.cnt, 0, tiles * sizeof(unsigned int), s));
         }
         return launch_tc_gemm(g, TC_STORE, s);
+    }
+    if (m > 1 && ((uintptr_t)A & 15) == 0 && ((uintptr_t)qs & 15) == 0) {
+        // a few rows: activations in registers, weights streamed once per 8 rows
+        cudaStream_t s = S(stream);
+        Scratch sc(s);
+        SkinnyWork w{};
+        const size_t cnt = skinny_counters(n);
+        TRY(sc.get(&w.part, skinny_part_floats(n, k)));
+        TRY(sc.get(&w.cnt, cnt));
+        JYC_CUDA(cudaMemsetAsync(w.cnt, 0, cnt * sizeof(unsigned int), s));
+        for (int r0 = 0; r0 < m; r0 += kSkMaxRows) {
+            SkinnyGemm g{};
+            g.x = A + (size_t)r0 * k; g.ldx = k; g.m = std::min(kSkMaxRows, m - r0); g.n = n; g.k = k;
+            g.qs = qs; g.d = d; g.y = C + (size_t)r0 * n; g.ldy = n;
+            TRY(launch_skinny(g, EPI_STORE, w, s));
+        }
+        return JYC_OK;
     }
     for (int r0 = 0; r0 < m; r0 += 8) {
         GemvArgs g{};

@@ -21,6 +21,7 @@
 #include "mega.cuh"
 #include "prefill.cuh"
 #include "tcgemm.cuh"
+#include "skinny.cuh"
 #include "batch.cuh"
 
 using namespace jyc;
@@ -1176,8 +1177,9 @@ JYC_API int jyc_model_length(jyc_model* m, void* stream) {
 // Batched decode: B independent sequences over one model, each with its own
 // int8 KV cache slot (the model's cache layout, [slot][layer][kv head][pos][hd])
 // and length; one step appends one greedy token to every sequence. The
-// matmuls run over the B rows together: generic GEMV kernels below
-// kTcMinRows sequences, tcgen05 token tiles from there on.
+// matmuls run over the B rows together: the few-row CUDA-core matmul
+// (8 sequences per launch) below kTcMinRows sequences, tcgen05 token tiles
+// from there on.
 // ===========================================================================
 struct jyc_batch {
     jyc_model* m = nullptr;
@@ -1189,7 +1191,7 @@ struct jyc_batch {
     int* lens = nullptr;               // [B]
     float* logits = nullptr;           // [B][V]
     unsigned long long* slots = nullptr;
-    float* xn = nullptr;               // [B][hidden] normalised rows (GEMV path)
+    SkinnyWork sk{};                   // workspace of the few-row matmuls (below kTcMinRows sequences)
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* arrive = nullptr;
     int chunk = 64, nsplit = 1;
@@ -1234,19 +1236,14 @@ int batch_gemm(jyc_batch* bt, const DevMat& w, const float* x, int ldx, const fl
         const int tepi = epi == EPI_BIAS ? TC_BIAS : epi == EPI_RESID ? TC_RESID : epi == EPI_SWIGLU ? TC_SWIGLU : TC_STORE;
         return run_tc_gemm(m, w, x, ldx, bt->B, norm, y, ldy, bias, tepi, device_error_word(), s);
     }
-    // RMSNorm once per row (not once per weight row inside the GEMV)
-    if (norm) {
-        TRY(launch_rmsnorm(x, bt->xn, norm, bt->B, w.k, 1e-5f, s));
-        x = bt->xn;
-        ldx = w.k;
-    }
-    for (int r0 = 0; r0 < bt->B; r0 += kMT) {
-        GemvArgs g{};
-        g.m = std::min(kMT, bt->B - r0); g.eps = 1e-5f;
-        g.x = x + (size_t)r0 * ldx; g.ldx = ldx; g.n = w.n; g.k = w.k;
-        g.qs = w.qs; g.d = w.d; g.wt = w.f;
+    // up to kSkMaxRows sequences per launch, RMSNorm fused
+    for (int r0 = 0; r0 < bt->B; r0 += kSkMaxRows) {
+        SkinnyGemm g{};
+        g.x = x + (size_t)r0 * ldx; g.ldx = ldx; g.m = std::min(kSkMaxRows, bt->B - r0);
+        g.n = w.n; g.k = w.k; g.qs = w.qs; g.d = w.d;
+        g.norm_w = norm; g.eps = 1e-5f;
         g.y = y + (size_t)r0 * ldy; g.ldy = ldy; g.bias = bias;
-        TRY(launch_gemv(g, w.f ? W_F32 : W_Q8, epi, s));
+        TRY(launch_skinny(g, epi, bt->sk, s));
     }
     return JYC_OK;
 }
@@ -1309,8 +1306,9 @@ int ensure_batch_graph(jyc_batch* bt) {
 
 int kernels_per_batch_step(const jyc_batch* bt) {
     const jyc_model* m = bt->m;
-    const int per_gemm = bt->tc ? 2 : (bt->B + kMT - 1) / kMT;  // split + GEMM, or GEMV row chunks
-    const int norms = bt->tc ? 0 : 1;  // the GEMV path normalises in its own kernel (QKV, gate/up, head)
+    const int passes = (bt->B + kSkMaxRows - 1) / kSkMaxRows;
+    const int per_gemm = bt->tc ? 2 : passes;  // split + GEMM, or one few-row matmul per 8 sequences
+    const int norms = bt->tc ? 0 : passes;     // the few-row path computes RMSNorm scales in a kernel
     // embed; per layer 4 matmuls (2 normalised) + RoPE/KV append + attention; LM head; argmax + append
     return 1 + m->L * (4 * per_gemm + 2 * norms + 2) + per_gemm + norms + 2;
 }
@@ -1359,7 +1357,25 @@ JYC_API jyc_batch* jyc_batch_create(jyc_model* m, int num_seqs) {
     if (r == JYC_OK) r = bt->alloc(&bt->lens, (size_t)num_seqs);
     if (r == JYC_OK) r = bt->alloc(&bt->logits, (size_t)num_seqs * m->V);
     if (r == JYC_OK) r = bt->alloc(&bt->slots, (size_t)num_seqs);
-    if (r == JYC_OK) r = bt->alloc(&bt->xn, (size_t)num_seqs * m->D);
+    if (r == JYC_OK && !bt->tc) {
+        size_t part = 1, cnt = 1;
+        auto need = [&](const DevMat& w) {
+            part = std::max(part, skinny_part_floats(w.n, w.k));
+            cnt = std::max(cnt, skinny_counters(w.n));
+        };
+        for (const DevLayer& ly : m->layers) {
+            need(ly.qkv); need(ly.o); need(ly.gateup); need(ly.down);
+        }
+        need(m->head);
+        r = prepare_skinny_kernels();
+        if (r == JYC_OK) r = bt->alloc(&bt->sk.part, part);
+        if (r == JYC_OK) r = bt->alloc(&bt->sk.cnt, cnt);
+        if (r == JYC_OK) r = bt->alloc(&bt->sk.sc, (size_t)kSkMaxRows);
+        if (r == JYC_OK) {
+            const cudaError_t e = cudaMemsetAsync(bt->sk.cnt, 0, cnt * sizeof(unsigned int), s);
+            if (e != cudaSuccess) r = cuda_fail(e, "cudaMemsetAsync");
+        }
+    }
     // attention split plan: about three CTAs per SM over (sequence, kv head, split)
     if (r == JYC_OK) {
         if (!bd_attention_supported(m->H, m->KV, m->hd))
