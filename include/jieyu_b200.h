@@ -134,10 +134,13 @@ JYC_API int jyc_q8_repack(const void* blocks, int n, int k,
 
 /* C[m][n] = A[m][k] . W^T for a Q8_0 weight W [n][k]; fp32 activations,
  * exact fp16->fp32 scale x int8 weight products, fp32 accumulation.
- * m < 16: GEMV kernels. m >= 16: tcgen05 tensor-core tiles over exact fp16
- * hi/lo splits of the dequantised weights and of A (fp32 accumulation in
- * tensor memory, drained every 128 of K); takes stream-ordered scratch
- * (cudaMallocAsync on `stream`) for the split copy of A.
+ * m == 1: GEMV kernel. 2 <= m < 16: the few-row matmul (8 rows of A per
+ * launch, activations held in registers, split-K partial sums summed in a
+ * fixed order), stream-ordered scratch (cudaMallocAsync on `stream`) for the
+ * partial sums. m >= 16: tcgen05 tensor-core tiles over exact fp16 hi/lo
+ * splits of the dequantised weights and of A (fp32 accumulation in tensor
+ * memory, drained every 128 of K); takes stream-ordered scratch for the
+ * split copy of A.
  * Replaces qmat::matmul_q(a,b,c,m,n,k,Q8_0) (libs/matmul_libs/matmul_q.h:134-162). */
 JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d,
                           float* C, int m, int n, int k, void* stream);
