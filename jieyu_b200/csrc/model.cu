@@ -1177,9 +1177,8 @@ JYC_API int jyc_model_length(jyc_model* m, void* stream) {
 // Batched decode: B independent sequences over one model, each with its own
 // int8 KV cache slot (the model's cache layout, [slot][layer][kv head][pos][hd])
 // and length; one step appends one greedy token to every sequence. The
-// matmuls run over the B rows together: the few-row CUDA-core matmul
-// (8 sequences per launch) below kTcMinRows sequences, tcgen05 token tiles
-// from there on.
+// matmuls run over the B rows together: the few-row CUDA-core matmul up to
+// kSkMaxRows (8) sequences, tcgen05 token tiles from 9 on.
 // ===========================================================================
 struct jyc_batch {
     jyc_model* m = nullptr;
@@ -1191,7 +1190,7 @@ struct jyc_batch {
     int* lens = nullptr;               // [B]
     float* logits = nullptr;           // [B][V]
     unsigned long long* slots = nullptr;
-    SkinnyWork sk{};                   // workspace of the few-row matmuls (below kTcMinRows sequences)
+    SkinnyWork sk{};                   // workspace of the few-row matmuls (up to 8 sequences)
     float *part_o = nullptr, *part_ml = nullptr;
     unsigned int* arrive = nullptr;
     int chunk = 64, nsplit = 1;
@@ -1306,9 +1305,8 @@ int ensure_batch_graph(jyc_batch* bt) {
 
 int kernels_per_batch_step(const jyc_batch* bt) {
     const jyc_model* m = bt->m;
-    const int passes = (bt->B + kSkMaxRows - 1) / kSkMaxRows;
-    const int per_gemm = bt->tc ? 2 : passes;  // split + GEMM, or one few-row matmul per 8 sequences
-    const int norms = bt->tc ? 0 : passes;     // the few-row path computes RMSNorm scales in a kernel
+    const int per_gemm = bt->tc ? 2 : 1;  // split + GEMM, or one few-row matmul
+    const int norms = bt->tc ? 0 : 1;     // the few-row path computes RMSNorm scales in a kernel
     // embed; per layer 4 matmuls (2 normalised) + RoPE/KV append + attention; LM head; argmax + append
     return 1 + m->L * (4 * per_gemm + 2 * norms + 2) + per_gemm + norms + 2;
 }
@@ -1339,7 +1337,7 @@ JYC_API jyc_batch* jyc_batch_create(jyc_model* m, int num_seqs) {
     bt->m = m;
     bt->B = num_seqs;
     bt->cap = m->max_seq;
-    bt->tc = num_seqs >= kTcMinRows;
+    bt->tc = num_seqs > kSkMaxRows;  // 9+ sequences: one padded 16-row tile beats two few-row passes
     auto fail = [&](int) -> jyc_batch* {
         delete bt;
         return nullptr;

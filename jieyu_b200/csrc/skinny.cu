@@ -8,7 +8,7 @@ namespace jyc {
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kSkMaxRW = 32;  // weight rows per warp unit at most
+constexpr int kSkMaxRW = 16;  // weight rows per warp unit at most
 constexpr int kSkThreads = kSkWarps * 32;
 constexpr int kSkSmemMax = kSkMaxRows * kSkSlice * 4 + kSkWarps * kSkMaxRW * (kSkSlice + 32);
 static_assert(kSkThreads == kSkSlice / 4, "one 16-byte column group of the slice per thread");
@@ -72,8 +72,8 @@ __device__ __forceinline__ void sk_store(const SkinnyGemm& g, int row, int t, bo
 // grid (row units / kSkWarps, K slices); warp w of CTA (bx, slice) owns rows
 // [(bx*kSkWarps + w)*RW, +RW) x columns [slice*512, +512).
 template <int MT, int EPI>
-__global__ void __launch_bounds__(kSkThreads, 2) skinny_kernel(SkinnyGemm g, SkinnyWork w, int RW, int npad,
-                                                              int nslices) {
+__global__ void __launch_bounds__(kSkThreads, MT <= 4 ? 3 : 2)
+    skinny_kernel(SkinnyGemm g, SkinnyWork w, int RW, int npad, int nslices) {
     constexpr int G = 32 / MT;  // weight rows per butterfly (G x MT = 32 sums)
     extern __shared__ __align__(16) unsigned char sk_smem[];
     float4* xs = reinterpret_cast<float4*>(sk_smem);                        // [MT][4 quads][32 lanes]
@@ -268,11 +268,13 @@ int launch_skinny(const SkinnyGemm& g, int epi, const SkinnyWork& w, cudaStream_
     const int nslices = (g.k + kSkSlice - 1) / kSkSlice;
     if (nslices > 1 && (!w.part || !w.cnt)) return arg_error("skinny: split-K workspace missing");
     if (g.norm_w && !w.sc) return arg_error("skinny: RMSNorm scale buffer missing");
-    // the largest unit with about two CTAs per SM (fewer rows per unit on short matrices)
+    // the largest unit that still fills every SM's CTA slots (fewer rows per
+    // unit on short matrices)
+    const int slots = 148 * (MT <= 4 ? 3 : 2);
     int RW = G;
     for (int cand = kSkMaxRW; cand >= G; cand >>= 1) {
         const long long ctas = (long long)((g.n + kSkWarps * cand - 1) / (kSkWarps * cand)) * nslices;
-        if (ctas >= 2 * 148) {
+        if (ctas >= slots) {
             RW = cand;
             break;
         }

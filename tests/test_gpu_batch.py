@@ -5,9 +5,9 @@ Every token a sequence appends is replayed through the oracle (bit-identical
 to the reference's forward, tests/test_oracle_golden.py) on that sequence's
 own history: it must be the oracle's argmax, or the oracle's top-2 logit gap
 at that step must be a near tie (below twice LOGIT_TOL of max|logit|, the
-bar of the model tests). B < 16 runs the few-row matmul (up to 8 sequences
-per launch, RMSNorm fused; B = 12 takes two launches), B >= 16 the tcgen05
-token tiles (B = 20 pads the last tile).
+bar of the model tests). B <= 8 runs the few-row matmul (RMSNorm fused),
+B >= 9 the tcgen05 token tiles (B = 12 pads one 16-row tile, B = 20 pads the
+last of two).
 """
 import ctypes as C
 
@@ -62,7 +62,7 @@ def _replay(oracle, hw, seq, prompt_len):
     return bad, ties
 
 
-@pytest.mark.parametrize("nseq,path", [(2, 1), (4, 1), (7, 1), (12, 1), (16, 2), (20, 2)])
+@pytest.mark.parametrize("nseq,path", [(2, 1), (4, 1), (7, 1), (8, 1), (12, 2), (16, 2), (20, 2)])
 def test_batch_follows_reference_per_sequence(c0, oracle, nseq, path):
     hw, m = c0
     prompts = _prompts(hw.cfg, nseq)
