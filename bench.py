@@ -443,8 +443,8 @@ def run_c4(args):
     GPU. B = 1, 4, 16, 32, 64 sequences, each prefilled with its own
     2048-token random prompt; one step = rewind every sequence to context
     2049 and decode 128 greedy tokens per sequence. B = 1 runs the
-    single-sequence decode kernel, B = 2..15 the few-row matmul (CUDA
-    cores, 8 sequences per launch), B >= 16 the tcgen05 tiles. Also times
+    single-sequence decode kernel, B = 2..8 the few-row matmul (CUDA
+    cores), B >= 9 the tcgen05 tiles. Also times
     the 2048-token prefill (configs[2]'s prefill)."""
     import numpy as np
     import torch

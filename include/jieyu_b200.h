@@ -319,7 +319,7 @@ JYC_API int jyc_model_prefill_partial(jyc_model* m, float** part, int* max_rows)
  * cache) and its own token buffer; every step appends one greedy token to
  * every sequence, with the same arithmetic per sequence as jyc_generate's
  * greedy steps. The matmuls of a step run over all num_seqs rows together:
- * GEMV kernels below 16 sequences, tcgen05 token tiles from 16 on. Needs a
+ * the few-row matmul up to 8 sequences, tcgen05 token tiles from 9 on. Needs a
  * Q8_0 model with the batched prefill; at most min(512, max_seq, 256)
  * sequences. While a batch runs, the model must not decode on its own (they
  * share the model's activation buffers). */
@@ -337,7 +337,7 @@ JYC_API int jyc_batch_rewind(jyc_batch* b, int len, void* stream);
 /* Copies up to cap ids of sequence `seq` (prompt + generated) to out_ids
  * (host); returns its length. Synchronises the device. */
 JYC_API int jyc_batch_tokens(jyc_batch* b, int seq, int* out_ids, int cap);
-/* 2: matmuls on the tcgen05 tiles, 1: GEMV kernels. */
+/* 2: matmuls on the tcgen05 tiles, 1: the few-row matmul. */
 JYC_API int jyc_batch_path(const jyc_batch* b);
 JYC_API int jyc_batch_kernels_per_step(const jyc_batch* b);
 /* KV-cache bytes one batched step reads with every sequence at context ctx. */
