@@ -16,6 +16,9 @@
  *   ffn                 libs/model_libs/ffn/ffn.h:7-19
  *   forward_cached      libs/model_libs/forward.h:47-96
  *   generate            libs/model_libs/generate.h:90-112
+ *   bfile::write_bfile  libs/model_libs/bfile.h:393-411 (model.bf writer)
+ *   bfile::View::open + bind_layers / bind_biases / bind_embed / bind_lm_head /
+ *   bind_final_norm     libs/model_libs/bfile.h:141-204, load_weights.h:97-155
  * Nothing here changes the reference's arithmetic; the harness only builds
  * WMat / LayerWeights / __KVcache objects over caller buffers.
  */
@@ -51,6 +54,9 @@
 #include "model_libs/transformer_layer.h"
 #include "model_libs/forward.h"
 #include "model_libs/generate.h"
+#include "model_libs/bfile.h"
+#include "model_libs/load_weights.h"
+#include <fstream>
 
 #include "jieyu_b200.h"
 
@@ -217,6 +223,87 @@ int jyref_generate(const jyc_model_desc* d, const int* prompt, int prompt_len,
         g_err = e.what();
         return -1;
     }
+}
+
+/* Writes a model.bf through the reference's writer. hdr = {hidden, layers,
+ * mode, num_heads, num_kv_heads, head_dim, intermediate, vocab}; tensor i has
+ * name names[i], dtype dtypes[i] (bfile::dtype_t), ndims[i] dims in
+ * shapes[4*i..], nbytes[i] bytes at data[i]. Returns 0, or -1 (message in
+ * jyref_last_error) when the writer rejects it. */
+int jyref_bfile_write(const char* path, const uint64_t* hdr, int n, const char* const* names,
+                      const uint8_t* dtypes, const uint8_t* ndims, const uint32_t* shapes,
+                      const void* const* data, const uint64_t* nbytes) {
+    try {
+        bfile::Header h;
+        h.hidden = hdr[0]; h.layers = hdr[1]; h.mode = (uint8_t)hdr[2];
+        h.num_heads = (uint8_t)hdr[3]; h.num_kv_heads = (uint8_t)hdr[4]; h.head_dim = (uint8_t)hdr[5];
+        h.intermediate = (uint32_t)hdr[6]; h.vocab_size = hdr[7];
+        std::vector<bfile::Tensor> ts((size_t)n);
+        for (int i = 0; i < n; i++) {
+            ts[i].name = names[i];
+            ts[i].dtype = dtypes[i];
+            ts[i].shape.assign(shapes + 4 * i, shapes + 4 * i + ndims[i]);
+            const unsigned char* p = static_cast<const unsigned char*>(data[i]);
+            ts[i].data.assign(p, p + nbytes[i]);
+        }
+        bfile::write_bfile(path, h, ts);
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+/* Opens a model.bf with the reference's reader (bfile::View::open over the
+ * file's bytes) and binds it with load_weights.h's rules. Per layer l,
+ * out[l*12 + k] = byte offset in the file of tensor k (0 input_layernorm,
+ * 1..4 q/k/v/o, 5 post_attention_layernorm, 6 gate, 7 down, 8 up, 9..11 q/k/v
+ * bias) or -1 when absent; then embed, lm_head, final norm at out[12 L ..].
+ * dt[...] gets the matching dtype codes (bfile::dtype_t, 255 when absent).
+ * Returns 0, 1 when the reader rejects the file, 2 when binding fails. */
+int jyref_bfile_bind(const char* path, int num_layers, int hidden, int vocab, int64_t* out, uint8_t* dt) {
+    static std::vector<unsigned char> bytes;
+    std::ifstream f(path, std::ios::binary);
+    if (!f) { g_err = "cannot open"; return 1; }
+    bytes.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
+    bfile::current().reset();
+    if (!bfile::current().open(bytes.data(), bytes.size())) { g_err = "reader rejected the file"; return 1; }
+    const unsigned char* base = bytes.data();
+    std::vector<LayerWeights> lw((size_t)num_layers);
+    std::string missing;
+    if (!bind_layers(lw.data(), num_layers, &missing)) { g_err = "missing " + missing; return 2; }
+    bind_biases(lw.data(), num_layers);
+    auto off = [&](const void* p) -> int64_t {
+        return p ? (int64_t)(static_cast<const unsigned char*>(p) - base) : -1;
+    };
+    auto wm = [&](const WMat& m, int64_t* o, uint8_t* d) {
+        if (m.f) { *o = off(m.f); *d = bfile::F32; }
+        else if (m.h) { *o = off(m.h); *d = bfile::F16; }
+        else if (m.q) { *o = off(m.q); *d = m.qt == qmat::Q8_0 ? bfile::Q8_0 : m.qt == qmat::Q4K ? bfile::Q4K
+                                       : m.qt == qmat::Q5K ? bfile::Q5K : bfile::Q6K; }
+        else { *o = -1; *d = 255; }
+    };
+    for (int l = 0; l < num_layers; l++) {
+        int64_t* o = out + 12 * l;
+        uint8_t* d = dt + 12 * l;
+        const LayerWeights& w = lw[(size_t)l];
+        o[0] = off(w.rms1_weight); d[0] = bfile::F32;
+        wm(w.Wq, o + 1, d + 1); wm(w.Wk, o + 2, d + 2); wm(w.Wv, o + 3, d + 3); wm(w.Wo, o + 4, d + 4);
+        o[5] = off(w.rms2_weight); d[5] = bfile::F32;
+        wm(w.W1, o + 6, d + 6); wm(w.W2, o + 7, d + 7); wm(w.W3, o + 8, d + 8);
+        o[9] = off(w.bq); o[10] = off(w.bk); o[11] = off(w.bv);
+        for (int b = 9; b < 12; b++) d[b] = o[b] < 0 ? 255 : bfile::F32;
+    }
+    int64_t* o = out + 12 * num_layers;
+    uint8_t* d = dt + 12 * num_layers;
+    const WMat emb = bind_embed();
+    if (emb.empty()) { g_err = "missing embedding"; return 2; }
+    wm(emb, o + 0, d + 0);
+    const WMat head = bind_lm_head(hidden, vocab);
+    if (head.empty()) { g_err = "lm_head missing or misshapen"; return 2; }
+    wm(head, o + 1, d + 1);
+    o[2] = off(bind_final_norm()); d[2] = o[2] < 0 ? 255 : bfile::F32;
+    return 0;
 }
 
 }  // extern "C"
