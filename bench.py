@@ -548,6 +548,122 @@ def run_c4(args):
     return 0
 
 
+def run_kquant(args):
+    """K-quant weights (the formats of the reference's published downloads):
+    one step = one m=1 matmul (jyc_matmul_qk) over every linear weight of the
+    configs[2] shape (Llama-3.2-1B: 16 layers x Q, K, V, O, gate, up, down;
+    0.55 / 0.67 / 0.80 GB per step for Q4_K / Q5_K / Q6_K, larger than L2),
+    captured in one CUDA graph per format,
+    seeded random blocks with finite scales. value = Q4_K weight GB/s; the
+    roofline is HBM (algorithmic bytes = the blocks). The CPU baseline is the
+    reference's own qmat::matmul_q on one layer's Q4_K matrices (oracle/_ref,
+    else the oracle port), all host threads."""
+    import numpy as np
+    import torch
+
+    from jieyu_b200 import _capi
+    from jieyu_b200.model import CONFIGS
+
+    if env_int("RANK", 0) != 0:
+        return 0
+    torch.cuda.set_device(env_int("LOCAL_RANK", 0))
+    cfg = CONFIGS["c2"]
+    D, F, qd, kvd = cfg.hidden, cfg.inter, cfg.q_dim, cfg.kv_dim
+    shapes = [(qd, D), (kvd, D), (kvd, D), (D, qd), (F, D), (F, D), (D, F)] * cfg.layers
+    lib = _capi.load()
+    peak, peak_kind = measured_peaks()
+    stream = torch.cuda.Stream()
+    x = torch.randn(max(D, F, qd), device="cuda", dtype=torch.float32)
+    y = torch.empty(max(D, F, qd), device="cuda", dtype=torch.float32)
+    bb = {0: 144, 1: 176, 2: 210}
+    names = {0: "q4_K", 1: "q5_K", 2: "q6_K"}
+    sweep = []
+    clocks = ClockSampler(env_int("LOCAL_RANK", 0))
+    clocks.start()
+    for qt in (0, 1, 2):
+        mats = []
+        for (n, k) in shapes:
+            w = torch.randint(0, 256, (n * (k // 256), bb[qt]), dtype=torch.uint8, device="cuda")
+            if qt == 2:
+                w[:, 208:210] = torch.tensor([0x00, 0x18], dtype=torch.uint8, device="cuda")  # fp16 2^-9
+            else:
+                w[:, 0:4] = torch.tensor([0x00, 0x18, 0x00, 0x14], dtype=torch.uint8, device="cuda")
+            mats.append((w, n, k))
+        nbytes = float(sum(w.numel() for w, _, _ in mats))
+
+        def launch_all():
+            for w, n, k in mats:
+                _capi.check(lib.jyc_matmul_qk(x.data_ptr(), w.data_ptr(), y.data_ptr(), 1, n, k, qt,
+                                              torch.cuda.current_stream().cuda_stream))
+        with torch.cuda.stream(stream):
+            launch_all()  # warm (module load)
+            stream.synchronize()
+        graph = torch.cuda.CUDAGraph()  # one step = one replay: no host launch gaps in the timing
+        with torch.cuda.graph(graph, stream=stream):
+            launch_all()
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                graph.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+            stream.synchronize()
+        del graph
+        ms = e0.elapsed_time(e1) / args.steps
+        gbs = nbytes / (ms / 1e3) / 1e9
+        sweep.append({"format": names[qt], "ms_per_step": ms, "bytes_per_step": nbytes, "gbs": gbs,
+                      "hbm_frac": gbs / peak, "launches_per_step": len(mats)})
+        del mats
+    clk = clocks.stop()
+    # CPU baseline: the reference's matmul_q over one layer's Q4_K matrices
+    rng = np.random.default_rng(7)
+    host = []
+    for (n, k) in shapes[:7]:
+        b = rng.integers(0, 256, size=(n * (k // 256), 144), dtype=np.uint8)
+        b[:, 0:4] = np.array([0x00, 0x18, 0x00, 0x14], np.uint8)
+        host.append((np.ascontiguousarray(b), n, k))
+    xa = np.random.default_rng(8).standard_normal(max(D, F)).astype(np.float32)
+    ya = np.empty(max(D, F, qd), np.float32)
+    cpu = None
+    try:
+        sys.path.insert(0, ROOT)
+        from oracle.bind import Oracle, Reference, reference_available
+        if reference_available():
+            ref, kind = Reference(), "reference"
+            fn = ref.lib.jyref_matmul_qk
+        else:
+            ref, kind = Oracle(), "port"
+            fn = ref.lib.jyo_matmul_qk
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 3.0:
+            for b, n, k in host:
+                fn(xa.ctypes.data, b.ctypes.data, ya.ctypes.data, 1, n, k, 0)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        lbytes = float(sum(b.nbytes for b, _, _ in host))
+        cpu = {"value": lbytes / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": kind,
+               "sample": f"one configs[2] layer's 7 Q4_K matrices ({lbytes / 1e6:.1f} MB), m=1, {reps} passes"}
+    except Exception as e:  # the checker is absent on this host: report why
+        cpu = {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port", "sample": f"unavailable: {e}"}
+    q4 = sweep[0]
+    line = {
+        "metric": "K-quant matmul weight GB/s (configs[2] shape, m=1)", "value": q4["gbs"], "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "jyc_matmul_qk over the 112 linear weights of the configs[2] shape, one activation row",
+                   "l2": "inputs larger than L2 (0.55 GB of Q4_K blocks per step)"},
+        "sweep": sweep,
+        "roofline": {"bound": "hbm", "kernel": "kq_gemv_kernel<Q4_K, 1>", "achieved": q4["gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": q4["gbs"] / peak, "traffic": None, "peak_kind": peak_kind},
+        "gpu_launches": len(shapes) * args.steps, "clocks": clk, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_prefill(args):
     """Prompt prefill of one config (the BASELINE metric's prefill tok/s):
     configs[1] 512 tokens, configs[2] 2048, configs[3] 4096, random seeded
@@ -658,9 +774,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp", "c4", "prefill"],
+    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp", "c4", "prefill", "kquant"],
                     help="c1: the headline decode line (default); c3-tp: configs[3] tensor parallel; "
-                         "c4: configs[4] batched decode sweep; prefill: prompt prefill of --model")
+                         "c4: configs[4] batched decode sweep; prefill: prompt prefill of --model; "
+                         "kquant: K-quant matmul bandwidth")
     ap.add_argument("--model", default="c1", choices=["c1", "c2", "c3"], help="prefill workload: which config")
     ap.add_argument("--seqs", default="1,4,16,32,64", help="c4: sequence counts of the sweep")
     ap.add_argument("--nvtx", action="store_true", help="mark the timed region as NVTX range 'timed' (profiling)")
@@ -676,6 +793,8 @@ def main():
         return run_tp(args)
     if args.workload == "c4":
         return run_c4(args)
+    if args.workload == "kquant":
+        return run_kquant(args)
     if args.workload == "prefill":
         return run_prefill(args)
     return run_b200(args)

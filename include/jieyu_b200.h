@@ -145,6 +145,17 @@ JYC_API int jyc_q8_repack(const void* blocks, int n, int k,
 JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d,
                           float* C, int m, int n, int k, void* stream);
 
+/* C[m][n] = A[m][k] . W^T for a K-quant weight W [n][k] given as the
+ * reference's super-blocks of 256 weights, row after row, on the device
+ * (qtype JYC_Q4K: 144 B per block, JYC_Q5K: 176 B, JYC_Q6K: 210 B; GGUF's
+ * block layout, as model.bf stores it). Each block is dequantised to the
+ * reference's fp32 values (Q4_K as its AVX2+FMA path: fma(q, d*sc, -dmin*m);
+ * Q5_K d*sc*q - dmin*m; Q6_K (d*sc)*q), accumulated in fp32. k % 256 == 0;
+ * A 16-byte aligned, blocks 4-byte aligned. One kernel launch per 8 rows of A.
+ * Replaces qmat::matmul_q(a,b,c,m,n,k,Q4K|Q5K|Q6K) (libs/matmul_libs/matmul_q.h:134-162). */
+JYC_API int jyc_matmul_qk(const float* A, const void* blocks, float* C, int m, int n, int k,
+                          int qtype, void* stream);
+
 /* C[m][n] = A[m][k] . B with B given TRANSPOSED on the device, Bt [n][k]
  * (jyc_f32_transpose makes it from the reference's [k][n]).
  * Replaces matmul(m,n,k,A,B,C) (libs/matmul_libs/matmul.h:7-76). */

@@ -83,6 +83,7 @@ SIGNATURES = [
     ("jyc_quantize_q8_0", _I, [_P, _P, _SZ, _SZ]),
     ("jyc_q8_repack", _I, [_P, _I, _I, _P, _P, _P]),
     ("jyc_matmul_q8", _I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    ("jyc_matmul_qk", _I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     ("jyc_matmul_f32", _I, [_P, _P, _P, _I, _I, _I, _P]),
     ("jyc_f32_transpose", _I, [_P, _P, _I, _I, _P]),
     ("jyc_rmsnorm", _I, [_P, _P, _P, _I, _I, _F, _P]),

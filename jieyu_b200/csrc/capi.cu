@@ -108,6 +108,13 @@ JYC_API int jyc_matmul_q8(const float* A, const uint8_t* qs, const uint16_t* d, 
     return JYC_OK;
 }
 
+JYC_API int jyc_matmul_qk(const float* A, const void* blocks, float* C, int m, int n, int k, int qtype,
+                          void* stream) {
+    clear_error();
+    if (!A || !blocks || !C) return arg_error("matmul_qk: null pointer");
+    return launch_kquant_matmul(A, m, n, k, static_cast<const uint8_t*>(blocks), qtype, C, S(stream));
+}
+
 JYC_API int jyc_f32_transpose(const float* B, float* Bt, int k, int n, void* stream) {
     clear_error();
     if (!B || !Bt) return arg_error("f32_transpose: null pointer");

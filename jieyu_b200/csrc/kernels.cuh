@@ -146,4 +146,9 @@ int launch_sample(float* logits, int V, float temperature, float penalty, const 
 int launch_set_state(DevState* st, int len, int max_new, int max_len, const int* eos, int n_eos,
                      cudaStream_t s);
 
+// Matmul over K-quant weights in the reference's block layout (qtype
+// JYC_Q4K / JYC_Q5K / JYC_Q6K, k % 256 == 0): y[m][n] = x[m][k] . W^T.
+int launch_kquant_matmul(const float* x, int m, int n, int k, const uint8_t* wq, int qtype, float* y,
+                         cudaStream_t s);
+
 }  // namespace jyc

@@ -1,0 +1,215 @@
+// kquant.cu — matmul over K-quant weights (Q4_K, Q5_K, Q6_K super-blocks of
+// 256 weights, the reference's block layouts read in place): y[t][r] =
+// sum_k W[r][k] x[t][k] for up to 8 activation rows per launch.
+//
+// Reference: qmat::matmul_q with t = Q4K / Q5K / Q6K
+// (libs/matmul_libs/matmul_q.h:134-162): every block is dequantised to fp32
+// (Q4_K as file_libs/q4/q4_fma.txt does, w = fma(q, d*sc, -(dmin*mn)); Q5_K
+// d1*q - n1, matmul_q.h:52-77; Q6_K (d*sc)*q, matmul_q.h:78-100) and dotted
+// with x in fp32. Here the dequantised values are the same floats; only the
+// summation order of the dot differs.
+//
+// One CTA per pair of consecutive weight rows (grid-stride), its 8 warps
+// splitting the rows' super-blocks (block bl to warp bl % 8); lane l
+// dequantises 8 of each super-block's 256 weights:
+//   Q4_K / Q5_K: group g = l/8 of 64 weights, byte quad p = 4 (l%8): the low
+//     nibbles are weights 64g+p..+3 (sub-block 2g), the high nibbles
+//     64g+32+p..+3 (sub-block 2g+1);
+//   Q6_K: position l of both 128-weight halves: weights 128h + l + 32j.
+// Per-lane fp32 FMAs, a warp sum, then the 8 warps' sums in warp order.
+#include <algorithm>
+
+#include "kernels.cuh"
+
+namespace jyc {
+
+namespace {
+
+constexpr int kKqWarps = 8;
+constexpr int kKqMaxRows = 8;
+// consecutive weight rows per CTA (bytes in flight, shared x loads; 4 rows
+// measured slower: registers halve the resident CTAs)
+constexpr int kKqRowsPerCta = 2;
+
+__device__ __forceinline__ float kq_h2f(uint32_t bits) { return __half2float(__ushort_as_half((uint16_t)bits)); }
+
+// 6-bit scale / min of sub-block j from the 12 scale bytes q
+// (matmul_q.h:24-33 get_scale_min_k4)
+__device__ __forceinline__ void kq_scale_min(int j, const uint8_t* q, unsigned& sc, unsigned& mn) {
+    if (j < 4) {
+        sc = q[j] & 63u;
+        mn = q[j + 4] & 63u;
+    } else {
+        sc = (q[j + 4] & 0xFu) | ((unsigned)(q[j - 4] >> 6) << 4);
+        mn = (unsigned)(q[j + 4] >> 4) | ((unsigned)(q[j] >> 6) << 4);
+    }
+}
+
+template <int QT>
+constexpr int kq_block_bytes() {
+    return QT == JYC_Q4K ? 144 : QT == JYC_Q5K ? 176 : 210;
+}
+
+// The 8 dequantised weights of lane `lane` in super-block `b` and the
+// offsets (within the block's 256) of the first four / last four of them
+// (Q6_K: o0 only, its weights sit at 128h + o0 + 32j).
+template <int QT>
+__device__ __forceinline__ void kq_dequant(const uint8_t* b, int lane, float (&w)[8], int& o0, int& o1) {
+    if (QT == JYC_Q6K) {
+        // ql[128] | qh[64] | int8 scales[16] | fp16 d
+        const float d = kq_h2f(*reinterpret_cast<const uint16_t*>(b + 208));
+        const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192);
+        const int is = lane >> 4;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const unsigned l0 = b[64 * h + lane], l1 = b[64 * h + lane + 32], hh = b[128 + 32 * h + lane];
+            const int q1 = (int)((l0 & 0xFu) | (((hh >> 0) & 3u) << 4)) - 32;
+            const int q2 = (int)((l1 & 0xFu) | (((hh >> 2) & 3u) << 4)) - 32;
+            const int q3 = (int)((l0 >> 4) | (((hh >> 4) & 3u) << 4)) - 32;
+            const int q4 = (int)((l1 >> 4) | (((hh >> 6) & 3u) << 4)) - 32;
+            const int s = 8 * h + is;
+            w[4 * h + 0] = __fmul_rn(__fmul_rn(d, (float)sc[s]), (float)q1);
+            w[4 * h + 1] = __fmul_rn(__fmul_rn(d, (float)sc[s + 2]), (float)q2);
+            w[4 * h + 2] = __fmul_rn(__fmul_rn(d, (float)sc[s + 4]), (float)q3);
+            w[4 * h + 3] = __fmul_rn(__fmul_rn(d, (float)sc[s + 6]), (float)q4);
+        }
+        o0 = lane;  // weights 128h + lane + 32j
+        o1 = 0;
+    } else {
+        const uint32_t dd = *reinterpret_cast<const uint32_t*>(b);  // fp16 d | fp16 dmin
+        const float d = kq_h2f(dd & 0xFFFFu), dmin = kq_h2f(dd >> 16);
+        const int g = lane >> 3, p = 4 * (lane & 7);
+        unsigned s0, m0, s1, m1;
+        kq_scale_min(2 * g, b + 4, s0, m0);
+        kq_scale_min(2 * g + 1, b + 4, s1, m1);
+        const float d1 = __fmul_rn(d, (float)s0), n1 = __fmul_rn(dmin, (float)m0);
+        const float d2 = __fmul_rn(d, (float)s1), n2 = __fmul_rn(dmin, (float)m1);
+        const uint8_t* qs = b + (QT == JYC_Q4K ? 16 : 48) + 32 * g + p;
+        const uint32_t q = *reinterpret_cast<const uint32_t*>(qs);
+        if (QT == JYC_Q4K) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                w[i] = __fmaf_rn((float)((q >> (8 * i)) & 0xFu), d1, -n1);
+                w[4 + i] = __fmaf_rn((float)((q >> (8 * i + 4)) & 0xFu), d2, -n2);
+            }
+        } else {
+            const uint32_t qh = *reinterpret_cast<const uint32_t*>(b + 16 + p);
+            const unsigned u1 = 1u << (2 * g), u2 = 2u << (2 * g);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const unsigned hb = (qh >> (8 * i)) & 0xFFu;
+                const unsigned lo = ((q >> (8 * i)) & 0xFu) + ((hb & u1) ? 16u : 0u);
+                const unsigned hi = ((q >> (8 * i + 4)) & 0xFu) + ((hb & u2) ? 16u : 0u);
+                w[i] = __fsub_rn(__fmul_rn(d1, (float)lo), n1);
+                w[4 + i] = __fsub_rn(__fmul_rn(d2, (float)hi), n2);
+            }
+        }
+        o0 = 64 * g + p;       // w[0..3]
+        o1 = 64 * g + 32 + p;  // w[4..7]
+    }
+}
+
+template <int QT, int MT>
+__global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_kernel(const float* __restrict__ x, int ldx, int m, int n,
+                                                                int k, const uint8_t* __restrict__ wq,
+                                                                float* __restrict__ y, int ldy) {
+    constexpr int BB = kq_block_bytes<QT>();
+    constexpr int R = kKqRowsPerCta;
+    __shared__ float s_part[kKqWarps][MT][R];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nblk = k >> 8;
+    const size_t rbytes = (size_t)nblk * BB;
+    for (int row0 = blockIdx.x * R; row0 < n; row0 += gridDim.x * R) {
+        const uint8_t* rp[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) rp[r] = wq + (size_t)min(row0 + r, n - 1) * rbytes;  // a missing last row re-reads row n-1
+        float acc[MT][R];
+#pragma unroll
+        for (int t = 0; t < MT; t++)
+#pragma unroll
+            for (int r = 0; r < R; r++) acc[t][r] = 0.0f;
+        // warp w takes super-blocks w, w + kKqWarps, ... of the CTA's rows
+#pragma unroll 2
+        for (int bl = warp; bl < nblk; bl += kKqWarps) {
+            float w[R][8];
+            int o0 = 0, o1 = 0;
+#pragma unroll
+            for (int r = 0; r < R; r++) kq_dequant<QT>(rp[r] + (size_t)bl * BB, lane, w[r], o0, o1);
+            const int base = bl * 256;
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+                if (t >= m) continue;
+                const float* xr = x + (size_t)t * ldx + base;
+                float xv[8];
+                if (QT == JYC_Q6K) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) xv[j] = __ldg(xr + 128 * (j >> 2) + o0 + 32 * (j & 3));
+                } else {
+                    const float4 xa = __ldg(reinterpret_cast<const float4*>(xr + o0));
+                    const float4 xb = __ldg(reinterpret_cast<const float4*>(xr + o1));
+                    xv[0] = xa.x; xv[1] = xa.y; xv[2] = xa.z; xv[3] = xa.w;
+                    xv[4] = xb.x; xv[5] = xb.y; xv[6] = xb.z; xv[7] = xb.w;
+                }
+#pragma unroll
+                for (int r = 0; r < R; r++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[t][r] = __fmaf_rn(w[r][j], xv[j], acc[t][r]);
+            }
+        }
+        // per warp, then the warps in order (fixed summation order)
+#pragma unroll
+        for (int t = 0; t < MT; t++)
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const float v = warp_sum(acc[t][r]);
+                if (lane == 0) s_part[warp][t][r] = v;
+            }
+        __syncthreads();
+        if (threadIdx.x < MT * R) {
+            const int t = threadIdx.x / R, r = threadIdx.x % R;
+            float v = 0.0f;
+            for (int w2 = 0; w2 < kKqWarps; w2++) v = __fadd_rn(v, s_part[w2][t][r]);
+            if (t < m && row0 + r < n) y[(size_t)t * ldy + row0 + r] = v;
+        }
+        __syncthreads();  // s_part is reused by the next rows
+    }
+}
+
+template <int QT, int MT>
+int kq_launch_t(const float* x, int ldx, int m, int n, int k, const uint8_t* wq, float* y, int ldy, cudaStream_t s) {
+    const int blocks = std::min((n + kKqRowsPerCta - 1) / kKqRowsPerCta, 148 * 8);
+    kq_gemv_kernel<QT, MT><<<blocks, kKqWarps * 32, 0, s>>>(x, ldx, m, n, k, wq, y, ldy);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+
+template <int QT>
+int kq_launch_qt(const float* x, int ldx, int m, int n, int k, const uint8_t* wq, float* y, int ldy, cudaStream_t s) {
+    if (m == 1) return kq_launch_t<QT, 1>(x, ldx, m, n, k, wq, y, ldy, s);
+    if (m <= 4) return kq_launch_t<QT, 4>(x, ldx, m, n, k, wq, y, ldy, s);
+    return kq_launch_t<QT, 8>(x, ldx, m, n, k, wq, y, ldy, s);
+}
+
+}  // namespace
+
+int launch_kquant_matmul(const float* x, int m, int n, int k, const uint8_t* wq, int qtype, float* y,
+                         cudaStream_t s) {
+    if (qtype != JYC_Q4K && qtype != JYC_Q5K && qtype != JYC_Q6K)
+        return arg_error("matmul_qk: qtype must be JYC_Q4K, JYC_Q5K or JYC_Q6K");
+    if (m <= 0 || n <= 0 || k <= 0 || k % 256) return arg_error("matmul_qk: need m, n > 0 and k % 256 == 0");
+    if (((uintptr_t)x & 15) || ((uintptr_t)wq & 3))
+        return arg_error("matmul_qk: A must be 16-byte and the blocks 4-byte aligned");
+    for (int r0 = 0; r0 < m; r0 += kKqMaxRows) {
+        const int mr = std::min(kKqMaxRows, m - r0);
+        const float* xr = x + (size_t)r0 * k;
+        float* yr = y + (size_t)r0 * n;
+        int r;
+        if (qtype == JYC_Q4K) r = kq_launch_qt<JYC_Q4K>(xr, k, mr, n, k, wq, yr, n, s);
+        else if (qtype == JYC_Q5K) r = kq_launch_qt<JYC_Q5K>(xr, k, mr, n, k, wq, yr, n, s);
+        else r = kq_launch_qt<JYC_Q6K>(xr, k, mr, n, k, wq, yr, n, s);
+        if (r != JYC_OK) return r;
+    }
+    return JYC_OK;
+}
+
+}  // namespace jyc

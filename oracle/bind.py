@@ -24,6 +24,7 @@ _P, _I, _F = C.c_void_p, C.c_int, C.c_float
 def _sig(lib, prefix: str):
     s = {
         "matmul_q8": (None, [_P, _P, _P, _I, _I, _I]),
+        "matmul_qk": (None, [_P, _P, _P, _I, _I, _I, _I]),
         "matmul_f32": (None, [_I, _I, _I, _P, _P, _P]),
         "rmsnorm": (None, [_P, _P, _P, _I, _F]),
         "rope_table": (None, [_I, _I, _F, _P, _P]),

@@ -114,6 +114,143 @@ void jyo_matmul_q8(const float* a, const void* b, float* c, int m, int n, int k)
     }
 }
 
+/* 6-bit scale and min of sub-block j of a Q4_K / Q5_K super-block
+ * (matmul_q.h:24-33 get_scale_min_k4). */
+static void kq_scale_min(int j, const uint8_t* q, unsigned* sc, unsigned* mn) {
+    if (j < 4) {
+        *sc = q[j] & 63u;
+        *mn = q[j + 4] & 63u;
+    } else {
+        *sc = (q[j + 4] & 0xFu) | ((unsigned)(q[j - 4] >> 6) << 4);
+        *mn = (unsigned)(q[j + 4] >> 4) | ((unsigned)(q[j] >> 6) << 4);
+    }
+}
+
+static float kq_f16(const uint8_t* p) {
+    uint16_t h;
+    memcpy(&h, p, 2);
+    return f16_to_f32(h);
+}
+
+/* Q4_K (144 B / 256): the AVX2+FMA dequant of file_libs/q4/q4_fma.txt,
+ * w = fma((float)q, d*sc, -(dmin*mn)) per 32-weight sub-block. */
+static void dequant_q4k(const uint8_t* b, float* dst) {
+    const float d = kq_f16(b), dmin = kq_f16(b + 2);
+    const uint8_t* scp = b + 4;
+    const uint8_t* qs = b + 16;
+    for (int g = 0; g < 4; g++) {
+        unsigned s0, m0, s1, m1;
+        kq_scale_min(2 * g, scp, &s0, &m0);
+        kq_scale_min(2 * g + 1, scp, &s1, &m1);
+        const float d1 = d * (float)s0, n1 = -(dmin * (float)m0);
+        const float d2 = d * (float)s1, n2 = -(dmin * (float)m1);
+        for (int l = 0; l < 32; l++) dst[g * 64 + l] = fmaf((float)(qs[l] & 0xF), d1, n1);
+        for (int l = 0; l < 32; l++) dst[g * 64 + 32 + l] = fmaf((float)(qs[l] >> 4), d2, n2);
+        qs += 32;
+    }
+}
+
+/* Q5_K (176 B / 256): matmul_q.h:52-77, d1*q - n1 as a separate multiply and
+ * subtract (generic code, baseline x86-64). */
+static void dequant_q5k(const uint8_t* b, float* dst) {
+    const float d = kq_f16(b), dmin = kq_f16(b + 2);
+    const uint8_t* sc = b + 4;
+    const uint8_t* qh = b + 16;
+    const uint8_t* qs = b + 48;
+    unsigned u1 = 1, u2 = 2;
+    for (int g = 0; g < 4; g++) {
+        unsigned s0, m0, s1, m1;
+        kq_scale_min(2 * g, sc, &s0, &m0);
+        kq_scale_min(2 * g + 1, sc, &s1, &m1);
+        const float d1 = d * (float)s0, n1 = dmin * (float)m0;
+        const float d2 = d * (float)s1, n2 = dmin * (float)m1;
+        for (int l = 0; l < 32; l++) {
+            const float w = d1 * (float)((qs[l] & 0xF) + ((qh[l] & u1) ? 16 : 0));
+            dst[g * 64 + l] = w - n1;
+        }
+        for (int l = 0; l < 32; l++) {
+            const float w = d2 * (float)((qs[l] >> 4) + ((qh[l] & u2) ? 16 : 0));
+            dst[g * 64 + 32 + l] = w - n2;
+        }
+        qs += 32;
+        u1 <<= 2;
+        u2 <<= 2;
+    }
+}
+
+/* Q6_K (210 B / 256): matmul_q.h:78-100, (d * sc) * q (exact in fp32). */
+static void dequant_q6k(const uint8_t* b, float* dst) {
+    const uint8_t* ql = b;
+    const uint8_t* qh = b + 128;
+    const int8_t* sc = (const int8_t*)(b + 192);
+    const float d = kq_f16(b + 208);
+    for (int nn = 0; nn < 2; nn++) {
+        for (int l = 0; l < 32; l++) {
+            const int is = l / 16;
+            const int q1 = (int)((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+            const int q2 = (int)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+            const int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+            const int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+            dst[nn * 128 + l] = d * (float)sc[is] * (float)q1;
+            dst[nn * 128 + l + 32] = d * (float)sc[is + 2] * (float)q2;
+            dst[nn * 128 + l + 64] = d * (float)sc[is + 4] * (float)q3;
+            dst[nn * 128 + l + 96] = d * (float)sc[is + 6] * (float)q4;
+        }
+        ql += 64;
+        qh += 32;
+        sc += 8;
+    }
+}
+
+static int kq_bytes(int t) { return t == JYC_Q4K ? 144 : t == JYC_Q5K ? 176 : t == JYC_Q6K ? 210 : 0; }
+
+static void kq_dequant(int t, const uint8_t* b, float* dst) {
+    if (t == JYC_Q4K) dequant_q4k(b, dst);
+    else if (t == JYC_Q5K) dequant_q5k(b, dst);
+    else dequant_q6k(b, dst);
+}
+
+/* qmat::matmul_q for the K-quants (matmul_q.h:134-162): m == 1 is
+ * dot_row_avx2 (four 8-lane FMA accumulators = acc[l % 32], then the same
+ * tail as Q8_0), m > 1 the scalar triple loop. Returns -1 for another t. */
+int jyo_matmul_qk(const float* a, const void* b, float* c, int m, int n, int k, int t) {
+    const int bb = kq_bytes(t);
+    if (bb == 0 || k % 256) return -1;
+    const uint8_t* base = (const uint8_t*)b;
+    const size_t rbytes = (size_t)(k / 256) * bb;
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < n; j++) {
+        float blk[256];
+        const uint8_t* row = base + (size_t)j * rbytes;
+        if (m == 1) {
+            float acc[32];
+            for (int l = 0; l < 32; l++) acc[l] = 0.0f;
+            for (int bl = 0; bl < k / 256; bl++) {
+                kq_dequant(t, row + (size_t)bl * bb, blk);
+                const float* av = a + (size_t)bl * 256;
+                for (int l = 0; l < 256; l++) acc[l & 31] = fmaf(av[l], blk[l], acc[l & 31]);
+            }
+            float tt[8];
+            for (int i = 0; i < 8; i++) tt[i] = (acc[i] + acc[8 + i]) + (acc[16 + i] + acc[24 + i]);
+            c[j] = hsum8(tt);
+        } else {
+            float* acc = (float*)malloc(sizeof(float) * (size_t)m);
+            for (int i = 0; i < m; i++) acc[i] = 0.0f;
+            for (int bl = 0; bl < k / 256; bl++) {
+                kq_dequant(t, row + (size_t)bl * bb, blk);
+                const size_t off = (size_t)bl * 256;
+                for (int l = 0; l < 256; l++) {
+                    const float bv = blk[l];
+                    for (int i = 0; i < m; i++) acc[i] = acc[i] + a[(size_t)i * k + off + l] * bv;
+                }
+            }
+            for (int i = 0; i < m; i++) c[(size_t)i * n + j] = acc[i];
+            free(acc);
+        }
+    }
+    return 0;
+}
+
 /* matmul x86_classic.txt:1-16: crow[j] = fma(a[p], B[p][j], crow[j]) for p in order. */
 void jyo_matmul_f32(int m, int n, int k, const float* A, const float* B, float* C) {
 #pragma omp parallel for schedule(static)

@@ -20,6 +20,8 @@ extern "C" {
 void jyo_set_threads(int n);
 /* qmat::matmul_q Q8_0 (libs/matmul_libs/matmul_q.h:134-162): m==1 AVX2 lane order, m>1 scalar. */
 void jyo_matmul_q8(const float* a, const void* b, float* c, int m, int n, int k);
+/* K-quant weights (t = JYC_Q4K, JYC_Q5K, JYC_Q6K; k % 256 == 0); -1 for another t. */
+int jyo_matmul_qk(const float* a, const void* b, float* c, int m, int n, int k, int t);
 /* matmul (libs/matmul_libs/matmul.h:7-76), B = [k][n]. */
 void jyo_matmul_f32(int m, int n, int k, const float* A, const float* B, float* C);
 /* rmsnorm (libs/model_libs/rmsnorm/x86/x86_classic.txt:1-27). */

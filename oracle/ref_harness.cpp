@@ -98,6 +98,11 @@ void jyref_matmul_q8(const float* a, const void* b, float* c, int m, int n, int 
     qmat::matmul_q(a, b, c, m, n, k, qmat::Q8_0);
 }
 
+/* qmat::matmul_q with a K-quant weight type (t = qmat::Q4K, Q5K or Q6K). */
+void jyref_matmul_qk(const float* a, const void* b, float* c, int m, int n, int k, int t) {
+    qmat::matmul_q(a, b, c, m, n, k, (uint8_t)t);
+}
+
 void jyref_matmul_f32(int m, int n, int k, const float* A, const float* B, float* C) {
     matmul(m, n, k, A, B, C);
 }
