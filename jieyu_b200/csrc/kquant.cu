@@ -17,6 +17,8 @@
 //     64g+32+p..+3 (sub-block 2g+1);
 //   Q6_K: position l of both 128-weight halves: weights 128h + l + 32j.
 // Per-lane fp32 FMAs, a warp sum, then the 8 warps' sums in warp order.
+// Rows whose bytes are a multiple of 16 are staged in shared memory first
+// (kq_gemv_smem_kernel); others are read in place (kq_gemv_kernel).
 #include <algorithm>
 
 #include "kernels.cuh"
@@ -45,6 +47,15 @@ __device__ __forceinline__ void kq_scale_min(int j, const uint8_t* q, unsigned& 
     }
 }
 
+// Small non-negative integers to exact floats without a conversion
+// instruction: the float with bits 0x4B000000 | v is 2^23 + v.
+__device__ __forceinline__ float kq_small_f32(unsigned v, float bias) {  // v < 2^23; bias = 2^23 + offset
+    return __fsub_rn(__uint_as_float(0x4B000000u | v), bias);
+}
+__device__ __forceinline__ float kq_byte_f32(uint32_t w, int i) {  // byte i of w
+    return __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + i)), 8388608.0f);
+}
+
 template <int QT>
 constexpr int kq_block_bytes() {
     return QT == JYC_Q4K ? 144 : QT == JYC_Q5K ? 176 : 210;
@@ -63,15 +74,16 @@ __device__ __forceinline__ void kq_dequant(const uint8_t* b, int lane, float (&w
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const unsigned l0 = b[64 * h + lane], l1 = b[64 * h + lane + 32], hh = b[128 + 32 * h + lane];
-            const int q1 = (int)((l0 & 0xFu) | (((hh >> 0) & 3u) << 4)) - 32;
-            const int q2 = (int)((l1 & 0xFu) | (((hh >> 2) & 3u) << 4)) - 32;
-            const int q3 = (int)((l0 >> 4) | (((hh >> 4) & 3u) << 4)) - 32;
-            const int q4 = (int)((l1 >> 4) | (((hh >> 6) & 3u) << 4)) - 32;
+            // 6-bit q as float minus 32: 2^23 + q - (2^23 + 32), exact
+            const float q1 = kq_small_f32((l0 & 0xFu) | (((hh >> 0) & 3u) << 4), 8388640.0f);
+            const float q2 = kq_small_f32((l1 & 0xFu) | (((hh >> 2) & 3u) << 4), 8388640.0f);
+            const float q3 = kq_small_f32((l0 >> 4) | (((hh >> 4) & 3u) << 4), 8388640.0f);
+            const float q4 = kq_small_f32((l1 >> 4) | (((hh >> 6) & 3u) << 4), 8388640.0f);
             const int s = 8 * h + is;
-            w[4 * h + 0] = __fmul_rn(__fmul_rn(d, (float)sc[s]), (float)q1);
-            w[4 * h + 1] = __fmul_rn(__fmul_rn(d, (float)sc[s + 2]), (float)q2);
-            w[4 * h + 2] = __fmul_rn(__fmul_rn(d, (float)sc[s + 4]), (float)q3);
-            w[4 * h + 3] = __fmul_rn(__fmul_rn(d, (float)sc[s + 6]), (float)q4);
+            w[4 * h + 0] = __fmul_rn(__fmul_rn(d, (float)sc[s]), q1);
+            w[4 * h + 1] = __fmul_rn(__fmul_rn(d, (float)sc[s + 2]), q2);
+            w[4 * h + 2] = __fmul_rn(__fmul_rn(d, (float)sc[s + 4]), q3);
+            w[4 * h + 3] = __fmul_rn(__fmul_rn(d, (float)sc[s + 6]), q4);
         }
         o0 = lane;  // weights 128h + lane + 32j
         o1 = 0;
@@ -86,22 +98,21 @@ __device__ __forceinline__ void kq_dequant(const uint8_t* b, int lane, float (&w
         const float d2 = __fmul_rn(d, (float)s1), n2 = __fmul_rn(dmin, (float)m1);
         const uint8_t* qs = b + (QT == JYC_Q4K ? 16 : 48) + 32 * g + p;
         const uint32_t q = *reinterpret_cast<const uint32_t*>(qs);
-        if (QT == JYC_Q4K) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                w[i] = __fmaf_rn((float)((q >> (8 * i)) & 0xFu), d1, -n1);
-                w[4 + i] = __fmaf_rn((float)((q >> (8 * i + 4)) & 0xFu), d2, -n2);
-            }
-        } else {
+        uint32_t lo = q & 0x0F0F0F0Fu, hi = (q >> 4) & 0x0F0F0F0Fu;  // 4 quants per word, one per byte
+        if (QT == JYC_Q5K) {  // + 16 where the high bit (bit 2g / 2g+1 of qh[l]) is set
             const uint32_t qh = *reinterpret_cast<const uint32_t*>(b + 16 + p);
-            const unsigned u1 = 1u << (2 * g), u2 = 2u << (2 * g);
+            lo |= ((qh >> (2 * g)) & 0x01010101u) << 4;
+            hi |= ((qh >> (2 * g + 1)) & 0x01010101u) << 4;
+        }
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const unsigned hb = (qh >> (8 * i)) & 0xFFu;
-                const unsigned lo = ((q >> (8 * i)) & 0xFu) + ((hb & u1) ? 16u : 0u);
-                const unsigned hi = ((q >> (8 * i + 4)) & 0xFu) + ((hb & u2) ? 16u : 0u);
-                w[i] = __fsub_rn(__fmul_rn(d1, (float)lo), n1);
-                w[4 + i] = __fsub_rn(__fmul_rn(d2, (float)hi), n2);
+        for (int i = 0; i < 4; i++) {
+            const float fl = kq_byte_f32(lo, i), fh = kq_byte_f32(hi, i);
+            if (QT == JYC_Q4K) {
+                w[i] = __fmaf_rn(fl, d1, -n1);
+                w[4 + i] = __fmaf_rn(fh, d2, -n2);
+            } else {
+                w[i] = __fsub_rn(__fmul_rn(d1, fl), n1);
+                w[4 + i] = __fsub_rn(__fmul_rn(d2, fh), n2);
             }
         }
         o0 = 64 * g + p;       // w[0..3]
@@ -175,8 +186,89 @@ __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_kernel(const float* __r
     }
 }
 
+// Rows staged in shared memory: a CTA copies R = 8 whole weight rows (row
+// bytes a multiple of 16) with 16-byte cp.async, every copy in flight at
+// once; then warp w dequantises row w's super-blocks from shared memory and
+// writes its warp sum (one warp per row: nothing to select or merge).
+__device__ __forceinline__ void kq_cp16(uint32_t dst, const void* src, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+template <int QT, int MT>
+__global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_smem_kernel(const float* __restrict__ x, int ldx, int m,
+                                                                     int n, int k, const uint8_t* __restrict__ wq,
+                                                                     float* __restrict__ y, int ldy) {
+    constexpr int BB = kq_block_bytes<QT>();
+    constexpr int R = kKqWarps;
+    extern __shared__ __align__(16) unsigned char kq_sm[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nblk = k >> 8;
+    const int rbytes = nblk * BB;  // a multiple of 16
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(kq_sm);
+    for (int row0 = blockIdx.x * R; row0 < n; row0 += gridDim.x * R) {
+        const int nr = min(R, n - row0);
+        const uint8_t* src = wq + (size_t)row0 * rbytes;
+        const int chunks = nr * (rbytes >> 4);
+        for (int c = tid; c < chunks; c += kKqWarps * 32) kq_cp16(sbase + 16 * c, src + (size_t)16 * c, 16);
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        if (warp < nr) {
+            const unsigned char* rowp = kq_sm + warp * rbytes;
+            float acc[MT];
+#pragma unroll
+            for (int t = 0; t < MT; t++) acc[t] = 0.0f;
+#pragma unroll 2
+            for (int bl = 0; bl < nblk; bl++) {
+                float w[8];
+                int o0 = 0, o1 = 0;
+                kq_dequant<QT>(rowp + bl * BB, lane, w, o0, o1);
+                const int base = bl * 256;
+#pragma unroll
+                for (int t = 0; t < MT; t++) {
+                    if (t >= m) continue;
+                    const float* xr = x + (size_t)t * ldx + base;
+                    float xv[8];
+                    if (QT == JYC_Q6K) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) xv[j] = __ldg(xr + 128 * (j >> 2) + o0 + 32 * (j & 3));
+                    } else {
+                        const float4 xa = __ldg(reinterpret_cast<const float4*>(xr + o0));
+                        const float4 xb = __ldg(reinterpret_cast<const float4*>(xr + o1));
+                        xv[0] = xa.x; xv[1] = xa.y; xv[2] = xa.z; xv[3] = xa.w;
+                        xv[4] = xb.x; xv[5] = xb.y; xv[6] = xb.z; xv[7] = xb.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc[t] = __fmaf_rn(w[j], xv[j], acc[t]);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < MT; t++) {
+                const float v = warp_sum(acc[t]);
+                if (lane == 0 && t < m) y[(size_t)t * ldy + row0 + warp] = v;
+            }
+        }
+        __syncthreads();  // the staged rows are reused by the next rows
+    }
+}
+
+constexpr int kKqSmemMax = 96 * 1024;  // staged rows per CTA at most
+
 template <int QT, int MT>
 int kq_launch_t(const float* x, int ldx, int m, int n, int k, const uint8_t* wq, float* y, int ldy, cudaStream_t s) {
+    constexpr int R = kKqWarps;
+    const size_t rbytes = (size_t)(k >> 8) * kq_block_bytes<QT>();
+    if (rbytes % 16 == 0 && ((uintptr_t)wq & 15) == 0 && (size_t)R * rbytes <= (size_t)kKqSmemMax) {
+        static bool attr = false;  // host-side, once per instantiation
+        if (!attr) {
+            JYC_CUDA(cudaFuncSetAttribute(kq_gemv_smem_kernel<QT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          kKqSmemMax));
+            attr = true;
+        }
+        const int blocks = std::min((n + R - 1) / R, 148 * 8);
+        kq_gemv_smem_kernel<QT, MT><<<blocks, kKqWarps * 32, R * rbytes, s>>>(x, ldx, m, n, k, wq, y, ldy);
+        JYC_LAUNCHED();
+        return JYC_OK;
+    }
     const int blocks = std::min((n + kKqRowsPerCta - 1) / kKqRowsPerCta, 148 * 8);
     kq_gemv_kernel<QT, MT><<<blocks, kKqWarps * 32, 0, s>>>(x, ldx, m, n, k, wq, y, ldy);
     JYC_LAUNCHED();
