@@ -120,6 +120,46 @@ __device__ __forceinline__ void kq_dequant(const uint8_t* b, int lane, float (&w
     }
 }
 
+// Q4_K / Q5_K, 16 weights per lane (l16 = 0..15 of a half warp): group
+// g = l16/4, byte octet p = 8 (l16%4): low nibbles -> weights 64g+p..+7 (w[0..7],
+// sub-block 2g), high nibbles -> 64g+32+p..+7 (w[8..15], sub-block 2g+1).
+template <int QT>
+__device__ __forceinline__ void kq_dequant16(const uint8_t* b, int l16, float (&w)[16], int& o0, int& o1) {
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(b);  // fp16 d | fp16 dmin
+    const float d = kq_h2f(dd & 0xFFFFu), dmin = kq_h2f(dd >> 16);
+    const int g = l16 >> 2, p = 8 * (l16 & 3);
+    unsigned s0, m0, s1, m1;
+    kq_scale_min(2 * g, b + 4, s0, m0);
+    kq_scale_min(2 * g + 1, b + 4, s1, m1);
+    const float d1 = __fmul_rn(d, (float)s0), n1 = __fmul_rn(dmin, (float)m0);
+    const float d2 = __fmul_rn(d, (float)s1), n2 = __fmul_rn(dmin, (float)m1);
+    const uint2 q = *reinterpret_cast<const uint2*>(b + (QT == JYC_Q4K ? 16 : 48) + 32 * g + p);
+    uint32_t lo[2] = {q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu};
+    uint32_t hi[2] = {(q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu};
+    if (QT == JYC_Q5K) {  // + 16 where the high bit (bit 2g / 2g+1 of qh[l]) is set
+        const uint2 qh = *reinterpret_cast<const uint2*>(b + 16 + p);
+        lo[0] |= ((qh.x >> (2 * g)) & 0x01010101u) << 4;
+        lo[1] |= ((qh.y >> (2 * g)) & 0x01010101u) << 4;
+        hi[0] |= ((qh.x >> (2 * g + 1)) & 0x01010101u) << 4;
+        hi[1] |= ((qh.y >> (2 * g + 1)) & 0x01010101u) << 4;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float fl = kq_byte_f32(lo[h], i), fh = kq_byte_f32(hi[h], i);
+            if (QT == JYC_Q4K) {
+                w[4 * h + i] = __fmaf_rn(fl, d1, -n1);
+                w[8 + 4 * h + i] = __fmaf_rn(fh, d2, -n2);
+            } else {
+                w[4 * h + i] = __fsub_rn(__fmul_rn(d1, fl), n1);
+                w[8 + 4 * h + i] = __fsub_rn(__fmul_rn(d2, fh), n2);
+            }
+        }
+    o0 = 64 * g + p;
+    o1 = 64 * g + 32 + p;
+}
+
 template <int QT, int MT>
 __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_kernel(const float* __restrict__ x, int ldx, int m, int n,
                                                                 int k, const uint8_t* __restrict__ wq,
@@ -189,7 +229,9 @@ __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_kernel(const float* __r
 // Rows staged in shared memory: a CTA copies R = 8 whole weight rows (row
 // bytes a multiple of 16) with 16-byte cp.async, every copy in flight at
 // once; then warp w dequantises row w's super-blocks from shared memory and
-// writes its warp sum (one warp per row: nothing to select or merge).
+// writes its warp sum (one warp per row: nothing to select or merge). Q4_K /
+// Q5_K lanes take 16 weights of a block (a half warp per block, two blocks
+// per step), Q6_K lanes 8 (a whole warp per block).
 __device__ __forceinline__ void kq_cp16(uint32_t dst, const void* src, int bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
@@ -217,6 +259,28 @@ __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_smem_kernel(const float
             float acc[MT];
 #pragma unroll
             for (int t = 0; t < MT; t++) acc[t] = 0.0f;
+            if (QT != JYC_Q6K) {  // half warp h takes blocks 2i + h, 16 weights per lane
+                const int h = lane >> 4, l16 = lane & 15;
+#pragma unroll 2
+                for (int bl = h; bl < nblk; bl += 2) {
+                    float w[16];
+                    int o0 = 0, o1 = 0;
+                    kq_dequant16<QT>(rowp + bl * BB, l16, w, o0, o1);
+#pragma unroll
+                    for (int t = 0; t < MT; t++) {
+                        if (t >= m) continue;
+                        const float* xr = x + (size_t)t * ldx + bl * 256;
+                        const float4 xa = __ldg(reinterpret_cast<const float4*>(xr + o0));
+                        const float4 xb = __ldg(reinterpret_cast<const float4*>(xr + o0 + 4));
+                        const float4 xc = __ldg(reinterpret_cast<const float4*>(xr + o1));
+                        const float4 xd = __ldg(reinterpret_cast<const float4*>(xr + o1 + 4));
+                        const float xv[16] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w,
+                                              xc.x, xc.y, xc.z, xc.w, xd.x, xd.y, xd.z, xd.w};
+#pragma unroll
+                        for (int j = 0; j < 16; j++) acc[t] = __fmaf_rn(w[j], xv[j], acc[t]);
+                    }
+                }
+            } else
 #pragma unroll 2
             for (int bl = 0; bl < nblk; bl++) {
                 float w[8];
