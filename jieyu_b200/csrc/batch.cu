@@ -130,10 +130,6 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                  : "memory");
 }
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-                 : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -376,14 +372,16 @@ int bd_attention_chunk(int cap, int nseq, int KV) {
 int launch_bd_attention(const BdAttn& a, int nseq, cudaStream_t s) {
     if (!bd_attention_supported(a.H, a.KV, a.hd)) return arg_error("bd_attention: unsupported head shape");
     if (a.chunk % (32 * kBdWarps)) return arg_error("bd_attention: chunk must be a multiple of 256");
-    static bool attr = false;
-    if (!attr) {
-        JYC_CUDA(cudaFuncSetAttribute(bd_attention_kernel<64, kBdWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      bd_attn_smem(64)));
-        JYC_CUDA(cudaFuncSetAttribute(bd_attention_kernel<128, kBdWarps>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, bd_attn_smem(128)));
-        attr = true;
-    }
+    // once per process (thread-safe static initialisation)
+    static const cudaError_t attr = [] {
+        cudaError_t e = cudaFuncSetAttribute(bd_attention_kernel<64, kBdWarps>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, bd_attn_smem(64));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(bd_attention_kernel<128, kBdWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     bd_attn_smem(128));
+        return e;
+    }();
+    if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute");
     const dim3 grid(a.nsplit, a.KV, nseq);
     if (a.hd == 64) bd_attention_kernel<64, kBdWarps><<<grid, kBdWarps * 32, bd_attn_smem(64), s>>>(a);
     else bd_attention_kernel<128, kBdWarps><<<grid, kBdWarps * 32, bd_attn_smem(128), s>>>(a);

@@ -647,12 +647,10 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs a) {
 
 // One-time kernel attributes (called at model creation, outside any capture).
 int prepare_kernels() {
-    static bool done = false;
-    if (done) return JYC_OK;
-    JYC_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  200 * 1024));
-    done = true;
-    return JYC_OK;
+    // once per process (thread-safe static initialisation)
+    static const cudaError_t e =
+        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    return e == cudaSuccess ? JYC_OK : cuda_fail(e, "cudaFuncSetAttribute");
 }
 #define TRY_PREPARE()                          \
     do {                                       \

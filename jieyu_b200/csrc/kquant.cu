@@ -322,12 +322,10 @@ int kq_launch_t(const float* x, int ldx, int m, int n, int k, const uint8_t* wq,
     constexpr int R = kKqWarps;
     const size_t rbytes = (size_t)(k >> 8) * kq_block_bytes<QT>();
     if (rbytes % 16 == 0 && ((uintptr_t)wq & 15) == 0 && (size_t)R * rbytes <= (size_t)kKqSmemMax) {
-        static bool attr = false;  // host-side, once per instantiation
-        if (!attr) {
-            JYC_CUDA(cudaFuncSetAttribute(kq_gemv_smem_kernel<QT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          kKqSmemMax));
-            attr = true;
-        }
+        // once per instantiation (thread-safe static initialisation)
+        static const cudaError_t attr = cudaFuncSetAttribute(
+            kq_gemv_smem_kernel<QT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKqSmemMax);
+        if (attr != cudaSuccess) return cuda_fail(attr, "cudaFuncSetAttribute");
         const int blocks = std::min((n + R - 1) / R, 148 * 8);
         kq_gemv_smem_kernel<QT, MT><<<blocks, kKqWarps * 32, R * rbytes, s>>>(x, ldx, m, n, k, wq, y, ldy);
         JYC_LAUNCHED();

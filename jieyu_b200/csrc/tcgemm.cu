@@ -1094,13 +1094,14 @@ int launch_tc_split(const float* x, int ldx, int T, int k, const float* norm_w, 
 }
 
 int prepare_tc_kernels() {
-    static bool done = false;
-    if (done) return JYC_OK;
-    int r = set_smem<16>();
-    if (r == JYC_OK) r = set_smem<32>();
-    if (r == JYC_OK) r = set_smem<64>();
-    if (r == JYC_OK) r = set_smem<128>();
-    done = r == JYC_OK;
+    // once per process (thread-safe static initialisation)
+    static const int r = [] {
+        int rr = set_smem<16>();
+        if (rr == JYC_OK) rr = set_smem<32>();
+        if (rr == JYC_OK) rr = set_smem<64>();
+        if (rr == JYC_OK) rr = set_smem<128>();
+        return rr;
+    }();
     return r;
 }
 
