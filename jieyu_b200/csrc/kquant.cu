@@ -160,6 +160,33 @@ __device__ __forceinline__ void kq_dequant16(const uint8_t* b, int l16, float (&
     o1 = 64 * g + 32 + p;
 }
 
+// Q6_K, 16 weights per lane (l16 = 0..15 of a half warp): positions
+// pp = 2 l16 and pp + 1 of both 128-weight halves h; w[8h + 4e + j] is the
+// weight at 128h + pp + e + 32j (its scale sc[8h + pp/16 + 2j] is shared by
+// both positions).
+__device__ __forceinline__ void kq_dequant16_q6(const uint8_t* b, int l16, float (&w)[16]) {
+    const float d = kq_h2f(*reinterpret_cast<const uint16_t*>(b + 208));
+    const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192);
+    const int pp = 2 * l16, is = l16 >> 3;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const unsigned ql0 = *reinterpret_cast<const uint16_t*>(b + 64 * h + pp);
+        const unsigned ql1 = *reinterpret_cast<const uint16_t*>(b + 64 * h + 32 + pp);
+        const unsigned hh = *reinterpret_cast<const uint16_t*>(b + 128 + 32 * h + pp);
+        float ds[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) ds[j] = __fmul_rn(d, (float)sc[8 * h + is + 2 * j]);
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const unsigned l0 = (ql0 >> (8 * e)) & 0xFFu, l1 = (ql1 >> (8 * e)) & 0xFFu, hb = (hh >> (8 * e)) & 0xFFu;
+            w[8 * h + 4 * e + 0] = __fmul_rn(ds[0], kq_small_f32((l0 & 0xFu) | ((hb & 3u) << 4), 8388640.0f));
+            w[8 * h + 4 * e + 1] = __fmul_rn(ds[1], kq_small_f32((l1 & 0xFu) | (((hb >> 2) & 3u) << 4), 8388640.0f));
+            w[8 * h + 4 * e + 2] = __fmul_rn(ds[2], kq_small_f32((l0 >> 4) | (((hb >> 4) & 3u) << 4), 8388640.0f));
+            w[8 * h + 4 * e + 3] = __fmul_rn(ds[3], kq_small_f32((l1 >> 4) | (((hb >> 6) & 3u) << 4), 8388640.0f));
+        }
+    }
+}
+
 template <int QT, int MT>
 __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_kernel(const float* __restrict__ x, int ldx, int m, int n,
                                                                 int k, const uint8_t* __restrict__ wq,
@@ -229,9 +256,8 @@ __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_kernel(const float* __r
 // Rows staged in shared memory: a CTA copies R = 8 whole weight rows (row
 // bytes a multiple of 16) with 16-byte cp.async, every copy in flight at
 // once; then warp w dequantises row w's super-blocks from shared memory and
-// writes its warp sum (one warp per row: nothing to select or merge). Q4_K /
-// Q5_K lanes take 16 weights of a block (a half warp per block, two blocks
-// per step), Q6_K lanes 8 (a whole warp per block).
+// writes its warp sum (one warp per row: nothing to select or merge). Lanes
+// take 16 weights of a block (a half warp per block, two blocks per step).
 __device__ __forceinline__ void kq_cp16(uint32_t dst, const void* src, int bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
 }
@@ -259,7 +285,27 @@ __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_smem_kernel(const float
             float acc[MT];
 #pragma unroll
             for (int t = 0; t < MT; t++) acc[t] = 0.0f;
-            if (QT != JYC_Q6K) {  // half warp h takes blocks 2i + h, 16 weights per lane
+            if (QT == JYC_Q6K) {  // half warp hw takes blocks 2i + hw, 16 weights per lane
+                const int hw = lane >> 4, l16 = lane & 15, pp = 2 * l16;
+#pragma unroll 2
+                for (int bl = hw; bl < nblk; bl += 2) {
+                    float w[16];
+                    kq_dequant16_q6(rowp + bl * BB, l16, w);
+#pragma unroll
+                    for (int t = 0; t < MT; t++) {
+                        if (t >= m) continue;
+                        const float* xr = x + (size_t)t * ldx + bl * 256 + pp;
+#pragma unroll
+                        for (int h = 0; h < 2; h++)
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const float2 xv = __ldg(reinterpret_cast<const float2*>(xr + 128 * h + 32 * j));
+                                acc[t] = __fmaf_rn(w[8 * h + j], xv.x, acc[t]);
+                                acc[t] = __fmaf_rn(w[8 * h + 4 + j], xv.y, acc[t]);
+                            }
+                    }
+                }
+            } else {  // Q4_K / Q5_K: half warp h takes blocks 2i + h, 16 weights per lane
                 const int h = lane >> 4, l16 = lane & 15;
 #pragma unroll 2
                 for (int bl = h; bl < nblk; bl += 2) {
@@ -279,30 +325,6 @@ __global__ void __launch_bounds__(kKqWarps * 32) kq_gemv_smem_kernel(const float
 #pragma unroll
                         for (int j = 0; j < 16; j++) acc[t] = __fmaf_rn(w[j], xv[j], acc[t]);
                     }
-                }
-            } else
-#pragma unroll 2
-            for (int bl = 0; bl < nblk; bl++) {
-                float w[8];
-                int o0 = 0, o1 = 0;
-                kq_dequant<QT>(rowp + bl * BB, lane, w, o0, o1);
-                const int base = bl * 256;
-#pragma unroll
-                for (int t = 0; t < MT; t++) {
-                    if (t >= m) continue;
-                    const float* xr = x + (size_t)t * ldx + base;
-                    float xv[8];
-                    if (QT == JYC_Q6K) {
-#pragma unroll
-                        for (int j = 0; j < 8; j++) xv[j] = __ldg(xr + 128 * (j >> 2) + o0 + 32 * (j & 3));
-                    } else {
-                        const float4 xa = __ldg(reinterpret_cast<const float4*>(xr + o0));
-                        const float4 xb = __ldg(reinterpret_cast<const float4*>(xr + o1));
-                        xv[0] = xa.x; xv[1] = xa.y; xv[2] = xa.z; xv[3] = xa.w;
-                        xv[4] = xb.x; xv[5] = xb.y; xv[6] = xb.z; xv[7] = xb.w;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; j++) acc[t] = __fmaf_rn(w[j], xv[j], acc[t]);
                 }
             }
 #pragma unroll
