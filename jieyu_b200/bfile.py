@@ -47,6 +47,10 @@ _ENTRY_DT = np.dtype([("name", "S64"), ("dtype", "u1"), ("ndim", "u1"), ("r0", "
                       ("r1", "<u4"), ("offset", "<u8"), ("nbytes", "<u8")])
 assert _ENTRY_DT.itemsize == ENTRY
 
+# bfile dtype codes of the K-quants <-> the descriptor's JYC_Q4K / Q5K / Q6K
+_KQ_CODE = {Q4K: 0, Q5K: 1, Q6K: 2}
+_KQ_FILE = {v: k for k, v in _KQ_CODE.items()}
+
 LAYER_SUFFIX = {  # load_weights.h:55-68, our tensor key -> reference name suffix
     "rms1": "input_layernorm.weight", "q": "self_attn.q_proj.weight", "k": "self_attn.k_proj.weight",
     "v": "self_attn.v_proj.weight", "o": "self_attn.o_proj.weight", "rms2": "post_attention_layernorm.weight",
@@ -221,10 +225,11 @@ def _info_int(info: dict, key: str, fallback: int) -> int:
 def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> HostWeights:
     """Binds a reference model directory (model.bf + model_info.json) for the
     device path, with the reference's binding rules: per layer the nine
-    tensors of load_weights.h:55-68 (norms f32; linear weights all Q8_0 or
-    all f32, the formats this device path runs), optional q/k/v biases,
-    model.embed_tokens.weight, lm_head.weight or (block formats only) the
-    embedding as a tied head, model.norm.weight; shapes as bind_model checks
+    tensors of load_weights.h:55-68 (norms f32; linear weights all Q8_0, or
+    any mix of f32 and the K-quants Q4_K / Q5_K / Q6_K, which the device
+    dequantises to fp32 once), optional q/k/v biases,
+    model.embed_tokens.weight (f32, Q8_0 or K-quant), lm_head.weight or
+    (block formats only) the embedding as a tied head, model.norm.weight; shapes as bind_model checks
     them (pipeline.h:99-139). max_seq 0 takes max_position_embeddings
     clamped to [64, 4096], as the reference's C ABI does (main.hpp:64-67);
     RoPE theta is model_info's integer rope_theta (default 10000)."""
@@ -247,13 +252,13 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
             raise BFileError(f"{path}: {t.name} has shape {list(t.shape)}, expected {list(shape)}")
 
     def linear(t: Tensor, inn: int, out: int) -> np.ndarray:
-        if t.dtype == Q8_0:
+        if t.dtype in _BLOCK:
             expect(t, (out, inn))
         elif t.dtype == F32:
             expect(t, (inn, out))
         else:
             raise BFileError(f"{path}: {t.name} is {DTYPE_NAMES.get(t.dtype, t.dtype)}; this device path runs "
-                             "Q8_0 and f32 weights")
+                             "Q8_0, Q4_K, Q5_K, Q6_K and f32 weights")
         return t.array()
 
     def norm(key: str) -> np.ndarray:
@@ -266,15 +271,22 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
     dims = {"q": (D, qd), "k": (D, kvd), "v": (D, kvd), "o": (qd, D), "gate": (D, F), "up": (D, F), "down": (F, D)}
     wdt = need(layer_name(0, LAYER_SUFFIX["q"])).dtype
     ts: dict = {}
+    qtypes: dict = {}  # K-quant tensors: their block type for the descriptor
+    kinds = set()
     for l in range(L):
         ts[f"rms1.{l}"] = norm(layer_name(l, LAYER_SUFFIX["rms1"]))
         ts[f"rms2.{l}"] = norm(layer_name(l, LAYER_SUFFIX["rms2"]))
         for key, (inn, out) in dims.items():
             t = need(layer_name(l, LAYER_SUFFIX[key]))
-            if t.dtype != wdt:
-                raise BFileError(f"{path}: {t.name} is {DTYPE_NAMES.get(t.dtype)} while layer 0's q_proj is "
-                                 f"{DTYPE_NAMES.get(wdt)}; the device path needs one weight format")
             ts[f"{key}.{l}"] = linear(t, inn, out)
+            kinds.add(t.dtype)
+            if t.dtype in _KQ_CODE:
+                qtypes[f"{key}.{l}"] = _KQ_CODE[t.dtype]
+    # Q8_0 runs on its own kernels and cannot mix; f32 and the K-quants
+    # (dequantised to f32 on the device) mix freely
+    if Q8_0 in kinds and len(kinds) > 1:
+        raise BFileError(f"{path}: Q8_0 linear weights mixed with {sorted(DTYPE_NAMES[k] for k in kinds - {Q8_0})}; "
+                         "the device path runs Q8_0 models alone")
     # biases: bind_biases decides by layer 0's q bias (load_weights.h:128-136)
     qkv_bias = bf.get(layer_name(0, BIAS_SUFFIX["bq"])) is not None
     if qkv_bias:
@@ -287,9 +299,9 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
                 ts[f"{key}.{l}"] = t.array()
     emb = need("model.embed_tokens.weight")
     expect(emb, (V, D))
-    if emb.dtype not in (F32, Q8_0):
+    if emb.dtype not in (F32,) + tuple(_BLOCK):
         raise BFileError(f"{path}: model.embed_tokens.weight is {DTYPE_NAMES.get(emb.dtype)}; the device path "
-                         "reads f32 or Q8_0 embeddings")
+                         "reads f32, Q8_0 or K-quant embeddings")
     head = bf.get("lm_head.weight")
     tied = head is None
     if tied:
@@ -297,8 +309,6 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
     if head.dtype in _BLOCK:
         if head.shape != (V, D):
             raise BFileError(f"{path}: {head.name} must be [vocab, hidden] = [{V}, {D}]")
-        if head.dtype != Q8_0:
-            raise BFileError(f"{path}: {head.name} is {DTYPE_NAMES[head.dtype]}; the device path runs Q8_0")
     elif head.dtype == F32:
         if head.shape != (D, V):
             raise BFileError(f"{path}: lm_head.weight missing or not [hidden, vocab] = [{D}, {V}]")
@@ -306,19 +316,24 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
         raise BFileError(f"{path}: {head.name} is {DTYPE_NAMES.get(head.dtype)}; the device path runs Q8_0 "
                          "and f32")
     ts["head"] = head.array()
+    if head.dtype in _KQ_CODE:
+        qtypes["head"] = _KQ_CODE[head.dtype]
     if tied:
         embed = "tied"
     else:
-        embed = "q8" if emb.dtype == Q8_0 else "f32"
+        embed = "f32" if emb.dtype == F32 else "q8"  # "q8": a separate block-quantised embedding
         ts["embed"] = emb.array()
+        if emb.dtype in _KQ_CODE:
+            qtypes["embed"] = _KQ_CODE[emb.dtype]
     ts["final_norm"] = norm("model.norm.weight")
     if max_seq <= 0:
         max_seq = min(max(_info_int(info, "max_position_embeddings", 1024), 64), 4096)
     theta = float(_info_int(info, "rope_theta", 10000))
+    wtype = "q8" if wdt == Q8_0 else "kq" if kinds & set(_KQ_CODE) else "f32"
     cfg = Config(name or os.path.basename(os.path.normpath(path)), D, L, H, KV, hd, F, V, theta,
-                 "q8" if wdt == Q8_0 else "f32", embed, qkv_bias, max_seq)
+                 wtype, embed, qkv_bias, max_seq)
     cos, sin = rope_table(cfg.max_seq, cfg.head_dim, cfg.theta)
-    hw = HostWeights(cfg, ts, cos, sin)
+    hw = HostWeights(cfg, ts, cos, sin, qtypes=qtypes)
     hw.bfile = bf  # keeps the mapping alive with the views
     return hw
 
@@ -333,12 +348,17 @@ def model_dir_tensors(hw: HostWeights) -> tuple[dict, list]:
     header = dict(hidden=D, layers=cfg.layers, mode=1, num_heads=cfg.heads, num_kv_heads=cfg.kv_heads,
                   head_dim=cfg.head_dim, intermediate=F, vocab=V)
 
-    def lin(a: np.ndarray, inn: int, out: int):
-        return (Q8_0, (out, inn), a) if a.dtype == np.uint8 else (F32, (inn, out), a)
+    def block_dtype(key: str) -> int:  # bfile dtype of a uint8 (block-quantised) tensor
+        return _KQ_FILE.get(hw.qt.get(key, -1), Q8_0)
+
+    def lin(key: str, inn: int, out: int):
+        a = hw.t[key]
+        return (block_dtype(key), (out, inn), a) if a.dtype == np.uint8 else (F32, (inn, out), a)
 
     ts = []
-    emb = hw.t["head"] if cfg.embed == "tied" else hw.t["embed"]
-    ts.append(("model.embed_tokens.weight", Q8_0 if emb.dtype == np.uint8 else F32, (V, D), emb))
+    emb_key = "head" if cfg.embed == "tied" else "embed"
+    emb = hw.t[emb_key]
+    ts.append(("model.embed_tokens.weight", block_dtype(emb_key) if emb.dtype == np.uint8 else F32, (V, D), emb))
     ts.append(("model.norm.weight", F32, (D,), hw.t["final_norm"]))
     dims = {"q": (D, qd), "k": (D, kvd), "v": (D, kvd), "o": (qd, D), "gate": (D, F), "down": (F, D), "up": (D, F)}
     for l in range(cfg.layers):
@@ -347,14 +367,15 @@ def model_dir_tensors(hw: HostWeights) -> tuple[dict, list]:
             if key.startswith("rms"):
                 ts.append((nm, F32, (D,), hw.t[f"{key}.{l}"]))
             else:
-                dt, shape, a = lin(hw.t[f"{key}.{l}"], *dims[key])
+                dt, shape, a = lin(f"{key}.{l}", *dims[key])
                 ts.append((nm, dt, shape, a))
         if cfg.qkv_bias:
             for key, n in (("bq", qd), ("bk", kvd), ("bv", kvd)):
                 ts.append((layer_name(l, BIAS_SUFFIX[key]), F32, (n,), hw.t[f"{key}.{l}"]))
     if cfg.embed != "tied":
         h = hw.t["head"]
-        ts.append(("lm_head.weight",) + ((Q8_0, (V, D), h) if h.dtype == np.uint8 else (F32, (D, V), h)))
+        ts.append(("lm_head.weight",) + ((block_dtype("head"), (V, D), h) if h.dtype == np.uint8
+                                         else (F32, (D, V), h)))
     return header, ts
 
 

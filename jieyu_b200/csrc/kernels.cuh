@@ -150,5 +150,11 @@ int launch_set_state(DevState* st, int len, int max_new, int max_len, const int*
 // JYC_Q4K / JYC_Q5K / JYC_Q6K, k % 256 == 0): y[m][n] = x[m][k] . W^T.
 int launch_kquant_matmul(const float* x, int m, int n, int k, const uint8_t* wq, int qtype, float* y,
                          cudaStream_t s);
+// K-quant rows [n][k/256 blocks] -> fp32 rows of `dst` ([.][k]), row r at
+// row_off + r * row_stride, with the reference's dequantised values.
+int launch_kquant_dequant(const uint8_t* blocks, int n, int k, int qtype, float* dst, int row_off, int row_stride,
+                          cudaStream_t s);
+// Bytes of one 256-weight super-block (0 for a type that is not a K-quant).
+size_t kquant_block_bytes(int qtype);
 
 }  // namespace jyc

@@ -366,6 +366,47 @@ int kq_launch_qt(const float* x, int ldx, int m, int n, int k, const uint8_t* wq
     return kq_launch_t<QT, 8>(x, ldx, m, n, k, wq, y, ldy, s);
 }
 
+// Dequantisation of whole rows into fp32 (the reference's dequant_block
+// values), for models whose K-quant weights run on the fp32 matmul path:
+// one warp per (row, super-block); row r lands at dst row row_off + r * row_stride.
+template <int QT>
+__global__ void __launch_bounds__(kKqWarps * 32) kq_dequant_rows_kernel(const uint8_t* __restrict__ blocks, int n,
+                                                                        int k, float* __restrict__ dst, int row_off,
+                                                                        int row_stride) {
+    constexpr int BB = kq_block_bytes<QT>();
+    const int lane = threadIdx.x & 31;
+    const int nblk = k >> 8;
+    const long long units = (long long)n * nblk;
+    for (long long u = (long long)blockIdx.x * kKqWarps + (threadIdx.x >> 5); u < units;
+         u += (long long)gridDim.x * kKqWarps) {
+        const int r = (int)(u / nblk), bl = (int)(u % nblk);
+        float w[8];
+        int o0 = 0, o1 = 0;
+        kq_dequant<QT>(blocks + (size_t)u * BB, lane, w, o0, o1);
+        float* out = dst + ((size_t)row_off + (size_t)r * row_stride) * k + (size_t)bl * 256;
+        if (QT == JYC_Q6K) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) out[128 * (j >> 2) + o0 + 32 * (j & 3)] = w[j];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                out[o0 + i] = w[i];
+                out[o1 + i] = w[4 + i];
+            }
+        }
+    }
+}
+
+template <int QT>
+int kq_dequant_launch(const uint8_t* blocks, int n, int k, float* dst, int row_off, int row_stride,
+                      cudaStream_t s) {
+    const long long units = (long long)n * (k >> 8);
+    const int grid = (int)std::min<long long>((units + kKqWarps - 1) / kKqWarps, 148 * 16);
+    kq_dequant_rows_kernel<QT><<<grid, kKqWarps * 32, 0, s>>>(blocks, n, k, dst, row_off, row_stride);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+
 }  // namespace
 
 int launch_kquant_matmul(const float* x, int m, int n, int k, const uint8_t* wq, int qtype, float* y,
@@ -386,6 +427,20 @@ int launch_kquant_matmul(const float* x, int m, int n, int k, const uint8_t* wq,
         if (r != JYC_OK) return r;
     }
     return JYC_OK;
+}
+
+int launch_kquant_dequant(const uint8_t* blocks, int n, int k, int qtype, float* dst, int row_off, int row_stride,
+                          cudaStream_t s) {
+    if (n <= 0 || k <= 0 || k % 256) return arg_error("K-quant weights need k % 256 == 0");
+    if (((uintptr_t)blocks & 3)) return arg_error("K-quant blocks must be 4-byte aligned");
+    if (qtype == JYC_Q4K) return kq_dequant_launch<JYC_Q4K>(blocks, n, k, dst, row_off, row_stride, s);
+    if (qtype == JYC_Q5K) return kq_dequant_launch<JYC_Q5K>(blocks, n, k, dst, row_off, row_stride, s);
+    if (qtype == JYC_Q6K) return kq_dequant_launch<JYC_Q6K>(blocks, n, k, dst, row_off, row_stride, s);
+    return arg_error("unknown K-quant type");
+}
+
+size_t kquant_block_bytes(int qtype) {
+    return qtype == JYC_Q4K ? 144 : qtype == JYC_Q5K ? 176 : qtype == JYC_Q6K ? 210 : 0;
 }
 
 }  // namespace jyc

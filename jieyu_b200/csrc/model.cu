@@ -184,20 +184,23 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
         set_error("fp16 weights are not supported by the B200 path");
         return JYC_ERR_UNSUPPORTED;
     }
-    const bool q8 = w.q != nullptr;
+    // K-quant blocks (Q4_K / Q5_K / Q6_K) are dequantised to the reference's
+    // fp32 values here and then run on the fp32 path
+    const bool kq = w.q != nullptr && w.f == nullptr && kquant_block_bytes(w.qt) != 0;
+    const bool q8 = w.q != nullptr && !kq;
     if (q8 && w.qt != JYC_Q8_0) {
-        set_error("only Q8_0 quantised weights are supported by the B200 path (got type " +
-                  std::to_string((int)w.qt) + ")");
+        set_error("quantised weights must be Q8_0, Q4_K, Q5_K or Q6_K (got type " + std::to_string((int)w.qt) + ")");
         return JYC_ERR_UNSUPPORTED;
     }
-    if (!q8 && w.f == nullptr) {
+    if (!q8 && !kq && w.f == nullptr) {
         set_error("missing weight tensor");
         return JYC_ERR_ARG;
     }
     if ((q8 ? W_Q8 : W_F32) != expect_type) {
-        set_error("mixed Q8_0 / fp32 linear weights are not supported");
+        set_error("Q8_0 linear weights mixed with fp32 or K-quant ones are not supported");
         return JYC_ERR_UNSUPPORTED;
     }
+    if (kq && k % 256) return arg_error("K-quant weights need an input dimension that is a multiple of 256");
     if (dst.n == 0) {  // first piece: allocate the whole (fused) matrix
         dst.n = n_total;
         dst.k = k;
@@ -213,16 +216,21 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
             TRY(m->alloc(&dst.f, (size_t)n_total * k));
         }
     }
-    const size_t bytes = q8 ? (size_t)n * (k / 32) * 34 : (size_t)n * k * 4;
+    const size_t bytes = q8   ? (size_t)n * (k / 32) * 34
+                         : kq ? (size_t)n * (k / 256) * kquant_block_bytes(w.qt)
+                              : (size_t)n * k * 4;
     if (bytes > staging_bytes) {
         set_error("internal: staging buffer too small");
         return JYC_ERR_ARG;
     }
-    JYC_CUDA(cudaMemcpyAsync(staging, q8 ? w.q : (const void*)w.f, bytes, cudaMemcpyHostToDevice, m->stream));
+    JYC_CUDA(cudaMemcpyAsync(staging, w.f ? (const void*)w.f : w.q, bytes, cudaMemcpyHostToDevice, m->stream));
     if (q8) {
         TRY(launch_q8_repack(staging, n, k, dst.qs, dst.d, row_off, row_stride, m->stream));
         if (dst.tiled)
             TRY(launch_q8_repack_tiled(staging, n, k, dst.tq, dst.td, n_total, row_off, row_stride, m->stream));
+    } else if (kq) {
+        TRY(launch_kquant_dequant(static_cast<const uint8_t*>(staging), n, k, w.qt, dst.f, row_off, row_stride,
+                                  m->stream));
     } else
         TRY(launch_transpose(static_cast<const float*>(staging), dst.f, k, n, row_off, row_stride, m->stream));
     // the staging buffer is reused by the next upload: wait for this one
@@ -360,7 +368,7 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     if (m->vocab_off < 0 || (long long)m->vocab_off + m->V > m->Ve)
         return arg_error("model: LM-head rows must be a slice of the embedding's vocabulary");
     m->q_dim = m->H * m->hd; m->kv_dim = m->KV * m->hd; m->nqkv = m->q_dim + 2 * m->kv_dim;
-    m->wtype = d->layers[0].Wq.q != nullptr ? W_Q8 : W_F32;
+    m->wtype = (d->layers[0].Wq.q != nullptr && d->layers[0].Wq.qt == JYC_Q8_0) ? W_Q8 : W_F32;  // K-quant: fp32 path
     const int kq = m->wtype == W_Q8 ? 32 : 8;
     if (m->D % kq || m->q_dim % kq || m->F % kq)
         return arg_error("model: hidden, heads*head_dim and intermediate must be multiples of " +
@@ -377,7 +385,7 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     auto tb = [&](int n, int k) { return m->wtype == W_Q8 ? (size_t)n * (k / 32) * 34 : (size_t)n * k * 4; };
     size_t stage = std::max({tb(m->q_dim, m->D), tb(m->kv_dim, m->D), tb(m->D, m->q_dim), tb(m->F, m->D),
                              tb(m->D, m->F)});
-    const bool head_q8 = d->lm_head.q != nullptr;
+    const bool head_q8 = d->lm_head.q != nullptr && d->lm_head.qt == JYC_Q8_0;
     const size_t head_bytes = head_q8 ? (size_t)std::max(m->V, m->Ve) * (m->D / 32) * 34
                                       : (size_t)std::max(m->V, m->Ve) * m->D * 4;
     stage = std::max(stage, head_bytes);
@@ -422,8 +430,21 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
         } else {
             TRY(upload_wmat(m, d->embed, m->Ve, m->D, m->embed_q, m->Ve, 0, 1, staging, stage, W_Q8));
         }
+    } else if (d->embed.q != nullptr && kquant_block_bytes(d->embed.qt) != 0) {
+        // K-quant embedding rows (the reference's wmat_row dequantises them): fp32 rows
+        if (m->D % 256) return arg_error("K-quant embedding needs hidden % 256 == 0");
+        const size_t eb = (size_t)m->Ve * (m->D / 256) * kquant_block_bytes(d->embed.qt);
+        if (eb > stage) {
+            set_error("internal: staging buffer too small for the embedding");
+            return JYC_ERR_ARG;
+        }
+        TRY(m->alloc(&m->embed_f, (size_t)m->Ve * m->D));
+        JYC_CUDA(cudaMemcpyAsync(staging, d->embed.q, eb, cudaMemcpyHostToDevice, m->stream));
+        TRY(launch_kquant_dequant(static_cast<const uint8_t*>(staging), m->Ve, m->D, d->embed.qt, m->embed_f, 0, 1,
+                                  m->stream));
+        JYC_CUDA(cudaStreamSynchronize(m->stream));
     } else {
-        set_error("embedding must be fp32 or Q8_0");
+        set_error("embedding must be fp32, Q8_0, Q4_K, Q5_K or Q6_K");
         return JYC_ERR_UNSUPPORTED;
     }
     m->weight_bytes += (m->embed_f ? 4.0 * m->D : m->D * 34.0 / 32.0) + 4.0 * m->D;  // row + final norm

@@ -34,7 +34,7 @@ class Config:
     inter: int
     vocab: int
     theta: float
-    wtype: str = "q8"          # linear weights: "q8" (Q8_0) or "f32"
+    wtype: str = "q8"          # linear weights: "q8" (Q8_0), "f32", or "kq" (Q4_K / Q5_K / Q6_K blocks)
     embed: str = "f32"         # "f32", "q8" (separate) or "tied" (Q8_0, = LM head)
     qkv_bias: bool = False
     max_seq: int = 512
@@ -131,9 +131,10 @@ def prompt_ids(cfg: Config, seed: int = 1234, index: int = 0, n: Optional[int] =
 class HostWeights:
     """Host tensors in the reference layouts + the descriptor pointing at them."""
 
-    def __init__(self, cfg: Config, tensors: dict, cos: np.ndarray, sin: np.ndarray):
+    def __init__(self, cfg: Config, tensors: dict, cos: np.ndarray, sin: np.ndarray, qtypes: Optional[dict] = None):
         self.cfg = cfg
         self.t = tensors          # keeps every buffer alive
+        self.qt = dict(qtypes or {})  # block type (JYC_Q4K / Q5K / Q6K) of uint8 tensors; Q8_0 when absent
         self.cos, self.sin = cos, sin
         self._build_desc()
 
@@ -236,7 +237,7 @@ class HostWeights:
     def _wmat(self, key: str) -> WMat:
         a = self.t[key]
         if a.dtype == np.uint8:
-            return WMat(None, None, _ptr(a), JYC_Q8_0)
+            return WMat(None, None, _ptr(a), self.qt.get(key, JYC_Q8_0))
         return WMat(_ptr(a), None, None, 0)
 
     def _build_desc(self) -> None:
@@ -274,12 +275,14 @@ class HostWeights:
         """Algorithmic weight bytes one decode token reads (Q8_0: 34 B / 32)."""
         cfg = self.cfg
         D, F = cfg.hidden, cfg.inter
-        per = 34.0 / 32.0 if cfg.wtype == "q8" else 4.0
+        per = 34.0 / 32.0 if cfg.wtype == "q8" else 4.0  # "kq": dequantised to fp32 on the device
         lin = (cfg.q_dim + 2 * cfg.kv_dim) * D + D * cfg.q_dim + 3 * F * D
         b = cfg.layers * (lin * per + 2 * D * 4 + (cfg.q_dim + 2 * cfg.kv_dim) * 4 * cfg.qkv_bias)
-        head_per = 34.0 / 32.0 if self.t["head"].dtype == np.uint8 else 4.0
-        b += cfg.vocab * D * head_per + 4 * D
-        b += D * (34.0 / 32.0 if cfg.embed in ("q8", "tied") else 4.0)
+        head_q8 = self.t["head"].dtype == np.uint8 and self.qt.get("head", JYC_Q8_0) == JYC_Q8_0
+        b += cfg.vocab * D * (34.0 / 32.0 if head_q8 else 4.0) + 4 * D
+        emb_key = "head" if cfg.embed == "tied" else "embed"
+        emb_q8 = self.t[emb_key].dtype == np.uint8 and self.qt.get(emb_key, JYC_Q8_0) == JYC_Q8_0
+        b += D * (34.0 / 32.0 if emb_q8 else 4.0)
         return b
 
 

@@ -477,10 +477,11 @@ void jyo_cache_read(void* p, int layer, int npos, int8_t* k, float* ks, int8_t* 
     memcpy(vs, c->vs + lay * c->KV, (size_t)npos * c->KV * sizeof(float));
 }
 
-/* matmul_w (wmat_kernel.h:9-16): fp32 [k][n] -> matmul, Q8_0 [n][k] -> matmul_q. */
+/* matmul_w (wmat_kernel.h:9-16): fp32 [k][n] -> matmul, Q8_0 / K-quant [n][k] -> matmul_q. */
 static int matmul_w(const jyc_wmat* w, int m, int n, int k, const float* A, float* Cc) {
     if (w->f) { jyo_matmul_f32(m, n, k, A, w->f, Cc); return 0; }
     if (w->q && w->qt == JYC_Q8_0) { jyo_matmul_q8(A, w->q, Cc, m, n, k); return 0; }
+    if (w->q && kq_bytes(w->qt)) return jyo_matmul_qk(A, w->q, Cc, m, n, k, w->qt);
     return -1;
 }
 
@@ -490,6 +491,12 @@ static int wmat_row(const jyc_wmat* w, size_t id, int width, float* dst) {
     if (w->q && w->qt == JYC_Q8_0) {
         const uint8_t* row = (const uint8_t*)w->q + id * (size_t)(width / 32) * 34;
         for (int bl = 0; bl < width / 32; bl++) dequant_q8(row + (size_t)bl * 34, dst + bl * 32);
+        return 0;
+    }
+    if (w->q && kq_bytes(w->qt) && width % 256 == 0) {  /* dequant_block per super-block */
+        const int bb = kq_bytes(w->qt);
+        const uint8_t* row = (const uint8_t*)w->q + id * (size_t)(width / 256) * bb;
+        for (int bl = 0; bl < width / 256; bl++) kq_dequant(w->qt, row + (size_t)bl * bb, dst + bl * 256);
         return 0;
     }
     return -1;

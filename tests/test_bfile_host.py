@@ -12,7 +12,9 @@ the CPU.
   offset, misaligned or overlong tensors, dimension count, dtype, size
   mismatch) are rejected here too, and the binding errors of bind_model
   (pipeline.h:63-153: missing tensors, transposed shapes) are raised;
-* a written directory loads back to the same host tensors and config.
+* a written directory loads back to the same host tensors and config,
+  including a model in the K-quant formats (Q4_K / Q5_K / Q6_K mixed per
+  matrix) that the reference's downloads use.
 """
 import ctypes as C
 import json
@@ -31,11 +33,13 @@ TINY_F32 = Config("tiny_f32", 32, 1, 2, 1, 8, 64, 50, 1e4, "f32", "f32", False, 
 
 
 def _models():
+    from _kquant import kquant_model
     return {
         "bind_kat": HostWeights.bind_test_kat(),
         "q8_tied_bias": HostWeights.synthetic(TINY_Q8_TIED, seed=5),
         "q8_separate": HostWeights.synthetic(TINY_Q8, seed=6),
         "f32_rect": HostWeights.synthetic(TINY_F32, seed=7),
+        "kquant_mixed": kquant_model(),
     }
 
 
@@ -117,7 +121,11 @@ def test_reference_binds_the_same_bytes(ref, tmp_path, model):
         for k, key in enumerate(order):
             assert out[12 * l + k] == off(f"{key}.{l}"), (l, key)
             if out[12 * l + k] >= 0 and key in ("q", "k", "v", "o", "gate", "down", "up"):
-                want = bfile.Q8_0 if hw.cfg.wtype == "q8" else bfile.F32
+                name = f"{key}.{l}"
+                if name in hw.qt:
+                    want = {0: bfile.Q4K, 1: bfile.Q5K, 2: bfile.Q6K}[hw.qt[name]]
+                else:
+                    want = bfile.Q8_0 if hw.cfg.wtype == "q8" else bfile.F32
                 assert dt[12 * l + k] == want
     emb_key = "head" if hw.cfg.embed == "tied" else "embed"
     assert out[12 * L] == off(emb_key)
@@ -135,6 +143,7 @@ def test_directory_round_trip(tmp_path, model):
         assert getattr(got.cfg, f) == getattr(hw.cfg, f), f
     assert got.cfg.theta == float(int(hw.cfg.theta))
     assert set(got.t) == set(hw.t)
+    assert got.qt == hw.qt
     for k in hw.t:
         a, b = np.asarray(hw.t[k]), np.asarray(got.t[k])
         assert a.dtype == b.dtype and np.array_equal(a.view(np.uint8), b.view(np.uint8)), k
