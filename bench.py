@@ -557,7 +557,9 @@ def run_kquant(args):
     seeded random blocks with finite scales. value = Q4_K weight GB/s; the
     roofline is HBM (algorithmic bytes = the blocks). The CPU baseline is the
     reference's own qmat::matmul_q on one layer's Q4_K matrices (oracle/_ref,
-    else the oracle port), all host threads."""
+    else the oracle port), all host threads. The line also carries the
+    decode tok/s of a configs[2]-shaped model in mixed K-quant formats
+    (model_decode: the model path, weights dequantised to fp32 at upload)."""
     import numpy as np
     import torch
 
@@ -617,6 +619,33 @@ def run_kquant(args):
         sweep.append({"format": names[qt], "ms_per_step": ms, "bytes_per_step": nbytes, "gbs": gbs,
                       "hbm_frac": gbs / peak, "launches_per_step": len(mats)})
         del mats
+    # the model path: a configs[2]-shaped model in mixed K-quant formats
+    # (HostWeights.synthetic_kquant), dequantised to fp32 once at upload,
+    # greedy decode on the generic kernels after a 128-token prompt
+    from jieyu_b200.model import DeviceModel, HostWeights, prompt_ids
+    khw = HostWeights.synthetic_kquant(cfg)
+    km = DeviceModel(khw)
+    kids = torch.from_numpy(prompt_ids(cfg, n=128)).cuda()
+    new = 64
+    with torch.cuda.stream(stream):
+        s = stream.cuda_stream
+        km.prefill_device(kids.data_ptr(), 128, s)
+        km.decode_device(8, s)  # warm (graph capture)
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        km.rewind(129, s)
+        e0.record(stream)
+        km.decode_device(new, s)
+        e1.record(stream)
+        stream.synchronize()
+    kms = e0.elapsed_time(e1) / new
+    kbytes = float(khw.weight_bytes_per_token())
+    model_line = {"tok_s": 1e3 / kms, "ms_per_token": kms, "bytes_per_token": kbytes,
+                  "hbm_gbs": kbytes / (kms / 1e3) / 1e9, "hbm_frac": kbytes / (kms / 1e3) / 1e9 / peak,
+                  "note": "Q4_K/Q5_K/Q6_K weights run as fp32 on the generic path (4 B per weight read)"}
+    assert lib.jyc_device_error(1) == 0
+    km.close()
+    del khw
     clk = clocks.stop()
     # CPU baseline: the reference's matmul_q over one layer's Q4_K matrices
     rng = np.random.default_rng(7)
@@ -655,8 +684,8 @@ def run_kquant(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "jyc_matmul_qk over the 112 linear weights of the configs[2] shape, one activation row",
                    "l2": "inputs larger than L2 (0.55 GB of Q4_K blocks per step)"},
-        "sweep": sweep,
-        "roofline": {"bound": "hbm", "kernel": "kq_gemv_kernel<Q4_K, 1>", "achieved": q4["gbs"], "peak": peak,
+        "sweep": sweep, "model_decode": model_line,
+        "roofline": {"bound": "hbm", "kernel": "kq_gemv_smem_kernel<Q4_K, 1>", "achieved": q4["gbs"], "peak": peak,
                      "unit": "GB/s", "frac": q4["gbs"] / peak, "traffic": None, "peak_kind": peak_kind},
         "gpu_launches": len(shapes) * args.steps, "clocks": clk, "cpu_baseline": cpu,
     }

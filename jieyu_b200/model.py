@@ -175,6 +175,59 @@ class HostWeights:
         return cls(cfg, t, cos, sin)
 
     @classmethod
+    def synthetic_kquant(cls, cfg: Config, seed: int = 1234) -> "HostWeights":
+        """Seeded K-quant weights (the formats of the reference's downloads),
+        mixed per matrix as Q4_K_M files mix them: Q, O, gate Q4_K; K, up
+        Q5_K; V, down, the LM head and the embedding Q6_K. Random quant bytes;
+        the fp16 block scales drawn so that weights stay O(0.01-0.1); unit
+        norms. Needs hidden, heads*head_dim and intermediate multiples of 256."""
+        D, F, V, qd, kvd = cfg.hidden, cfg.inter, cfg.vocab, cfg.q_dim, cfg.kv_dim
+        bb = {0: 144, 1: 176, 2: 210}
+        rng = np.random.default_rng(seed)
+        stream = [seed * 0x9E3779B9 & 0xFFFFFFFF]
+
+        def hash_bytes(nbytes: int) -> np.ndarray:
+            # counter-based bytes (the lowbias32 integer mix), fast for GBs
+            x = np.arange(stream[0], stream[0] + (nbytes + 3) // 4, dtype=np.uint64).astype(np.uint32)
+            stream[0] = (stream[0] + (nbytes + 3) // 4) & 0xFFFFFFFF
+            x ^= x >> np.uint32(16)
+            x *= np.uint32(0x7FEB352D)
+            x ^= x >> np.uint32(15)
+            x *= np.uint32(0x846CA68B)
+            x ^= x >> np.uint32(16)
+            return x.view(np.uint8)[:nbytes]
+
+        def blocks(q: int, n: int, k: int, lo: float, hi: float) -> np.ndarray:
+            nb = n * (k // 256)
+            b = hash_bytes(nb * bb[q]).reshape(nb, bb[q]).copy()
+            d = rng.uniform(lo, hi, size=nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+            if q == 2:
+                b[:, 208:210] = d
+            else:
+                b[:, 0:2] = d
+                b[:, 2:4] = rng.uniform(lo, hi, size=nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+            return np.ascontiguousarray(b.reshape(-1))
+
+        kinds = {"q": 0, "k": 1, "v": 2, "o": 0, "gate": 0, "up": 1, "down": 2}
+        dims = {"q": (qd, D), "k": (kvd, D), "v": (kvd, D), "o": (D, qd), "gate": (F, D), "up": (F, D),
+                "down": (D, F)}
+        t, qt = {}, {}
+        ones = np.ones(D, dtype=np.float32)
+        for l in range(cfg.layers):
+            t[f"rms1.{l}"] = ones
+            t[f"rms2.{l}"] = ones
+            for key, q in kinds.items():
+                lo, hi = (2.0 ** -17, 2.0 ** -15) if q == 2 else (2.0 ** -13, 2.0 ** -11)
+                t[f"{key}.{l}"] = blocks(q, *dims[key], lo, hi)
+                qt[f"{key}.{l}"] = q
+        t["head"] = blocks(2, V, D, 2.0 ** -15, 2.0 ** -13)
+        t["embed"] = blocks(2, V, D, 2.0 ** -12, 2.0 ** -10)
+        qt["head"] = qt["embed"] = 2
+        t["final_norm"] = ones
+        cos, sin = rope_table(cfg.max_seq, cfg.head_dim, cfg.theta)
+        return cls(replace(cfg, wtype="kq", embed="q8", qkv_bias=False), t, cos, sin, qtypes=qt)
+
+    @classmethod
     def bind_test_kat(cls) -> "HostWeights":
         """The fp32 model of the reference's check_bind_weights
         (libs/text/text.h:485-541 gen_weights::build with make_weights' lm_head,
