@@ -45,8 +45,8 @@ enum { JYC_Q4K = 0, JYC_Q5K = 1, JYC_Q6K = 2, JYC_Q8_0 = 3 };
 
 /* Weight handle. Field order and types equal `struct WMat`
  * (libs/date_libs/wmat.h:32-44): exactly one of f (fp32, row-major [in][out]),
- * h (fp16, [in][out]) or q (quantised blocks, [out][in/32] x 34 B for Q8_0)
- * is non-null. */
+ * h (fp16, [in][out]) or q (quantised blocks: [out][in/32] x 34 B for Q8_0,
+ * [out][in/256] x 144 / 176 / 210 B for Q4_K / Q5_K / Q6_K) is non-null. */
 typedef struct jyc_wmat {
     const float*    f;
     const uint16_t* h;
@@ -235,8 +235,11 @@ typedef struct jyc_model jyc_model;
 
 /* Uploads every weight once (the bind_model point, libs/model_libs/pipeline.h:63-153):
  * Q8_0 blocks are re-laid into the device layout, fp32 [in][out] matrices are
- * transposed, Q/K/V and gate/up are fused. Allocates a device KV cache of
- * desc->max_seq positions. Returns NULL on error. */
+ * transposed, Q4_K / Q5_K / Q6_K blocks (any mix, with fp32 too; input
+ * dimensions multiples of 256) are dequantised once to the reference's fp32
+ * values and run on the fp32 kernels; Q/K/V and gate/up are fused. Q8_0 layer
+ * weights cannot mix with the other types; fp16 weights are not supported.
+ * Allocates a device KV cache of desc->max_seq positions. Returns NULL on error. */
 JYC_API jyc_model* jyc_model_create(const jyc_model_desc* desc);
 JYC_API void jyc_model_free(jyc_model* m);
 /* Bytes of weights one decode token streams (algorithmic, for rooflines). */
