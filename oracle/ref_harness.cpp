@@ -19,6 +19,8 @@
  *   bfile::write_bfile  libs/model_libs/bfile.h:393-411 (model.bf writer)
  *   bfile::View::open + bind_layers / bind_biases / bind_embed / bind_lm_head /
  *   bind_final_norm     libs/model_libs/bfile.h:141-204, load_weights.h:97-155
+ *   json_libs::Tokenizer libs/tokenizer_libs/include/tokenizer.h (load, encode,
+ *                       decode, add_special_token)
  * Nothing here changes the reference's arithmetic; the harness only builds
  * WMat / LayerWeights / __KVcache objects over caller buffers.
  */
@@ -56,6 +58,7 @@
 #include "model_libs/generate.h"
 #include "model_libs/bfile.h"
 #include "model_libs/load_weights.h"
+#include "tokenizer_libs/include/tokenizer.h"
 #include <fstream>
 
 #include "jieyu_b200.h"
@@ -309,6 +312,43 @@ int jyref_bfile_bind(const char* path, int num_layers, int hidden, int vocab, in
     wm(head, o + 1, d + 1);
     o[2] = off(bind_final_norm()); d[2] = o[2] < 0 ? 255 : bfile::F32;
     return 0;
+}
+
+/* The reference's tokenizer over vocab.json / merges.txt files. */
+void* jyref_tok_load(const char* vocab, const char* merges) {
+    json_libs::Tokenizer* t = new json_libs::Tokenizer();
+    if (!t->load(vocab, merges)) {
+        delete t;
+        return nullptr;
+    }
+    return t;
+}
+
+void jyref_tok_free(void* t) { delete static_cast<json_libs::Tokenizer*>(t); }
+
+/* ids of `text` (len bytes); returns their count (only the first `cap` are stored). */
+int jyref_tok_encode(void* t, const char* text, int len, int* out, int cap) {
+    const std::vector<int32_t> ids = static_cast<json_libs::Tokenizer*>(t)->encode(std::string(text, (size_t)len));
+    for (size_t i = 0; i < ids.size() && (int)i < cap; i++) out[i] = ids[i];
+    return (int)ids.size();
+}
+
+/* bytes of decode(ids); returns their count (only the first `cap` are stored). */
+int jyref_tok_decode(void* t, const int* ids, int n, char* out, int cap) {
+    const std::string s = static_cast<json_libs::Tokenizer*>(t)->decode(std::vector<int32_t>(ids, ids + n));
+    memcpy(out, s.data(), std::min<size_t>(s.size(), (size_t)std::max(cap, 0)));
+    return (int)s.size();
+}
+
+/* {bos, eos, unk, word_end, vocab_size} */
+void jyref_tok_info(void* t, int* out) {
+    const json_libs::Tokenizer* k = static_cast<json_libs::Tokenizer*>(t);
+    out[0] = k->bos_id(); out[1] = k->eos_id(); out[2] = k->unk_id(); out[3] = k->word_end_id();
+    out[4] = (int)k->vocab_size();
+}
+
+int jyref_tok_add_special(void* t, const char* piece) {
+    return static_cast<json_libs::Tokenizer*>(t)->add_special_token(piece);
 }
 
 }  // extern "C"
