@@ -1,0 +1,141 @@
+"""Text in, text out on the device path: the reference's `jieyu_load` /
+`jieyu_generate` flow (main.hpp:85-227 over pipeline.h:280-436
+`load_model_dir` + `generate_text`) with the token loop on the GPU.
+
+A model directory is bound as the reference binds it: weights from
+`model.bf` (jieyu_b200.bfile.load_model_dir), the tokenizer from vocab.json /
+merges.txt (jieyu_b200.tokenizer), and from model_info.json the BOS rule
+(add_bos_token, default 1) and the chat strings (message_start,
+message_end, text_end, user_start, assistant_start, bos_text, turn_end), each
+registered as a special token when the vocabulary holds it.
+
+`TextModel.generate` follows generate_text: encode the prompt, prepend BOS,
+reject ids outside the model's vocabulary (-1), keep at most max_seq prompt
+tokens and at most max_seq - prompt tokens of output, stop on the tokenizer's
+EOS and the registered text_end / message_end ids, and build the output text
+token by token: a registered message_start / message_end / text_end token
+ends the text without being added; otherwise the token's bytes are added and
+the text is cut (and generation stops) at the first chat string or "<|name"
+marker it now holds.
+"""
+from __future__ import annotations
+
+import json
+import os
+from typing import Optional
+
+from .bfile import _info_int, load_model_dir
+from .model import DeviceModel
+from .tokenizer import _TO_CHAR, Tokenizer, load_tokenizer
+
+
+def write_byte_level_vocab(vocab_path: str, merges_path: str) -> None:
+    """The reference's byte-level vocabulary (tokenizer_libs/include/
+    byte_vocab.h): byte b's symbol has id b; no merges."""
+    parts = []
+    for b, piece in enumerate(_TO_CHAR):
+        esc = piece.replace(b"\\", b"\\\\").replace(b'"', b'\\"')
+        parts.append(b'"' + esc + b'":' + str(b).encode())
+    with open(vocab_path, "wb") as f:
+        f.write(b"{" + b",".join(parts) + b"}")
+    with open(merges_path, "wb") as f:
+        f.write(b"#version: 0.2\n")
+
+
+def _is_marker_char(c: int) -> bool:
+    return 0x61 <= c <= 0x7A or 0x41 <= c <= 0x5A or 0x30 <= c <= 0x39 or c in (0x5F, 0x2D)
+
+
+def marker_at(s: bytes, stops: list) -> int:
+    """First position of a chat string or of "<|" + 1..24 marker characters
+    (pipeline.h:201-217); -1 when there is none."""
+    best = -1
+    for st in stops:
+        if st:
+            at = s.find(st)
+            if at >= 0 and (best < 0 or at < best):
+                best = at
+    lt = s.find(b"<|")
+    while lt >= 0:
+        n = 0
+        while lt + 2 + n < len(s) and n < 24 and _is_marker_char(s[lt + 2 + n]):
+            n += 1
+        if n >= 1 and (best < 0 or lt < best):
+            best = lt
+        lt = s.find(b"<|", lt + 1)
+    return best
+
+
+class TextModel:
+    """A reference model directory bound for text generation on the device."""
+
+    def __init__(self, path: str, max_seq: int = 0, tokenizer: Optional[Tokenizer] = None):
+        self.hw = load_model_dir(path, max_seq=max_seq)
+        self.tok = tokenizer or load_tokenizer(path)
+        with open(os.path.join(path, "model_info.json"), encoding="utf-8") as f:
+            info = json.load(f)
+
+        def text(key: str) -> bytes:
+            v = info.get(key, "")
+            return v.encode("utf-8") if isinstance(v, str) else b""
+
+        self.add_bos = _info_int(info, "add_bos_token", 1) != 0
+        self.s_start, self.s_end, self.s_text = text("message_start"), text("message_end"), text("text_end")
+        self.s_user, self.s_asst, self.s_turn = text("user_start"), text("assistant_start"), text("turn_end")
+        s_bos = text("bos_text")
+
+        def register(piece: bytes) -> int:  # register_special: 0 when absent
+            i = self.tok.add_special_token(piece) if piece else -1
+            return i if i >= 0 else 0
+
+        self.id_start = register(self.s_start)
+        self.id_end = register(self.s_end)
+        self.id_text = register(self.s_text)
+        for piece in (self.s_user, self.s_asst, s_bos, self.s_turn):
+            register(piece)
+        self.model = DeviceModel(self.hw)
+
+    def close(self) -> None:
+        self.model.close()
+
+    def generate(self, prompt, max_new: int = 256, temperature: float = 0.7,
+                 repetition_penalty: float = 1.1) -> tuple[int, bytes]:
+        """(new tokens, generated text bytes); (0, b"") when nothing can be
+        produced, (-1, b"") when the prompt's ids do not fit the model."""
+        cfg = self.hw.cfg
+        V, max_seq = cfg.vocab, cfg.max_seq
+        ids = self.tok.encode(prompt)
+        if self.add_bos and 0 <= self.tok.bos_id < V:
+            ids.insert(0, self.tok.bos_id)
+        if not ids:
+            return 0, b""
+        if max_new <= 0:
+            max_new = max_seq
+        if any(i < 0 or i >= V for i in ids):
+            return -1, b""
+        ids = ids[:max_seq]
+        if len(ids) + max_new > max_seq:
+            max_new = max_seq - len(ids)
+        if max_new <= 0:
+            return 0, b""
+        eos: list = []
+        for e in (self.tok.eos_id, self.id_text, self.id_end):
+            if 0 <= e < V and e not in eos and len(eos) < 3:
+                eos.append(e)
+        stops = [s for s in (self.s_start, self.s_end, self.s_text, self.s_user, self.s_asst, self.s_turn) if s]
+        specials = [i for i in (self.id_start, self.id_end, self.id_text) if i != 0]
+        out = bytearray()
+
+        def on_token(i: int) -> bool:  # echo_token (pipeline.h:230-260): True stops the loop
+            if i in specials:
+                return True
+            out.extend(self.tok.decode([i]))
+            at = marker_at(bytes(out), stops)
+            if at >= 0:
+                del out[at:]
+                return True
+            return False
+
+        seq = self.model.generate(ids, max_new, eos=eos or None, temperature=temperature,
+                                  repetition_penalty=repetition_penalty, cb=on_token)
+        return len(seq) - len(ids), bytes(out)

@@ -59,6 +59,7 @@
 #include "model_libs/bfile.h"
 #include "model_libs/load_weights.h"
 #include "tokenizer_libs/include/tokenizer.h"
+#include "tokenizer_libs/include/byte_vocab.h"
 #include <fstream>
 
 #include "jieyu_b200.h"
@@ -349,6 +350,17 @@ void jyref_tok_info(void* t, int* out) {
 
 int jyref_tok_add_special(void* t, const char* piece) {
     return static_cast<json_libs::Tokenizer*>(t)->add_special_token(piece);
+}
+
+/* The reference's byte-level vocabulary files (byte_vocab.h write_byte_level_vocab). */
+int jyref_write_byte_vocab(const char* vocab, const char* merges) {
+    try {
+        json_libs::write_byte_level_vocab(vocab, merges);
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
 }
 
 }  // extern "C"
