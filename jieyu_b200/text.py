@@ -102,40 +102,59 @@ class TextModel:
                  repetition_penalty: float = 1.1) -> tuple[int, bytes]:
         """(new tokens, generated text bytes); (0, b"") when nothing can be
         produced, (-1, b"") when the prompt's ids do not fit the model."""
-        cfg = self.hw.cfg
-        V, max_seq = cfg.vocab, cfg.max_seq
-        ids = self.tok.encode(prompt)
-        if self.add_bos and 0 <= self.tok.bos_id < V:
-            ids.insert(0, self.tok.bos_id)
-        if not ids:
-            return 0, b""
-        if max_new <= 0:
-            max_new = max_seq
-        if any(i < 0 or i >= V for i in ids):
-            return -1, b""
-        ids = ids[:max_seq]
-        if len(ids) + max_new > max_seq:
-            max_new = max_seq - len(ids)
-        if max_new <= 0:
-            return 0, b""
-        eos: list = []
-        for e in (self.tok.eos_id, self.id_text, self.id_end):
-            if 0 <= e < V and e not in eos and len(eos) < 3:
-                eos.append(e)
-        stops = [s for s in (self.s_start, self.s_end, self.s_text, self.s_user, self.s_asst, self.s_turn) if s]
-        specials = [i for i in (self.id_start, self.id_end, self.id_text) if i != 0]
-        out = bytearray()
+        chat = ChatStrings(self.s_start, self.s_end, self.s_text, self.s_user, self.s_asst, self.s_turn,
+                           self.id_start, self.id_end, self.id_text)
+        return generate_text(self.tok, prompt, self.hw.cfg.vocab, self.hw.cfg.max_seq, self.add_bos, chat,
+                             self.model.generate, max_new, temperature, repetition_penalty)
 
-        def on_token(i: int) -> bool:  # echo_token (pipeline.h:230-260): True stops the loop
-            if i in specials:
-                return True
-            out.extend(self.tok.decode([i]))
-            at = marker_at(bytes(out), stops)
-            if at >= 0:
-                del out[at:]
-                return True
-            return False
 
-        seq = self.model.generate(ids, max_new, eos=eos or None, temperature=temperature,
-                                  repetition_penalty=repetition_penalty, cb=on_token)
-        return len(seq) - len(ids), bytes(out)
+class ChatStrings:
+    """model_info.json's chat strings and the ids of the three registered as
+    stop tokens (0 when the vocabulary lacks them, as register_special)."""
+
+    def __init__(self, s_start=b"", s_end=b"", s_text=b"", s_user=b"", s_asst=b"", s_turn=b"",
+                 id_start=0, id_end=0, id_text=0):
+        self.stops = [x for x in (s_start, s_end, s_text, s_user, s_asst, s_turn) if x]
+        self.id_start, self.id_end, self.id_text = id_start, id_end, id_text
+
+
+def generate_text(tok: Tokenizer, prompt, vocab: int, max_seq: int, add_bos: bool, chat: ChatStrings, gen,
+                  max_new: int = 256, temperature: float = 0.7, repetition_penalty: float = 1.1) -> tuple[int, bytes]:
+    """The reference's generate_text (pipeline.h:280-374) over a token
+    generator `gen(ids, max_new, eos=, temperature=, repetition_penalty=, cb=)`
+    with generate()'s contract (returns prompt + new ids; cb(id) -> True
+    stops after that token)."""
+    ids = tok.encode(prompt)
+    if add_bos and 0 <= tok.bos_id < vocab:
+        ids.insert(0, tok.bos_id)
+    if not ids:
+        return 0, b""
+    if max_new <= 0:
+        max_new = max_seq
+    if any(i < 0 or i >= vocab for i in ids):
+        return -1, b""
+    ids = ids[:max_seq]
+    if len(ids) + max_new > max_seq:
+        max_new = max_seq - len(ids)
+    if max_new <= 0:
+        return 0, b""
+    eos: list = []
+    for e in (tok.eos_id, chat.id_text, chat.id_end):  # want_eos: in range, distinct, at most 3
+        if 0 <= e < vocab and e not in eos and len(eos) < 3:
+            eos.append(e)
+    specials = [i for i in (chat.id_start, chat.id_end, chat.id_text) if i != 0]
+    out = bytearray()
+
+    def on_token(i: int) -> bool:  # echo_token (pipeline.h:230-260): True stops the loop
+        if i in specials:
+            return True
+        out.extend(tok.decode([i]))
+        at = marker_at(bytes(out), chat.stops)
+        if at >= 0:
+            del out[at:]
+            return True
+        return False
+
+    seq = gen(ids, max_new, eos=eos or None, temperature=temperature, repetition_penalty=repetition_penalty,
+              cb=on_token)
+    return len(seq) - len(ids), bytes(out)

@@ -48,3 +48,60 @@ def test_check_pipeline_tokenizer_cases(tmp_path):
 ])
 def test_marker_at(s, stops, want):
     assert X.marker_at(s, stops) == want
+
+
+class _Script:
+    """A generator with generate()'s contract that emits a fixed id list
+    (stopping early on EOS or when the callback asks)."""
+
+    def __init__(self, new_ids):
+        self.new_ids = list(new_ids)
+        self.calls = []
+
+    def __call__(self, ids, max_new, eos=None, temperature=0.0, repetition_penalty=1.0, cb=None):
+        self.calls.append((list(ids), max_new, list(eos or []), temperature, repetition_penalty))
+        seq = list(ids)
+        for t in self.new_ids[:max_new]:
+            seq.append(t)
+            if (eos and t in eos) or (cb and cb(t)):
+                break
+        return seq
+
+
+@pytest.fixture
+def bytetok(tmp_path):
+    X.write_byte_level_vocab(str(tmp_path / "vocab.json"), str(tmp_path / "merges.txt"))
+    tok = Tokenizer()
+    assert tok.load(str(tmp_path / "vocab.json"), str(tmp_path / "merges.txt"))
+    return tok
+
+
+def test_generate_text_rules(bytetok):
+    tok = bytetok
+    V = 259
+    plain = X.ChatStrings()
+    # BOS first, EOS list = {eos, 0 (text_end absent, as register_special gives 0)}
+    g = _Script([ord(c) for c in "hi there"])
+    assert X.generate_text(tok, "ab", V, 64, True, plain, g, 8, 0.0, 1.0) == (8, b"hi there")
+    ids, max_new, eos, _, _ = g.calls[0]
+    assert ids == [tok.bos_id, 97, 98] and max_new == 8 and eos == [tok.eos_id, 0]
+    # max_new clamped by max_seq; a prompt longer than max_seq is cut
+    g = _Script([ord("z")] * 50)
+    assert X.generate_text(tok, "abcdef", V, 10, False, plain, g, 20, 0.0, 1.0)[0] == 4
+    assert X.generate_text(tok, "x" * 30, V, 10, False, plain, g, 5, 0.0, 1.0) == (0, b"")
+    # a chat string in the output ends it (cut before the string) and stops the loop
+    chat = X.ChatStrings(s_end=b"END")
+    g = _Script([ord(c) for c in "okENDmore"])
+    n, out = X.generate_text(tok, "q", V, 64, False, chat, g, 20, 0.0, 1.0)
+    assert out == b"ok" and n == 5
+    # a "<|name" marker too
+    g = _Script([ord(c) for c in "fine<|im_end|>tail"])
+    n, out = X.generate_text(tok, "q", V, 64, False, plain, g, 30, 0.0, 1.0)
+    assert out == b"fine" and n == len("fine<|i")
+    # a registered stop token ends the text without being added
+    chat = X.ChatStrings(id_end=258)
+    g = _Script([ord("a"), 258, ord("b")])
+    assert X.generate_text(tok, "q", V, 64, False, chat, g, 10, 0.0, 1.0) == (2, b"a")
+    # ids outside the model's vocabulary: -1
+    assert X.generate_text(tok, "q", 100, 64, False, plain, _Script([]), 4, 0.0, 1.0) == (-1, b"")
+    assert X.generate_text(tok, "", V, 64, False, plain, _Script([]), 4, 0.0, 1.0) == (0, b"")
