@@ -1,4 +1,5 @@
-"""ctypes binding of libjieyu_b200.so (the C ABI declared in include/jieyu_b200.h).
+"""ctypes binding of libjieyu_b200.so (the C ABIs declared in include/jieyu_b200.h
+and include/jieyu.h).
 
 The library is the product: every compute call below runs a CUDA kernel of
 that library. There is no fallback; if the shared object is missing the import
@@ -127,6 +128,21 @@ SIGNATURES = [
     ("jyc_batch_path", _I, [_P]),
     ("jyc_batch_kernels_per_step", _I, [_P]),
     ("jyc_batch_kv_bytes_per_step", C.c_double, [_P, _I]),
+    # text C ABI (include/jieyu.h)
+    ("jieyu_load", _P, [C.c_char_p, _I]),
+    ("jieyu_free", None, [_P]),
+    ("jieyu_last_error", C.c_char_p, [_P]),
+    ("jieyu_version", C.c_char_p, []),
+    ("jieyu_context_length", _I, [_P]),
+    ("jieyu_model_dir", C.c_char_p, [_P]),
+    ("jieyu_generate", _I, [_P, C.c_char_p, _P, _I, _I, C.c_float, C.c_float]),
+    ("jieyu_generate_jsonl", _I, [_P, C.c_char_p, C.c_char_p, C.c_char_p, _P, _I, _I, C.c_float, C.c_float]),
+    ("jyt_tok_load", _P, [C.c_char_p, C.c_char_p]),
+    ("jyt_tok_free", None, [_P]),
+    ("jyt_tok_encode", _I, [_P, C.c_char_p, _I, _P, _I]),
+    ("jyt_tok_decode", _I, [_P, _P, _I, _P, _I]),
+    ("jyt_tok_add_special", _I, [_P, C.c_char_p, _I]),
+    ("jyt_tok_info", _I, [_P, _P]),
 ]
 
 _lib = None

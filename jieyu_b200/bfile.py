@@ -204,22 +204,52 @@ def write_bfile(path: str, header: dict, tensors: list) -> None:
             written = off + len(memoryview(data).cast("B"))
 
 
+def _first_pairs(pairs: list) -> dict:
+    """An object's members with the first of duplicate keys kept, as the
+    reference's json_file::find returns the first match."""
+    out: dict = {}
+    for k, v in pairs:
+        out.setdefault(k, v)
+    return out
+
+
 def _read_info(path: str) -> dict:
+    """model_info.json with numbers kept as their source text (the
+    reference's parser keeps every value's raw text, json_parser.h:99)."""
     if not os.path.exists(path):
         raise BFileError(f"{path} not found")
     with open(path, encoding="utf-8") as f:
-        return json.load(f)
+        return json.load(f, parse_int=str, parse_float=str, parse_constant=str, object_pairs_hook=_first_pairs)
+
+
+def _info_text(info: dict, key: str) -> str:
+    """json_file::GetJsonData (json.h:57-63): a string's text, else the
+    value's source text; "" when the key is absent."""
+    if key not in info:
+        return ""
+    v = info[key]
+    if isinstance(v, str):
+        return v
+    if isinstance(v, bool):
+        return "true" if v else "false"
+    if v is None:
+        return "null"
+    return json.dumps(v, separators=(",", ":"))
 
 
 def _info_int(info: dict, key: str, fallback: int) -> int:
-    """The reference reads these keys as integers (pipeline.h:53-61)."""
-    v = info.get(key)
-    if v is None or v == "":
+    """json_file::GetJsonInt (json.h:73-83): std::stoi of the value's text
+    (leading white space, a sign, then the digits it starts with), the
+    fallback when the text is empty, has no digits or leaves the int range."""
+    s = _info_text(info, key).lstrip(" \t\n\v\f\r")
+    j = 1 if s[:1] in ("+", "-") else 0
+    k = j
+    while k < len(s) and s[k] in "0123456789":
+        k += 1
+    if k == j:
         return fallback
-    try:
-        return int(float(v))
-    except (TypeError, ValueError):
-        return fallback
+    v = int(s[:k])
+    return v if -2 ** 31 <= v < 2 ** 31 else fallback
 
 
 def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> HostWeights:

@@ -20,11 +20,10 @@ marker it now holds.
 """
 from __future__ import annotations
 
-import json
 import os
 from typing import Optional
 
-from .bfile import _info_int, load_model_dir
+from .bfile import _info_int, _info_text, _read_info, load_model_dir
 from .model import DeviceModel
 from .tokenizer import _TO_CHAR, Tokenizer, load_tokenizer
 
@@ -72,12 +71,10 @@ class TextModel:
     def __init__(self, path: str, max_seq: int = 0, tokenizer: Optional[Tokenizer] = None):
         self.hw = load_model_dir(path, max_seq=max_seq)
         self.tok = tokenizer or load_tokenizer(path)
-        with open(os.path.join(path, "model_info.json"), encoding="utf-8") as f:
-            info = json.load(f)
+        info = _read_info(os.path.join(path, "model_info.json"))
 
-        def text(key: str) -> bytes:
-            v = info.get(key, "")
-            return v.encode("utf-8") if isinstance(v, str) else b""
+        def text(key: str) -> bytes:  # read_info_str (pipeline.h:155-160)
+            return _info_text(info, key).encode("utf-8", "surrogatepass")
 
         self.add_bos = _info_int(info, "add_bos_token", 1) != 0
         self.s_start, self.s_end, self.s_text = text("message_start"), text("message_end"), text("text_end")

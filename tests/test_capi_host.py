@@ -19,13 +19,14 @@ def declared_symbols():
         if fn.endswith(".h"):
             src = open(os.path.join(ROOT, "include", fn)).read()
             names += re.findall(r"JYC_API\s+[^;(]*?\b(jyc_\w+)\s*\(", src)
+            names += re.findall(r"JIEYU_API\s+[^;(]*?\b((?:jieyu|jyt)_\w+)\s*\(", src)
     return sorted(set(names))
 
 
 def test_library_exports_every_declared_symbol():
     lib = _capi.load()
     names = declared_symbols()
-    assert len(names) >= 30
+    assert len(names) >= 30 and "jieyu_generate" in names and "jyt_tok_encode" in names
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, missing
     bound = {n for n, _, _ in _capi.SIGNATURES}

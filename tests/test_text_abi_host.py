@@ -1,0 +1,165 @@
+"""CPU: the text C ABI's host side (include/jieyu.h, jieyu_b200/csrc/text.cpp).
+Its tokenizer gives the same ids and bytes as the restatement that is pinned
+to the reference's own tokenizer (tokenizer_host tests), and as the reference
+itself when oracle/_ref is built; model-directory problems are rejected
+before any device work with the reference's error behaviour (NULL handle,
+the reason in jieyu_last_error(NULL)); NULL handles and paths give -1."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from jieyu_b200 import _capi, bfile
+from jieyu_b200 import tokenizer as T
+from jieyu_b200.model import HostWeights
+from jieyu_b200.text import write_byte_level_vocab
+from oracle.bind import REF_SO
+from test_tokenizer_host import CORPUS, TEXTS, _train, _write
+
+
+def _enc(lib, h, data: bytes):
+    n = lib.jyt_tok_encode(h, data, len(data), None, 0)
+    out = np.zeros(max(n, 1), np.int32)
+    assert lib.jyt_tok_encode(h, data, len(data), out.ctypes.data, n) == n
+    return [int(x) for x in out[:n]]
+
+
+def _dec(lib, h, ids):
+    a = np.asarray(ids, np.int32)
+    n = lib.jyt_tok_decode(h, a.ctypes.data, len(a), None, 0)
+    buf = C.create_string_buffer(max(n, 1))
+    assert lib.jyt_tok_decode(h, a.ctypes.data, len(a), buf, n) == n
+    return buf.raw[:n]
+
+
+@pytest.mark.parametrize("word_end", [True, False])
+def test_native_tokenizer_matches_restatement(tmp_path, word_end):
+    lib = _capi.load()
+    vocab, merges = _train(CORPUS, 400, word_end)
+    vp, mp = _write(str(tmp_path), vocab, merges, extra=["<|im_end|>"])
+    h = lib.jyt_tok_load(vp.encode(), mp.encode())
+    assert h
+    try:
+        tok = T.Tokenizer()
+        assert tok.load(vp, mp)
+        info = np.zeros(6, np.int32)
+        assert lib.jyt_tok_info(h, info.ctypes.data) == 0
+        assert [int(x) for x in info] == [tok.vocab_size, tok.bos_id, tok.eos_id, tok.unk_id, tok.word_end_id,
+                                          len(tok.merge_result)]
+        rng = np.random.default_rng(11)
+        pool = [t if isinstance(t, bytes) else t.encode() for t in TEXTS]
+        fuzz = [bytes(rng.integers(0, 256, size=int(rng.integers(1, 40)), dtype=np.uint8)) for _ in range(150)]
+        mixed = [b"".join(pool[int(i)][: int(rng.integers(0, 20))] for i in rng.integers(0, len(pool), 4))
+                 for _ in range(100)]
+        for data in pool + fuzz + mixed:
+            ids = _enc(lib, h, data)
+            assert ids == tok.encode(data), data
+            assert _dec(lib, h, ids) == tok.decode(ids), data
+        assert lib.jyt_tok_add_special(h, b"<|im_end|>", 10) == tok.add_special_token(b"<|im_end|>") >= 0
+        assert lib.jyt_tok_add_special(h, b"<|absent|>", 10) == -1
+        for data in [b"chat<|im_end|>next", b"<|im_end|><|im_end|>", b"a <|im_end|> b"]:
+            assert _enc(lib, h, data) == tok.encode(data)
+        # ids outside the vocabulary decode to nothing
+        assert _dec(lib, h, [-5, 10 ** 8]) == b""
+    finally:
+        lib.jyt_tok_free(h)
+    assert not lib.jyt_tok_load(str(tmp_path / "missing.json").encode(), mp.encode())
+
+
+def test_native_tokenizer_matches_reference(tmp_path):
+    if not os.path.exists(REF_SO):
+        pytest.skip("reference harness not built (reference tree absent)")
+    ref = C.CDLL(REF_SO)
+    P = C.c_void_p
+    ref.jyref_tok_load.restype = P
+    ref.jyref_tok_load.argtypes = [C.c_char_p, C.c_char_p]
+    ref.jyref_tok_free.argtypes = [P]
+    ref.jyref_tok_encode.restype = C.c_int
+    ref.jyref_tok_encode.argtypes = [P, C.c_char_p, C.c_int, P, C.c_int]
+    lib = _capi.load()
+    vocab, merges = _train(CORPUS, 300, True)
+    vp, mp = _write(str(tmp_path), vocab, merges)
+    hr = ref.jyref_tok_load(vp.encode(), mp.encode())
+    h = lib.jyt_tok_load(vp.encode(), mp.encode())
+    try:
+        for text in TEXTS:
+            data = text if isinstance(text, bytes) else text.encode()
+            out = np.zeros(4 * len(data) + 16, np.int32)
+            n = ref.jyref_tok_encode(hr, data, len(data), out.ctypes.data, len(out))
+            assert _enc(lib, h, data) == [int(x) for x in out[:n]], data
+    finally:
+        ref.jyref_tok_free(hr)
+        lib.jyt_tok_free(h)
+
+
+def test_byte_level_vocabulary_ids(tmp_path):
+    lib = _capi.load()
+    write_byte_level_vocab(str(tmp_path / "v.json"), str(tmp_path / "m.txt"))
+    h = lib.jyt_tok_load(str(tmp_path / "v.json").encode(), str(tmp_path / "m.txt").encode())
+    try:
+        data = bytes(range(256))
+        tok = T.Tokenizer()
+        assert tok.load(str(tmp_path / "v.json"), str(tmp_path / "m.txt"))
+        assert _enc(lib, h, data) == tok.encode(data)
+        assert _dec(lib, h, list(range(256))) == data
+    finally:
+        lib.jyt_tok_free(h)
+
+
+def _model_dir(tmp_path, drop=None, reshape=None):
+    hw = HostWeights.shift_demo_kat()
+    d = str(tmp_path)
+    bfile.save_model_dir(hw, d)
+    header, ts = bfile.model_dir_tensors(hw)
+    if drop or reshape:
+        out = []
+        for name, dt, shape, data in ts:
+            if name == drop:
+                continue
+            if name == reshape:
+                shape = tuple(reversed(shape))
+            out.append((name, dt, shape, data))
+        bfile.write_bfile(os.path.join(d, "model.bf"), header, out)
+    write_byte_level_vocab(os.path.join(d, "vocab.json"), os.path.join(d, "merges.txt"))
+    return d
+
+
+@pytest.mark.parametrize("case", ["no_dir", "missing", "shape", "no_vocab"])
+def test_load_rejects_bad_directories(tmp_path, case):
+    """Each case fails before the device upload, with the same rejection the
+    restatement (bfile.load_model_dir / load_tokenizer) gives."""
+    lib = _capi.load()
+    if case == "no_dir":
+        d, want = str(tmp_path / "absent"), b"model.bf"
+    elif case == "missing":
+        d, want = _model_dir(tmp_path, drop="model.layers.1.mlp.up_proj.weight"), b"missing tensor"
+    elif case == "shape":
+        d, want = _model_dir(tmp_path, reshape="model.layers.0.self_attn.k_proj.weight"), b"shape"
+    else:
+        d = _model_dir(tmp_path)
+        os.remove(os.path.join(d, "vocab.json"))
+        want = None  # the device upload comes first; on a CPU host it is what fails
+    if case != "no_vocab":
+        with pytest.raises((bfile.BFileError, OSError, ValueError)):
+            bfile.load_model_dir(d)
+    h = lib.jieyu_load(d.encode(), 0)
+    assert not h
+    err = lib.jieyu_last_error(None)
+    assert err
+    if want is not None:
+        assert want in err, err
+
+
+def test_null_arguments_and_version():
+    lib = _capi.load()
+    assert lib.jieyu_version() == b"1.0.0"
+    assert lib.jieyu_context_length(None) == 0
+    assert lib.jieyu_model_dir(None) == b""
+    assert not lib.jieyu_load(None, 0)
+    assert lib.jieyu_last_error(None) == b"dir is NULL"
+    assert lib.jieyu_generate(None, b"x", None, 0, 4, 0.0, 1.0) == -1
+    assert lib.jieyu_last_error(None) == b"handle is NULL"
+    assert lib.jieyu_generate_jsonl(None, b"x.jsonl", b"", b"", None, 0, 4, 0.0, 1.0) == -1
+    lib.jieyu_free(None)
+    assert lib.jyt_tok_encode(None, b"x", 1, None, 0) == -1
