@@ -163,3 +163,34 @@ def test_null_arguments_and_version():
     assert lib.jieyu_generate_jsonl(None, b"x.jsonl", b"", b"", None, 0, 4, 0.0, 1.0) == -1
     lib.jieyu_free(None)
     assert lib.jyt_tok_encode(None, b"x", 1, None, 0) == -1
+
+
+def test_header_builds_as_c_and_cpp(tmp_path):
+    """include/jieyu.h compiles as C and as C++ (with the RAII wrapper), and a
+    program links against the library: a failed load throws jieyu::error
+    carrying the load error."""
+    import shutil
+    import subprocess
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if not shutil.which("gcc") or not shutil.which("g++"):
+        pytest.skip("no host compiler")
+    inc, libdir = os.path.join(root, "include"), os.path.join(root, "jieyu_b200")
+    c_src = tmp_path / "t.c"
+    c_src.write_text('#include "jieyu.h"\n#include <stdio.h>\nint main(void){jieyu_model h=jieyu_load("/nonexistent",0);'
+                     'printf("%d %s %s\\n",h==0,jieyu_last_error(0),jieyu_version());return 0;}\n')
+    cpp_src = tmp_path / "t.cpp"
+    cpp_src.write_text('#include "jieyu.h"\n#include <cstdio>\nint main(){try{jieyu m("/nonexistent");return 1;}'
+                       'catch(const jieyu::error& e){std::printf("%s\\n",e.what());}'
+                       'jieyu none; try{none.generate("x");}catch(const jieyu::error&){std::printf("closed\\n");}'
+                       'return jieyu::version()=="1.0.0"?0:2;}\n')
+    outs = []
+    for cc, src, std in (("gcc", c_src, "-std=c99"), ("g++", cpp_src, "-std=c++17")):
+        exe = str(tmp_path / (src.name + ".out"))
+        subprocess.run([cc, std, "-I", inc, str(src), "-o", exe, "-L", libdir, "-ljieyu_b200",
+                        f"-Wl,-rpath,{libdir}"], check=True, capture_output=True)
+        r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+        assert r.returncode == 0, r.stderr
+        outs.append(r.stdout)
+    assert outs[0].startswith("1 /nonexistent/model.bf: cannot open 1.0.0")
+    assert "load failed: /nonexistent/model.bf: cannot open" in outs[1] and "closed" in outs[1]
