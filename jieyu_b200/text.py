@@ -155,3 +155,90 @@ def generate_text(tok: Tokenizer, prompt, vocab: int, max_seq: int, add_bos: boo
     seq = gen(ids, max_new, eos=eos or None, temperature=temperature, repetition_penalty=repetition_penalty,
               cb=on_token)
     return len(seq) - len(ids), bytes(out)
+
+
+class JieyuError(RuntimeError):
+    """jieyu::error (JieyuAI_api.h:76-79)."""
+
+
+class Jieyu:
+    """The reference's `class jieyu` (JieyuAI_api.h:74-142) over the text C
+    ABI of libjieyu_b200.so (include/jieyu.h): one model per process shared
+    by every open handle, text handling in C++, token steps on the GPU."""
+
+    def __init__(self, path: Optional[str] = None, max_seq: int = 0):
+        from . import _capi
+
+        self._lib = _capi.load()
+        self._h = None
+        if path is not None:
+            self.open(path, max_seq)
+
+    def open(self, path: str, max_seq: int = 0) -> None:
+        self.close()
+        h = self._lib.jieyu_load(os.fsencode(path), max_seq)
+        if not h:
+            raise JieyuError("load failed: " + self._lib.jieyu_last_error(None).decode("utf-8", "replace"))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.jieyu_free(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def is_open(self) -> bool:
+        return bool(self._h)
+
+    def context_length(self) -> int:
+        return self._lib.jieyu_context_length(self._h) if self._h else 0
+
+    def dir(self) -> str:
+        return self._lib.jieyu_model_dir(self._h).decode("utf-8", "replace") if self._h else ""
+
+    def last_error(self) -> str:
+        return self._lib.jieyu_last_error(self._h).decode("utf-8", "replace")
+
+    @staticmethod
+    def version() -> str:
+        from . import _capi
+
+        return _capi.load().jieyu_version().decode()
+
+    def _buffer(self, max_new: int):
+        import ctypes
+
+        return ctypes.create_string_buffer((max_new if max_new > 0 else 4096) * 16 + 256)
+
+    def generate(self, prompt, max_new: int = 256, temperature: float = 0.7,
+                 repetition_penalty: float = 1.1) -> bytes:
+        """The generated text (bytes: the model's output need not be valid
+        UTF-8); raises JieyuError when jieyu_generate returns -1."""
+        if not self._h:
+            raise JieyuError("no model loaded (call open first)")
+        p = prompt.encode("utf-8") if isinstance(prompt, str) else bytes(prompt)
+        buf = self._buffer(max_new)
+        if self._lib.jieyu_generate(self._h, p, buf, len(buf), max_new, temperature, repetition_penalty) < 0:
+            raise JieyuError(self.last_error())
+        return buf.value
+
+    def generate_jsonl(self, jsonl: str, qb: str = "", qe: str = "", max_new: int = 256,
+                       temperature: float = 0.7, repetition_penalty: float = 1.1) -> bytes:
+        if not self._h:
+            raise JieyuError("no model loaded (call open first)")
+        buf = self._buffer(max_new)
+        if self._lib.jieyu_generate_jsonl(self._h, os.fsencode(jsonl), qb.encode(), qe.encode(), buf, len(buf),
+                                          max_new, temperature, repetition_penalty) < 0:
+            raise JieyuError(self.last_error())
+        return buf.value

@@ -80,3 +80,14 @@ def test_text_c_abi_check_pipeline(cuda, tmp_path):
         assert b"jsonl_no_srch" in lib.jieyu_last_error(h)
     finally:
         lib.jieyu_free(h)
+
+
+def test_python_wrapper(cuda, tmp_path):
+    from jieyu_b200.text import Jieyu
+
+    d = _shift_dir(tmp_path)
+    with Jieyu(d) as j:
+        assert j.context_length() == 1024 and j.dir() == d
+        assert j.generate("abcdefgh", max_new=16, temperature=0.0, repetition_penalty=1.0) == b"ijklmnopqrstuvwx"
+        assert j.last_error() == ""
+    assert not j.is_open()

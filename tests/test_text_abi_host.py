@@ -194,3 +194,16 @@ def test_header_builds_as_c_and_cpp(tmp_path):
         outs.append(r.stdout)
     assert outs[0].startswith("1 /nonexistent/model.bf: cannot open 1.0.0")
     assert "load failed: /nonexistent/model.bf: cannot open" in outs[1] and "closed" in outs[1]
+
+
+def test_python_wrapper_errors(tmp_path):
+    from jieyu_b200.text import Jieyu, JieyuError
+
+    assert Jieyu.version() == "1.0.0"
+    j = Jieyu()
+    assert not j.is_open() and j.context_length() == 0 and j.dir() == ""
+    with pytest.raises(JieyuError, match="no model loaded"):
+        j.generate("x")
+    with pytest.raises(JieyuError, match="cannot open"):
+        j.open(str(tmp_path / "absent"))
+    assert not j.is_open()
