@@ -78,6 +78,12 @@ JIEYU_API int jyt_tok_decode(const jyt_tokenizer* t, const int* ids, int n, char
 JIEYU_API int jyt_tok_add_special(jyt_tokenizer* t, const char* piece, int len);
 /* vocab_size, bos, eos, unk, "</w>" id (-1 if absent), merge count */
 JIEYU_API int jyt_tok_info(const jyt_tokenizer* t, int* out6);
+/* jieyu_load's directory binding without the device upload: 0 and
+ * out13 = {layers, hidden, heads, kv heads, head dim, intermediate, vocab,
+ * max_seq, QKV bias, tied head, bit mask of the layer weights' model.bf
+ * dtypes, rope_theta, (head block-quantised) | 2 * (embedding
+ * block-quantised)}, or -1 and the reason in err (cap bytes with NUL). */
+JIEYU_API int jyt_model_dir_probe(const char* dir, int max_seq, int* out13, char* err, int cap);
 
 #ifdef __cplusplus
 }

@@ -143,6 +143,7 @@ SIGNATURES = [
     ("jyt_tok_decode", _I, [_P, _P, _I, _P, _I]),
     ("jyt_tok_add_special", _I, [_P, C.c_char_p, _I]),
     ("jyt_tok_info", _I, [_P, _P]),
+    ("jyt_model_dir_probe", _I, [C.c_char_p, _I, _P, _P, _I]),
 ]
 
 _lib = None

@@ -671,9 +671,20 @@ std::string shape_str(const std::vector<uint64_t>& s) {
     return o + "]";
 }
 
-// The device model of a model directory; throws with the reason on failure.
-jyc_model* bind_model_dir(const std::string& dir, int max_seq, int* vocab_out) {
+// A model directory bound to a device-model descriptor whose pointers
+// reach into the mapped file; throws with the reason on failure.
+struct BoundDir {
     BFile bf;
+    std::vector<jyc_layer_weights> lw;
+    std::vector<float> cos_t, sin_t;
+    jyc_model_desc d{};
+    bool bias = false, tied = false;
+    unsigned kinds = 0;  // bit per bfile dtype of the layer weights
+    int theta = 0;
+};
+
+void bind_dir(const std::string& dir, int max_seq, BoundDir& b) {
+    BFile& bf = b.bf;
     bf.open(dir + "/model.bf");
     const int L = (int)bf.layers, D = (int)bf.hidden, H = bf.heads, KV = bf.kv_heads, hd = bf.head_dim;
     const int F = (int)bf.inter, V = (int)bf.vocab;
@@ -712,8 +723,9 @@ jyc_model* bind_model_dir(const std::string& dir, int max_seq, int* vocab_out) {
         return reinterpret_cast<const float*>(t.data);
     };
     auto lname = [](int l, const char* s) { return "model.layers." + std::to_string(l) + "." + s; };
-    std::vector<jyc_layer_weights> lw((size_t)L);
-    const bool bias = bf.get(lname(0, "self_attn.q_proj.bias")) != nullptr;  // bind_biases: layer 0 decides
+    std::vector<jyc_layer_weights>& lw = b.lw;
+    lw.resize((size_t)L);
+    const bool bias = b.bias = bf.get(lname(0, "self_attn.q_proj.bias")) != nullptr;  // bind_biases: layer 0 decides
     for (int l = 0; l < L; ++l) {
         jyc_layer_weights& w = lw[(size_t)l];
         w.rms1_weight = f32(lname(l, "input_layernorm.weight"), D);
@@ -752,6 +764,7 @@ jyc_model* bind_model_dir(const std::string& dir, int max_seq, int* vocab_out) {
     const BTensor* head = bf.get("lm_head.weight");
     const char* head_name = "lm_head.weight";
     if (!head) {  // bind_lm_head's fallback (load_weights.h:142-144)
+        b.tied = true;
         head = &emb;
         head_name = "model.embed_tokens.weight";
     }
@@ -770,12 +783,17 @@ jyc_model* bind_model_dir(const std::string& dir, int max_seq, int* vocab_out) {
     if (!read_json(dir + "/model_info.json", info)) throw std::runtime_error(dir + "/model_info.json: missing or not JSON");
     if (max_seq <= 0)
         max_seq = std::max(64, std::min(stoi_or(info_text(info, "max_position_embeddings"), 1024), 4096));
-    const float theta = (float)stoi_or(info_text(info, "rope_theta"), 10000);
-    std::vector<float> cos_t((size_t)max_seq * (hd / 2)), sin_t(cos_t.size());
+    b.theta = stoi_or(info_text(info, "rope_theta"), 10000);
+    const float theta = (float)b.theta;
+    std::vector<float>& cos_t = b.cos_t;
+    std::vector<float>& sin_t = b.sin_t;
+    cos_t.assign((size_t)max_seq * (hd / 2), 0.f);
+    sin_t.assign(cos_t.size(), 0.f);
     if (jyc_rope_table(max_seq, hd, theta, cos_t.data(), sin_t.data()) != JYC_OK)
         throw std::runtime_error(std::string("RoPE table: ") + jyc_last_error());
 
-    jyc_model_desc d{};
+    for (int k : kinds) b.kinds |= 1u << k;
+    jyc_model_desc& d = b.d;
     d.layers = lw.data();
     d.num_layers = L;
     d.embed = embed;
@@ -790,9 +808,16 @@ jyc_model* bind_model_dir(const std::string& dir, int max_seq, int* vocab_out) {
     d.num_kv_heads = KV;
     d.head_dim = hd;
     d.intermediate = F;
-    jyc_model* m = jyc_model_create(&d);  // uploads every weight; the mapping can go after this
+}
+
+// The device model of a model directory (every weight uploaded; the file
+// mapping is released on return).
+jyc_model* bind_model_dir(const std::string& dir, int max_seq, int* vocab_out) {
+    BoundDir b;
+    bind_dir(dir, max_seq, b);
+    jyc_model* m = jyc_model_create(&b.d);
     if (!m) throw std::runtime_error(std::string("device upload failed: ") + jyc_last_error());
-    *vocab_out = V;
+    *vocab_out = b.d.vocab_size;
     return m;
 }
 
@@ -1116,6 +1141,24 @@ JIEYU_API int jyt_tok_decode(const jyt_tokenizer* t, const int* ids, int n, char
 JIEYU_API int jyt_tok_add_special(jyt_tokenizer* t, const char* piece, int len) {
     if (!t || !piece || len < 0) return -1;
     return t->add_special(std::string(piece, (size_t)len));
+}
+
+JIEYU_API int jyt_model_dir_probe(const char* dir, int max_seq, int* out13, char* err, int cap) {
+    if (!dir || !out13) return -1;
+    try {
+        BoundDir b;
+        bind_dir(dir, max_seq, b);
+        const jyc_model_desc& d = b.d;
+        const int v[13] = {d.num_layers, d.hidden, d.num_heads, d.num_kv_heads, d.head_dim, d.intermediate,
+                           d.vocab_size, d.max_seq, b.bias, b.tied, (int)b.kinds, b.theta,
+                           (d.lm_head.q ? 1 : 0) | (d.embed.q ? 2 : 0)};
+        memcpy(out13, v, sizeof v);
+        if (err && cap > 0) err[0] = '\0';
+        return 0;
+    } catch (const std::exception& e) {
+        if (err && cap > 0) set_text(err, (size_t)cap, e.what());
+        return -1;
+    }
 }
 
 JIEYU_API int jyt_tok_info(const jyt_tokenizer* t, int* out6) {

@@ -207,3 +207,78 @@ def test_python_wrapper_errors(tmp_path):
     with pytest.raises(JieyuError, match="cannot open"):
         j.open(str(tmp_path / "absent"))
     assert not j.is_open()
+
+
+def _probe(lib, d, max_seq=0):
+    out = np.zeros(13, np.int32)
+    err = C.create_string_buffer(256)
+    r = lib.jyt_model_dir_probe(d.encode(), max_seq, out.ctypes.data, err, 256)
+    return r, [int(x) for x in out], err.value.decode()
+
+
+def _bfile_models():
+    from test_bfile_host import _models
+    return _models()
+
+
+@pytest.mark.parametrize("model", ["bind_kat", "q8_tied_bias", "q8_separate", "f32_rect", "kquant_mixed"])
+def test_native_binding_matches_restatement(tmp_path, model):
+    """jieyu_load's binding (without the device upload) reads every model
+    directory the restatement reads, with the same hyper-parameters, bias,
+    tied head, weight formats and RoPE base."""
+    lib = _capi.load()
+    hw = _bfile_models()[model]
+    d = str(tmp_path)
+    bfile.save_model_dir(hw, d)
+    got = bfile.load_model_dir(d)
+    c = got.cfg
+    r, v, err = _probe(lib, d)
+    assert r == 0, err
+    kinds = {bfile.Q8_0} if c.wtype == "q8" else None
+    assert v[:8] == [c.layers, c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab, c.max_seq]
+    assert v[8] == int(c.qkv_bias) and v[9] == int(c.embed == "tied") and v[11] == int(c.theta)
+    if kinds:
+        assert v[10] == 1 << bfile.Q8_0
+    elif c.wtype == "f32":
+        assert v[10] == 1 << bfile.F32
+    else:
+        assert v[10] & ~((1 << bfile.F32) | (1 << bfile.Q4K) | (1 << bfile.Q5K) | (1 << bfile.Q6K)) == 0
+    assert (v[12] & 1) == int(got.t["head"].dtype == np.uint8)
+    r2, v2, _ = _probe(lib, d, 77)
+    assert r2 == 0 and v2[7] == 77
+
+
+def test_native_binding_rejects_what_the_restatement_rejects(tmp_path):
+    from test_bfile_host import CORRUPT, _save
+
+    lib = _capi.load()
+    hw = _bfile_models()["q8_tied_bias"]
+    for how, corrupt in CORRUPT.items():
+        d = tmp_path / how
+        d.mkdir()
+        path = _save(hw, d)
+        corrupt(path, os.path.getsize(path))
+        with pytest.raises(bfile.BFileError):
+            bfile.load_model_dir(str(d))
+        r, _, err = _probe(lib, str(d))
+        assert r == -1 and err, how
+
+
+@pytest.mark.parametrize("info,want", [({"max_position_embeddings": "100000"}, 4096),
+                                       ({"max_position_embeddings": 10}, 64),
+                                       ({"max_position_embeddings": "2048"}, 2048), ({}, 1024),
+                                       ({"max_position_embeddings": 3900.5}, 3900),
+                                       ({"max_position_embeddings": "4e3"}, 64),
+                                       ({"max_position_embeddings": " 300x"}, 300),
+                                       ({"max_position_embeddings": True}, 1024)])
+def test_max_seq_rule_native_and_restatement(tmp_path, info, want):
+    import json
+
+    lib = _capi.load()
+    hw = _bfile_models()["f32_rect"]
+    bfile.save_model_dir(hw, str(tmp_path))
+    with open(tmp_path / "model_info.json", "w") as f:
+        json.dump(info, f)
+    assert bfile.load_model_dir(str(tmp_path)).cfg.max_seq == want
+    r, v, err = _probe(lib, str(tmp_path))
+    assert r == 0 and v[7] == want, err
