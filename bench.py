@@ -1,19 +1,26 @@
 #!/usr/bin/env python
 """Benchmark of the B200 decode path (driver contract: one JSON line on rank 0).
 
-Workload (Qwen2.5-0.5B shape, synthetic seeded Q8_0
-weights): a 512-token prompt is prefilled once; one bench step = 256 greedy
-batch-1 decode tokens from that context (positions 513..768), every weight
-streamed from HBM (525 MB of weights per token > 126 MB L2). Metric: decode
-tokens/s (device-timed with CUDA events), plus achieved HBM GB/s vs the
-measured peak, prefill tokens/s, the end-to-end number through the C ABI with
-host buffers, and the reference's own CPU path timed on this host.
+Headline workload (default): BASELINE.json configs[3], the Llama-3-8B shape
+with synthetic seeded Q8_0 weights (7.98 GB per token, far above the 126 MB
+L2): a 4096-token random prompt is prefilled, then one bench step = rewind to
+that context and decode 64 greedy batch-1 tokens (positions 4097..4160).
+Metric: decode tokens/s (CUDA events on the launching stream, max over
+ranks), with the decode kernel's HBM roofline, the 4096-token prefill tok/s,
+the end-to-end numbers through the public calls with host buffers, and the
+reference's own CPU decode at the same context timed on this host.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-N > 1 (torchrun): independent replicas, one per GPU (the batch-1 decode of
-configs[1] does not shard; no collective on the data path), value = all
-tokens / max-over-ranks time, "scaling": "weak".
+N > 1 (torchrun): tensor parallel over the N ranks (QKV / gate-up column
+split, O / down row split, the decode kernel's own NVLink exchange of the
+partial sums; prefill with NCCL all-reduces), value = tokens / max-over-ranks
+time, "scaling": "strong"; rank 0 also checks its tokens against the whole
+model on one GPU. --impl reference times the reference (oracle/_ref) on the
+host cores, on rank 0 only.
+
+Other workloads (not the driver's line): --workload c1 (configs[1] decode),
+c4 (configs[4] batched decode sweep), prefill (--model c1/c2/c3), kquant.
 """
 import argparse
 import ctypes as C
@@ -29,8 +36,14 @@ sys.path.insert(0, ROOT)
 
 METRIC = "batch-1 decode tok/s"
 UNIT = "tok/s"
-PROMPT = 512
+PROMPT = 512            # --workload c1: prompt and decode tokens per step
 DECODE = 256
+HEAD_CFG = "c3"         # the headline: configs[3] at context CTX
+CTX = 4096
+HEAD_MAX_SEQ = 4352
+DECODE_C3 = 64          # decode tokens per step of the headline
+E2E_NEW = 128           # new tokens of one end-to-end call
+REF_TOKENS_PER_STEP = 2  # reference arm: decode tokens of its bounded sample per step
 KCLASSES = ["embed", "qkv_gemv", "rope_quant", "attention", "o_proj_gemv", "gate_up_gemv",
             "down_gemv", "lm_head_gemv_argmax"]
 
@@ -118,42 +131,91 @@ def reference_decode_sample(hw, threads, new_tokens=16, prompt_len=16, reps=2):
     return dec_tok / dec_s, (reps * new_tokens) / tot_s, ref.lib.jyref_threads()
 
 
+class RefContextDecode:
+    """The reference's decode at context CTX, timed on this host's cores:
+    oracle/_ref (the jieyu headers compiled unmodified) runs generate_cached's
+    step body (embedding row, forward_cached, LM head, greedy pick;
+    generate.h:40-60) from a KV cache holding a seeded context of `ctx`
+    positions (oracle.synth.context_kv), i.e. the decode work of position
+    ctx, ctx + 1, ... without the CPU prefill of the prompt (hours at the
+    8B shape on the scalar m>1 path). `desc` is any jyc_model_desc-layout
+    ctypes structure over host weights."""
+
+    def __init__(self, desc, layers, kv_heads, head_dim, max_seq, ctx, threads):
+        from oracle import synth
+        from oracle.bind import Reference
+        self.ref = Reference("fma", threads)
+        self.desc, self.ctx = desc, ctx
+        self.cache = self.ref.cache_create(layers, max_seq, kv_heads, head_dim)
+        for l, k, ks, v, vs in synth.context_kv(layers, ctx, kv_heads, head_dim):
+            self.ref.cache_write(self.cache, l, ctx, k.ctypes.data, ks.ctypes.data, v.ctypes.data, vs.ctypes.data)
+        self.cores = self.ref.lib.jyref_threads()
+
+    def run(self, n: int):
+        """n greedy decode tokens from position ctx; returns seconds per token."""
+        _, t = self.ref.decode_steps(self.desc, self.cache, self.ctx, 1, n)
+        return t
+
+    def close(self):
+        if self.cache:
+            self.ref.cache_free(self.cache)
+            self.cache = None
+
+
+def head_config():
+    """The headline's config keys (shared by both arms)."""
+    return {"workload": f"configs[3] Llama-3-8B shape (Q8_0 weights N(0, 0.02), seeded): batch-1 greedy decode "
+                        f"at context {CTX} ({DECODE_C3} tokens per step after a {CTX}-token random prompt)",
+            "model": "c3_llama3_8b", "global_batch": 1, "seq_len": CTX + 1 + DECODE_C3,
+            "l2": "inputs larger than L2 (7.98 GB of weights per token / N ranks vs 126 MB L2)"}
+
+
 def run_reference_arm(args):
+    """The reference arm: the reference's own CPU decode (oracle/_ref) of the
+    headline workload (configs[3] shape, Q8_0, context 4096) on this host's
+    cores, a bounded sample per step (REF_TOKENS_PER_STEP decode tokens).
+    The seeded weights come from liboracle.so's generator (oracle.synth),
+    byte-identical to the GPU arm's: the product library is not loaded."""
     rank = env_int("RANK", 0)
     if rank != 0:
         return 0
-    from jieyu_b200.model import CONFIGS, HostWeights
-    cfg = CONFIGS["c1"]
-    hw = HostWeights.synthetic(cfg)
+    from oracle import synth
+    from oracle.bind import reference_available
+    if not reference_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libjyref.so was not built"}))
+        return 0
+    shape = synth.SHAPES[HEAD_CFG]
     threads = os.cpu_count() or 1
+    sm = synth.SynthModel(shape, HEAD_MAX_SEQ)
+    rd = RefContextDecode(sm.desc, shape.layers, shape.kv_heads, shape.head_dim, HEAD_MAX_SEQ, CTX, threads)
     for _ in range(args.warmup):
-        reference_decode_sample(hw, threads, new_tokens=8, prompt_len=16, reps=1)
-    vals, e2es = [], []
+        rd.run(1)
+    toks, secs = 0, 0.0
     t0 = time.time()
     for _ in range(args.steps):
-        v, e, cores = reference_decode_sample(hw, threads, new_tokens=8, prompt_len=16, reps=1)
-        vals.append(v)
-        e2es.append(e)
+        t = rd.run(REF_TOKENS_PER_STEP)
+        toks += len(t)
+        secs += float(t.sum())
     wall = time.time() - t0
-    value = statistics.mean(vals)
-    sample = ("jieyu reference generate() (oracle/_ref, unmodified headers, JIEYU_ISA=fma, OpenMP) "
-              "on configs[1] weights: 16-token prompt + 8 greedy tokens per step; value = decode "
-              "tokens/s (first->last token, as -tokenspeed)")
+    value = toks / secs
+    rd.close()
+    sample = (f"jieyu reference (oracle/_ref: the unmodified headers, JIEYU_ISA=fma, OpenMP, {rd.cores} threads) "
+              f"decoding configs[3]-shaped seeded Q8_0 weights at context {CTX} (a seeded int8 K/V context "
+              f"written into its __KVcache; generate_cached's step body per token), {REF_TOKENS_PER_STEP} "
+              f"tokens per step; value = decode tokens / their seconds")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "configs[1] qwen2.5-0.5b shape, CPU sample",
-                                        "parallelism": "host threads"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference",
-                         "sample": sample},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": dict(head_config(), parallelism="host threads"),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": rd.cores, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_b200(args):
+def run_c1(args):
     import numpy as np
     import torch
 
@@ -336,21 +398,45 @@ def run_b200(args):
     return 0
 
 
-def run_tp(args):
-    """configs[3] (Llama-3-8B shape) batch-1 decode at context 4096,
-    tensor-parallel over the launched ranks (jieyu_b200.tp); N=1 runs the
-    whole model with the single-launch decode kernel. Not the driver's
-    headline line: `python bench.py --workload c3-tp` (under torchrun for N>1)."""
+def traffic_capture(kernel_src: str, key: str):
+    """DRAM bytes per launch of the decode kernel from a stored ncu capture
+    (profiles/traffic_decode.json), used only while the kernel source it was
+    taken on is unchanged (sha256 of mega.cu); else None."""
+    import hashlib
+    path = os.path.join(ROOT, "profiles", "traffic_decode.json")
+    if not os.path.exists(path):
+        return None, "no stored capture"
+    with open(path) as f:
+        d = json.load(f)
+    with open(kernel_src, "rb") as f:
+        sha = hashlib.sha256(f.read()).hexdigest()[:16]
+    e = d.get(key)
+    if not e:
+        return None, f"no stored capture for {key}"
+    if e.get("mega_cu_sha16") != sha:
+        return None, f"stored capture is of another kernel source ({e.get('mega_cu_sha16')} != {sha})"
+    return float(e["bytes_per_launch"]), e.get("how", "")
+
+
+def run_headline(args):
+    """The headline line: configs[3] (Llama-3-8B shape, Q8_0) batch-1 greedy
+    decode at context 4096. One step = rewind to the 4096-token prompt + its
+    first token and decode DECODE_C3 tokens (positions 4097..). N = 1: the
+    whole model on one GPU, one decode-kernel launch per token. N > 1
+    (torchrun): tensor parallel over the N ranks (jieyu_b200.tp.TPDecoder,
+    the kernel's own NVLink exchange of the O / down partials), value = tokens
+    / max-over-ranks time ("scaling": "strong": the same model whatever N).
+    The same line carries the 4096-token prefill (tensor parallel at N > 1),
+    the end-to-end numbers through the public calls with host buffers, the
+    roofline of the decode kernel and, at N > 1, a check of rank 0's tokens
+    against the whole model on one GPU."""
     import numpy as np
     import torch
 
     from jieyu_b200 import _capi
-    from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids
-    from jieyu_b200.tp import TPDecoder
+    from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids, with_max_seq
 
-    world = env_int("WORLD_SIZE", 1)
-    rank = env_int("RANK", 0)
-    local = env_int("LOCAL_RANK", 0)
+    world, rank, local = env_int("WORLD_SIZE", 1), env_int("RANK", 0), env_int("LOCAL_RANK", 0)
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -359,83 +445,207 @@ def run_tp(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    cfg = CONFIGS["c3"]
-    ctx = 4096
-    new = 64
-    hw = HostWeights.synthetic(cfg)
-    prompt = prompt_ids(cfg, n=ctx)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     lib = _capi.load()
+    cfg = with_max_seq(CONFIGS[HEAD_CFG], HEAD_MAX_SEQ)
+    hw = HostWeights.synthetic(cfg)
+    prompt = prompt_ids(cfg, n=CTX)
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     if world == 1:
         m = DeviceModel(hw)
-        stream = torch.cuda.Stream()
-        s = stream.cuda_stream
-        ids = torch.from_numpy(prompt).cuda()
-        with torch.cuda.stream(stream):
-            m.prefill_device(ids.data_ptr(), ctx, s)
-            def step():
-                m.rewind(ctx + 1, s)
-                m.decode_device(new, s)
-            for _ in range(args.warmup):
-                step()
-            e0, e1 = ev(), ev()
-            e0.record(stream)
-            for _ in range(args.steps):
-                step()
-            e1.record(stream)
-            stream.synchronize()
-        ms = e0.elapsed_time(e1)
-        graphed = True
-        close = m.close
         h = m.h
-    else:
-        tp = TPDecoder(hw, rank, world, mode=args.tp_mode)
-        graphed = tp.capture()
-        tp.prefill_by_steps(prompt)
-        stream = tp.stream
-        s = stream.cuda_stream
+        stream = torch.cuda.Stream()
+        ids = torch.from_numpy(prompt).cuda()
+
+        def prefill():
+            m.prefill_device(ids.data_ptr(), CTX, stream.cuda_stream)
+
         def step():
-            _capi.check(lib.jyc_model_rewind(tp.m.h, ctx + 1, s))
-            tp.step(new)
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                step()
-            stream.synchronize()
-            dist.barrier()
-            e0, e1 = ev(), ev()
-            e0.record(stream)
-            for _ in range(args.steps):
-                step()
-            e1.record(stream)
-            stream.synchronize()
-        ms = e0.elapsed_time(e1)
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        close = tp.close
+            m.rewind(CTX + 1, stream.cuda_stream)
+            m.decode_device(DECODE_C3, stream.cuda_stream)
+        parallelism = "single GPU"
+    else:
+        from jieyu_b200.tp import TPDecoder
+        tp = TPDecoder(hw, rank, world, mode="kernel")
         h = tp.m.h
-    ms_tok = ms / (args.steps * new)
-    w_rank = float(lib.jyc_model_weight_bytes_per_token(h))
-    kv_rank = float(lib.jyc_model_kv_bytes_per_token(h, ctx + new // 2))
+        stream = tp.stream
+
+        def prefill():
+            tp.prefill(prompt)
+
+        def step():
+            _capi.check(lib.jyc_model_rewind(tp.m.h, CTX + 1, stream.cuda_stream))
+            tp.step(DECODE_C3)
+        parallelism = f"tp{world}"
+    s = stream.cuda_stream
+
+    # prefill of the 4096-token prompt (KV of positions 0..4095 stays resident)
+    with torch.cuda.stream(stream):
+        prefill()
+        stream.synchronize()
+        barrier()
+        pf_ms = []
+        for _ in range(2):
+            a, b = ev(), ev()
+            a.record(stream)
+            prefill()
+            b.record(stream)
+            stream.synchronize()
+            pf_ms.append(a.elapsed_time(b))
+        pf_ms = max_over_ranks(min(pf_ms))
+        first_tokens = None
+        for i in range(args.warmup):
+            step()
+            if i == 0:
+                stream.synchronize()
+                n_tok = CTX + 1 + DECODE_C3
+                dev_toks = torch.as_tensor(_DevBuf(lib.jyc_model_tokens_device(h), n_tok), device="cuda")
+                first_tokens = dev_toks[CTX:n_tok].cpu().numpy().copy()
+        stream.synchronize()
+        barrier()
+        sampler = ClockSampler(local)
+        sampler.start()
+        launches0 = lib.jyc_kernel_launches()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        stream.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        launches = lib.jyc_kernel_launches() - launches0
+        clocks = sampler.stop()
+    assert lib.jyc_device_error(1) == 0, "a bounded wait of the decode kernel gave up"
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    tokens = args.steps * DECODE_C3
+    value = tokens / (ms / 1e3)
+    ms_tok = ms / tokens
+
+    # roofline of the decode kernel (one launch per token): algorithmic bytes
+    # of one launch on this rank (its weights + the KV rows it reads at the
+    # mean context of a step) over the event-timed time per launch
     peak, peak_kind = measured_peaks()
-    gbs = (w_rank + kv_rank) / (ms_tok / 1e3) / 1e9
-    close()
+    w_rank = float(lib.jyc_model_weight_bytes_per_token(h))
+    kv_rank = float(lib.jyc_model_kv_bytes_per_token(h, CTX + 1 + DECODE_C3 // 2))
+    bytes_launch = w_rank + kv_rank
+    achieved = bytes_launch / (ms_tok / 1e3) / 1e9
+    traffic, traffic_note = traffic_capture(os.path.join(ROOT, "jieyu_b200", "csrc", "mega.cu"),
+                                            f"{HEAD_CFG}_tp{world}")
+
+    # end to end through the public calls with host buffers: the prompt from
+    # pinned host memory, the 4096-token prefill, DECODE_C3 new tokens read
+    # back to the host in blocks (jyc_generate with a token callback at N = 1,
+    # TPDecoder.generate at N > 1); decode tok/s first -> last token as the
+    # reference's -tokenspeed splits it (pipeline.h:356-367), and the whole call
+    e2e_n = E2E_NEW
+    stamps = []
+
+    def cb(tok):
+        stamps.append(time.perf_counter())
+        return False
+    pin_prompt = torch.from_numpy(prompt).pin_memory()
+    e2e_runs = []
+    for _ in range(2):
+        stamps.clear()
+        barrier()
+        t0 = time.perf_counter()
+        if world == 1:
+            got = m.generate(pin_prompt.numpy(), e2e_n, cb=cb)
+        else:
+            got = tp.generate(pin_prompt.numpy(), e2e_n, cb=cb)
+        t1 = time.perf_counter()
+        assert len(got) == CTX + e2e_n
+        e2e_runs.append((t1 - t0, stamps[0] - t0, stamps[-1] - stamps[0]))
+    whole, to_first, first_last = e2e_runs[-1]
+    whole = max_over_ranks(whole)
+    to_first = max_over_ranks(to_first)
+    first_last = max_over_ranks(first_last)
+    e2e_decode = (e2e_n - 1) / first_last
+
+    # N > 1: rank 0's tokens against the whole model on one GPU
+    tp_check = None
+    if world > 1:
+        tp.close()
+        barrier()
+        if rank == 0:
+            m1 = DeviceModel(hw)
+            one = m1.generate(prompt, DECODE_C3 + 1)[CTX:CTX + DECODE_C3 + 1]
+            same = int(np.argmax(one != first_tokens)) if not np.array_equal(one, first_tokens) else None
+            tp_check = {"tokens": int(DECODE_C3 + 1), "identical": same is None, "first_difference": same}
+            if same is not None:  # the top-2 gap of the whole model's logits at that step
+                lg = m1.forward_logits(np.array([one[same - 1] if same else prompt[-1]], np.int32),
+                                       CTX + same - 1)
+                top = np.sort(lg.astype(np.float64))[-2:]
+                tp_check["top2_gap_rel"] = float((top[1] - top[0]) / np.abs(lg).max())
+            m1.close()
+    else:
+        m.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rd = RefContextDecode(hw.desc, cfg.layers, cfg.kv_heads, cfg.head_dim, cfg.max_seq, CTX,
+                              os.cpu_count() or 1)
+        rd.run(1)
+        t = rd.run(REF_TOKENS_PER_STEP)
+        rd.close()
+        cpu = {"value": len(t) / float(t.sum()), "unit": UNIT, "cores": rd.cores, "kind": "reference",
+               "sample": f"jieyu reference (oracle/_ref, unmodified headers, JIEYU_ISA=fma) decoding "
+                         f"{REF_TOKENS_PER_STEP} tokens at context {CTX} on the same configs[3] weights "
+                         f"(seeded int8 K/V context in its __KVcache; generate_cached's step body)"}
     if dist is not None:
         dist.destroy_process_group()
     if rank != 0:
         return 0
     line = {
-        "metric": "batch-1 decode tok/s (configs[3], tensor parallel)", "value": 1e3 / ms_tok, "unit": "tok/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_token": ms_tok,
-        "higher_is_better": True, "scaling": "strong", "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"configs[3] Llama-3-8B shape, Q8_0, context {ctx}, {new} greedy tokens per step",
-                   "parallelism": f"tp{world}" if world > 1 else "single GPU", "graphed": graphed,
-                   "tp_mode": args.tp_mode if world > 1 else None},
-        "hbm_per_gpu": {"bytes_per_token": w_rank + kv_rank, "gbs": gbs, "frac_of_peak": gbs / peak,
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(head_config(), parallelism=parallelism),
+        "ms_per_token": ms_tok,
+        "hbm_per_gpu": {"bytes_per_token": bytes_launch, "gbs": achieved, "frac_of_peak": achieved / peak,
                         "peak_gbs": peak, "peak_kind": peak_kind},
+        "roofline": {"bound": "hbm", "kernel": "mega_step_kernel", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_note,
+                     "bytes_per_launch": bytes_launch, "launch_ms": ms_tok, "peak_kind": peak_kind},
+        "prefill": {"value": CTX / (pf_ms / 1e3), "unit": "tok/s", "prompt": CTX, "ms": pf_ms,
+                    "parallelism": parallelism},
+        "e2e": {"value": e2e_decode, "unit": UNIT, "h2d_bytes_per_step": CTX * 4,
+                "d2h_bytes_per_step": e2e_n * 4,
+                "whole_call_s": whole, "whole_call_new_tok_s": e2e_n / whole, "prefill_s": to_first,
+                "note": f"{'jyc_generate' if world == 1 else 'TPDecoder.generate'}: {CTX} prompt ids from pinned "
+                        f"host memory, prefill, {e2e_n} greedy tokens read back to the host in blocks of "
+                        f"1..32 (token callback); value = decode tokens/s first -> last new token, as the "
+                        f"reference's -tokenspeed; whole_call includes the prefill"},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
     }
+    if tp_check is not None:
+        line["tp_check"] = tp_check
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
     return 0
+
+
+class _DevBuf:
+    """A device buffer of the library seen by torch (zero copy)."""
+
+    def __init__(self, ptr: int, n: int, typestr: str = "<i4"):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
 
 
 def run_c4(args):
@@ -803,30 +1013,28 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c1", choices=["c1", "c3-tp", "c4", "prefill", "kquant"],
-                    help="c1: the headline decode line (default); c3-tp: configs[3] tensor parallel; "
-                         "c4: configs[4] batched decode sweep; prefill: prompt prefill of --model; "
-                         "kquant: K-quant matmul bandwidth")
+    ap.add_argument("--workload", default="c3", choices=["c3", "c1", "c4", "prefill", "kquant"],
+                    help="c3: the headline (configs[3] decode at context 4096, tensor parallel under "
+                         "torchrun); c1: configs[1] decode; c4: configs[4] batched decode sweep; prefill: "
+                         "prompt prefill of --model; kquant: K-quant matmul bandwidth")
     ap.add_argument("--model", default="c1", choices=["c1", "c2", "c3"], help="prefill workload: which config")
     ap.add_argument("--seqs", default="1,4,16,32,64", help="c4: sequence counts of the sweep")
     ap.add_argument("--nvtx", action="store_true", help="mark the timed region as NVTX range 'timed' (profiling)")
     ap.add_argument("--decode-tokens", type=int, default=128, help="c4: greedy tokens per sequence per step")
-    ap.add_argument("--tp-mode", default="kernel", choices=["kernel", "nccl"],
-                    help="c3-tp: in-kernel NVLink exchange (default) or NCCL between kernel windows")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
-    if args.workload == "c3-tp":
-        return run_tp(args)
+    if args.workload == "c3":
+        return run_headline(args)
     if args.workload == "c4":
         return run_c4(args)
     if args.workload == "kquant":
         return run_kquant(args)
     if args.workload == "prefill":
         return run_prefill(args)
-    return run_b200(args)
+    return run_c1(args)
 
 
 if __name__ == "__main__":

@@ -40,6 +40,7 @@
 // a second of clock cycles and record an error word the host reads).
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "mega.cuh"
 #include "sample.cuh"
@@ -169,6 +170,13 @@ static __device__ __forceinline__ void load_tile(const MegaMat& M, int r0, int r
              pol);
 }
 
+// The same tile, prefetched into L2 only (runs ahead of the ring).
+static __device__ __forceinline__ void prefetch_tile(const MegaMat& M, int r0, int rows, int cb) {
+    const int w = min(kMegaCB, M.k - cb * kMegaCB);
+    bulk_prefetch_l2(M.qs + (size_t)cb * M.n * kMegaCB + (size_t)r0 * w, (uint32_t)(rows * w));
+    bulk_prefetch_l2(M.d + (size_t)cb * M.n * (kMegaCB / 32) + (size_t)r0 * (w / 32), (uint32_t)(rows * (w / 32) * 2));
+}
+
 // Walk over one CTA's tiles of the whole step, in consumer order: per layer
 // QKV, O, gate/up, down, then the LM head (l == L). Row tiles outer, column
 // blocks inner, as consume_mat takes them.
@@ -224,13 +232,25 @@ static __device__ bool cursor_next(const StepMats& sm, TileCursor& c, int b) {
 // Producer (one thread): every tile of the step into the ring, in consumer
 // order, a slot refilled as soon as every consumer warp released it. It never
 // waits on activations, so weights keep streaming across the grid barriers.
-static __device__ bool produce_step(const StepMats& smats, int l0, int m0, int b, int ns, uint64_t* full,
+// A second cursor runs `pf` tiles ahead of the ring and prefetches them into
+// L2: while the consumers wait (grid barriers, attention) HBM keeps filling
+// L2 with the tiles they take next, and those later arrive at L2 speed.
+static __device__ bool produce_step(const StepMats& smats, int l0, int m0, int b, int ns, int pf, uint64_t* full,
                                     uint64_t* empty, unsigned char* ring, int* err) {
     const uint64_t pol = policy_evict_first();
     TileCursor c{l0, m0, 0, 0, 0, 0, 0, nullptr};
     bool have = cursor_enter(smats, c, b);
+    TileCursor pc = c;
+    bool pf_have = have;
+    int pt = 0;  // tiles the prefetch cursor has passed
     RingPos rp{0, 0};
+    if (pf <= 0) pf_have = false;
     for (int t = 0; have; t++) {
+        while (pf_have && pt < t + pf) {  // the ring's first ns tiles need no prefetch
+            if (pt >= ns) prefetch_tile(*pc.M, pc.r0, min(pc.M->rt, pc.r_end - pc.r0), pc.cb);
+            pf_have = cursor_next(smats, pc, b);
+            pt++;
+        }
         if (t >= ns && !mbar_wait_err(&empty[rp.s], rp.ph ^ 1, err, 3)) return false;
         load_tile(*c.M, c.r0, min(c.M->rt, c.r_end - c.r0), c.cb, ring + (size_t)rp.s * kMegaSlotBytes, &full[rp.s],
                   pol);
@@ -970,6 +990,32 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     return true;
 }
 
+// L2 prefetch of the cached K/V rows (and their scales) that this CTA's
+// attention items of `layer` will read: issued a phase ahead, so the items
+// find them in L2 instead of queueing behind the weight stream in HBM.
+static __device__ void prefetch_attn_rows(const MegaArgs& a, int layer, int pos, int nvalid) {
+    const int ngrp = a.H / a.KV / a.gsz, n_items = a.KV * ngrp * nvalid;
+    int last = -1;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const int kv_h = it / (ngrp * nvalid), rem = it - kv_h * ngrp * nvalid, split = rem % nvalid;
+        const int key = kv_h * nvalid + split;
+        if (key == last) continue;
+        last = key;
+        const int j0 = split * a.chunk, jb = min(j0 + a.chunk, pos);  // cached rows of the item
+        if (jb <= j0) continue;
+        const size_t row0 = ((size_t)layer * a.KV + kv_h) * a.max_seq + j0;
+        const uint32_t kvb = (uint32_t)((jb - j0) * a.hd);
+        bulk_prefetch_l2(a.k8 + row0 * a.hd, kvb);
+        bulk_prefetch_l2(a.v8 + row0 * a.hd, kvb);
+        // scales: 16-byte aligned start (rounded down inside the array) and length (rounded down)
+        const uintptr_t k0 = reinterpret_cast<uintptr_t>(a.ks + row0), v0 = reinterpret_cast<uintptr_t>(a.vs + row0);
+        const uint32_t sb = (uint32_t)((jb - j0) * 4 + (k0 & 15)) & ~15u;
+        const uint32_t vb = (uint32_t)((jb - j0) * 4 + (v0 & 15)) & ~15u;
+        if (sb) bulk_prefetch_l2(reinterpret_cast<const void*>(k0 & ~(uintptr_t)15), sb);
+        if (vb) bulk_prefetch_l2(reinterpret_cast<const void*>(v0 & ~(uintptr_t)15), vb);
+    }
+}
+
 // One instantiation per attention shape (query heads per kv head <= MAXG,
 // head_dim HD) and per exchange mode (TP: in-kernel tensor-parallel
 // exchange): each kernel carries only the code its model runs.
@@ -1005,8 +1051,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
 
     if (warp == kMegaCW) {  // ---- producer warp: the step's weight tiles, in consumer order
         if (lane == 0)
-            produce_step(StepMats{a.layers, a.head_dev, a.L, 2 * a.win1}, a.win0 >> 1, (a.win0 & 1) * 2, b, ns, full,
-                         empty, ring, a.err);
+            produce_step(StepMats{a.layers, a.head_dev, a.L, 2 * a.win1}, a.win0 >> 1, (a.win0 & 1) * 2, b, ns,
+                         a.pf_tiles, full, empty, ring, a.err);
         return;
     }
 
@@ -1043,6 +1089,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         if (a.trace != nullptr && tid == 0) a.trace[(size_t)b * kMegaTracePts + (idx)] = clock64(); \
     } while (0)
     TRACE(0);
+    if (a.kv_prefetch && tid == 0 && (a.win0 & 1) == 0 && a.win0 < 2 * a.L)
+        prefetch_attn_rows(a, a.win0 >> 1, pos, nvalid);
 
     // half-layer phases p = 2 l + h of this launch's window (h 0: QKV,
     // attention, O; h 1: gate/up, down); p = 2 L is the LM head
@@ -1094,6 +1142,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
                                          &s_ok, tr);
             }
             if (!ok) break;
+            // the next layer's cached K/V rows travel to L2 meanwhile
+            if (a.kv_prefetch && tid == 0 && l + 1 < a.L && 2 * (l + 1) < a.win1)
+                prefetch_attn_rows(a, l + 1, pos, nvalid);
             TRACE(tb + 3);
             ok = grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
             TRACE(tb + 4);
@@ -1229,6 +1280,16 @@ int mega_num_ctas() {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
     }
     return n;
+}
+
+// L2 prefetch distance of the copy issuer (tiles beyond the ring's ns). The
+// window over all CTAs (148 x distance x 26 KB) stays well inside the 126 MB
+// L2. JYC_MEGA_PREFETCH overrides it (tuning).
+int mega_prefetch_tiles(int ns) {
+    (void)ns;
+    int pf = 0;
+    if (const char* e = std::getenv("JYC_MEGA_PREFETCH")) pf = std::max(0, std::min(64, std::atoi(e)));
+    return pf;
 }
 
 // Work split of a matrix: for every column-group count (split-K only when

@@ -90,6 +90,8 @@ struct MegaArgs {
     int kmax;                 // largest GEMV input length (x / digit buffers)
     int xs_bytes;             // shared bytes of the x / digits / attention union
     int nslots;               // ring depth
+    int pf_tiles;             // L2 prefetch distance of the copy issuer, in tiles beyond the ring (0: none)
+    int kv_prefetch;          // 1: prefetch each layer's cached K/V rows into L2 a phase ahead
     int win0, win1;           // phases of this launch: [win0, win1) of 2 l + h (h 0: QKV..O, 1: gate/up..down), 2 L = head
     long long* trace;         // optional: SM clock at each phase boundary, [CTA][kMegaTracePts]
     // tensor parallel inside the kernel (tp > 1): every CTA stores its O / down
@@ -119,6 +121,7 @@ int mega_smem_bytes(const MegaArgs& a);
 int mega_xs_bytes(int kmax, int G, int hd, int S);
 int mega_attn_sub(int kmax, int G, int hd, int chunk);
 int mega_num_ctas();
+int mega_prefetch_tiles(int ns);
 int launch_mega_step(const MegaArgs& a, cudaStream_t s);
 int prepare_mega_kernel(int smem, int G, int hd);
 int mega_static_smem(int G, int hd);  // -1 when the kernel image cannot be queried

@@ -13,6 +13,7 @@
 // CUDA graph. Prompt rows go through the generic kernels in chunks of 8 rows.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -343,6 +344,9 @@ int setup_mega(jyc_model* m) {
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
     const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
     a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
+    a.pf_tiles = mega_prefetch_tiles(a.nslots);
+    a.kv_prefetch = 0;
+    if (const char* e = std::getenv("JYC_MEGA_KV_PREFETCH")) a.kv_prefetch = std::atoi(e) != 0;
     a.win0 = 0;
     a.win1 = 2 * m->L + 1;  // the whole step
     if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode

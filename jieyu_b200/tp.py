@@ -235,6 +235,44 @@ class TPDecoder:
             check(self.lib.jyc_model_rewind(self.m.h, T, s))
             self.step(1)
 
+    def generate(self, prompt: np.ndarray, max_new: int, cb=None) -> np.ndarray:
+        """The tensor-parallel counterpart of generate() (generate.h:90-112,
+        greedy; call on every rank): the prompt ids go from pinned host
+        memory to the device, the tensor-parallel prefill appends the first
+        new id, then decode steps run in blocks of 1, 2, 4, .. 32 tokens,
+        each block's ids read back to the host and handed to cb in order
+        (every rank runs the same blocks and holds the same ids). Stops after
+        max_new ids or at the context limit; returns prompt + new ids."""
+        torch = self.torch
+        T = len(prompt)
+        pin = torch.from_numpy(np.ascontiguousarray(prompt, dtype=np.int32)).pin_memory()
+        max_new = min(max_new, self.cfg.max_seq - T)
+        out = list(np.asarray(prompt, dtype=np.int32))
+        if max_new <= 0:
+            return np.asarray(out, dtype=np.int32)
+        self.prefill(pin.numpy())
+        tok_ptr = self.lib.jyc_model_tokens_device(self.m.h)
+        toks = torch.as_tensor(_DevBuf(tok_ptr, self.cfg.max_seq + 1, "<i4"), device="cuda")
+        host = torch.empty(self.cfg.max_seq + 1, dtype=torch.int32).pin_memory()
+        done, have, block = 1, T, 1
+        while True:
+            n_new = T + done - have
+            with torch.cuda.stream(self.stream):
+                host[have:have + n_new].copy_(toks[have:have + n_new], non_blocking=True)
+            self.stream.synchronize()
+            for i in range(have, have + n_new):
+                out.append(int(host[i]))
+                if cb is not None:
+                    cb(int(host[i]))
+            have += n_new
+            if done >= max_new:
+                break
+            n = min(block, max_new - done)
+            self.step(n)
+            done += n
+            block = min(2 * block, 32)
+        return np.asarray(out, dtype=np.int32)
+
     def tokens(self, n: int) -> np.ndarray:
         torch = self.torch
         self.stream.synchronize()

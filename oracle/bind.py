@@ -35,6 +35,7 @@ def _sig(lib, prefix: str):
         "cache_create": (_P, [_I, _I, _I, _I]),
         "cache_free": (None, [_P]),
         "cache_read": (None, [_P, _I, _I, _P, _P, _P, _P]),
+        "cache_write": (None, [_P, _I, _I, _P, _P, _P, _P]),
         "forward_logits": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     }
     for name, (res, args) in s.items():
@@ -96,6 +97,8 @@ class Reference(_Checker):
         self.lib.jyref_generate.restype = _I
         self.lib.jyref_generate.argtypes = [_P, _P, _I, _P, _I, _I, _F, _P, _F, _P]
         self.lib.jyref_last_error.restype = C.c_char_p
+        self.lib.jyref_decode_steps.restype = _I
+        self.lib.jyref_decode_steps.argtypes = [_P, _P, _I, _I, _I, _P, _P]
         self.lib.jyref_init(isa.encode(), threads)
 
     def generate(self, desc, prompt, max_new, eos=None, temperature=0.0, rep=1.0, max_seq=None,
@@ -112,6 +115,17 @@ class Reference(_Checker):
         if times is not None:
             times[:] = t
         return out[:n].copy()
+
+
+    def decode_steps(self, desc, cache, start_pos: int, first_id: int, n: int):
+        """n greedy steps of generate_cached's body from a cache holding
+        [0, start_pos); returns (new ids, seconds per step)."""
+        out = np.zeros(n, np.int32)
+        t = np.zeros(n, np.float64)
+        r = self.lib.jyref_decode_steps(C.byref(desc), cache, start_pos, first_id, n, out.ctypes.data, t.ctypes.data)
+        if r < 0:
+            raise RuntimeError(self.lib.jyref_last_error().decode())
+        return out, t
 
 
 def reference_available() -> bool:

@@ -477,6 +477,17 @@ void jyo_cache_read(void* p, int layer, int npos, int8_t* k, float* ks, int8_t* 
     memcpy(vs, c->vs + lay * c->KV, (size_t)npos * c->KV * sizeof(float));
 }
 
+/* Writes one layer's first npos positions (the inverse of jyo_cache_read). */
+void jyo_cache_write(void* p, int layer, int npos, const int8_t* k, const float* ks, const int8_t* v,
+                     const float* vs) {
+    jyo_cache* c = (jyo_cache*)p;
+    const size_t row = (size_t)c->KV * c->hd, lay = (size_t)layer * c->max_seq;
+    memcpy(c->k + lay * row, k, (size_t)npos * row);
+    memcpy(c->v + lay * row, v, (size_t)npos * row);
+    memcpy(c->ks + lay * c->KV, ks, (size_t)npos * c->KV * sizeof(float));
+    memcpy(c->vs + lay * c->KV, vs, (size_t)npos * c->KV * sizeof(float));
+}
+
 /* matmul_w (wmat_kernel.h:9-16): fp32 [k][n] -> matmul, Q8_0 / K-quant [n][k] -> matmul_q. */
 static int matmul_w(const jyc_wmat* w, int m, int n, int k, const float* A, float* Cc) {
     if (w->f) { jyo_matmul_f32(m, n, k, A, w->f, Cc); return 0; }
@@ -659,4 +670,88 @@ int jyo_generate(const jyc_model_desc* d, const int* prompt, int prompt_len, con
     free(logits);
     jyo_cache_free(c);
     return err ? -1 : len;
+}
+
+/* ---- seeded synthetic inputs ----------------------------------------------
+ * The counter-based generator that defines the synthetic weights and prompts
+ * of the tests and benches (the same integer function as the library's
+ * jyc_synth_*: splitmix64's finaliser over (seed, stream, index), a sum of
+ * four 16-bit uniforms as a bell-shaped integer, the Q8_0 rule d =
+ * fp16(amax/127), q = lrintf(x/d) clamped to +-127). Restated here so that
+ * the CPU checker and the reference arm of the bench build their inputs
+ * without the product library; a host test holds the two byte-identical. */
+static uint64_t syn_mix(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static uint64_t syn_base(uint64_t seed, uint64_t stream) {
+    return syn_mix(syn_mix(seed) ^ (stream * 0xD1B54A32D192ED03ull));
+}
+static int syn_bell(uint64_t base, uint64_t idx) {
+    const uint64_t r = syn_mix(base + idx);
+    return (int)(r & 0xFFFFu) + (int)((r >> 16) & 0xFFFFu) + (int)((r >> 32) & 0xFFFFu) + (int)(r >> 48) -
+           2 * 65535;
+}
+/* binary32 -> binary16, round to nearest even */
+static uint16_t syn_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t mag = x & 0x7FFFFFFFu;
+    if (mag >= 0x7F800000u) return (uint16_t)(sign | (mag > 0x7F800000u ? 0x7E00u : 0x7C00u));
+    if (mag >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u);
+    if (mag < 0x38800000u) {
+        if (mag < 0x33000000u) return (uint16_t)sign;
+        const uint32_t e = mag >> 23, m = (mag & 0x7FFFFFu) | 0x800000u;
+        const int shift = 126 - (int)e;
+        const uint32_t q = m >> shift, rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1);
+        return (uint16_t)(sign | (q + ((rem > half || (rem == half && (q & 1u))) ? 1u : 0u)));
+    }
+    uint32_t h = (((mag >> 23) - 112u) << 10) | ((mag & 0x7FFFFFu) >> 13);
+    const uint32_t rem = mag & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)(sign | h);
+}
+
+void jyo_synth_f32(uint64_t seed, uint64_t stream, float std_dev, float* out, size_t n) {
+    const uint64_t base = syn_base(seed, stream);
+    const float sc = std_dev / 37837.227f;
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; i++) out[i] = (float)syn_bell(base, (uint64_t)i) * sc;
+}
+
+void jyo_synth_q8_0(uint64_t seed, uint64_t stream, float std_dev, void* out_blocks, size_t rows, size_t k) {
+    const uint64_t base = syn_base(seed, stream);
+    const float sc = std_dev / 37837.227f;
+    uint8_t* dst = (uint8_t*)out_blocks;
+    const size_t nb = k / 32;
+#pragma omp parallel for schedule(static)
+    for (long long r = 0; r < (long long)rows; r++) {
+        float x[32];
+        for (size_t bl = 0; bl < nb; bl++) {
+            const size_t i0 = (size_t)r * k + bl * 32;
+            float amax = 0.0f;
+            for (int i = 0; i < 32; i++) {
+                x[i] = (float)syn_bell(base, i0 + i) * sc;
+                amax = fmaxf(amax, fabsf(x[i]));
+            }
+            uint8_t* blk = dst + ((size_t)r * nb + bl) * 34;
+            const uint16_t dh = syn_f16(amax / 127.0f);
+            const float d = f16_to_f32(dh);
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            memcpy(blk, &dh, 2);
+            for (int i = 0; i < 32; i++) {
+                float v = x[i] * id;
+                v = v > 127.0f ? 127.0f : (v < -127.0f ? -127.0f : v);
+                blk[2 + i] = (uint8_t)(int8_t)lrintf(v);
+            }
+        }
+    }
+}
+
+void jyo_synth_ids(uint64_t seed, uint64_t stream, int vocab, int* out, size_t n) {
+    const uint64_t base = syn_base(seed, stream);
+    for (size_t i = 0; i < n; i++) out[i] = (int)(((syn_mix(base + i) >> 32) * (uint64_t)vocab) >> 32);
 }

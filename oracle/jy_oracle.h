@@ -10,6 +10,7 @@
  */
 #ifndef JY_ORACLE_H
 #define JY_ORACLE_H
+#include <stddef.h>
 #include <stdint.h>
 #include "jieyu_b200.h"
 
@@ -45,6 +46,8 @@ void jyo_silu(const float* x, float* y, int n);
 void* jyo_cache_create(int L, int max_seq, int KV, int hd);
 void jyo_cache_free(void* c);
 void jyo_cache_read(void* c, int layer, int npos, int8_t* k, float* ks, int8_t* v, float* vs);
+void jyo_cache_write(void* c, int layer, int npos, const int8_t* k, const float* ks, const int8_t* v,
+                     const float* vs);
 /* generate_cached step body (generate.h:43-49): embed rows, forward_cached, LM head. */
 int jyo_forward_logits(const jyc_model_desc* d, void* cache, const int* ids, int seq,
                        int start_pos, float* logits, float* hidden_out);
@@ -53,6 +56,11 @@ int jyo_sample(float* logits, int V, float temperature, float rep_penalty, const
                int prompt_len, int len, unsigned* rng);
 int jyo_generate(const jyc_model_desc* d, const int* prompt, int prompt_len, const int* eos,
                  int num_eos, int max_new, float temperature, int* out_ids, float rep_penalty);
+
+/* Seeded synthetic weights / prompt ids (byte-identical to jyc_synth_*). */
+void jyo_synth_f32(uint64_t seed, uint64_t stream, float std_dev, float* out, size_t n);
+void jyo_synth_q8_0(uint64_t seed, uint64_t stream, float std_dev, void* out_blocks, size_t rows, size_t k);
+void jyo_synth_ids(uint64_t seed, uint64_t stream, int vocab, int* out, size_t n);
 
 #ifdef __cplusplus
 }

@@ -16,6 +16,7 @@
  *   ffn                 libs/model_libs/ffn/ffn.h:7-19
  *   forward_cached      libs/model_libs/forward.h:47-96
  *   generate            libs/model_libs/generate.h:90-112
+ *   generate_cached's step body (generate.h:40-60) over a pre-filled cache
  *   bfile::write_bfile  libs/model_libs/bfile.h:393-411 (model.bf writer)
  *   bfile::View::open + bind_layers / bind_biases / bind_embed / bind_lm_head /
  *   bind_final_norm     libs/model_libs/bfile.h:141-204, load_weights.h:97-155
@@ -166,6 +167,53 @@ void jyref_cache_read(void* cp, int layer, int npos, int8_t* k, float* ks, int8_
     std::memcpy(v, c->v_ptr(layer, 0), (size_t)npos * row);
     std::memcpy(ks, c->ks_ptr(layer, 0), (size_t)npos * c->num_kv_heads * sizeof(float));
     std::memcpy(vs, c->vs_ptr(layer, 0), (size_t)npos * c->num_kv_heads * sizeof(float));
+}
+
+/* Writes one layer's first npos positions in the cache's native layout (the
+ * inverse of jyref_cache_read): a context filled without running a prefill. */
+void jyref_cache_write(void* cp, int layer, int npos, const int8_t* k, const float* ks, const int8_t* v,
+                       const float* vs) {
+    __KVcache* c = static_cast<__KVcache*>(cp);
+    const size_t row = (size_t)c->num_kv_heads * c->head_dim;
+    std::memcpy(c->k_ptr(layer, 0), k, (size_t)npos * row);
+    std::memcpy(c->v_ptr(layer, 0), v, (size_t)npos * row);
+    std::memcpy(c->ks_ptr(layer, 0), ks, (size_t)npos * c->num_kv_heads * sizeof(float));
+    std::memcpy(c->vs_ptr(layer, 0), vs, (size_t)npos * c->num_kv_heads * sizeof(float));
+}
+
+/* n greedy decode steps of generate_cached's loop body (generate.h:40-60,
+ * seq = 1) from a cache already holding positions [0, start_pos): the LM-head
+ * prefetch, the embedding row of the last id, forward_cached, matmul_w of the
+ * LM head and the greedy pick (first index of the maximum). first_id is the
+ * token at start_pos; out_ids[i] receives the i-th new id. step_s (optional,
+ * n doubles) receives each step's seconds. Returns n, or -1. */
+int jyref_decode_steps(const jyc_model_desc* d, void* cache, int start_pos, int first_id, int n, int* out_ids,
+                       double* step_s) {
+    try {
+        __KVcache& c = *static_cast<__KVcache*>(cache);
+        std::vector<float> X((size_t)d->hidden), logits((size_t)d->vocab_size);
+        const WMat embed = to_wmat(d->embed), head = to_wmat(d->lm_head);
+        int id = first_id;
+        for (int i = 0; i < n; i++) {
+            const auto t0 = std::chrono::steady_clock::now();
+            prefetch::range(prefetch::data_of(head), prefetch::bytes_of(head, (size_t)d->vocab_size, (size_t)d->hidden));
+            wmat_row(embed, (size_t)id, d->hidden, X.data());
+            forward_cached(X.data(), reinterpret_cast<const LayerWeights*>(d->layers), d->num_layers,
+                           d->final_rms_weight, d->cos_table, d->sin_table, 1, start_pos + i, c, d->hidden,
+                           d->num_heads, d->num_kv_heads, d->head_dim, d->intermediate);
+            matmul_w(head, 1, d->vocab_size, d->hidden, X.data(), logits.data());
+            int next = 0;
+            for (int v = 1; v < d->vocab_size; v++)
+                if (logits[(size_t)v] > logits[(size_t)next]) next = v;
+            out_ids[i] = next;
+            id = next;
+            if (step_s) step_s[i] = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        }
+        return n;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
 }
 
 /* The step body of generate_cached (generate.h:43-49): embedding rows,

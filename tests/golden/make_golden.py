@@ -2,7 +2,7 @@
 itself (oracle/_ref/libjyref.so, the jieyu headers compiled unmodified) on
 seeded inputs. Run from the repository root, where the reference tree exists:
 
-    make -C oracle all && python tests/golden/make_golden.py
+    make -C oracle all REF=<reference tree> && python tests/golden/make_golden.py
 
 The fixtures hold seeds, token ids, a few values and SHA-256 digests of
 outputs, never large tensors. JIEYU_ISA=fma pins the reference's code path
