@@ -1006,6 +1006,102 @@ def run_prefill(args):
     return 0
 
 
+def run_c2(args):
+    """configs[2] (Llama-3.2-1B shape, Q8_0 and fp32 weights, one GPU): batch-1
+    greedy decode at KV contexts of 1024, 4096 and 16384 positions, and the
+    prefill of a 2048-token random prompt. The context is a seeded int8 K/V
+    cache written into the device cache (oracle.synth.context_kv through
+    jyc_model_write_kv; the decode step reads it exactly as it reads a
+    prefilled one), then one step = rewind to ctx + 1 tokens and decode
+    DECODE_C2 tokens. Per (weights, context): tok/s, the bytes one token
+    reads (weights + the KV rows of its positions) and their HBM rate against
+    the measured peak. value = the Q8_0 decode tok/s at context 4096."""
+    import numpy as np
+    import torch
+
+    from jieyu_b200 import _capi
+    from jieyu_b200.model import CONFIGS, DeviceModel, HostWeights, prompt_ids
+    from oracle.synth import context_kv
+
+    if env_int("RANK", 0) != 0:
+        return 0
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    lib = _capi.load()
+    peak, peak_kind = measured_peaks()
+    DECODE_C2 = 64
+    stream = torch.cuda.Stream()
+    s = stream.cuda_stream
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    sweep, prefill = [], None
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = lib.jyc_kernel_launches()
+    for key in ("c2", "c2f"):
+        cfg = CONFIGS[key]
+        hw = HostWeights.synthetic(cfg)
+        m = DeviceModel(hw)
+        w_bytes = float(lib.jyc_model_weight_bytes_per_token(m.h))
+        if key == "c2":  # the 2048-token prefill (configs[2]'s prefill line)
+            ids = torch.from_numpy(prompt_ids(cfg, n=2048)).cuda()
+            with torch.cuda.stream(stream):
+                m.prefill_device(ids.data_ptr(), 2048, s)
+                a, b = ev(), ev()
+                a.record(stream)
+                m.prefill_device(ids.data_ptr(), 2048, s)
+                b.record(stream)
+                stream.synchronize()
+            prefill = {"value": 2048 / (a.elapsed_time(b) / 1e3), "unit": "tok/s", "prompt": 2048,
+                       "ms": a.elapsed_time(b)}
+        tok = int(prompt_ids(cfg, n=1, index=7)[0])
+        for ctx in (1024, 4096, 16384):
+            for l, k, ks, v, vs in context_kv(cfg.layers, ctx, cfg.kv_heads, cfg.head_dim):
+                m.write_kv(l, k, ks, v, vs)
+            m.forward_logits(np.array([tok], np.int32), ctx)  # token at ctx, its KV row appended
+
+            def step():
+                m.rewind(ctx + 1, s)
+                m.decode_device(DECODE_C2, s)
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    step()
+                stream.synchronize()
+                e0, e1 = ev(), ev()
+                e0.record(stream)
+                for _ in range(args.steps):
+                    step()
+                e1.record(stream)
+                stream.synchronize()
+            assert lib.jyc_device_error(1) == 0, "a bounded wait of the decode kernel gave up"
+            ms_tok = e0.elapsed_time(e1) / (args.steps * DECODE_C2)
+            kv = float(lib.jyc_model_kv_bytes_per_token(m.h, ctx + 1 + DECODE_C2 // 2))
+            gbs = (w_bytes + kv) / (ms_tok / 1e3) / 1e9
+            sweep.append({"weights": "q8_0" if key == "c2" else "f32", "ctx": ctx, "tok_s": 1e3 / ms_tok,
+                          "ms_per_token": ms_tok, "bytes_per_token": w_bytes + kv, "kv_bytes": kv,
+                          "hbm_gbs": gbs, "hbm_frac": gbs / peak,
+                          "path": "decode kernel" if lib.jyc_model_decode_path(m.h) == 2 else "generic kernels"})
+        m.close()
+        del hw
+    clk = clocks.stop()
+    head = next(r for r in sweep if r["weights"] == "q8_0" and r["ctx"] == 4096)
+    line = {
+        "metric": "batch-1 decode tok/s (configs[2])", "value": head["tok_s"], "unit": "tok/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_token"] * DECODE_C2,
+        "higher_is_better": True, "scaling": "weak", "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"configs[2] Llama-3.2-1B shape, Q8_0 and fp32 weights (N(0, 0.02), seeded): "
+                               f"batch-1 greedy decode of {DECODE_C2} tokens per step at seeded KV contexts "
+                               f"1024 / 4096 / 16384; prefill of a 2048-token random prompt",
+                   "l2": "inputs larger than L2 (1.3 GB / 4.9 GB of weights per token)"},
+        "roofline": {"bound": "hbm", "kernel": head["path"], "achieved": head["hbm_gbs"], "peak": peak,
+                     "unit": "GB/s", "frac": head["hbm_frac"], "bytes_per_launch": head["bytes_per_token"],
+                     "launch_ms": head["ms_per_token"], "peak_kind": peak_kind, "traffic": None},
+        "sweep": sweep, "prefill": prefill,
+        "gpu_launches": int(lib.jyc_kernel_launches() - launches0), "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1013,10 +1109,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c3", choices=["c3", "c1", "c4", "prefill", "kquant"],
+    ap.add_argument("--workload", default="c3", choices=["c3", "c1", "c2", "c4", "prefill", "kquant"],
                     help="c3: the headline (configs[3] decode at context 4096, tensor parallel under "
-                         "torchrun); c1: configs[1] decode; c4: configs[4] batched decode sweep; prefill: "
-                         "prompt prefill of --model; kquant: K-quant matmul bandwidth")
+                         "torchrun); c1: configs[1] decode; c2: configs[2] decode at contexts 1024 / 4096 / "
+                         "16384 (Q8_0 and fp32) + its 2048-token prefill; c4: configs[4] batched decode sweep; "
+                         "prefill: prompt prefill of --model; kquant: K-quant matmul bandwidth")
     ap.add_argument("--model", default="c1", choices=["c1", "c2", "c3"], help="prefill workload: which config")
     ap.add_argument("--seqs", default="1,4,16,32,64", help="c4: sequence counts of the sweep")
     ap.add_argument("--nvtx", action="store_true", help="mark the timed region as NVTX range 'timed' (profiling)")
@@ -1030,6 +1127,8 @@ def main():
         return run_headline(args)
     if args.workload == "c4":
         return run_c4(args)
+    if args.workload == "c2":
+        return run_c2(args)
     if args.workload == "kquant":
         return run_kquant(args)
     if args.workload == "prefill":

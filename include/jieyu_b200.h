@@ -230,6 +230,46 @@ JYC_API int jyc_argmax(const float* logits, int n, int* out_index, void* stream)
 JYC_API int jyc_sample(float* logits, int vocab_size, float temperature, float repetition_penalty,
                        const int* out_ids, int prompt_len, int len, unsigned int* rng, int* next, void* stream);
 
+/* ---- operator entry points with the reference's calling convention ------
+ * HOST pointers in the reference's own layouts, caller-owned, synchronous:
+ * each call copies its operands to the device, runs the device entry point
+ * above (same kernels, same results) and copies the result back; the
+ * reference's weight blocks are used as they are (Q8_0 34-byte blocks are
+ * re-laid on the device inside the call). include/jieyu_b200_shim.hpp binds
+ * them under the reference's C++ names. Errors as the device entry points. */
+/* qmat::matmul_q(a,b,c,m,n,k,t) (libs/matmul_libs/matmul_q.h:134-162):
+ * C[m][n] = A[m][k] . W^T, W [n][k/block] blocks of qtype (JYC_Q8_0, JYC_Q4K,
+ * JYC_Q5K, JYC_Q6K). */
+JYC_API int jyc_host_matmul_q(const float* a, const void* b, float* c, int m, int n, int k, int qtype);
+/* matmul(m,n,k,A,B,C) (libs/matmul_libs/matmul.h:7-76): B fp32 [k][n]. */
+JYC_API int jyc_host_matmul_f32(int m, int n, int k, const float* A, const float* B, float* C);
+/* matmul_w(B,m,n,k,A,C) (libs/model_libs/wmat_kernel.h:9-16): the WMat
+ * dispatch (fp32 -> matmul, blocks -> matmul_q, none -> C = 0; fp16 weights
+ * return JYC_ERR_UNSUPPORTED). */
+JYC_API int jyc_host_matmul_w(const jyc_wmat* B, int m, int n, int k, const float* A, float* C);
+/* rmsnorm(x,y,w,n,eps) (libs/model_libs/rmsnorm/rmsnorm.h:8-78). */
+JYC_API int jyc_host_rmsnorm(const float* x, float* y, const float* w, int n, float eps);
+/* rope_pos(q,seq,start_pos,heads,hd,cos,sin) (libs/model_libs/rope/rope.h:108-110):
+ * in place; tables [max_seq][hd/2] as RoPETable. */
+JYC_API int jyc_host_rope_pos(float* q, int seq, int start_pos, int num_heads, int head_dim,
+                              const float* cos_table, const float* sin_table);
+/* kv_pack_q8(src,dst,sc,heads,hd,n) (libs/model_libs/attention/attention_q8.h:20-37). */
+JYC_API int jyc_host_kv_pack_q8(const float* src, int8_t* dst, float* sc, int heads, int head_dim, int n);
+/* attention_q8(Q,K,V,out,seq,start_pos,H,KV,hd,kvq) (attention_q8.h:38-184):
+ * the cache is the caller's __KVq (k,v [cap][KV][hd] int8, ks,vs [cap][KV]
+ * fp32); rows [start_pos, start_pos+seq) are appended to it. An incomplete
+ * cache (a null pointer or cap <= 0) works on a temporary one of seq rows at
+ * position 0, as the reference does. */
+JYC_API int jyc_host_attention_q8(const float* Q, const float* K, const float* V, float* out, int seq,
+                                  int start_pos, int num_heads, int num_kv_heads, int head_dim,
+                                  int8_t* kc, float* ks, int8_t* vc, float* vs, int cap);
+/* silu(x,y,n) (libs/model_libs/silu/silu.h:7-81). */
+JYC_API int jyc_host_silu(const float* x, float* y, int n);
+/* ffn(x,w1,w2,w3,out,seq,hidden,inter) (libs/model_libs/ffn/ffn.h:7-19):
+ * out = W2 (silu(W1 x) * (W3 x)). */
+JYC_API int jyc_host_ffn(const float* x, const jyc_wmat* w1, const jyc_wmat* w2, const jyc_wmat* w3,
+                         float* out, int seq, int hidden, int intermediate);
+
 /* ---- model entry points ------------------------------------------------ */
 typedef struct jyc_model jyc_model;
 
@@ -273,6 +313,12 @@ JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_
  * k,v [npos][num_kv_heads][head_dim] int8, ks,vs [npos][num_kv_heads] fp32. */
 JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos,
                               int8_t* k, float* ks, int8_t* v, float* vs);
+/* The reverse: positions [0, npos) of one layer's device KV cache from host
+ * arrays in the same __KVcache order, so that a long context can be set up
+ * without prefilling it (the reference's cache is a plain host array that
+ * its tests may fill the same way, date.h:89-147). Synchronous. */
+JYC_API int jyc_model_write_kv(jyc_model* m, int layer, int npos,
+                               const int8_t* k, const float* ks, const int8_t* v, const float* vs);
 
 /* ---- device-resident stepping (bench / device loop) -------------------- */
 /* `stream` is used as given (0 = the legacy default stream). */

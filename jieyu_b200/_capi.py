@@ -19,7 +19,7 @@ JYC_ERR_CUDA = -2
 JYC_ERR_KV_OOM = -3
 JYC_ERR_UNSUPPORTED = -4
 JYC_ERR_NOMEM = -5
-JYC_Q8_0 = 3
+JYC_Q4K, JYC_Q5K, JYC_Q6K, JYC_Q8_0 = 0, 1, 2, 3  # qmat block types (matmul_q.h:15)
 
 
 class JycError(RuntimeError):
@@ -93,6 +93,15 @@ SIGNATURES = [
     ("jyc_attention_q8", _I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P]),
     ("jyc_attention_q8_noalloc", _I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P]),
     ("jyc_silu", _I, [_P, _P, _I, _P]),
+    ("jyc_host_matmul_q", _I, [_P, _P, _P, _I, _I, _I, _I]),
+    ("jyc_host_matmul_f32", _I, [_I, _I, _I, _P, _P, _P]),
+    ("jyc_host_matmul_w", _I, [_P, _I, _I, _I, _P, _P]),
+    ("jyc_host_rmsnorm", _I, [_P, _P, _P, _I, _F]),
+    ("jyc_host_rope_pos", _I, [_P, _I, _I, _I, _I, _P, _P]),
+    ("jyc_host_kv_pack_q8", _I, [_P, _P, _P, _I, _I, _I]),
+    ("jyc_host_attention_q8", _I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I]),
+    ("jyc_host_silu", _I, [_P, _P, _I]),
+    ("jyc_host_ffn", _I, [_P, _P, _P, _P, _P, _I, _I, _I]),
     ("jyc_argmax", _I, [_P, _I, _P, _P]),
     ("jyc_sample", _I, [_P, _I, C.c_float, C.c_float, _P, _I, _I, _P, _P, _P]),
     ("jyc_model_create", _P, [C.POINTER(ModelDesc)]),
@@ -102,6 +111,7 @@ SIGNATURES = [
     ("jyc_generate", _I, [_P, _P, _I, _P, _I, _I, _F, _P, _F, TOKEN_CB, _P]),
     ("jyc_forward_logits", _I, [_P, _P, _I, _I, _P, _P]),
     ("jyc_model_read_kv", _I, [_P, _I, _I, _P, _P, _P, _P]),
+    ("jyc_model_write_kv", _I, [_P, _I, _I, _P, _P, _P, _P]),
     ("jyc_prefill_device", _I, [_P, _P, _I, _P]),
     ("jyc_decode_device", _I, [_P, _I, _P]),
     ("jyc_model_rewind", _I, [_P, _I, _P]),

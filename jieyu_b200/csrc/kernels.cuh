@@ -34,6 +34,7 @@ struct DevState {
     unsigned int rng;          // the sampler's LCG state
     int prompt_len;            // generated ids start here (penalty range)
     int fresh;                 // the last head appended a token not yet re-picked by the sampler
+    unsigned int apar;         // decode kernel: which half of its attention arrival counters this step uses
 };
 
 // Where a kernel finds its first position: from the step state (decode graph,

@@ -13,8 +13,11 @@
 //           -> Q|K|V rows (+ bias)                          [grid barrier]
 //   ATTN    per (kv head, position split): RoPE + int8 quantisation of the
 //           group's Q heads, K/V append at pos (owner split), int8 dot
-//           scores, online softmax, PV -> split partials      [grid barrier]
-//   O       x = merge of the split partials -> X += Wo x    [grid barrier]
+//           scores, online softmax, PV -> split partials, one arrival count
+//           per item on its (layer, kv head) counter
+//   O       (no grid barrier: each CTA waits for the kv heads its columns
+//           read) x = merge of those heads' split partials -> X += Wo x
+//                                                            [grid barrier]
 //   GATE/UP x = RMSNorm(X) -> h = silu(gate) * up           [grid barrier]
 //   DOWN    x = h -> X += W2 h                              [grid barrier]
 // then the LM head on RMSNorm(X) with a per-CTA argmax -> one atomicMax,
@@ -52,7 +55,8 @@ constexpr int kMegaThreads = (kMegaCW + 1) * 32;  // consumer warps + one copy-i
 
 // Error word of the device kernels (non-zero: a bounded wait gave up; the
 // value tells which: 3 ring slot free, 4 ring slot full, 5 grid barrier,
-// 6 attention K/V copy, 7 prefill digit copy, 8 tensor-parallel exchange).
+// 6 attention K/V copy, 7 prefill digit copy, 8 tensor-parallel exchange,
+// 9 attention arrivals before the O projection).
 __device__ int g_err_word;
 
 int* device_error_word() {
@@ -451,18 +455,9 @@ static __device__ void x_norm(float* x_s, int k, const float* w, float eps, floa
     csync();
 }
 
-// x_s[0..k) = src (16-byte loads, all independent)
-static __device__ void x_load(float* x_s, const float* src, int k) {
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    float4* d4 = reinterpret_cast<float4*>(x_s);
-#pragma unroll 4
-    for (int i = threadIdx.x; i < (k >> 2); i += kMegaCW * 32) d4[i] = __ldcg(s4 + i);
-    csync();
-}
-
-// x_s[0..k) = base + sum of np (<= kMaxParts) partial rows (stride k), in that
-// order; `out` (one CTA) also receives the sum. 16-byte loads, two partial
-// rows issued ahead of their adds.
+// x_s[0..k) = base + sum of np partial rows (stride k), in that order; `out`
+// (one CTA) also receives the sum. 16-byte loads, two partial rows issued
+// ahead of their adds.
 constexpr int kMaxParts = 8;
 static __device__ void x_resid(float* x_s, const float* base, const float* parts, int np, int k, float* out) {
     const float4* b4 = reinterpret_cast<const float4*>(base);
@@ -492,17 +487,23 @@ static __device__ void x_resid(float* x_s, const float* base, const float* parts
     csync();
 }
 
-// x_s (k floats) -> three int8 digit planes + per-32 block scales. A lane
-// takes 4 consecutive elements, 8 lanes one 32-element block.
-static __device__ void x_digitize(const float* x_s, int k, int8_t* xd, float* xsc) {
+// x_s (k floats) -> three int8 digit planes + per-32 block scales, for the
+// 32-element blocks [blk0, blk1) (default: all). A lane takes 4 consecutive
+// elements, 8 lanes one block.
+// GLOBAL: x is a global row written by other CTAs in this launch (read
+// through L2 straight into the digits, no shared-memory copy).
+template <bool GLOBAL = false>
+static __device__ void x_digitize(const float* x_s, int k, int8_t* xd, float* xsc, int blk0 = 0, int blk1 = -1) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sub = lane & 7;  // lane within its block
-    const int nblk = k >> 5;
-    for (int base = warp * 4; base < nblk; base += kMegaCW * 4) {
+    const int nblk = blk1 < 0 ? (k >> 5) : blk1;
+    for (int base = blk0 + warp * 4; base < nblk; base += kMegaCW * 4) {
         const int blk = base + (lane >> 3);
         const bool valid = blk < nblk;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid) v = reinterpret_cast<const float4*>(x_s + blk * 32)[sub];
+        if (valid)
+            v = GLOBAL ? __ldcg(reinterpret_cast<const float4*>(x_s + blk * 32) + sub)
+                       : reinterpret_cast<const float4*>(x_s + blk * 32)[sub];
         float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
@@ -734,13 +735,13 @@ static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const floa
 // (owner split), then per sub-chunk of up to S positions: a TMA bulk copy of
 // the K and V rows, int8 dot scores (dp4a, rotated word order so the 32 lanes
 // of a warp read 32 different banks of 32 different rows), online softmax,
-// P.V with V decoded once per 4 dims. Writes the split partials (o, m, l);
-// the last item of the kv head to finish merges all splits of its query
-// heads into the attention rows buffer (the O projection's input).
+// P.V with V decoded once per 4 dims. Writes the split partials (o, m, l)
+// and counts itself in the (layer, kv head) arrival counter `cnt`; the O
+// projection's CTAs merge the splits of the heads they read.
 template <int MAXG, int HD>
-static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, int kvh, int grp, int split, int nv,
-                                                 int pos, unsigned char* sm, uint64_t* abar, uint32_t& aph,
-                                                 int* s_flag, long long* tr) {
+static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, int kvh, int grp, int split,
+                                                 int chunk, int pos, unsigned char* sm, uint64_t* abar,
+                                                 uint32_t& aph, unsigned int* cnt, long long* tr) {
     constexpr int hd = HD, half = HD / 2, hw = HD / 4, HC = HD / 16;  // words, 16-byte chunks per row
     const int GA = a.H / a.KV, S = a.asub, lS = 31 - __clz(S);
     const int G = a.gsz, g0 = grp * G;  // this item's query heads: kvh * GA + g0 .. + G
@@ -765,7 +766,7 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     float* s_l = reinterpret_cast<float*>(sm + P.l);
     float* s_al = reinterpret_cast<float*>(sm + P.al);
 
-    const int c0 = split * a.chunk, c1 = min(c0 + a.chunk, pos + 1);
+    const int c0 = split * chunk, c1 = min(c0 + chunk, pos + 1);
     const size_t lh = (size_t)layer * a.KV + kvh;
     int8_t* kb = a.k8 + lh * a.max_seq * hd;
     int8_t* vb = a.v8 + lh * a.max_seq * hd;
@@ -934,66 +935,114 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
         a.part_ml[((size_t)h * a.nsplit + split) * 2] = s_m[gq];
         a.part_ml[((size_t)h * a.nsplit + split) * 2 + 1] = s_l[gq];
     }
-    // last finisher of this kv head merges its splits (the barrier orders the
-    // CTA's partial writes before thread 0's fence and arrival)
+    // arrival: the barrier orders the CTA's partial writes before thread 0's
+    // fence and count
     csync();
     ATR(6);
     if (tid == 0) {
         __threadfence();
-        unsigned int* cnt = a.acnt + kvh * (GA / G) + grp;
-        const unsigned int old = atomicAdd(cnt, 1u);
-        *s_flag = old == (unsigned int)(nv - 1);
-        if (*s_flag) atomicExch(cnt, 0u);
+        atomicAdd(cnt + kvh, 1u);
     }
-    csync();
     ATR(7);
-    if (!*s_flag) return true;
-    __threadfence();
-    // every output element merges its splits itself: (m, l, o) of four splits
-    // per round trip, rescaled online to the running maximum
-    for (int e = tid; e < G * hd; e += nthr) {
-        const int gq = e / hd, dd = e - gq * hd, h = kvh * GA + g0 + gq;
-        const float* ml = a.part_ml + (size_t)h * a.nsplit * 2;
-        const float* po = a.part_o + (size_t)h * a.nsplit * hd + dd;
-        float M = -INFINITY, L = 0.0f, O = 0.0f;
-        for (int s0 = 0; s0 < nv; s0 += 4) {
-            float mv[4], lv[4], ov[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                mv[i] = -INFINITY;
-                lv[i] = ov[i] = 0.0f;
-                if (s0 + i < nv) {
-                    const float2 m2 = __ldcg(reinterpret_cast<const float2*>(ml) + s0 + i);
-                    mv[i] = m2.x;
-                    lv[i] = m2.y;
-                    ov[i] = __ldcg(po + (size_t)(s0 + i) * hd);
-                }
-            }
-            const float Mn = fmaxf(M, fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3])));
-            if (Mn == -INFINITY) continue;
-            const float r = (M == -INFINITY) ? 0.0f : expf(M - Mn);
-            L = __fmul_rn(L, r);
-            O = __fmul_rn(O, r);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float w = (mv[i] == -INFINITY) ? 0.0f : expf(mv[i] - Mn);
-                L = __fmaf_rn(w, lv[i], L);
-                O = __fmaf_rn(w, ov[i], O);
-            }
-            M = Mn;
-        }
-        a.attn[(size_t)h * hd + dd] = __fdiv_rn(O, L);
-    }
-    csync();
     ATR(8);
 #undef ATR
     return true;
 }
 
+// Wait (bounded; error word 9) until every attention item of kv heads
+// [kv0, kv1] arrived (cnt[kv] >= need).
+static __device__ bool attn_wait(const unsigned int* cnt, int kv0, int kv1, unsigned int need, int* err, int* s_ok) {
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const long long t0 = clock64();
+        for (int kv = kv0; kv <= kv1 && ok; kv++) {
+            while ((int)(ld_acquire_gpu(cnt + kv) - need) < 0) {
+                if (clock64() - t0 > (1LL << 31)) {
+                    atomicExch(err, 9);
+                    ok = 0;
+                    break;
+                }
+                if (*(volatile int*)err != 0) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        *s_ok = ok;
+    }
+    csync();
+    return *s_ok != 0;
+}
+
+// x_s[e] for e in [c0, c1) = the attention row element e (head e / hd): its
+// nv split partials (o, m, l) merged as sum_s w_s o_s, w_s = exp(m_s - M) / L
+// (M the largest m_s, L = sum_s exp(m_s - M) l_s). The partials of the heads
+// involved arrive in shared memory first (16-byte cp.async copies into the
+// x region behind x_s[0, H hd), as many heads per round as fit): one L2
+// round trip per round. part_ml's split stride (nsplit) is even, so a head's
+// (m, l) pairs are whole 16-byte chunks.
+static __device__ void attn_merge(const MegaArgs& a, float* x_s, int c0, int c1, int nv) {
+    constexpr int nthr = kMegaCW * 32;
+    const int tid = threadIdx.x, hd = a.hd, hd4 = hd >> 2, q_dim = a.H * hd;
+    const int nv2 = (nv + 1) & ~1;  // (m, l) pairs staged per head
+    float* stg = x_s + q_dim;
+    const int per_head = nv * hd + 2 * nv2;
+    const int hpr = max(1, (a.xs_bytes / 4 - q_dim) / per_head);
+    const int h0 = c0 / hd, h1 = (c1 + hd - 1) / hd;
+    for (int hb = h0; hb < h1; hb += hpr) {
+        const int nh = min(h1 - hb, hpr);
+        float* so = stg;                          // [nh][nv][hd]
+        float* sml = stg + (size_t)nh * nv * hd;  // [nh][nv2][2]
+        for (int idx = tid; idx < nh * nv * hd4; idx += nthr) {
+            const int hh = idx / (nv * hd4), rem = idx - hh * nv * hd4, sp = rem / hd4, i = rem - sp * hd4;
+            cp_async16_cg(so + ((size_t)hh * nv + sp) * hd + 4 * i,
+                          a.part_o + ((size_t)(hb + hh) * a.nsplit + sp) * hd + 4 * i);
+        }
+        for (int idx = tid; idx < nh * (nv2 >> 1); idx += nthr) {
+            const int hh = idx / (nv2 >> 1), c = idx - hh * (nv2 >> 1);
+            cp_async16_cg(sml + ((size_t)hh * nv2 + 2 * c) * 2, a.part_ml + ((size_t)(hb + hh) * a.nsplit + 2 * c) * 2);
+        }
+        cp_async_wait_all();
+        csync();
+        // per (head, split): its weight exp(m_s - M) / L, M the head's largest
+        // split maximum and L the weighted sum of the split sums (one warp per
+        // head); the weights replace the (m, l) pairs in shared memory
+        for (int hh = (int)(threadIdx.x >> 5); hh < nh; hh += kMegaCW) {
+            const int lane = threadIdx.x & 31;
+            float* ml = sml + (size_t)hh * nv2 * 2;
+            float M = -INFINITY;
+            for (int sp = lane; sp < nv; sp += 32) M = fmaxf(M, ml[2 * sp]);
+            M = warp_max(M);
+            float L = 0.0f;
+            for (int sp = lane; sp < nv; sp += 32) {
+                const float m = ml[2 * sp];
+                L = __fmaf_rn(m == -INFINITY ? 0.0f : expf(m - M), ml[2 * sp + 1], L);
+            }
+            L = warp_sum(L);
+            __syncwarp();
+            for (int sp = lane; sp < nv; sp += 32) {
+                const float m = ml[2 * sp];
+                ml[2 * sp] = (m == -INFINITY || M == -INFINITY) ? 0.0f : __fdiv_rn(expf(m - M), L);
+            }
+        }
+        csync();
+        const int e0 = max(c0, hb * hd), e1 = min(c1, (hb + nh) * hd);
+        for (int e = e0 + tid; e < e1; e += nthr) {
+            const int hh = e / hd - hb, dd = e - (hb + hh) * hd;
+            const float* wv = sml + (size_t)hh * nv2 * 2;
+            const float* po = so + (size_t)hh * nv * hd + dd;
+            float O = 0.0f;
+            for (int sp = 0; sp < nv; sp++) O = __fmaf_rn(wv[2 * sp], po[(size_t)sp * hd], O);
+            x_s[e] = O;
+        }
+        csync();
+    }
+}
+
 // L2 prefetch of the cached K/V rows (and their scales) that this CTA's
 // attention items of `layer` will read: issued a phase ahead, so the items
 // find them in L2 instead of queueing behind the weight stream in HBM.
-static __device__ void prefetch_attn_rows(const MegaArgs& a, int layer, int pos, int nvalid) {
+static __device__ void prefetch_attn_rows(const MegaArgs& a, int layer, int pos, int chunk, int nvalid) {
     const int ngrp = a.H / a.KV / a.gsz, n_items = a.KV * ngrp * nvalid;
     int last = -1;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
@@ -1001,7 +1050,7 @@ static __device__ void prefetch_attn_rows(const MegaArgs& a, int layer, int pos,
         const int key = kv_h * nvalid + split;
         if (key == last) continue;
         last = key;
-        const int j0 = split * a.chunk, jb = min(j0 + a.chunk, pos);  // cached rows of the item
+        const int j0 = split * chunk, jb = min(j0 + chunk, pos);  // cached rows of the item
         if (jb <= j0) continue;
         const size_t row0 = ((size_t)layer * a.KV + kv_h) * a.max_seq + j0;
         const uint32_t kvb = (uint32_t)((jb - j0) * a.hd);
@@ -1027,9 +1076,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     uint64_t* abar = empty + kMegaMaxSlots;  // attention K/V copies
     static_assert(kMegaMaxSlots * 2 * 8 + 8 <= 128, "mbarriers exceed the shared-memory header");
     unsigned char* xs_region = sm + 128;
-    float* x_s = reinterpret_cast<float*>(xs_region);
-    int8_t* xd = reinterpret_cast<int8_t*>(xs_region + (size_t)a.kmax * 4);
-    float* xsc = reinterpret_cast<float*>(xs_region + (size_t)a.kmax * 7);
+    float* x_s = reinterpret_cast<float*>(xs_region);  // kx floats, then the digits of up to kmax
+    int8_t* xd = reinterpret_cast<int8_t*>(xs_region + (size_t)a.kx * 4);
+    float* xsc = reinterpret_cast<float*>(xs_region + (size_t)a.kx * 4 + (size_t)a.kmax * 3);
     unsigned char* ring = sm + 128 + a.xs_bytes;
     __shared__ float s_part[kMegaCW * kMegaRT];
     __shared__ float s_res[kMegaRT];
@@ -1079,18 +1128,26 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     const int pos = (*(volatile const int*)&st->len) - 1;
     const unsigned int base = *(volatile const unsigned int*)&st->bar_base;
     const unsigned int xb = *(volatile const unsigned int*)&st->xbase;  // tensor-parallel exchange epoch
+    // attention arrival counters of this step: [apar][L][KV] (the other half,
+    // the previous step's, is cleared layer by layer during this one)
+    const unsigned int apar = *(volatile const unsigned int*)&st->apar & 1u;
     const unsigned int nct = gridDim.x;
     int bi = 0;
     uint32_t aph = 0;  // parity of abar's current phase
     bool ok = true;
-    const int nvalid = min(pos / a.chunk + 1, a.nsplit);
+    // positions per attention split at this context: about per_head splits
+    // per kv head (at least chunk_min positions, a multiple of 64)
+    int chunk = (pos + a.per_head) / a.per_head;
+    chunk = max(a.chunk_min, (chunk + 63) / 64 * 64);
+    const int nvalid = (pos + chunk) / chunk;
+    const int ngrp = a.H / a.KV / a.gsz;  // query-head groups per kv head
 #define TRACE(idx)                                                               \
     do {                                                                         \
         if (a.trace != nullptr && tid == 0) a.trace[(size_t)b * kMegaTracePts + (idx)] = clock64(); \
     } while (0)
     TRACE(0);
     if (a.kv_prefetch && tid == 0 && (a.win0 & 1) == 0 && a.win0 < 2 * a.L)
-        prefetch_attn_rows(a, a.win0 >> 1, pos, nvalid);
+        prefetch_attn_rows(a, a.win0 >> 1, pos, chunk, nvalid);
 
     // half-layer phases p = 2 l + h of this launch's window (h 0: QKV,
     // attention, O; h 1: gate/up, down); p = 2 L is the LM head
@@ -1134,24 +1191,38 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             TRACE(tb + 2);
             if (!ok) break;
             // attention items (kv head, split), round-robin over CTAs
-            const int ngrp = a.H / a.KV / a.gsz;  // query-head groups per kv head
+            unsigned int* acnt = a.acnt + ((size_t)apar * a.L + l) * a.KV;
+            if (b == 0 && tid == 0)  // the previous step's counters of this layer: long read
+                for (int kv = 0; kv < a.KV; kv++) a.acnt[((size_t)(apar ^ 1u) * a.L + l) * a.KV + kv] = 0u;
             for (int it = b; it < a.KV * ngrp * nvalid && ok; it += nct) {
                 long long* tr = (a.trace && it == b) ? a.trace + (size_t)b * kMegaTracePts + tb + 14 : nullptr;
                 const int kv_h = it / (ngrp * nvalid), rem = it - kv_h * ngrp * nvalid, gr = rem / nvalid;
-                ok = attn_item<MAXG, HD>(a, l, kv_h, gr, rem - gr * nvalid, nvalid, pos, xs_region, abar, aph,
-                                         &s_ok, tr);
+                ok = attn_item<MAXG, HD>(a, l, kv_h, gr, rem - gr * nvalid, chunk, pos, xs_region, abar, aph,
+                                         acnt, tr);
             }
             if (!ok) break;
             // the next layer's cached K/V rows travel to L2 meanwhile
             if (a.kv_prefetch && tid == 0 && l + 1 < a.L && 2 * (l + 1) < a.win1)
-                prefetch_attn_rows(a, l + 1, pos, nvalid);
+                prefetch_attn_rows(a, l + 1, pos, chunk, nvalid);
             TRACE(tb + 3);
-            ok = grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
-            TRACE(tb + 4);
-            if (!ok) break;
-            // O projection (partials; the residual add happens in the next reader)
-            x_load(x_s, a.attn, a.H * a.hd);  // merged attention rows
-            x_digitize(x_s, a.H * a.hd, xd, xsc);
+            // O projection (partials; the residual add happens in the next
+            // reader). No grid barrier: a CTA waits for the attention items of
+            // the kv heads whose query heads its columns hold, merges their
+            // splits into its columns of the attention rows and digitises them.
+            {
+                const MatRange R = mat_range(ly.o, b);
+                if (R.r1 > R.r0) {
+                    const int c0 = R.cb0 * kMegaCB, c1 = min(R.cb1 * kMegaCB, a.H * a.hd);
+                    const int gw = (a.H / a.KV) * a.hd;  // attention columns of one kv head
+                    ok = attn_wait(acnt, c0 / gw, (c1 - 1) / gw, (unsigned int)(ngrp * nvalid), a.err, &s_ok);
+                    if (!ok) break;
+                    TRACE(tb + 4);
+                    attn_merge(a, x_s, c0, c1, nvalid);
+                    x_digitize(x_s, a.H * a.hd, xd, xsc, c0 >> 5, c1 >> 5);
+                } else {
+                    TRACE(tb + 4);
+                }
+            }
             TRACE(tb + 5);
             if (TP) {
                 ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err,
@@ -1183,9 +1254,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
             TRACE(tb + 10);
             if (!ok) break;
-            // down projection + residual
-            x_load(x_s, a.h, a.F);
-            x_digitize(x_s, a.F, xd, xsc);
+            // down projection + residual (SwiGLU rows digitised from L2)
+            x_digitize<true>(a.h, a.F, xd, xsc);
             TRACE(tb + 11);
             if (TP) {
                 ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best, a.err,
@@ -1265,6 +1335,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         st->amax = 0ull;
         st->bar_base = base + (unsigned int)bi * nct;
         if (TP) st->xbase = xb + (unsigned int)a.L;
+        st->apar = apar ^ 1u;
         st->fresh = 0;
         if (stop) st->active = 0;
         __threadfence();
@@ -1296,10 +1367,22 @@ int mega_prefetch_tiles(int ns) {
 // `splittable`, at most kMaxParts groups) the least rows per CTA that fit the
 // CTAs, costed as the bytes one CTA streams + a hand-off cost per tile + an
 // epilogue cost per row tile + the readers' extra round trips; the cheapest
-// wins (fewer groups on ties).
-int mega_plan(MegaMat& m, int nctas, bool splittable) {
+// wins (fewer groups on ties). only_cpg > 0 asks for that many column blocks
+// per group instead (when the groups fit).
+int mega_plan(MegaMat& m, int nctas, bool splittable, int only_cpg) {
     if (m.n <= 0 || m.n % 16 || m.k % 32 || m.k <= 0) return JYC_ERR_UNSUPPORTED;
     const int ncb = (m.k + kMegaCB - 1) / kMegaCB;
+    if (only_cpg > 0 && (ncb + only_cpg - 1) / only_cpg <= std::min(nctas, kMaxParts)) {
+        // the caller's split: only_cpg column blocks per group
+        const int cpg = std::min(only_cpg, ncb), spl = (ncb + cpg - 1) / cpg;
+        int rpc = (m.n + nctas / spl - 1) / (nctas / spl);
+        rpc = (rpc + 15) / 16 * 16;
+        m.rpc = rpc;
+        m.rt = std::min(kMegaRT, rpc);
+        m.spl = spl;
+        m.cpg = cpg;
+        return JYC_OK;
+    }
     // readers sum the groups two at a time: every pair beyond the first costs
     // them one more L2 round trip
     const double kTileCost = 8192.0, kRowTileCost = 24576.0, kGroupCost = 2048.0, kTripCost = 24576.0;
@@ -1325,19 +1408,23 @@ int mega_plan(MegaMat& m, int nctas, bool splittable) {
     return JYC_OK;
 }
 
-// x (4 B) + three digit planes (3 B) + block scales (1/8 B) per element; the
-// attention item's plan (sub-chunks of S positions) shares the region.
-int mega_xs_bytes(int kmax, int G, int hd, int S) {
-    const int xk = kmax * 4 + kmax * 3 + (kmax / 32) * 4;
+// x (4 B per element of the longest row kept in shared memory, kx) + three
+// digit planes (3 B) + block scales (1/8 B) per element of the longest GEMV
+// input (kmax); the attention item's plan (sub-chunks of S positions) shares
+// the region.
+static int mega_xk_bytes(int kx, int kmax) { return kx * 4 + kmax * 3 + (kmax / 32) * 4; }
+
+int mega_xs_bytes(int kx, int kmax, int G, int hd, int S) {
+    const int xk = mega_xk_bytes(kx, kmax);
     const int samp = (kSampleThreads + 1) * (int)sizeof(double);  // the sampler's scratch (head phase)
     return (std::max(std::max(xk, samp), attn_plan(G, hd, S).total) + 127) / 128 * 128;
 }
 
 // Attention sub-chunk: the split length rounded up to a power of two, halved
-// while the item's plan would need more than max(x region, 96 KB).
-int mega_attn_sub(int kmax, int G, int hd, int chunk) {
-    const int xk = kmax * 4 + kmax * 3 + (kmax / 32) * 4;
-    const int cap = std::max(xk, 96 * 1024);
+// while the item's plan would need more than max(x region, attn_cap bytes).
+int mega_attn_sub(int kx, int kmax, int G, int hd, int chunk, int attn_cap) {
+    const int xk = mega_xk_bytes(kx, kmax);
+    const int cap = std::max(xk, attn_cap);
     int S = 16;
     while (S < chunk) S <<= 1;
     while (S > 16 && attn_plan(G, hd, S).total > cap) S >>= 1;

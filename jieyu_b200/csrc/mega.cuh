@@ -78,16 +78,19 @@ struct MegaArgs {
     unsigned int* stag;       // the sampler's penalty tags [2 V]
     float* part_o;            // attention split partials [H][nsplit][hd]
     float* part_ml;           // [H][nsplit][2]
-    int chunk, nsplit;
+    int chunk, nsplit;        // largest split length (at max_seq), split stride of part_o / part_ml
+    int per_head;             // splits per kv head a step aims at (positions per split follow the context)
+    int chunk_min;            // shortest split length
     int asub;                 // attention sub-chunk (power of two, positions per K/V copy)
     int gsz;                  // query heads per attention item (a divisor of H / KV)
-    unsigned int* acnt;       // per kv head: finished split items of the current layer
+    unsigned int* acnt;       // [L][KV]: finished attention items of (layer, kv head) in this step
     float scale;              // 1/sqrtf(hd)
     DevState* st;
     int* tokens;
     unsigned int* bar;        // grid-barrier counter (monotonic)
     int* err;                 // device error word
-    int kmax;                 // largest GEMV input length (x / digit buffers)
+    int kmax;                 // largest GEMV input length (digit buffers)
+    int kx;                   // longest row kept as floats in shared memory (max(D, H hd))
     int xs_bytes;             // shared bytes of the x / digits / attention union
     int nslots;               // ring depth
     int pf_tiles;             // L2 prefetch distance of the copy issuer, in tiles beyond the ring (0: none)
@@ -116,10 +119,10 @@ constexpr int kMegaTracePts = 1 + 64 * kMegaTraceLayer + 4;  // up to 64 layers
 
 int launch_q8_repack_tiled(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d, int n_total,
                            int row_off, int row_stride, cudaStream_t s);
-int mega_plan(MegaMat& m, int nctas, bool splittable);
+int mega_plan(MegaMat& m, int nctas, bool splittable, int only_cpg = 0);
 int mega_smem_bytes(const MegaArgs& a);
-int mega_xs_bytes(int kmax, int G, int hd, int S);
-int mega_attn_sub(int kmax, int G, int hd, int chunk);
+int mega_xs_bytes(int kx, int kmax, int G, int hd, int S);
+int mega_attn_sub(int kx, int kmax, int G, int hd, int chunk, int attn_cap);
 int mega_num_ctas();
 int mega_prefetch_tiles(int ns);
 int launch_mega_step(const MegaArgs& a, cudaStream_t s);

@@ -259,14 +259,32 @@ bool mega_eligible(const jyc_model* m, const jyc_model_desc* d) {
     return (m->hd == 64 || m->hd == 128) && m->H / m->KV <= 8;
 }
 
-MegaMat mega_mat(const DevMat& w, int nctas, bool splittable) {
+MegaMat mega_mat(const DevMat& w, int nctas, bool splittable, int only_cpg = 0) {
     MegaMat mm{};
     mm.qs = w.tq;
     mm.d = w.td;
     mm.n = w.n;
     mm.k = w.k;
-    mega_plan(mm, nctas, splittable);
+    mega_plan(mm, nctas, splittable, only_cpg);
     return mm;
+}
+
+// Shared bytes an attention item's plan may take before its sub-chunk is
+// halved (JYC_MEGA_ATTN_CAP in KB overrides: tuning of ring depth against
+// attention copies).
+static int mega_attn_cap() {
+    int kb = 96;
+    if (const char* e = std::getenv("JYC_MEGA_ATTN_CAP")) kb = std::max(8, std::atoi(e));
+    return kb * 1024;
+}
+
+// Column blocks per group of the O projection: one (each group then waits
+// only for the attention items of the kv heads inside its 512 columns and
+// merges just those). JYC_MEGA_O_CPG overrides it (0: the cost model).
+static int mega_o_cpg() {
+    int c = 1;
+    if (const char* e = std::getenv("JYC_MEGA_O_CPG")) c = std::max(0, std::atoi(e));
+    return c;
 }
 
 int setup_mega(jyc_model* m) {
@@ -281,7 +299,7 @@ int setup_mega(jyc_model* m) {
         // QKV, O and down may split K (their readers sum the partials);
         // gate/up (SwiGLU) and the LM head (argmax) need whole rows
         ml[l].qkv = mega_mat(ly.qkv, nctas, true);
-        ml[l].o = mega_mat(ly.o, nctas, true);
+        ml[l].o = mega_mat(ly.o, nctas, true, mega_o_cpg());
         ml[l].gu = mega_mat(ly.gateup, nctas, false);
         ml[l].dn = mega_mat(ly.down, nctas, true);
         sq = std::max(sq, ml[l].qkv.spl);
@@ -316,12 +334,19 @@ int setup_mega(jyc_model* m) {
     TRY(m->alloc(&a.po, (size_t)so * m->D));
     TRY(m->alloc(&a.pd, (size_t)sd * m->D));
     TRY(m->alloc(&a.attn, (size_t)m->q_dim));
-    // attention split plan: about one (kv head, split) item per CTA at full context
+    // attention split plan: about one (kv head, split) item per CTA at the
+    // step's context (the kernel sizes the splits from the position: at
+    // least chunk_min positions, a multiple of 64; at most `chunk`, the
+    // length at max_seq, which sizes the sub-chunk copies)
     const int per_head = std::max(1, nctas / m->KV);
     int chunk = (m->max_seq + per_head - 1) / per_head;
     chunk = std::max(128, (chunk + 63) / 64 * 64);  // >= 128: few splits to merge at short contexts
     a.chunk = chunk;
-    a.nsplit = (m->max_seq + chunk - 1) / chunk;
+    a.chunk_min = 128;
+    a.per_head = per_head;
+    const int nsplit_max = (m->max_seq + chunk - 1) / chunk;  // splits at max_seq
+    a.nsplit = std::max(nsplit_max, per_head);                // any step has at most per_head
+    a.nsplit += a.nsplit & 1;  // even: a head's (m, l) pairs are whole 16-byte chunks
     TRY(m->alloc(&a.part_o, (size_t)m->H * a.nsplit * m->hd));
     TRY(m->alloc(&a.part_ml, (size_t)m->H * a.nsplit * 2));
     a.scale = 1.0f / sqrtf((float)m->hd);
@@ -331,14 +356,22 @@ int setup_mega(jyc_model* m) {
     JYC_CUDA(cudaMemset(a.bar, 0, sizeof(unsigned int)));
     a.err = device_error_word();
     a.kmax = std::max({m->D, m->q_dim, m->F});
+    a.kx = std::max(m->D, m->q_dim);
     // attention items: one per (kv head, split) at long contexts; one per
     // (query head, split) when those fit the CTAs at full context (short
     // contexts: more parallelism, fewer splits to merge per item)
-    a.gsz = (m->KV * (m->H / m->KV) * a.nsplit <= nctas) ? 1 : m->H / m->KV;
-    a.asub = mega_attn_sub(a.kmax, m->H / m->KV, m->hd, a.chunk);
-    a.xs_bytes = mega_xs_bytes(a.kmax, m->H / m->KV, m->hd, a.asub);
-    TRY(m->alloc(&a.acnt, (size_t)m->H));  // one per (kv head, query-head group)
-    JYC_CUDA(cudaMemset(a.acnt, 0, sizeof(unsigned int) * m->H));
+    a.gsz = (m->KV * (m->H / m->KV) * nsplit_max <= nctas) ? 1 : m->H / m->KV;
+    a.asub = mega_attn_sub(a.kx, a.kmax, m->H / m->KV, m->hd, a.chunk, mega_attn_cap());
+    a.xs_bytes = mega_xs_bytes(a.kx, a.kmax, m->H / m->KV, m->hd, a.asub);
+    // the x region also stages one head's split partials behind the
+    // attention rows, and a 16-byte slice of up to 8 x 8 partial rows (+ the
+    // base row) behind the residual row
+    a.xs_bytes = std::max({a.xs_bytes, 4 * (m->q_dim + a.nsplit * m->hd + 2 * a.nsplit),
+                           4 * (m->D + (kMegaMaxTP * 8 + 1) * 4)});
+    a.xs_bytes = (a.xs_bytes + 127) / 128 * 128;
+    // attention arrival counters: [2][L][KV] (two steps' worth; see the kernel)
+    TRY(m->alloc(&a.acnt, (size_t)2 * m->L * m->KV));
+    JYC_CUDA(cudaMemset(a.acnt, 0, sizeof(unsigned int) * 2 * m->L * m->KV));
     // ring as deep as the shared memory allows (227 KB per CTA, at least 2 slots)
     const int st_smem = mega_static_smem(a.gsz, m->hd);
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
@@ -777,6 +810,14 @@ JYC_API double jyc_model_kv_bytes_per_token(const jyc_model* m, int ctx) {
     return (double)m->L * m->KV * ctx * (2.0 * m->hd + 8.0);
 }
 
+// (Re)starts the device step state; a decode-kernel model also clears its
+// attention arrival counters (a step that gave up part-way leaves them dirty).
+static int set_state(jyc_model* m, int len, int max_new, int max_len, const int* eos, int n_eos, cudaStream_t s) {
+    if (m->mega && m->margs.acnt)
+        JYC_CUDA(cudaMemsetAsync(m->margs.acnt, 0, sizeof(unsigned int) * 2 * m->L * m->KV, s));
+    return launch_set_state(m->st, len, max_new, max_len, eos, n_eos, s);
+}
+
 JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_pos, float* logits,
                                float* hidden_out) {
     clear_error();
@@ -789,7 +830,7 @@ JYC_API int jyc_forward_logits(jyc_model* m, const int* ids, int seq, int start_
         if (ids[i] < 0 || ids[i] >= m->Ve) return arg_error("forward_logits: token id out of range");
     cudaStream_t s = m->stream;
     JYC_CUDA(cudaMemcpyAsync(m->tokens + start_pos, ids, seq * sizeof(int), cudaMemcpyHostToDevice, s));
-    TRY(launch_set_state(m->st, start_pos + seq, 1 << 30, m->max_seq + 1, nullptr, 0, s));
+    TRY(set_state(m, start_pos + seq, 1 << 30, m->max_seq + 1, nullptr, 0, s));
     if (seq == 1 && m->mega) {
         // a single token goes through the decode kernel (the path generate's steps use)
         TRY(launch_mega_step(m->margs, s));
@@ -830,6 +871,34 @@ JYC_API int jyc_model_read_kv(jyc_model* m, int layer, int npos, int8_t* k, floa
     return JYC_OK;
 }
 
+JYC_API int jyc_model_write_kv(jyc_model* m, int layer, int npos, const int8_t* k, const float* ks, const int8_t* v,
+                               const float* vs) {
+    clear_error();
+    if (!m || layer < 0 || layer >= m->L || npos < 0 || npos > m->max_seq || !k || !ks || !v || !vs)
+        return arg_error("write_kv: bad arguments");
+    if (npos == 0) return JYC_OK;
+    JYC_CUDA(cudaStreamSynchronize(m->stream));
+    const KVView kv = m->kv_layer(layer);
+    // reference order [pos][kv head] -> the device's [kv head][pos], one copy per head
+    std::vector<int8_t> kb((size_t)npos * m->hd), vb(kb.size());
+    std::vector<float> ksb((size_t)npos), vsb(ksb.size());
+    for (int h = 0; h < m->KV; h++) {
+        for (int p = 0; p < npos; p++) {
+            const size_t src = (size_t)p * m->KV + h;
+            std::memcpy(kb.data() + (size_t)p * m->hd, k + src * m->hd, m->hd);
+            std::memcpy(vb.data() + (size_t)p * m->hd, v + src * m->hd, m->hd);
+            ksb[p] = ks[src];
+            vsb[p] = vs[src];
+        }
+        const size_t row0 = (size_t)h * m->max_seq;
+        JYC_CUDA(cudaMemcpy(kv.k + row0 * m->hd, kb.data(), kb.size(), cudaMemcpyHostToDevice));
+        JYC_CUDA(cudaMemcpy(kv.v + row0 * m->hd, vb.data(), vb.size(), cudaMemcpyHostToDevice));
+        JYC_CUDA(cudaMemcpy(kv.ks + row0, ksb.data(), ksb.size() * 4, cudaMemcpyHostToDevice));
+        JYC_CUDA(cudaMemcpy(kv.vs + row0, vsb.data(), vsb.size() * 4, cudaMemcpyHostToDevice));
+    }
+    return JYC_OK;
+}
+
 JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, const int* eos_ids, int num_eos,
                          int max_new_tokens, float temperature, int* out_ids, float repetition_penalty,
                          jyc_token_cb cb, void* cb_ud) {
@@ -850,7 +919,7 @@ JYC_API int jyc_generate(jyc_model* m, const int* prompt_ids, int prompt_len, co
     cudaStream_t s = m->stream;
     TRY(ensure_step_graph(m));
     JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids, prompt_len * sizeof(int), cudaMemcpyHostToDevice, s));
-    TRY(launch_set_state(m->st, prompt_len, max_new_tokens, m->max_seq, eos_ids, num_eos, s));
+    TRY(set_state(m, prompt_len, max_new_tokens, m->max_seq, eos_ids, num_eos, s));
     // the reference's sampler state: LCG seed 12345 per call (generate.h:36)
     if (sampling) {
         TRY(launch_set_sampling(m->st, temperature, repetition_penalty, 12345u, prompt_len, s));
@@ -910,7 +979,7 @@ JYC_API int jyc_prefill_device(jyc_model* m, const int* prompt_ids_dev, int prom
         return arg_error("prefill_device: bad arguments");
     cudaStream_t s = (cudaStream_t)stream;  // as given: 0 is the legacy default stream
     JYC_CUDA(cudaMemcpyAsync(m->tokens, prompt_ids_dev, prompt_len * sizeof(int), cudaMemcpyDeviceToDevice, s));
-    TRY(launch_set_state(m->st, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s));
+    TRY(set_state(m, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s));
     return run_prefill(m, 0, prompt_len, s);
 }
 
@@ -943,7 +1012,7 @@ JYC_API int jyc_model_rewind(jyc_model* m, int len, void* stream) {
     clear_error();
     if (!m || len <= 0 || len >= m->max_seq) return arg_error("rewind: bad length");
     cudaStream_t s = (cudaStream_t)stream;  // as given: 0 is the legacy default stream
-    return launch_set_state(m->st, len, 1 << 30, m->max_seq, nullptr, 0, s);
+    return set_state(m, len, 1 << 30, m->max_seq, nullptr, 0, s);
 }
 
 JYC_API int jyc_decode_device(jyc_model* m, int n_steps, void* stream) {
@@ -1451,7 +1520,7 @@ JYC_API int jyc_batch_prefill(jyc_batch* bt, int seq, const int* prompt_ids, int
     m->ks = bt->ks + (size_t)seq * bt->slot_s;
     m->vs = bt->vs + (size_t)seq * bt->slot_s;
     m->tokens = tok;
-    int r = launch_set_state(m->st, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s);
+    int r = set_state(m, prompt_len, 1 << 30, m->max_seq, nullptr, 0, s);
     if (r == JYC_OK) r = run_prefill(m, 0, prompt_len, s);
     m->k8 = k8; m->v8 = v8; m->ks = ks; m->vs = vs; m->tokens = tokens;
     TRY(r);

@@ -61,10 +61,11 @@ CONFIGS = {
     "c1": Config("c1_qwen2.5_0.5b", 896, 24, 14, 2, 64, 4864, 151936, 1e6, "q8", "tied", True,
                  1024, 512, 256),
     # Llama-3.2-1B shape (Q8_0 and fp32 variants)
+    # max_seq covers the longest decode context it is measured at (16384) + steps
     "c2": Config("c2_llama3.2_1b", 2048, 16, 32, 8, 64, 8192, 128256, 5e5, "q8", "q8", False,
-                 4352, 2048, 128),
+                 16512, 2048, 128),
     "c2f": Config("c2_llama3.2_1b_f32", 2048, 16, 32, 8, 64, 8192, 128256, 5e5, "f32", "f32",
-                  False, 4352, 2048, 128),
+                  False, 16512, 2048, 128),
     # Llama-3-8B shape
     "c3": Config("c3_llama3_8b", 4096, 32, 32, 8, 128, 14336, 128256, 5e5, "q8", "q8", False,
                  4352, 4096, 128),
@@ -391,6 +392,16 @@ class DeviceModel:
         vs = np.empty_like(ks)
         check(self.lib.jyc_model_read_kv(self.h, layer, npos, _ptr(k), _ptr(ks), _ptr(v), _ptr(vs)))
         return k, ks, v, vs
+
+    def write_kv(self, layer: int, k: np.ndarray, ks: np.ndarray, v: np.ndarray, vs: np.ndarray) -> None:
+        """Positions [0, npos) of one layer's cache from host arrays in the
+        reference's __KVcache order (k, v int8 [npos][kv][hd]; ks, vs fp32 [npos][kv])."""
+        cfg = self.cfg
+        npos = len(ks) // cfg.kv_heads
+        k, v = (np.ascontiguousarray(a, dtype=np.int8) for a in (k, v))
+        ks, vs = (np.ascontiguousarray(a, dtype=np.float32) for a in (ks, vs))
+        assert k.size == npos * cfg.kv_dim and v.size == k.size and vs.size == ks.size
+        check(self.lib.jyc_model_write_kv(self.h, layer, npos, _ptr(k), _ptr(ks), _ptr(v), _ptr(vs)))
 
     # device-resident stepping (bench)
     def prefill_device(self, ids_dev_ptr: int, n: int, stream: int) -> None:

@@ -79,3 +79,17 @@ def test_reference_build_still_matches_golden():
     want = golden("ops.json")["ops"]
     got = make_golden.run_ops(ref)
     assert got == want
+
+
+@pytest.mark.parametrize("name", ["c2_4096_2l", "c2_16384_2l"])
+def test_oracle_long_context_matches_reference(oracle, name):
+    """Teacher-forced steps from a seeded 4096- / 16384-position int8 K/V
+    context (tests/golden/longctx.json, the reference's own fma path): the
+    oracle's logits are bit-identical at every step."""
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import make_golden_longctx as mgl
+    case = golden("longctx.json")[name]
+    hw = HostWeights.synthetic(mgl.long_cfg(case["config"], case["ctx"], case["layers"]))
+    out, fed = mgl.run(oracle, hw, case["ctx"], None)
+    assert fed == case["fed"]
+    assert [sha(x) for x in out] == [r["sha"] for r in case["steps"]]
