@@ -199,6 +199,9 @@ JYC_API int jyc_attention_q8(const float* Q, const float* K, const float* V, flo
  * it); larger calls return JYC_ERR_ARG before launching anything. The first
  * call on a device resolves the array's address (cudaGetSymbolAddress with
  * that device current): make that first call before any stream capture. The
+ * address is kept per device for the life of the process; after
+ * cudaDeviceReset (or anything else that tears down the device's primary
+ * context) it is stale, so do not call this entry point again after a reset. The
  * arrival counters must be zero when a call starts: they are at load and
  * every completed call leaves them so. Calls overlapping in time (other
  * streams, other host threads) share the array and race: serialise them. */

@@ -55,8 +55,8 @@ constexpr int kMegaThreads = (kMegaCW + 1) * 32;  // consumer warps + one copy-i
 
 // Error word of the device kernels (non-zero: a bounded wait gave up; the
 // value tells which: 3 ring slot free, 4 ring slot full, 5 grid barrier,
-// 6 attention K/V copy, 7 prefill digit copy, 8 tensor-parallel exchange,
-// 9 attention arrivals before the O projection).
+// 7 prefill digit copy, 8 tensor-parallel exchange, 9 attention arrivals
+// before the O projection).
 __device__ int g_err_word;
 
 int* device_error_word() {
@@ -174,13 +174,6 @@ static __device__ __forceinline__ void load_tile(const MegaMat& M, int r0, int r
              pol);
 }
 
-// The same tile, prefetched into L2 only (runs ahead of the ring).
-static __device__ __forceinline__ void prefetch_tile(const MegaMat& M, int r0, int rows, int cb) {
-    const int w = min(kMegaCB, M.k - cb * kMegaCB);
-    bulk_prefetch_l2(M.qs + (size_t)cb * M.n * kMegaCB + (size_t)r0 * w, (uint32_t)(rows * w));
-    bulk_prefetch_l2(M.d + (size_t)cb * M.n * (kMegaCB / 32) + (size_t)r0 * (w / 32), (uint32_t)(rows * (w / 32) * 2));
-}
-
 // Walk over one CTA's tiles of the whole step, in consumer order: per layer
 // QKV, O, gate/up, down, then the LM head (l == L). Row tiles outer, column
 // blocks inner, as consume_mat takes them.
@@ -236,25 +229,13 @@ static __device__ bool cursor_next(const StepMats& sm, TileCursor& c, int b) {
 // Producer (one thread): every tile of the step into the ring, in consumer
 // order, a slot refilled as soon as every consumer warp released it. It never
 // waits on activations, so weights keep streaming across the grid barriers.
-// A second cursor runs `pf` tiles ahead of the ring and prefetches them into
-// L2: while the consumers wait (grid barriers, attention) HBM keeps filling
-// L2 with the tiles they take next, and those later arrive at L2 speed.
-static __device__ bool produce_step(const StepMats& smats, int l0, int m0, int b, int ns, int pf, uint64_t* full,
+static __device__ bool produce_step(const StepMats& smats, int l0, int m0, int b, int ns, uint64_t* full,
                                     uint64_t* empty, unsigned char* ring, int* err) {
     const uint64_t pol = policy_evict_first();
     TileCursor c{l0, m0, 0, 0, 0, 0, 0, nullptr};
     bool have = cursor_enter(smats, c, b);
-    TileCursor pc = c;
-    bool pf_have = have;
-    int pt = 0;  // tiles the prefetch cursor has passed
     RingPos rp{0, 0};
-    if (pf <= 0) pf_have = false;
     for (int t = 0; have; t++) {
-        while (pf_have && pt < t + pf) {  // the ring's first ns tiles need no prefetch
-            if (pt >= ns) prefetch_tile(*pc.M, pc.r0, min(pc.M->rt, pc.r_end - pc.r0), pc.cb);
-            pf_have = cursor_next(smats, pc, b);
-            pt++;
-        }
         if (t >= ns && !mbar_wait_err(&empty[rp.s], rp.ph ^ 1, err, 3)) return false;
         load_tile(*c.M, c.r0, min(c.M->rt, c.r_end - c.r0), c.cb, ring + (size_t)rp.s * kMegaSlotBytes, &full[rp.s],
                   pol);
@@ -603,41 +584,40 @@ static __device__ bool grid_barrier(unsigned int* ctr, unsigned int target, int*
     return *s_ok != 0;
 }
 
-// Shared-memory plan of one attention item (byte offsets inside the region
-// the x vector also uses): K and V sub-chunk tiles (TMA destinations; after
-// the PV loop the same bytes hold the cross-warp partial sums, and in the
-// split merge the (m, l) pairs and merge weights), scores, K/V scales, the
-// quantised query heads, the new position's K/V row, softmax state.
+// Shared-memory plan of one attention item (byte offsets inside the x
+// region): the quantised query heads, their scales, the new position's K and
+// V rows (+ their two scales), then per consumer warp its K/V tiles
+// ([nb][kAttTR][hd] each, 16-byte chunks rotated per row) and the tile's
+// weights ([kAttTR][maxg]); after the tiles the same bytes hold the warps'
+// (m, l, o) for the cross-warp merge.
+constexpr int kAttTR = 16;  // positions per warp tile (two lanes per position)
+
 struct AttnPlan {
-    int kv, sc, ks, vs, q8, row, qsc, m, l, al, total;
+    int q8, qsc, row, warps, wbytes, total;
 };
 
-static __host__ __device__ __forceinline__ AttnPlan attn_plan(int G, int hd, int S) {
+static __host__ __device__ __forceinline__ AttnPlan attn_plan(int maxg, int hd, int nb) {
     AttnPlan p;
-    const int red = kMegaCW * G * hd * 4;  // partial rows of the P.V reduction
     int o = 0;
-    p.kv = o;
-    o += (max(2 * S * hd, red) + 15) / 16 * 16;
-    p.sc = o;
-    o += G * S * 4;
-    p.ks = o;
-    o += S * 4;
-    p.vs = o;
-    o += S * 4;
     p.q8 = o;
-    o += (G * hd + 15) / 16 * 16;
+    o += (maxg * hd + 15) / 16 * 16;
+    p.qsc = o;
+    o += (maxg * 4 + 15) / 16 * 16;
     p.row = o;
     o += (2 * hd + 8 + 15) / 16 * 16;
-    p.qsc = o;
-    o += G * 4;
-    p.m = o;
-    o += G * 4;
-    p.l = o;
-    o += G * 4;
-    p.al = o;
-    o += G * 4;
+    p.warps = o;
+    p.wbytes = (nb * 2 * kAttTR * hd + kAttTR * maxg * 4 + 15) / 16 * 16;
+    const int merge = kMegaCW * (2 * maxg + maxg * hd) * 4;
+    o += max(kMegaCW * p.wbytes, merge);
     p.total = (o + 127) / 128 * 128;
     return p;
+}
+
+// physical 16-byte chunk of logical chunk c in tile row r (conflict-free
+// reads of 16 rows by two lanes each)
+template <int HD>
+static __device__ __forceinline__ int att_chunk(int c, int r) {
+    return HD == 128 ? ((c + r) & 7) : ((c + (r >> 1)) & 3);
 }
 
 // RoPE (when ct; rotated pairs stored in the reference's slot order) +
@@ -710,230 +690,282 @@ static __device__ __forceinline__ void rq_warp(const float* src, int nsrc, size_
     }
 }
 
-// P.V over one sub-chunk for a (column group of 4 dims, position lane)
-// thread: acc[g][i] += p[g][j] * v[j][4cg + i] for j = pl, pl + NPL, ...
-template <int MAXG, int HD>
-static __device__ __forceinline__ void attn_pv(float (&acc)[MAXG][4], const float* s_sc, const int8_t* s_v, int lS,
-                                               int G, int cg, int pl, int n) {
-    constexpr int NPL = kMegaCW * 32 / (HD / 4);
-    for (int j = pl; j < n; j += NPL) {
-        float f[4];
-        u8x4_to_f32(*reinterpret_cast<const uint32_t*>(s_v + j * HD + 4 * cg) ^ 0x80808080u, f);
-#pragma unroll
-        for (int gq = 0; gq < MAXG; gq++)
-            if (gq < G) {
-                const float p = s_sc[(gq << lS) + j];
-#pragma unroll
-                for (int i = 0; i < 4; i++) acc[gq][i] = __fmaf_rn(p, f[i], acc[gq][i]);
-            }
-    }
-}
-
-// One (layer, kv head, position split) attention item with the consumer
-// threads (reference: attention over the int8 cache, transformer_layer.h:35-70):
-// RoPE + int8 quantisation of the group's query heads, the K/V append at pos
-// (owner split), then per sub-chunk of up to S positions: a TMA bulk copy of
-// the K and V rows, int8 dot scores (dp4a, rotated word order so the 32 lanes
-// of a warp read 32 different banks of 32 different rows), online softmax,
-// P.V with V decoded once per 4 dims. Writes the split partials (o, m, l)
-// and counts itself in the (layer, kv head) arrival counter `cnt`; the O
-// projection's CTAs merge the splits of the heads they read.
+// One (layer, kv head, query-head group, position split) attention item
+// with the consumer warps (reference: attention over the int8 cache,
+// attention_q8.h:38-184 with the score scaling dot * ((ks * qs) * 1/sqrt(hd)),
+// fp32 softmax, the V scale folded into the weights). Each warp owns a
+// contiguous run of the split's positions and keeps its own online-softmax
+// state, so the position loop has no CTA-wide barrier: its K/V rows arrive by
+// 16-byte cp.async into the warp's tiles (issued before the query heads are
+// quantised, so the copies overlap that work; two tiles in flight when a warp
+// has more than one); lanes (r, h) score half h of row r against every query
+// head of the group (dp4a, halves added by one shuffle); each lane then
+// accumulates P.V for hd/32 dims of every head. The new position's K and V
+// (RoPE + kv_pack_q8 of the QKV rows, appended to the cache by the group-0
+// item) come from shared memory. The warps merge at the end; the item writes
+// its split partials (o, m, l) and counts itself in `cnt` (per kv head).
 template <int MAXG, int HD>
 static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, int kvh, int grp, int split,
-                                                 int chunk, int pos, unsigned char* sm, uint64_t* abar,
-                                                 uint32_t& aph, unsigned int* cnt, long long* tr) {
-    constexpr int hd = HD, half = HD / 2, hw = HD / 4, HC = HD / 16;  // words, 16-byte chunks per row
-    const int GA = a.H / a.KV, S = a.asub, lS = 31 - __clz(S);
-    const int G = a.gsz, g0 = grp * G;  // this item's query heads: kvh * GA + g0 .. + G
-#define ATR(k)                                      \
-    do {                                            \
+                                                 int chunk, int pos, unsigned char* sm, unsigned int* cnt,
+                                                 long long* tr) {
+    constexpr int half = HD / 2, HC = HD / 16, HH = HC / 2, DPL = HD / 32;
+    const int GA = a.H / a.KV, G = a.gsz, g0 = grp * G;
+    const int nb = a.att_nb;
+#define ATR(k)                                         \
+    do {                                               \
         if (tr && threadIdx.x == 0) tr[k] = clock64(); \
     } while (0)
     ATR(0);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    constexpr int nthr = kMegaCW * 32;
-    const AttnPlan P = attn_plan(GA, hd, S);
-    int8_t* s_k = reinterpret_cast<int8_t*>(sm + P.kv);
-    int8_t* s_v = s_k + S * hd;
-    float* s_sc = reinterpret_cast<float*>(sm + P.sc);
-    float* s_ks = reinterpret_cast<float*>(sm + P.ks);
-    float* s_vs = reinterpret_cast<float*>(sm + P.vs);
+    const AttnPlan P = attn_plan(MAXG, HD, nb);
     int8_t* s_q8 = reinterpret_cast<int8_t*>(sm + P.q8);
-    int8_t* s_row = reinterpret_cast<int8_t*>(sm + P.row);  // new K row | V row | k scale | v scale
-    float* s_rsc = reinterpret_cast<float*>(s_row + 2 * hd);
     float* s_qsc = reinterpret_cast<float*>(sm + P.qsc);
-    float* s_m = reinterpret_cast<float*>(sm + P.m);
-    float* s_l = reinterpret_cast<float*>(sm + P.l);
-    float* s_al = reinterpret_cast<float*>(sm + P.al);
+    int8_t* s_row = reinterpret_cast<int8_t*>(sm + P.row);  // new K row | V row | k scale | v scale
+    float* s_rsc = reinterpret_cast<float*>(s_row + 2 * HD);
+    unsigned char* wb = sm + P.warps + (size_t)warp * P.wbytes;
+    int8_t* tk = reinterpret_cast<int8_t*>(wb);                     // [nb][TR][HD]
+    int8_t* tv = tk + nb * kAttTR * HD;                             // [nb][TR][HD]
+    float* sp = reinterpret_cast<float*>(tv + nb * kAttTR * HD);    // [TR][MAXG]
 
     const int c0 = split * chunk, c1 = min(c0 + chunk, pos + 1);
     const size_t lh = (size_t)layer * a.KV + kvh;
-    int8_t* kb = a.k8 + lh * a.max_seq * hd;
-    int8_t* vb = a.v8 + lh * a.max_seq * hd;
+    int8_t* kb = a.k8 + lh * a.max_seq * HD;
+    int8_t* vb = a.v8 + lh * a.max_seq * HD;
     float* ksb = a.ks + lh * a.max_seq;
     float* vsb = a.vs + lh * a.max_seq;
     const float* ct = a.cos_t + (size_t)pos * half;
     const float* stb = a.sin_t + (size_t)pos * half;
-    const int q_dim = a.H * hd, kv_dim = a.KV * hd;
+    const int q_dim = a.H * HD, kv_dim = a.KV * HD;
     const bool owner = pos < c1;
 
-    // TMA of the cached rows [j0, min(j0 + S, c1, pos)) of a sub-chunk; false when none
-    auto issue = [&](int j0) -> bool {
-        const int jb = min(min(j0 + S, c1), pos);
-        if (jb <= j0) return false;
-        if (tid == 0) {
-            const uint32_t bytes = (uint32_t)((jb - j0) * hd);
-            fence_proxy_async_smem();
-            mbar_expect_tx(abar, 2 * bytes);
-            const uint64_t pol = policy_evict_first();
-            bulk_g2s(s_k, kb + (size_t)j0 * hd, bytes, abar, pol);
-            bulk_g2s(s_v, vb + (size_t)j0 * hd, bytes, abar, pol);
+    // this warp's positions [w0, w1); rows below pos come from the cache
+    const int per = (chunk + kMegaCW - 1) / kMegaCW;
+    const int w0 = c0 + warp * per, w1 = min(w0 + per, c1), wc = min(w1, pos);
+    const int ntile = w1 > w0 ? (w1 - w0 + kAttTR - 1) / kAttTR : 0;
+    const int r = lane & (kAttTR - 1), hsel = lane >> 4;
+    // lane (r, h) copies half h of K and V row r of tile t (one commit group per call)
+    auto issue = [&](int t) {
+        const int j = w0 + t * kAttTR + r;
+        if (t < ntile && j < wc) {
+            const int buf = nb == 2 ? (t & 1) : 0;
+            int8_t* dk = tk + (buf * kAttTR + r) * HD;
+            int8_t* dv = tv + (buf * kAttTR + r) * HD;
+#pragma unroll
+            for (int c = hsel * HH; c < (hsel + 1) * HH; c++) {
+                const int ph = att_chunk<HD>(c, r) * 16;
+                cp_async16_cg(dk + ph, kb + (size_t)j * HD + c * 16);
+                cp_async16_cg(dv + ph, vb + (size_t)j * HD + c * 16);
+            }
         }
-        return true;
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    bool pending = issue(c0);
+    issue(0);
+    if (nb == 2) issue(1);
+    // row scales of tile 0 (the cached rows; pos's come from s_row later)
+    float ksr = 0.0f, vsr = 0.0f;
+    {
+        const int j = w0 + r;
+        if (ntile > 0 && j < wc) {
+            ksr = __ldcg(ksb + j);
+            vsr = __ldcg(vsb + j);
+        }
+    }
+    ATR(1);
 
+    // RoPE + int8 quantisation of the group's query heads; the owner item
+    // also forms the new K (roped) and V rows, and the group-0 item appends
+    // them to the cache
     const MegaLayer& ly = a.layers[layer];
     const int nq = ly.qkv.spl;
     const size_t nqkv = (size_t)ly.qkv.n;
     const float* bq = ly.bias;
     for (int gq = warp; gq < G; gq += kMegaCW) {
-        const size_t o = (size_t)(kvh * GA + g0 + gq) * hd;
-        rq_warp(a.pq + o, nq, nqkv, bq ? bq + o : nullptr, hd, ct, stb, s_q8 + gq * hd, s_qsc + gq, lane);
+        const size_t o = (size_t)(kvh * GA + g0 + gq) * HD;
+        rq_warp(a.pq + o, nq, nqkv, bq ? bq + o : nullptr, HD, ct, stb, s_q8 + gq * HD, s_qsc + gq, lane);
     }
-    if (owner) {  // K (roped) and V at pos into the tile; the head group 0 item appends them to the cache
-        const size_t ok = (size_t)q_dim + (size_t)kvh * hd, ov = ok + kv_dim;
+    if (owner) {
+        const size_t ok = (size_t)q_dim + (size_t)kvh * HD, ov = ok + kv_dim;
         const bool app = g0 == 0;
         if (warp == kMegaCW - 1)
-            rq_warp(a.pq + ok, nq, nqkv, bq ? bq + ok : nullptr, hd, ct, stb, app ? kb + (size_t)pos * hd : s_row,
+            rq_warp(a.pq + ok, nq, nqkv, bq ? bq + ok : nullptr, HD, ct, stb, app ? kb + (size_t)pos * HD : s_row,
                     app ? ksb + pos : s_rsc, lane, app ? s_row : nullptr, app ? s_rsc : nullptr);
         else if (warp == kMegaCW - 2)
-            rq_warp(a.pq + ov, nq, nqkv, bq ? bq + ov : nullptr, hd, nullptr, nullptr,
-                    app ? vb + (size_t)pos * hd : s_row + hd, app ? vsb + pos : s_rsc + 1, lane,
-                    app ? s_row + hd : nullptr, app ? s_rsc + 1 : nullptr);
+            rq_warp(a.pq + ov, nq, nqkv, bq ? bq + ov : nullptr, HD, nullptr, nullptr,
+                    app ? vb + (size_t)pos * HD : s_row + HD, app ? vsb + pos : s_rsc + 1, lane,
+                    app ? s_row + HD : nullptr, app ? s_rsc + 1 : nullptr);
     }
-    for (int gq = tid; gq < G; gq += nthr) {
-        s_m[gq] = -INFINITY;
-        s_l[gq] = 0.0f;
-    }
-    ATR(1);
-    constexpr int ncg = HD / 4, npl = nthr / ncg;
-    const int cg = tid % ncg, pl = tid / ncg;
-    float acc[MAXG][4];
-#pragma unroll
-    for (int gq = 0; gq < MAXG; gq++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) acc[gq][i] = 0.0f;
+    ATR(2);
     csync();
+    ATR(3);
 
-    for (int j0 = c0; j0 < c1; j0 += S) {
-        const int n = min(S, c1 - j0);
-        const int jb = min(j0 + n, pos);  // rows from the cache; pos (if inside) from s_row
-        if (pending) {
-            if (!mbar_wait_err(abar, aph, a.err, 6)) return false;
-            aph ^= 1;
-        }
-        for (int j = tid; j < n; j += nthr) {
-            const int jj = j0 + j;
-            s_ks[j] = jj < jb ? __ldcg(ksb + jj) : s_rsc[0];
-            s_vs[j] = jj < jb ? __ldcg(vsb + jj) : s_rsc[1];
-        }
-        if (jb < j0 + n) {  // this sub-chunk holds pos: its row from s_row
-            const int r = pos - j0;
-            for (int e = tid; e < hw; e += nthr) {
-                reinterpret_cast<uint32_t*>(s_k + r * hd)[e] = reinterpret_cast<const uint32_t*>(s_row)[e];
-                reinterpret_cast<uint32_t*>(s_v + r * hd)[e] = reinterpret_cast<const uint32_t*>(s_row + hd)[e];
-            }
-        }
-        csync();
-        ATR(2);
-        // scores: entry (gq, j); 16-byte chunks in an order rotated with j so
-        // the 8 lanes of a shared-memory phase read 8 different bank groups
-        for (int e = tid; e < (G << lS); e += nthr) {
-            const int gq = e >> lS, j = e & (S - 1);
-            float sc = -INFINITY;
-            if (j < n) {
-                const uint4* qc = reinterpret_cast<const uint4*>(s_q8 + gq * hd);
-                const uint4* kc = reinterpret_cast<const uint4*>(s_k + j * hd);
-                const int rot = HC >= 8 ? j : (j >> (3 - (HC == 4 ? 2 : HC == 2 ? 1 : 0)));
-                int dot = 0;
+    float m[MAXG], l[MAXG], o[MAXG][DPL];
 #pragma unroll
-                for (int c = 0; c < HC; c++) {
-                    const int i = (c + rot) & (HC - 1);
-                    const uint4 qv = qc[i], kv = kc[i];
-                    dot = __dp4a((int)qv.x, (int)kv.x, dot);
-                    dot = __dp4a((int)qv.y, (int)kv.y, dot);
-                    dot = __dp4a((int)qv.z, (int)kv.z, dot);
-                    dot = __dp4a((int)qv.w, (int)kv.w, dot);
-                }
-                const float ksc = __fmul_rn(__fmul_rn(s_ks[j], s_qsc[gq]), a.scale);
-                sc = __fmul_rn((float)dot, ksc);
-            }
-            s_sc[e] = sc;
-        }
-        csync();
-        ATR(3);
-        for (int gq = warp; gq < G; gq += kMegaCW) {
-            float mx = -INFINITY;
-            for (int j = lane; j < n; j += 32) mx = fmaxf(mx, s_sc[(gq << lS) + j]);
-            mx = warp_max(mx);
-            const float m_old = s_m[gq], m_new = fmaxf(m_old, mx);
-            float sum = 0.0f;
-            for (int j = lane; j < n; j += 32) {
-                const float sv = s_sc[(gq << lS) + j];
-                const float e = (sv == -INFINITY) ? 0.0f : expf(sv - m_new);
-                sum += e;
-                s_sc[(gq << lS) + j] = e * s_vs[j];
-            }
-            sum = warp_sum(sum);
-            if (lane == 0) {
-                const float alpha = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
-                s_al[gq] = alpha;
-                s_l[gq] = s_l[gq] * alpha + sum;
-                s_m[gq] = m_new;
-            }
-        }
-        csync();
-        ATR(4);
+    for (int g = 0; g < MAXG; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
 #pragma unroll
-        for (int gq = 0; gq < MAXG; gq++)
-            if (gq < G) {
-                const float al = s_al[gq];
-#pragma unroll
-                for (int i = 0; i < 4; i++) acc[gq][i] = __fmul_rn(acc[gq][i], al);
-            }
-        attn_pv<MAXG, HD>(acc, s_sc, s_v, lS, G, cg, pl, n);
-        csync();
-        ATR(5);
-        if (j0 + S < c1) pending = issue(j0 + S);
+        for (int i = 0; i < DPL; i++) o[g][i] = 0.0f;
     }
-    // partial sums of the position lanes: inside a warp, then across warps
-    float* red = reinterpret_cast<float*>(sm + P.kv);
-    for (int off = ncg; off < 32; off <<= 1)
+    for (int t = 0; t < ntile; t++) {
+        const int buf = nb == 2 ? (t & 1) : 0;
+        const int jt = w0 + t * kAttTR, nj = min(kAttTR, w1 - jt);
+        const float ksc = ksr, vsc = vsr;
+        {
+            ksr = vsr = 0.0f;  // the next tile's scales, loaded ahead
+            const int j = jt + kAttTR + r;
+            if (t + 1 < ntile && j < wc) {
+                ksr = __ldcg(ksb + j);
+                vsr = __ldcg(vsb + j);
+            }
+        }
+        if (nb == 2)
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncwarp();
+        int8_t* rk = tk + buf * kAttTR * HD;
+        int8_t* rv = tv + buf * kAttTR * HD;
+        float ks_r = ksc, vs_r = vsc;
+        if (pos >= jt && pos < jt + nj) {  // the new position: its rows from s_row
+            const int rp = pos - jt;
+            for (int c = lane; c < 2 * HC; c += 32) {
+                const int cc = c < HC ? c : c - HC;
+                int8_t* d = (c < HC ? rk : rv) + rp * HD + att_chunk<HD>(cc, rp) * 16;
+                *reinterpret_cast<uint4*>(d) = reinterpret_cast<const uint4*>(s_row + (c < HC ? 0 : HD))[cc];
+            }
+            if (r == rp) {
+                ks_r = s_rsc[0];
+                vs_r = s_rsc[1];
+            }
+            __syncwarp();
+        }
+        if (t == 0) ATR(4);
+        // scores of row r for every head: half hsel of the dot, halves added
+        const bool valid = r < nj;
+        uint4 kr[HH];
 #pragma unroll
-        for (int gq = 0; gq < MAXG; gq++)
+        for (int c = 0; c < HH; c++)
+            kr[c] = *reinterpret_cast<const uint4*>(rk + r * HD + att_chunk<HD>(hsel * HH + c, r) * 16);
+        // every head's dot first, then the reductions side by side (the
+        // heads' shuffle chains overlap)
+        float sc[MAXG], mx[MAXG];
 #pragma unroll
-            for (int i = 0; i < 4; i++) acc[gq][i] = __fadd_rn(acc[gq][i], __shfl_xor_sync(0xffffffffu, acc[gq][i], off));
-    const int nred = ncg >= 32 ? npl : kMegaCW;  // partial rows after the in-warp step
-    const int rrow = ncg >= 32 ? pl : warp;
-    if (ncg >= 32 || lane < ncg) {
+        for (int g = 0; g < MAXG; g++) {
+            int dot = 0;
+            if (g < G) {
+                const uint4* qrow = reinterpret_cast<const uint4*>(s_q8 + g * HD) + hsel * HH;
 #pragma unroll
-        for (int gq = 0; gq < MAXG; gq++)
-            if (gq < G)
-                *reinterpret_cast<float4*>(red + ((size_t)rrow * G + gq) * hd + 4 * cg) =
-                    make_float4(acc[gq][0], acc[gq][1], acc[gq][2], acc[gq][3]);
+                for (int c = 0; c < HH; c++) {
+                    const uint4 qw = qrow[c];
+                    dot = __dp4a((int)qw.x, (int)kr[c].x, dot);
+                    dot = __dp4a((int)qw.y, (int)kr[c].y, dot);
+                    dot = __dp4a((int)qw.z, (int)kr[c].z, dot);
+                    dot = __dp4a((int)qw.w, (int)kr[c].w, dot);
+                }
+            }
+            sc[g] = (float)dot;
+        }
+#pragma unroll
+        for (int g = 0; g < MAXG; g++) {
+            const float d2 = sc[g] + __shfl_xor_sync(0xffffffffu, sc[g], 16);  // exact: integers below 2^24
+            sc[g] = (valid && g < G) ? __fmul_rn(d2, __fmul_rn(__fmul_rn(ks_r, s_qsc[g]), a.scale)) : -INFINITY;
+            mx[g] = sc[g];
+        }
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1)  // rows live in lanes 0-15 and again in 16-31
+#pragma unroll
+            for (int g = 0; g < MAXG; g++) mx[g] = fmaxf(mx[g], __shfl_xor_sync(0xffffffffu, mx[g], off));
+        float pw[MAXG];
+#pragma unroll
+        for (int g = 0; g < MAXG; g++) {
+            pw[g] = 0.0f;
+            if (g >= G) continue;
+            const float mn = fmaxf(m[g], mx[g]);
+            const float e = sc[g] == -INFINITY ? 0.0f : expf(sc[g] - mn);
+            const float al = m[g] == -INFINITY ? 0.0f : expf(m[g] - mn);
+            m[g] = mn;
+            l[g] = __fmaf_rn(l[g], al, hsel == 0 ? e : 0.0f);  // each row counted once (lanes h = 0)
+#pragma unroll
+            for (int i = 0; i < DPL; i++) o[g][i] = __fmul_rn(o[g][i], al);
+            pw[g] = __fmul_rn(e, vs_r);
+        }
+        if (hsel == 0) {
+#pragma unroll
+            for (int g = 0; g < MAXG; g++)
+                if (g < G) sp[r * MAXG + g] = pw[g];
+        }
+        __syncwarp();
+        // P.V: lane owns dims [DPL lane, DPL lane + DPL) of every head
+        const int cl = (DPL * lane) >> 4, off = (DPL * lane) & 15;
+        for (int jj = 0; jj < nj; jj++) {
+            const int8_t* vr = rv + jj * HD + att_chunk<HD>(cl, jj) * 16 + off;
+            float f[4];
+            if (DPL == 4)
+                u8x4_to_f32(*reinterpret_cast<const uint32_t*>(vr) ^ 0x80808080u, f);
+            else
+                u8x4_to_f32((uint32_t)(*reinterpret_cast<const uint16_t*>(vr)) ^ 0x80808080u, f);
+#pragma unroll
+            for (int g = 0; g < MAXG; g++)
+                if (g < G) {
+                    const float p = sp[jj * MAXG + g];
+#pragma unroll
+                    for (int i = 0; i < DPL; i++) o[g][i] = __fmaf_rn(p, f[i], o[g][i]);
+                }
+        }
+        __syncwarp();  // the next copies into this buffer come after every lane's reads
+        if (nb == 2)
+            issue(t + 2);
+        else
+            issue(t + 1);
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    ATR(5);
+    // merge the warps: (m, l, o) per warp -> shared memory, then per head
+#pragma unroll
+    for (int g = 0; g < MAXG; g++) l[g] = warp_sum(l[g]);
+    csync();  // every warp is done with its tiles: reuse the area
+    float* mw = reinterpret_cast<float*>(sm + P.warps);  // [warps][MAXG]
+    float* lw = mw + kMegaCW * MAXG;                     // [warps][MAXG]
+    float* ow = lw + kMegaCW * MAXG;                     // [warps][G][HD]
+    if (lane < MAXG) {
+        float mv = m[0], lv = l[0];
+#pragma unroll
+        for (int g = 1; g < MAXG; g++)
+            if (lane == g) {
+                mv = m[g];
+                lv = l[g];
+            }
+        mw[warp * MAXG + lane] = mv;
+        lw[warp * MAXG + lane] = lv;
+    }
+#pragma unroll
+    for (int g = 0; g < MAXG; g++)
+        if (g < G)
+#pragma unroll
+            for (int i = 0; i < DPL; i++) ow[(warp * G + g) * HD + DPL * lane + i] = o[g][i];
+    csync();
+    // per head: the largest warp maximum M, each warp's weight exp(m_w - M)
+    // (in place of m_w) and L = sum of weight * l_w; one warp per head
+    for (int g = warp; g < G; g += kMegaCW) {
+        const float mv = lane < kMegaCW ? mw[lane * MAXG + g] : -INFINITY;
+        const float M = warp_max(mv);
+        const float wgt = mv == -INFINITY ? 0.0f : expf(mv - M);
+        const float L = warp_sum(lane < kMegaCW ? __fmul_rn(wgt, lw[lane * MAXG + g]) : 0.0f);
+        __syncwarp();
+        if (lane < kMegaCW) mw[lane * MAXG + g] = wgt;
+        if (lane == 0) {
+            const int h = kvh * GA + g0 + g;
+            a.part_ml[((size_t)h * a.nsplit + split) * 2] = M;
+            a.part_ml[((size_t)h * a.nsplit + split) * 2 + 1] = L;
+        }
     }
     csync();
-    for (int e = tid; e < G * hd; e += nthr) {
-        float o = 0.0f;
-        for (int r = 0; r < nred; r++) o = __fadd_rn(o, red[(size_t)r * G * hd + e]);
-        const int gq = e / hd, dd = e - gq * hd, h = kvh * GA + g0 + gq;
-        a.part_o[((size_t)h * a.nsplit + split) * hd + dd] = o;
-    }
-    for (int gq = tid; gq < G; gq += nthr) {
-        const int h = kvh * GA + g0 + gq;
-        a.part_ml[((size_t)h * a.nsplit + split) * 2] = s_m[gq];
-        a.part_ml[((size_t)h * a.nsplit + split) * 2 + 1] = s_l[gq];
+    for (int e = tid; e < G * HD; e += kMegaCW * 32) {
+        const int g = e / HD, d = e - g * HD, h = kvh * GA + g0 + g;
+        float O = 0.0f;
+#pragma unroll 4
+        for (int w = 0; w < kMegaCW; w++) O = __fmaf_rn(mw[w * MAXG + g], ow[(w * G + g) * HD + d], O);
+        a.part_o[((size_t)h * a.nsplit + split) * HD + d] = O;
     }
     // arrival: the barrier orders the CTA's partial writes before thread 0's
     // fence and count
@@ -1039,32 +1071,6 @@ static __device__ void attn_merge(const MegaArgs& a, float* x_s, int c0, int c1,
     }
 }
 
-// L2 prefetch of the cached K/V rows (and their scales) that this CTA's
-// attention items of `layer` will read: issued a phase ahead, so the items
-// find them in L2 instead of queueing behind the weight stream in HBM.
-static __device__ void prefetch_attn_rows(const MegaArgs& a, int layer, int pos, int chunk, int nvalid) {
-    const int ngrp = a.H / a.KV / a.gsz, n_items = a.KV * ngrp * nvalid;
-    int last = -1;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-        const int kv_h = it / (ngrp * nvalid), rem = it - kv_h * ngrp * nvalid, split = rem % nvalid;
-        const int key = kv_h * nvalid + split;
-        if (key == last) continue;
-        last = key;
-        const int j0 = split * chunk, jb = min(j0 + chunk, pos);  // cached rows of the item
-        if (jb <= j0) continue;
-        const size_t row0 = ((size_t)layer * a.KV + kv_h) * a.max_seq + j0;
-        const uint32_t kvb = (uint32_t)((jb - j0) * a.hd);
-        bulk_prefetch_l2(a.k8 + row0 * a.hd, kvb);
-        bulk_prefetch_l2(a.v8 + row0 * a.hd, kvb);
-        // scales: 16-byte aligned start (rounded down inside the array) and length (rounded down)
-        const uintptr_t k0 = reinterpret_cast<uintptr_t>(a.ks + row0), v0 = reinterpret_cast<uintptr_t>(a.vs + row0);
-        const uint32_t sb = (uint32_t)((jb - j0) * 4 + (k0 & 15)) & ~15u;
-        const uint32_t vb = (uint32_t)((jb - j0) * 4 + (v0 & 15)) & ~15u;
-        if (sb) bulk_prefetch_l2(reinterpret_cast<const void*>(k0 & ~(uintptr_t)15), sb);
-        if (vb) bulk_prefetch_l2(reinterpret_cast<const void*>(v0 & ~(uintptr_t)15), vb);
-    }
-}
-
 // One instantiation per attention shape (query heads per kv head <= MAXG,
 // head_dim HD) and per exchange mode (TP: in-kernel tensor-parallel
 // exchange): each kernel carries only the code its model runs.
@@ -1073,8 +1079,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     extern __shared__ __align__(128) unsigned char sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + kMegaMaxSlots;
-    uint64_t* abar = empty + kMegaMaxSlots;  // attention K/V copies
-    static_assert(kMegaMaxSlots * 2 * 8 + 8 <= 128, "mbarriers exceed the shared-memory header");
+    static_assert(kMegaMaxSlots * 2 * 8 <= 128, "mbarriers exceed the shared-memory header");
     unsigned char* xs_region = sm + 128;
     float* x_s = reinterpret_cast<float*>(xs_region);  // kx floats, then the digits of up to kmax
     int8_t* xd = reinterpret_cast<int8_t*>(xs_region + (size_t)a.kx * 4);
@@ -1093,7 +1098,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kMegaCW);
         }
-        mbar_init(abar, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -1101,7 +1105,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     if (warp == kMegaCW) {  // ---- producer warp: the step's weight tiles, in consumer order
         if (lane == 0)
             produce_step(StepMats{a.layers, a.head_dev, a.L, 2 * a.win1}, a.win0 >> 1, (a.win0 & 1) * 2, b, ns,
-                         a.pf_tiles, full, empty, ring, a.err);
+                         full, empty, ring, a.err);
         return;
     }
 
@@ -1133,7 +1137,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     const unsigned int apar = *(volatile const unsigned int*)&st->apar & 1u;
     const unsigned int nct = gridDim.x;
     int bi = 0;
-    uint32_t aph = 0;  // parity of abar's current phase
     bool ok = true;
     // positions per attention split at this context: about per_head splits
     // per kv head (at least chunk_min positions, a multiple of 64)
@@ -1146,8 +1149,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
         if (a.trace != nullptr && tid == 0) a.trace[(size_t)b * kMegaTracePts + (idx)] = clock64(); \
     } while (0)
     TRACE(0);
-    if (a.kv_prefetch && tid == 0 && (a.win0 & 1) == 0 && a.win0 < 2 * a.L)
-        prefetch_attn_rows(a, a.win0 >> 1, pos, chunk, nvalid);
 
     // half-layer phases p = 2 l + h of this launch's window (h 0: QKV,
     // attention, O; h 1: gate/up, down); p = 2 L is the LM head
@@ -1197,13 +1198,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             for (int it = b; it < a.KV * ngrp * nvalid && ok; it += nct) {
                 long long* tr = (a.trace && it == b) ? a.trace + (size_t)b * kMegaTracePts + tb + 14 : nullptr;
                 const int kv_h = it / (ngrp * nvalid), rem = it - kv_h * ngrp * nvalid, gr = rem / nvalid;
-                ok = attn_item<MAXG, HD>(a, l, kv_h, gr, rem - gr * nvalid, chunk, pos, xs_region, abar, aph,
-                                         acnt, tr);
+                ok = attn_item<MAXG, HD>(a, l, kv_h, gr, rem - gr * nvalid, chunk, pos, xs_region, acnt, tr);
             }
             if (!ok) break;
-            // the next layer's cached K/V rows travel to L2 meanwhile
-            if (a.kv_prefetch && tid == 0 && l + 1 < a.L && 2 * (l + 1) < a.win1)
-                prefetch_attn_rows(a, l + 1, pos, chunk, nvalid);
             TRACE(tb + 3);
             // O projection (partials; the residual add happens in the next
             // reader). No grid barrier: a CTA waits for the attention items of
@@ -1353,16 +1350,6 @@ int mega_num_ctas() {
     return n;
 }
 
-// L2 prefetch distance of the copy issuer (tiles beyond the ring's ns). The
-// window over all CTAs (148 x distance x 26 KB) stays well inside the 126 MB
-// L2. JYC_MEGA_PREFETCH overrides it (tuning).
-int mega_prefetch_tiles(int ns) {
-    (void)ns;
-    int pf = 0;
-    if (const char* e = std::getenv("JYC_MEGA_PREFETCH")) pf = std::max(0, std::min(64, std::atoi(e)));
-    return pf;
-}
-
 // Work split of a matrix: for every column-group count (split-K only when
 // `splittable`, at most kMaxParts groups) the least rows per CTA that fit the
 // CTAs, costed as the bytes one CTA streams + a hand-off cost per tile + an
@@ -1414,21 +1401,23 @@ int mega_plan(MegaMat& m, int nctas, bool splittable, int only_cpg) {
 // the region.
 static int mega_xk_bytes(int kx, int kmax) { return kx * 4 + kmax * 3 + (kmax / 32) * 4; }
 
-int mega_xs_bytes(int kx, int kmax, int G, int hd, int S) {
+// query heads an attention item instantiation holds (the kernel's MAXG)
+static int mega_maxg(int gsz) { return gsz <= 1 ? 1 : gsz <= 4 ? 4 : 8; }
+
+int mega_xs_bytes(int kx, int kmax, int gsz, int hd, int nb) {
     const int xk = mega_xk_bytes(kx, kmax);
     const int samp = (kSampleThreads + 1) * (int)sizeof(double);  // the sampler's scratch (head phase)
-    return (std::max(std::max(xk, samp), attn_plan(G, hd, S).total) + 127) / 128 * 128;
+    return (std::max(std::max(xk, samp), attn_plan(mega_maxg(gsz), hd, nb).total) + 127) / 128 * 128;
 }
 
-// Attention sub-chunk: the split length rounded up to a power of two, halved
-// while the item's plan would need more than max(x region, attn_cap bytes).
-int mega_attn_sub(int kx, int kmax, int G, int hd, int chunk, int attn_cap) {
-    const int xk = mega_xk_bytes(kx, kmax);
-    const int cap = std::max(xk, attn_cap);
-    int S = 16;
-    while (S < chunk) S <<= 1;
-    while (S > 16 && attn_plan(G, hd, S).total > cap) S >>= 1;
-    return S;
+// Tiles in flight per attention warp: two when a warp's share of the longest
+// split spans more than one tile and the double tiles fit max(x region,
+// attn_cap bytes), else one.
+int mega_attn_nb(int kx, int kmax, int gsz, int hd, int chunk, int attn_cap) {
+    const int per = (chunk + kMegaCW - 1) / kMegaCW;
+    if (per <= kAttTR) return 1;
+    const int cap = std::max(mega_xk_bytes(kx, kmax), attn_cap);
+    return attn_plan(mega_maxg(gsz), hd, 2).total <= cap ? 2 : 1;
 }
 
 int mega_smem_bytes(const MegaArgs& a) { return 128 + a.xs_bytes + a.nslots * kMegaSlotBytes; }

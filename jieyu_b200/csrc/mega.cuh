@@ -81,7 +81,7 @@ struct MegaArgs {
     int chunk, nsplit;        // largest split length (at max_seq), split stride of part_o / part_ml
     int per_head;             // splits per kv head a step aims at (positions per split follow the context)
     int chunk_min;            // shortest split length
-    int asub;                 // attention sub-chunk (power of two, positions per K/V copy)
+    int att_nb;               // K/V tiles in flight per attention warp (1 or 2)
     int gsz;                  // query heads per attention item (a divisor of H / KV)
     unsigned int* acnt;       // [L][KV]: finished attention items of (layer, kv head) in this step
     float scale;              // 1/sqrtf(hd)
@@ -93,8 +93,6 @@ struct MegaArgs {
     int kx;                   // longest row kept as floats in shared memory (max(D, H hd))
     int xs_bytes;             // shared bytes of the x / digits / attention union
     int nslots;               // ring depth
-    int pf_tiles;             // L2 prefetch distance of the copy issuer, in tiles beyond the ring (0: none)
-    int kv_prefetch;          // 1: prefetch each layer's cached K/V rows into L2 a phase ahead
     int win0, win1;           // phases of this launch: [win0, win1) of 2 l + h (h 0: QKV..O, 1: gate/up..down), 2 L = head
     long long* trace;         // optional: SM clock at each phase boundary, [CTA][kMegaTracePts]
     // tensor parallel inside the kernel (tp > 1): every CTA stores its O / down
@@ -121,10 +119,9 @@ int launch_q8_repack_tiled(const void* blocks, int n, int k, uint8_t* qs, uint16
                            int row_off, int row_stride, cudaStream_t s);
 int mega_plan(MegaMat& m, int nctas, bool splittable, int only_cpg = 0);
 int mega_smem_bytes(const MegaArgs& a);
-int mega_xs_bytes(int kx, int kmax, int G, int hd, int S);
-int mega_attn_sub(int kx, int kmax, int G, int hd, int chunk, int attn_cap);
+int mega_xs_bytes(int kx, int kmax, int gsz, int hd, int nb);
+int mega_attn_nb(int kx, int kmax, int gsz, int hd, int chunk, int attn_cap);
 int mega_num_ctas();
-int mega_prefetch_tiles(int ns);
 int launch_mega_step(const MegaArgs& a, cudaStream_t s);
 int prepare_mega_kernel(int smem, int G, int hd);
 int mega_static_smem(int G, int hd);  // -1 when the kernel image cannot be queried

@@ -361,8 +361,8 @@ int setup_mega(jyc_model* m) {
     // (query head, split) when those fit the CTAs at full context (short
     // contexts: more parallelism, fewer splits to merge per item)
     a.gsz = (m->KV * (m->H / m->KV) * nsplit_max <= nctas) ? 1 : m->H / m->KV;
-    a.asub = mega_attn_sub(a.kx, a.kmax, m->H / m->KV, m->hd, a.chunk, mega_attn_cap());
-    a.xs_bytes = mega_xs_bytes(a.kx, a.kmax, m->H / m->KV, m->hd, a.asub);
+    a.att_nb = mega_attn_nb(a.kx, a.kmax, a.gsz, m->hd, a.chunk, mega_attn_cap());
+    a.xs_bytes = mega_xs_bytes(a.kx, a.kmax, a.gsz, m->hd, a.att_nb);
     // the x region also stages one head's split partials behind the
     // attention rows, and a 16-byte slice of up to 8 x 8 partial rows (+ the
     // base row) behind the residual row
@@ -377,9 +377,6 @@ int setup_mega(jyc_model* m) {
     if (st_smem < 0) return cuda_fail(cudaGetLastError(), "mega: kernel attributes");
     const int budget = 227 * 1024 - st_smem - 128 - a.xs_bytes;
     a.nslots = std::min(kMegaMaxSlots, budget / kMegaSlotBytes);
-    a.pf_tiles = mega_prefetch_tiles(a.nslots);
-    a.kv_prefetch = 0;
-    if (const char* e = std::getenv("JYC_MEGA_KV_PREFETCH")) a.kv_prefetch = std::atoi(e) != 0;
     a.win0 = 0;
     a.win1 = 2 * m->L + 1;  // the whole step
     if (a.nslots < 2) return JYC_OK;  // does not fit: generic decode

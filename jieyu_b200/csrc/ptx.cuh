@@ -66,11 +66,6 @@ static __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
-// Bulk prefetch of [src, src + bytes) into L2 (no completion to wait for;
-// 16-byte aligned address and size).
-static __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 // orders this thread's earlier shared-memory accesses (generic proxy) before
 // later async-proxy (TMA) writes to shared memory
 static __device__ __forceinline__ void fence_proxy_async_smem() {

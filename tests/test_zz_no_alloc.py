@@ -16,6 +16,7 @@ CASES = [
     (14, 2, 64, 100, 5, 1, 1024),   # configs[1] heads, decode-sized second call
     (8, 4, 64, 0, 9, 3, 512),       # configs[0] heads, prompt then a short step
     (32, 8, 128, 700, 1, 1, 4352),  # configs[3] heads
+    (32, 8, 64, 40, 20, 20, 512),   # 20 rows: the 8-row loop reuses the scratch inside one call
 ]
 
 
@@ -45,8 +46,9 @@ def test_noalloc_attention_matches_allocating_entry(cuda, H, KV, hd, start, s1, 
     lib = _capi.load()
     want, wcache = _run(lib, torch, lib.jyc_attention_q8, H, KV, hd, start, (s1, s2), cap)
     got, gcache = _run(lib, torch, lib.jyc_attention_q8_noalloc, H, KV, hd, start, (s1, s2), cap)
+    # the same kernels with the same split plan: bit-identical outputs
     for g, w in zip(got, want):
-        assert np.abs(g - w).max() <= 1e-5 * (np.abs(w).max() + 1e-30)
+        assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
     for g, w in zip(gcache, wcache):
         assert np.array_equal(g.view(np.uint8), w.view(np.uint8))
 
@@ -59,6 +61,13 @@ def test_noalloc_rejects_calls_beyond_its_scratch(cuda):
     s = stream(torch)
     # 40 heads x 256 dims = 10240 > 8192 query elements per row
     assert lib.jyc_attention_q8_noalloc(p, p, p, p, 1, 0, 40, 40, 256, p, p, p, p, 16, s) == _capi.JYC_ERR_ARG
+    assert "fixed scratch" in _capi.last_error()
+    # split partials: 8 rows x 128 heads x 64 dims x 17 splits (start 1024,
+    # 4 kv heads) = 1,114,112 floats > 1,048,576
+    assert lib.jyc_attention_q8_noalloc(p, p, p, p, 1, 1024, 128, 4, 64, p, p, p, p, 1025, s) == _capi.JYC_ERR_ARG
+    assert "fixed scratch" in _capi.last_error()
+    # arrival counters: one per kv head, 256 of them
+    assert lib.jyc_attention_q8_noalloc(p, p, p, p, 1, 0, 257, 257, 4, p, p, p, p, 16, s) == _capi.JYC_ERR_ARG
     assert "fixed scratch" in _capi.last_error()
     # the usual argument checks still apply
     assert lib.jyc_attention_q8_noalloc(p, p, p, p, 4, 14, 8, 4, 64, p, p, p, p, 16, s) == _capi.JYC_ERR_KV_OOM
