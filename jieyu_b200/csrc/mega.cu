@@ -904,12 +904,25 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
                 u8x4_to_f32(*reinterpret_cast<const uint32_t*>(vr) ^ 0x80808080u, f);
             else
                 u8x4_to_f32((uint32_t)(*reinterpret_cast<const uint16_t*>(vr)) ^ 0x80808080u, f);
+            float pj[MAXG];
+            if (MAXG >= 4) {  // the row's weights in 16-byte loads
+#pragma unroll
+                for (int g4 = 0; g4 < MAXG; g4 += 4) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(sp + jj * MAXG + g4);
+                    pj[g4] = q4.x;
+                    pj[g4 + 1] = q4.y;
+                    pj[g4 + 2] = q4.z;
+                    pj[g4 + 3] = q4.w;
+                }
+            } else {
+#pragma unroll
+                for (int g = 0; g < MAXG; g++) pj[g] = sp[jj * MAXG + g];
+            }
 #pragma unroll
             for (int g = 0; g < MAXG; g++)
                 if (g < G) {
-                    const float p = sp[jj * MAXG + g];
 #pragma unroll
-                    for (int i = 0; i < DPL; i++) o[g][i] = __fmaf_rn(p, f[i], o[g][i]);
+                    for (int i = 0; i < DPL; i++) o[g][i] = __fmaf_rn(pj[g], f[i], o[g][i]);
                 }
         }
         __syncwarp();  // the next copies into this buffer come after every lane's reads
@@ -971,10 +984,8 @@ static __device__ __forceinline__ bool attn_item(const MegaArgs& a, int layer, i
     // fence and count
     csync();
     ATR(6);
-    if (tid == 0) {
-        __threadfence();
-        atomicAdd(cnt + kvh, 1u);
-    }
+    if (tid == 0)  // a release reduction: the CTA barrier above orders every thread's writes before it
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(cnt + kvh), "r"(1u) : "memory");
     ATR(7);
     ATR(8);
 #undef ATR

@@ -499,7 +499,9 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     JYC_CUDA(cudaMemsetAsync(m->vs, 0, kvn * 4, m->stream));
     // batched prefill (tcgen05 token tiles) for Q8_0 models
     const bool pf_ok = m->wtype == W_Q8 && pf_attention_supported(m->H, m->KV, m->hd);
-    m->pf_rows = pf_ok ? std::min(kPfChunk, m->max_seq) : 0;
+    int pf_chunk = kPfChunk;  // JYC_PF_ROWS overrides the tokens per pass (tuning)
+    if (const char* e = std::getenv("JYC_PF_ROWS")) pf_chunk = std::max(16, std::min(16384, std::atoi(e)));
+    m->pf_rows = pf_ok ? std::min(pf_chunk, m->max_seq) : 0;
     const size_t arows = std::max(kMT, m->pf_rows);
     TRY(m->alloc(&m->X, arows * m->D));
     TRY(m->alloc(&m->qkv, arows * m->nqkv));
