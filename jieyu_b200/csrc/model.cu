@@ -518,7 +518,7 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
         const int N = tc_token_tile(m->pf_rows);
         TRY(m->alloc(&m->tc_xs, tc_split_halves(m->pf_rows, N, kmax)));
         TRY(m->alloc(&m->tc_xe, (size_t)tc_padded_tokens(m->pf_rows, N)));
-        m->tc_part_floats = (size_t)kTcMaxSplits * m->pf_rows * std::max({m->nqkv, m->D});
+        m->tc_part_floats = (size_t)kTcMaxSplits * std::min(m->pf_rows, kPfPartRows) * std::max({m->nqkv, m->D});
         TRY(m->alloc(&m->tc_part, m->tc_part_floats));
         const size_t tiles = (size_t)((nmax + kTcRows - 1) / kTcRows) * ((m->pf_rows + 15) / 16);
         TRY(m->alloc(&m->tc_cnt, tiles));

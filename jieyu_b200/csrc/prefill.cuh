@@ -5,7 +5,8 @@
 namespace jyc {
 
 constexpr int kPfQT = 16;    // query tokens per attention CTA
-constexpr int kPfChunk = 512;  // tokens per batched prefill pass
+constexpr int kPfChunk = 4096;  // tokens per batched prefill pass (up to max_seq)
+constexpr int kPfPartRows = 512;  // rows the K-split partial sums are sized for (fewer splits above)
 
 struct PfAttn {
     const int8_t* q8;    // [T][H * hd] roped, quantised queries

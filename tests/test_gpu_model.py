@@ -257,6 +257,36 @@ def test_decode_kernel_step_from_the_oracle_state(cuda, oracle, key):
         m.close()
 
 
+def test_prefill_in_several_passes(cuda, oracle, monkeypatch):
+    """A prompt longer than one prefill pass (JYC_PF_ROWS=64: a 256-token
+    prompt in 4 passes, each pass attending over the cache rows the earlier
+    ones wrote) gives the logits of one pass within the model tolerance, and
+    both stay within it of the oracle."""
+    cfg = CONFIGS["c0"]
+    hw = HostWeights.synthetic(cfg)
+    pr = np.ascontiguousarray(prompt_ids(cfg, n=256), np.int32)
+    want = np.empty(cfg.vocab, np.float32)
+    cache = oracle.cache_create(cfg.layers, cfg.max_seq, cfg.kv_heads, cfg.head_dim)
+    try:
+        assert oracle.forward_logits(C.byref(hw.desc), cache, ptr(pr), len(pr), 0, ptr(want), None) == 0
+    finally:
+        oracle.cache_free(cache)
+    got = {}
+    for rows in ("64", None):
+        if rows:
+            monkeypatch.setenv("JYC_PF_ROWS", rows)
+        else:
+            monkeypatch.delenv("JYC_PF_ROWS", raising=False)
+        m = DeviceModel(hw)
+        got[rows] = m.forward_logits(pr, 0)
+        m.close()
+    tol = _tol(golden("c0.json")["isa_spread"], 0)
+    for rows, g in got.items():
+        _check_logits(g, want, tol=tol, label=f"c0 prompt of 256 in passes of {rows or 'one'}")
+    amax = np.abs(want).max()
+    assert np.abs(got["64"] - got[None]).max() <= tol * amax
+
+
 def test_generate_contract_edges(c0):
     hw, m = c0
     pr = prompt_ids(hw.cfg)

@@ -27,6 +27,8 @@ def test_tp2_decode_matches_single_gpu(cuda, mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", JIEYU_TP_MODE=mode)
+    if mode == "prefill":
+        env["JYC_PF_ROWS"] = "512"  # the 700-token prompt in two passes
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(HERE, "tp_worker.py")]
