@@ -285,30 +285,11 @@ static __device__ __forceinline__ void mma_s8(uint32_t a0, uint32_t a1, uint32_t
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-// Exact float of an integer |c| < 2^22 with one integer and one float add
-// (the 1.5 * 2^23 bias puts c in the mantissa), avoiding the conversion unit.
-static __device__ __forceinline__ float small_i2f(int c) {
-    return __fadd_rn(__int_as_float(c + 0x4B400000), -12582912.0f);
-}
-
 // Scale pair (rows g, g+8 of a 16-row group, one Q8 block) -> both fp16
-// values as fp32 times 2^-112: exponent and mantissa moved to the fp32
-// position (exact, subnormals included; scales are non-negative, checked at
-// repack). The caller's factor carries the 2^112.
-static __device__ __forceinline__ float d_lo(uint32_t w) { return __int_as_float((w << 13) & 0x0FFFE000u); }
-static __device__ __forceinline__ float d_hi(uint32_t w) { return __int_as_float((w >> 3) & 0x0FFFE000u); }
+// values as fp32 (exact conversions).
+static __device__ __forceinline__ float d_lo(uint32_t w) { return h2f((uint16_t)(w & 0xffffu)); }
+static __device__ __forceinline__ float d_hi(uint32_t w) { return h2f((uint16_t)(w >> 16)); }
 
-// y[rows of this CTA] = W . x for one matrix; x given as 3 int8 digit planes
-// xd[0..2][k] and per-32 block scales xsc[k/32].
-//
-// Fragment use of m16n8k32: B column j < 3 holds digit j of x (lanes g < 3
-// load it), columns 3..7 are zero. Lane (g, tq) receives C columns 2tq, 2tq+1
-// of rows g and g+8: lane tq=0 digit sums a, b, lane tq=1 digit sum c and a
-// zero, lanes tq=2,3 zeros. Every lane forms u = s1 * f(C0) + f(C1) (s1 = 2^7
-// on tq=0, 1 elsewhere) and accumulates u * d * sx * m (m = 2^7 on tq=0), i.e.
-// 2^14 a + 2^7 b on tq=0 and c on tq=1; the two meet once per row tile.
-// Accumulators carry a 2^-28 factor (scale products stay normal for block
-// maxima down to 2^-54 and finite up to 2^57), removed at the end.
 // Peer stores of partial rows (tensor parallel): row values of column group kg
 // also go to dst[q][off + kg * n + row] for every rank q < n_dst.
 struct PeerPush {
@@ -317,16 +298,50 @@ struct PeerPush {
     size_t off;
 };
 
+// One 16-row group of one Q8 block: the warp's mma and the scaled digit sums
+// added to (acc0, acc1) (rows g, g+8). `ap` points at the lane's A bytes of
+// row g, `stride8` is 8 rows of the tile, `dw` the scale pair.
+static __device__ __forceinline__ void group_dot(const unsigned char* ap, int stride8, uint32_t dw, uint2 bf,
+                                                 float kx, int im, float& acc0, float& acc1) {
+    const uint2 A0 = *reinterpret_cast<const uint2*>(ap);
+    const uint2 A1 = *reinterpret_cast<const uint2*>(ap + stride8);
+    int c0, c1, c2, c3;
+    mma_s8(A0.x, A1.x, A0.y, A1.y, bf.x, bf.y, c0, c1, c2, c3);
+    // im * C0 + C1 is exact in int32 (|C| < 2^18); one rounding to fp32
+    const float va = (float)(c0 * im + c1);
+    const float vb = (float)(c2 * im + c3);
+    acc0 = __fmaf_rn(va, __fmul_rn(d_lo(dw), kx), acc0);
+    acc1 = __fmaf_rn(vb, __fmul_rn(d_hi(dw), kx), acc1);
+}
+
+// y[rows of this CTA] = W . x for one matrix; x given as 3 int8 digit planes
+// xd[0..2][k] and per-32 block scales xsc[k/32].
+//
+// Fragment use of m16n8k32: B column j < 3 holds digit j of x (lanes g < 3
+// load it), columns 3..7 are zero. Lane (g, tq) receives C columns 2tq, 2tq+1
+// of rows g and g+8: lane tq=0 digit sums a, b, lane tq=1 digit sum c and a
+// zero, lanes tq=2,3 zeros. Every lane forms u = im * C0 + C1 (im = 2^7 on
+// tq=0, 1 elsewhere) and accumulates u * d * sx * m (m = 2^7 on tq=0), i.e.
+// 2^14 a + 2^7 b on tq=0 and c on tq=1; the two meet once per row tile.
+// Accumulators carry a 2^-28 factor (scale products stay normal for block
+// maxima down to 2^-54 and finite up to 2^57), removed at the end.
+//
+// Cross-warp sums are deferred: after each row tile a warp stores its row
+// sums in s_acc[warp][cap] (no CTA barrier); the 16 warps' rows are added in
+// warp order (the same order for every row, deterministic) once the buffer
+// holds `cap` rows or the matrix ends. Full tiles (rows kMegaRT, 512 columns)
+// take a path with constant strides.
 template <int EPI>
-static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, Ring& rg_, float* s_part,
-                                   float* s_res, float* y, unsigned long long* s_best, int* err,
-                                   PeerPush push = PeerPush{nullptr, 0, 0}, int idx_off = 0) {
+static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_t* xd, const float* xsc, Ring& rg_,
+                                                   float* s_acc, int cap, float* y, unsigned long long* s_best,
+                                                   int* err, PeerPush push = PeerPush{nullptr, 0, 0},
+                                                   int idx_off = 0) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int g = lane >> 2, tq = lane & 3;
-    const float s1 = tq == 0 ? 128.0f : 1.0f;
-    const float km = tq == 0 ? 0x1p91f : 0x1p84f;  // 2^112 * 2^-28 * m
+    const int im = tq == 0 ? 128 : 1;
+    const float km = tq == 0 ? 0x1p-21f : 0x1p-28f;  // 2^-28 * m
     const MatRange R = mat_range(M, b);
-    const int r_begin = R.r0, r_end = R.r1;
+    const int r_begin = R.r0, r_end = R.r1, rt = M.rt;
     const int ncb = (M.k + kMegaCB - 1) / kMegaCB;
     const int wl = M.k - (ncb - 1) * kMegaCB;  // width of the last column block
     // Warp w takes the 32-column blocks w + i * kMegaCW (i < BPW) of each tile.
@@ -342,8 +357,9 @@ static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_
     }
     const int8_t* xb = xd + (size_t)min(g, 2) * M.k + 32 * warp + 8 * tq;
     constexpr int NRG = kMegaRT / 16;
-    for (int r0 = r_begin; r0 < r_end; r0 += M.rt) {
-        const int rows = min(M.rt, r_end - r0), nrg = rows >> 4;
+    int rbase = r_begin;  // first row held in s_acc
+    for (int r0 = r_begin; r0 < r_end; r0 += rt) {
+        const int rows = min(rt, r_end - r0), nrg = rows >> 4;
         float acc[NRG][2];
 #pragma unroll
         for (int j = 0; j < NRG; j++) acc[j][0] = acc[j][1] = 0.0f;
@@ -352,28 +368,36 @@ static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_
             const bool lastb = cb == ncb - 1;
             const int w = lastb ? wl : kMegaCB, nblk = w >> 5;
             const unsigned char* slot = rg_.ring + (size_t)rg_.rp.s * kMegaSlotBytes;
+            if (w == kMegaCB && nrg == NRG) {  // full tile: constant strides
 #pragma unroll
-            for (int i = 0; i < BPW; i++) {
-                const int bw = warp + i * kMegaCW;
-                if (bw < nblk) {
+                for (int i = 0; i < BPW; i++) {
+                    const int bw = warp + i * kMegaCW;
                     const uint32_t* dp = reinterpret_cast<const uint32_t*>(slot + kMegaRT * kMegaCB) + bw * 8 + g;
                     uint2 bf = make_uint2(0u, 0u);
                     if (g < 3) bf = *reinterpret_cast<const uint2*>(xb + cb * kMegaCB + 32 * i * kMegaCW);
                     const float kx = __fmul_rn(xsc[cb * (kMegaCB / 32) + bw], km);
-                    const unsigned char* ap = slot + (lastb ? a_last[i] : a_full[i]);
+                    const unsigned char* ap = slot + a_full[i];
 #pragma unroll
-                    for (int rg = 0; rg < NRG; rg++) {
-                        if (rg < nrg) {
-                            const uint2 A0 = *reinterpret_cast<const uint2*>(ap + rg * 16 * w);
-                            const uint2 A1 = *reinterpret_cast<const uint2*>(ap + (rg * 16 + 8) * w);
-                            const uint32_t dw = dp[rg * nblk * 8];
-                            int c0, c1, c2, c3;
-                            mma_s8(A0.x, A1.x, A0.y, A1.y, bf.x, bf.y, c0, c1, c2, c3);
-                            const float va = __fmaf_rn(s1, small_i2f(c0), small_i2f(c1));
-                            const float vb = __fmaf_rn(s1, small_i2f(c2), small_i2f(c3));
-                            acc[rg][0] = __fmaf_rn(va, __fmul_rn(d_lo(dw), kx), acc[rg][0]);
-                            acc[rg][1] = __fmaf_rn(vb, __fmul_rn(d_hi(dw), kx), acc[rg][1]);
-                        }
+                    for (int rg = 0; rg < NRG; rg++)
+                        group_dot(ap + rg * 16 * kMegaCB, 8 * kMegaCB, dp[rg * (kMegaCB / 32) * 8], bf, kx, im,
+                                  acc[rg][0], acc[rg][1]);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < BPW; i++) {
+                    const int bw = warp + i * kMegaCW;
+                    if (bw < nblk) {
+                        const uint32_t* dp =
+                            reinterpret_cast<const uint32_t*>(slot + kMegaRT * kMegaCB) + bw * 8 + g;
+                        uint2 bf = make_uint2(0u, 0u);
+                        if (g < 3) bf = *reinterpret_cast<const uint2*>(xb + cb * kMegaCB + 32 * i * kMegaCW);
+                        const float kx = __fmul_rn(xsc[cb * (kMegaCB / 32) + bw], km);
+                        const unsigned char* ap = slot + (lastb ? a_last[i] : a_full[i]);
+#pragma unroll
+                        for (int rg = 0; rg < NRG; rg++)
+                            if (rg < nrg)
+                                group_dot(ap + rg * 16 * w, 8 * w, dp[rg * nblk * 8], bf, kx, im, acc[rg][0],
+                                          acc[rg][1]);
                     }
                 }
             }
@@ -384,30 +408,38 @@ static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_
             acc[rg][0] = __fadd_rn(acc[rg][0], __shfl_down_sync(0xffffffffu, acc[rg][0], 1));
             acc[rg][1] = __fadd_rn(acc[rg][1], __shfl_down_sync(0xffffffffu, acc[rg][1], 1));
         }
+        const int ro = r0 - rbase;
         if (tq == 0) {
 #pragma unroll
             for (int rg = 0; rg < NRG; rg++)
                 if (rg < nrg) {
-                    s_part[warp * kMegaRT + rg * 16 + g] = acc[rg][0];
-                    s_part[warp * kMegaRT + rg * 16 + g + 8] = acc[rg][1];
+                    s_acc[warp * cap + ro + rg * 16 + g] = acc[rg][0];
+                    s_acc[warp * cap + ro + rg * 16 + g + 8] = acc[rg][1];
                 }
         }
-        csync();
-        for (int e = tid; e < rows; e += kMegaCW * 32) {
-            float v = 0.0f;
-#pragma unroll
-            for (int w2 = 0; w2 < kMegaCW; w2++) v = __fadd_rn(v, s_part[w2 * kMegaRT + e]);
-            s_res[e] = __fmul_rn(v, 0x1p28f);
-        }
+        if (r0 + rt < r_end && ro + rows + rt <= cap) continue;  // room for the next row tile
+        // rows [rbase, r0 + rows): every warp's sums, in warp order
+        const int nr = ro + rows;
         csync();
         if (EPI == ME_SWIGLU) {
-            for (int e = tid; e < rows / 2; e += kMegaCW * 32)
-                y[(r0 >> 1) + e] = __fmul_rn(silu_ref(s_res[2 * e]), s_res[2 * e + 1]);
+            for (int e = tid; e < nr / 2; e += kMegaCW * 32) {
+                float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+                for (int w2 = 0; w2 < kMegaCW; w2++) {
+                    v0 = __fadd_rn(v0, s_acc[w2 * cap + 2 * e]);
+                    v1 = __fadd_rn(v1, s_acc[w2 * cap + 2 * e + 1]);
+                }
+                y[(rbase >> 1) + e] = __fmul_rn(silu_ref(__fmul_rn(v0, 0x1p28f)), __fmul_rn(v1, 0x1p28f));
+            }
         } else if (EPI == ME_ARGMAX) {
             unsigned long long best = 0ull;
-            for (int e = tid; e < rows; e += kMegaCW * 32) {
-                y[r0 + e] = s_res[e];
-                const unsigned long long p = argmax_pack(s_res[e], idx_off + r0 + e);
+            for (int e = tid; e < nr; e += kMegaCW * 32) {
+                float v = 0.0f;
+#pragma unroll
+                for (int w2 = 0; w2 < kMegaCW; w2++) v = __fadd_rn(v, s_acc[w2 * cap + e]);
+                v = __fmul_rn(v, 0x1p28f);
+                y[rbase + e] = v;
+                const unsigned long long p = argmax_pack(v, idx_off + rbase + e);
                 best = p > best ? p : best;
             }
 #pragma unroll
@@ -417,13 +449,18 @@ static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_
             }
             if (lane == 0 && best) atomicMax(s_best, best);
         } else {
-            for (int e = tid; e < rows; e += kMegaCW * 32) {
-                const size_t o = (size_t)R.kg * M.n + r0 + e;
-                y[o] = s_res[e];
-                for (int q = 0; q < push.n_dst; q++) push.dst[q][push.off + o] = s_res[e];
+            for (int e = tid; e < nr; e += kMegaCW * 32) {
+                float v = 0.0f;
+#pragma unroll
+                for (int w2 = 0; w2 < kMegaCW; w2++) v = __fadd_rn(v, s_acc[w2 * cap + e]);
+                v = __fmul_rn(v, 0x1p28f);
+                const size_t o = (size_t)R.kg * M.n + rbase + e;
+                y[o] = v;
+                for (int q = 0; q < push.n_dst; q++) push.dst[q][push.off + o] = v;
             }
         }
         csync();
+        rbase = r0 + rt;
     }
     return true;
 }
@@ -1109,7 +1146,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     float* xsc = reinterpret_cast<float*>(xs_region + (size_t)a.kx * 4 + (size_t)a.kmax * 3);
     unsigned char* ring = sm + 128 + a.xs_bytes;
     __shared__ float s_part[kMegaCW * kMegaRT];
-    __shared__ float s_res[kMegaRT];
+    // the GEMV phases' per-warp row sums: the float part of the x region (free
+    // once x is digitised) when it holds a row tile per warp, else s_part
+    const bool big = a.kx >= kMegaCW * kMegaRT;
+    const int cap = big ? (a.kx / kMegaCW) & ~15 : kMegaRT;
+    float* s_acc = big ? x_s : s_part;
     __shared__ float s_red[kMegaCW];
     __shared__ unsigned long long s_best;
     __shared__ int s_ok;
@@ -1208,7 +1249,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             x_norm(x_s, a.D, ly.rms1, 1e-5f, s_red);
             x_digitize(x_s, a.D, xd, xsc);
             TRACE(tb + 0);
-            ok = consume_mat<ME_PART>(ly.qkv, xd, xsc, rg, s_part, s_res, a.pq, &s_best,
+            ok = consume_mat<ME_PART>(ly.qkv, xd, xsc, rg, s_acc, cap, a.pq, &s_best,
                                       a.err);
             TRACE(tb + 1);
             ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
@@ -1245,11 +1286,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             }
             TRACE(tb + 5);
             if (TP) {
-                ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err,
+                ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_acc, cap, a.po, &s_best, a.err,
                                           PeerPush{a.peer_xo, a.tp, (size_t)a.tp_rank * a.xo_stride});
                 if (ok) xchg_arrive(a, 0);
             } else {
-                ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_part, s_res, a.po, &s_best, a.err);
+                ok = consume_mat<ME_PART>(ly.o, xd, xsc, rg, s_acc, cap, a.po, &s_best, a.err);
             }
             TRACE(tb + 6);
             // (tensor parallel: the readers' wait on every rank's arrival counts
@@ -1268,7 +1309,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             x_norm(x_s, a.D, ly.rms2, 1e-5f, s_red);
             x_digitize(x_s, a.D, xd, xsc);
             TRACE(tb + 8);
-            ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, rg, s_part, s_res, a.h, &s_best,
+            ok = consume_mat<ME_SWIGLU>(ly.gu, xd, xsc, rg, s_acc, cap, a.h, &s_best,
                                         a.err);
             TRACE(tb + 9);
             ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
@@ -1278,11 +1319,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             x_digitize<true>(a.h, a.F, xd, xsc);
             TRACE(tb + 11);
             if (TP) {
-                ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best, a.err,
+                ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_acc, cap, a.pd, &s_best, a.err,
                                           PeerPush{a.peer_xdn, a.tp, (size_t)a.tp_rank * a.xdn_stride});
                 if (ok) xchg_arrive(a, 1);
             } else {
-                ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_part, s_res, a.pd, &s_best, a.err);
+                ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_acc, cap, a.pd, &s_best, a.err);
             }
             TRACE(tb + 12);
             if (!TP) ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
@@ -1306,7 +1347,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
     x_norm(x_s, a.D, a.final_norm, 1e-5f, s_red);
     x_digitize(x_s, a.D, xd, xsc);
     TRACE(th + 0);
-    if (!consume_mat<ME_ARGMAX>(*a.head_dev, xd, xsc, rg, s_part, s_res, a.logits, &s_best,
+    if (!consume_mat<ME_ARGMAX>(*a.head_dev, xd, xsc, rg, s_acc, cap, a.logits, &s_best,
                                 a.err, PeerPush{nullptr, 0, 0}, a.vocab_off))
         return;
     TRACE(th + 1);

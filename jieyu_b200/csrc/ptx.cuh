@@ -57,7 +57,7 @@ static __device__ __forceinline__ uint64_t policy_evict_first() {
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
-// 1-D TMA bulk copy global -> this CTA's shared memory (no multicast).
+// 1-D TMA bulk copy global -> this CTA's shared memory (one destination CTA).
 static __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
     asm volatile(
