@@ -517,47 +517,70 @@ static __device__ JYC_COLD void x_resid(float* x_s, const float* base, const flo
     csync();
 }
 
+// Digits of one lane's 4 consecutive elements of a 32-element block whose 8
+// lanes are lanes 8 q .. 8 q + 7 of the warp (all 32 lanes call; `valid`
+// false contributes zeros and stores nothing). N = rint(x * 2^20 / amax)
+// (round to nearest even: the 1.5 * 2^23 bias, exact for |N| < 2^22), split
+// into three signed 7-bit digits N = 2^14 a + 2^7 b + c; the block scale
+// amax / 2^20 is exact.
+static __device__ __forceinline__ void digits4(float4 v, bool valid, int blk, int sub, int k, int8_t* xd,
+                                               float* xsc) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    if (!valid) return;
+    // 2^20 * RN(1 / amax) == RN(2^20 / amax) (a power-of-two scaling of a
+    // normal result)
+    const float inv = amax > 0.0f ? __fmul_rn(__frcp_rn(amax), 1048576.0f) : 0.0f;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t pa = 0, pb = 0, pc = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        int N = __float_as_int(__fadd_rn(__fmul_rn(vv[e], inv), 12582912.0f)) - 0x4B400000;
+        N = max(-1048576, min(1048576, N));
+        const int c = ((N + 64) & 127) - 64;
+        const int n1 = (N - c) >> 7;
+        const int bd = ((n1 + 64) & 127) - 64;
+        const int a = (n1 - bd) >> 7;
+        pa |= (uint32_t)(a & 255) << (8 * e);
+        pb |= (uint32_t)(bd & 255) << (8 * e);
+        pc |= (uint32_t)(c & 255) << (8 * e);
+    }
+    reinterpret_cast<uint32_t*>(xd)[blk * 8 + sub] = pa;
+    reinterpret_cast<uint32_t*>(xd + k)[blk * 8 + sub] = pb;
+    reinterpret_cast<uint32_t*>(xd + 2 * k)[blk * 8 + sub] = pc;
+    if (sub == 0) xsc[blk] = __fmul_rn(amax, 1.0f / 1048576.0f);  // exact: power of two
+}
+
 // x_s (k floats) -> three int8 digit planes + per-32 block scales, for the
 // 32-element blocks [blk0, blk1) (default: all). A lane takes 4 consecutive
 // elements, 8 lanes one block.
 // GLOBAL: x is a global row written by other CTAs in this launch (read
-// through L2 straight into the digits, no shared-memory copy).
+// through L2 straight into the digits, no shared-memory copy); a lane's
+// loads of up to kDigBatch passes are issued before their digits.
+constexpr int kDigBatch = 8;
 template <bool GLOBAL = false>
 static __device__ void x_digitize(const float* x_s, int k, int8_t* xd, float* xsc, int blk0 = 0, int blk1 = -1) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sub = lane & 7;  // lane within its block
     const int nblk = blk1 < 0 ? (k >> 5) : blk1;
-    for (int base = blk0 + warp * 4; base < nblk; base += kMegaCW * 4) {
-        const int blk = base + (lane >> 3);
-        const bool valid = blk < nblk;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (valid)
-            v = GLOBAL ? __ldcg(reinterpret_cast<const float4*>(x_s + blk * 32) + sub)
-                       : reinterpret_cast<const float4*>(x_s + blk * 32)[sub];
-        float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-        if (!valid) continue;
-        const float inv = amax > 0.0f ? __fdiv_rn(1048576.0f, amax) : 0.0f;
-        const float vv[4] = {v.x, v.y, v.z, v.w};
-        uint32_t pa = 0, pb = 0, pc = 0;
+    constexpr int NB = GLOBAL ? kDigBatch : 1;
+    for (int base0 = blk0 + warp * 4; base0 < nblk; base0 += NB * kMegaCW * 4) {
+        float4 v[NB];
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            int N = __float2int_rn(__fmul_rn(vv[e], inv));
-            N = max(-1048576, min(1048576, N));
-            const int c = ((N + 64) & 127) - 64;
-            const int n1 = (N - c) >> 7;
-            const int bd = ((n1 + 64) & 127) - 64;
-            const int a = (n1 - bd) >> 7;
-            pa |= (uint32_t)(a & 255) << (8 * e);
-            pb |= (uint32_t)(bd & 255) << (8 * e);
-            pc |= (uint32_t)(c & 255) << (8 * e);
+        for (int u = 0; u < NB; u++) {
+            const int blk = base0 + u * kMegaCW * 4 + (lane >> 3);
+            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (blk < nblk)
+                v[u] = GLOBAL ? __ldcg(reinterpret_cast<const float4*>(x_s + blk * 32) + sub)
+                              : reinterpret_cast<const float4*>(x_s + blk * 32)[sub];
         }
-        reinterpret_cast<uint32_t*>(xd)[blk * 8 + sub] = pa;
-        reinterpret_cast<uint32_t*>(xd + k)[blk * 8 + sub] = pb;
-        reinterpret_cast<uint32_t*>(xd + 2 * k)[blk * 8 + sub] = pc;
-        if (sub == 0) xsc[blk] = __fmul_rn(amax, 1.0f / 1048576.0f);  // exact: power of two
+#pragma unroll
+        for (int u = 0; u < NB; u++) {
+            const int blk = base0 + u * kMegaCW * 4 + (lane >> 3);
+            if (base0 + u * kMegaCW * 4 < nblk) digits4(v[u], blk < nblk, blk, sub, k, xd, xsc);
+        }
     }
     csync();
 }
