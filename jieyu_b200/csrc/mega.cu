@@ -465,12 +465,19 @@ static __device__ __forceinline__ bool consume_mat(const MegaMat& M, const int8_
     return true;
 }
 
-// x_s = RMSNorm(x_s) * w over k (sum of squares: per-thread FMA chains + warp/CTA tree)
+// x_s = RMSNorm(x_s) * w over k (sum of squares: per-thread FMA chains + warp/CTA tree).
+// The weights of a thread's first kNormW elements are requested before the
+// sum of squares, so their L2 round trip overlaps it.
+constexpr int kNormW = 8;
 static __device__ void x_norm(float* x_s, int k, const float* w, float eps, float* s_red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NT = kMegaCW * 32;
+    float wr[kNormW];
+#pragma unroll
+    for (int j = 0; j < kNormW; j++) wr[j] = tid + j * NT < k ? __ldg(w + tid + j * NT) : 0.0f;
     csync();
     float ss = 0.0f;
-    for (int i = tid; i < k; i += kMegaCW * 32) ss = __fmaf_rn(x_s[i], x_s[i], ss);
+    for (int i = tid; i < k; i += NT) ss = __fmaf_rn(x_s[i], x_s[i], ss);
     ss = warp_sum(ss);
     if (lane == 0) s_red[warp] = ss;
     csync();
@@ -478,7 +485,12 @@ static __device__ void x_norm(float* x_s, int k, const float* w, float eps, floa
     for (int i = 0; i < kMegaCW; i++) tsum += s_red[i];
     const float den = __fadd_rn(__fdiv_rn(tsum, (float)k), eps);
     const float sc = den <= 0.0f ? 0.0f : __fdiv_rn(1.0f, __fsqrt_rn(den));
-    for (int i = tid; i < k; i += kMegaCW * 32) x_s[i] = __fmul_rn(__fmul_rn(x_s[i], sc), __ldg(w + i));
+#pragma unroll
+    for (int j = 0; j < kNormW; j++) {
+        const int i = tid + j * NT;
+        if (i < k) x_s[i] = __fmul_rn(__fmul_rn(x_s[i], sc), wr[j]);
+    }
+    for (int i = tid + kNormW * NT; i < k; i += NT) x_s[i] = __fmul_rn(__fmul_rn(x_s[i], sc), __ldg(w + i));
     csync();
 }
 
@@ -709,6 +721,17 @@ static __device__ __forceinline__ void rq_warp(const float* src, int nsrc, size_
         x0[tt] = 0.0f;
         x1[tt] = 0.0f;
         if (p < half) {
+            // RoPE factors and bias first (independent of the partials: their
+            // round trips overlap)
+            float c = 1.0f, sn = 0.0f, b0 = 0.0f, b1 = 0.0f;
+            if (ct) {
+                c = __ldg(ct + p);
+                sn = __ldg(stb + p);
+            }
+            if (bias) {
+                b0 = __ldg(bias + 2 * p);
+                b1 = __ldg(bias + 2 * p + 1);
+            }
             // the row = sum of the column groups' partials (+ bias), loaded
             // two groups at a time ahead of the adds
             float v0 = 0.0f, v1 = 0.0f;
@@ -725,11 +748,10 @@ static __device__ __forceinline__ void rq_warp(const float* src, int nsrc, size_
                     }
             }
             if (bias) {
-                v0 = __fadd_rn(v0, __ldg(bias + 2 * p));
-                v1 = __fadd_rn(v1, __ldg(bias + 2 * p + 1));
+                v0 = __fadd_rn(v0, b0);
+                v1 = __fadd_rn(v1, b1);
             }
             if (ct) {
-                const float c = ct[p], sn = stb[p];
                 const float r0 = __fmaf_rn(v0, c, -__fmul_rn(v1, sn));
                 const float r1 = __fmaf_rn(v0, sn, __fmul_rn(v1, c));
                 v0 = r0;
