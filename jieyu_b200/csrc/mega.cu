@@ -1351,6 +1351,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             } else {
                 x_resid(x_s, a.X, a.po, ly.o.spl, a.D, b == 0 ? a.Xb : nullptr);
             }
+            // the down projection's column blocks of this CTA (its plan read
+            // here: the round trip overlaps the norm, not the down prologue)
+            int dn_b0 = 0, dn_b1 = 0;
+            {
+                const MatRange R = mat_range(ly.dn, b);
+                if (R.r1 > R.r0) {
+                    dn_b0 = R.cb0 * (kMegaCB / 32);
+                    dn_b1 = min(R.cb1 * (kMegaCB / 32), a.F / 32);
+                }
+            }
             x_norm(x_s, a.D, ly.rms2, 1e-5f, s_red);
             x_digitize(x_s, a.D, xd, xsc);
             TRACE(tb + 8);
@@ -1360,8 +1370,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) mega_step_kernel(MegaArgs a) 
             ok = ok && grid_barrier(a.bar, base + (++bi) * nct, a.err, &s_ok);
             TRACE(tb + 10);
             if (!ok) break;
-            // down projection + residual (SwiGLU rows digitised from L2)
-            x_digitize<true>(a.h, a.F, xd, xsc);
+            // down projection + residual (SwiGLU rows digitised from L2: only
+            // the column blocks this CTA's tiles read)
+            if (dn_b1 > dn_b0) x_digitize<true>(a.h, a.F, xd, xsc, dn_b0, dn_b1);
             TRACE(tb + 11);
             if (TP) {
                 ok = consume_mat<ME_PART>(ly.dn, xd, xsc, rg, s_acc, cap, a.pd, &s_best, a.err,
