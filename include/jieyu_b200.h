@@ -163,6 +163,15 @@ JYC_API int jyc_matmul_f32(const float* A, const float* Bt, float* C,
                            int m, int n, int k, void* stream);
 JYC_API int jyc_f32_transpose(const float* B, float* Bt, int k, int n, void* stream);
 
+/* C[m][n] = A[m][k] . B for fp16 (IEEE half) weights given TRANSPOSED on the
+ * device, Bt [n][k] (jyc_f16_transpose makes it from the reference's [k][n]):
+ * each half is converted to fp32 exactly and accumulated with fp32 FMAs.
+ * Replaces matmul_f16_avx_fma / matmul_f16_classic(a,b,c,m,n,k)
+ * (libs/matmul_libs/matmul_f16.h:8-41). */
+JYC_API int jyc_matmul_f16(const float* A, const uint16_t* Bt, float* C,
+                           int m, int n, int k, void* stream);
+JYC_API int jyc_f16_transpose(const uint16_t* B, uint16_t* Bt, int k, int n, void* stream);
+
 /* y = x * (1/sqrtf(sum(x^2)/n + eps)) * w, for `rows` rows of n.
  * Replaces rmsnorm(x,y,w,n,eps) (libs/model_libs/rmsnorm/rmsnorm.h:8-78). */
 JYC_API int jyc_rmsnorm(const float* x, float* y, const float* w, int rows, int n,
@@ -246,9 +255,11 @@ JYC_API int jyc_sample(float* logits, int vocab_size, float temperature, float r
 JYC_API int jyc_host_matmul_q(const float* a, const void* b, float* c, int m, int n, int k, int qtype);
 /* matmul(m,n,k,A,B,C) (libs/matmul_libs/matmul.h:7-76): B fp32 [k][n]. */
 JYC_API int jyc_host_matmul_f32(int m, int n, int k, const float* A, const float* B, float* C);
+/* matmul_f16_avx_fma(a,b,c,m,n,k) (libs/matmul_libs/matmul_f16.h:19-41): b fp16 [k][n]. */
+JYC_API int jyc_host_matmul_f16(const float* a, const uint16_t* b, float* c, int m, int n, int k);
 /* matmul_w(B,m,n,k,A,C) (libs/model_libs/wmat_kernel.h:9-16): the WMat
- * dispatch (fp32 -> matmul, blocks -> matmul_q, none -> C = 0; fp16 weights
- * return JYC_ERR_UNSUPPORTED). */
+ * dispatch (fp32 -> matmul, blocks -> matmul_q, fp16 -> matmul_f16, none ->
+ * C = 0). */
 JYC_API int jyc_host_matmul_w(const jyc_wmat* B, int m, int n, int k, const float* A, float* C);
 /* rmsnorm(x,y,w,n,eps) (libs/model_libs/rmsnorm/rmsnorm.h:8-78). */
 JYC_API int jyc_host_rmsnorm(const float* x, float* y, const float* w, int n, float eps);
@@ -280,8 +291,11 @@ typedef struct jyc_model jyc_model;
  * Q8_0 blocks are re-laid into the device layout, fp32 [in][out] matrices are
  * transposed, Q4_K / Q5_K / Q6_K blocks (any mix, with fp32 too; input
  * dimensions multiples of 256) are dequantised once to the reference's fp32
- * values and run on the fp32 kernels; Q/K/V and gate/up are fused. Q8_0 layer
- * weights cannot mix with the other types; fp16 weights are not supported.
+ * values and run on the fp32 kernels; fp16 [in][out] matrices (matmul_f16.h)
+ * are transposed and stay fp16 (2 bytes per weight streamed, converted to fp32
+ * exactly in the GEMV; an fp16 embedding becomes fp32 rows); Q/K/V and
+ * gate/up are fused. The layer weights are all Q8_0, all fp16, or fp32 and
+ * K-quant mixed.
  * Allocates a device KV cache of desc->max_seq positions. Returns NULL on error. */
 JYC_API jyc_model* jyc_model_create(const jyc_model_desc* desc);
 JYC_API void jyc_model_free(jyc_model* m);

@@ -17,6 +17,7 @@
  *   reference (file:line)                                  here
  *   qmat::matmul_q  libs/matmul_libs/matmul_q.h:134        jieyu_b200::qmat::matmul_q
  *   matmul          libs/matmul_libs/matmul.h:7            jieyu_b200::matmul
+ *   matmul_f16_avx_fma libs/matmul_libs/matmul_f16.h:19     jieyu_b200::matmul_f16_avx_fma
  *   matmul_w        libs/model_libs/wmat_kernel.h:9        jieyu_b200::matmul_w
  *   rmsnorm         libs/model_libs/rmsnorm/rmsnorm.h:8    jieyu_b200::rmsnorm
  *   rope_pos        libs/model_libs/rope/rope.h:108        jieyu_b200::rope_pos
@@ -142,7 +143,12 @@ inline void matmul(const int m, const int n, const int k, const float* A, const 
     detail::check(jyc_host_matmul_f32(m, n, k, A, B, C), "matmul");
 }
 
-/* matmul_w (wmat_kernel.h:9-16): the WMat dispatch. */
+/* matmul_f16_avx_fma (matmul_f16.h:19-41): c[m][n] = a[m][k] . b[k][n], b fp16. */
+inline void matmul_f16_avx_fma(const float* a, const uint16_t* b, float* c, int m, int n, int k) {
+    detail::check(jyc_host_matmul_f16(a, b, c, m, n, k), "matmul_f16");
+}
+
+/* matmul_w (wmat_kernel.h:9-16): the WMat dispatch (fp32, fp16, blocks). */
 template <class WMatT>
 inline void matmul_w(const WMatT& B, const int m, const int n, const int k, const float* A, float* C) {
     const jyc_wmat w = detail::to_wmat(B);

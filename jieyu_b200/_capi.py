@@ -87,6 +87,8 @@ SIGNATURES = [
     ("jyc_matmul_qk", _I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     ("jyc_matmul_f32", _I, [_P, _P, _P, _I, _I, _I, _P]),
     ("jyc_f32_transpose", _I, [_P, _P, _I, _I, _P]),
+    ("jyc_matmul_f16", _I, [_P, _P, _P, _I, _I, _I, _P]),
+    ("jyc_f16_transpose", _I, [_P, _P, _I, _I, _P]),
     ("jyc_rmsnorm", _I, [_P, _P, _P, _I, _I, _F, _P]),
     ("jyc_rope_pos", _I, [_P, _I, _I, _I, _I, _P, _P, _P]),
     ("jyc_kv_pack_q8", _I, [_P, _P, _P, _I, _I, _I, _P]),
@@ -95,6 +97,7 @@ SIGNATURES = [
     ("jyc_silu", _I, [_P, _P, _I, _P]),
     ("jyc_host_matmul_q", _I, [_P, _P, _P, _I, _I, _I, _I]),
     ("jyc_host_matmul_f32", _I, [_I, _I, _I, _P, _P, _P]),
+    ("jyc_host_matmul_f16", _I, [_P, _P, _P, _I, _I, _I]),
     ("jyc_host_matmul_w", _I, [_P, _I, _I, _I, _P, _P]),
     ("jyc_host_rmsnorm", _I, [_P, _P, _P, _I, _F]),
     ("jyc_host_rope_pos", _I, [_P, _I, _I, _I, _I, _P, _P]),

@@ -255,10 +255,10 @@ def _info_int(info: dict, key: str, fallback: int) -> int:
 def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> HostWeights:
     """Binds a reference model directory (model.bf + model_info.json) for the
     device path, with the reference's binding rules: per layer the nine
-    tensors of load_weights.h:55-68 (norms f32; linear weights all Q8_0, or
-    any mix of f32 and the K-quants Q4_K / Q5_K / Q6_K, which the device
-    dequantises to fp32 once), optional q/k/v biases,
-    model.embed_tokens.weight (f32, Q8_0 or K-quant), lm_head.weight or
+    tensors of load_weights.h:55-68 (norms f32; linear weights all Q8_0, all
+    f16, or any mix of f32 and the K-quants Q4_K / Q5_K / Q6_K, which the
+    device dequantises to fp32 once), optional q/k/v biases,
+    model.embed_tokens.weight (f32, f16, Q8_0 or K-quant), lm_head.weight or
     (block formats only) the embedding as a tied head, model.norm.weight; shapes as bind_model checks
     them (pipeline.h:99-139). max_seq 0 takes max_position_embeddings
     clamped to [64, 4096], as the reference's C ABI does (main.hpp:64-67);
@@ -284,11 +284,11 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
     def linear(t: Tensor, inn: int, out: int) -> np.ndarray:
         if t.dtype in _BLOCK:
             expect(t, (out, inn))
-        elif t.dtype == F32:
+        elif t.dtype in (F32, F16):  # tensor_wmat: F16 -> WMat.h (load_weights.h:30-36)
             expect(t, (inn, out))
         else:
             raise BFileError(f"{path}: {t.name} is {DTYPE_NAMES.get(t.dtype, t.dtype)}; this device path runs "
-                             "Q8_0, Q4_K, Q5_K, Q6_K and f32 weights")
+                             "Q8_0, Q4_K, Q5_K, Q6_K, f16 and f32 weights")
         return t.array()
 
     def norm(key: str) -> np.ndarray:
@@ -317,6 +317,9 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
     if Q8_0 in kinds and len(kinds) > 1:
         raise BFileError(f"{path}: Q8_0 linear weights mixed with {sorted(DTYPE_NAMES[k] for k in kinds - {Q8_0})}; "
                          "the device path runs Q8_0 models alone")
+    if F16 in kinds and len(kinds) > 1:  # fp16 runs on its own GEMV variant
+        raise BFileError(f"{path}: f16 linear weights mixed with {sorted(DTYPE_NAMES[k] for k in kinds - {F16})}; "
+                         "the device path runs f16 models alone")
     # biases: bind_biases decides by layer 0's q bias (load_weights.h:128-136)
     qkv_bias = bf.get(layer_name(0, BIAS_SUFFIX["bq"])) is not None
     if qkv_bias:
@@ -329,9 +332,9 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
                 ts[f"{key}.{l}"] = t.array()
     emb = need("model.embed_tokens.weight")
     expect(emb, (V, D))
-    if emb.dtype not in (F32,) + tuple(_BLOCK):
+    if emb.dtype not in (F32, F16) + tuple(_BLOCK):
         raise BFileError(f"{path}: model.embed_tokens.weight is {DTYPE_NAMES.get(emb.dtype)}; the device path "
-                         "reads f32, Q8_0 or K-quant embeddings")
+                         "reads f32, f16, Q8_0 or K-quant embeddings")
     head = bf.get("lm_head.weight")
     tied = head is None
     if tied:
@@ -339,19 +342,19 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
     if head.dtype in _BLOCK:
         if head.shape != (V, D):
             raise BFileError(f"{path}: {head.name} must be [vocab, hidden] = [{V}, {D}]")
-    elif head.dtype == F32:
+    elif head.dtype in (F32, F16):  # bind_lm_head (load_weights.h:142-155)
         if head.shape != (D, V):
             raise BFileError(f"{path}: lm_head.weight missing or not [hidden, vocab] = [{D}, {V}]")
     else:
-        raise BFileError(f"{path}: {head.name} is {DTYPE_NAMES.get(head.dtype)}; the device path runs Q8_0 "
-                         "and f32")
+        raise BFileError(f"{path}: {head.name} is {DTYPE_NAMES.get(head.dtype)}; the device path runs Q8_0, "
+                         "K-quant, f16 and f32")
     ts["head"] = head.array()
     if head.dtype in _KQ_CODE:
         qtypes["head"] = _KQ_CODE[head.dtype]
     if tied:
         embed = "tied"
     else:
-        embed = "f32" if emb.dtype == F32 else "q8"  # "q8": a separate block-quantised embedding
+        embed = {F32: "f32", F16: "f16"}.get(emb.dtype, "q8")  # "q8": a separate block-quantised embedding
         ts["embed"] = emb.array()
         if emb.dtype in _KQ_CODE:
             qtypes["embed"] = _KQ_CODE[emb.dtype]
@@ -359,7 +362,7 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
     if max_seq <= 0:
         max_seq = min(max(_info_int(info, "max_position_embeddings", 1024), 64), 4096)
     theta = float(_info_int(info, "rope_theta", 10000))
-    wtype = "q8" if wdt == Q8_0 else "kq" if kinds & set(_KQ_CODE) else "f32"
+    wtype = "q8" if wdt == Q8_0 else "f16" if wdt == F16 else "kq" if kinds & set(_KQ_CODE) else "f32"
     cfg = Config(name or os.path.basename(os.path.normpath(path)), D, L, H, KV, hd, F, V, theta,
                  wtype, embed, qkv_bias, max_seq)
     cos, sin = rope_table(cfg.max_seq, cfg.head_dim, cfg.theta)
@@ -370,7 +373,7 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
 
 def model_dir_tensors(hw: HostWeights) -> tuple[dict, list]:
     """The header and tensor list (name, dtype, shape, bytes) of `hw` in the
-    reference's names and layouts (Q8_0 [out, in], f32 [in, out]), in the
+    reference's names and layouts (Q8_0 [out, in], f32 / f16 [in, out]), in the
     order the reference's converter writes a model: embedding, final norm,
     per layer the nine weights (+ biases), lm_head unless tied."""
     cfg = hw.cfg
@@ -381,14 +384,18 @@ def model_dir_tensors(hw: HostWeights) -> tuple[dict, list]:
     def block_dtype(key: str) -> int:  # bfile dtype of a uint8 (block-quantised) tensor
         return _KQ_FILE.get(hw.qt.get(key, -1), Q8_0)
 
+    def plain(a: np.ndarray) -> int:  # bfile dtype of an [in, out] tensor
+        return F16 if a.dtype == np.uint16 else F32
+
     def lin(key: str, inn: int, out: int):
         a = hw.t[key]
-        return (block_dtype(key), (out, inn), a) if a.dtype == np.uint8 else (F32, (inn, out), a)
+        return (block_dtype(key), (out, inn), a) if a.dtype == np.uint8 else (plain(a), (inn, out), a)
 
     ts = []
     emb_key = "head" if cfg.embed == "tied" else "embed"
     emb = hw.t[emb_key]
-    ts.append(("model.embed_tokens.weight", block_dtype(emb_key) if emb.dtype == np.uint8 else F32, (V, D), emb))
+    ts.append(("model.embed_tokens.weight", block_dtype(emb_key) if emb.dtype == np.uint8 else plain(emb), (V, D),
+               emb))
     ts.append(("model.norm.weight", F32, (D,), hw.t["final_norm"]))
     dims = {"q": (D, qd), "k": (D, kvd), "v": (D, kvd), "o": (qd, D), "gate": (D, F), "down": (F, D), "up": (D, F)}
     for l in range(cfg.layers):
@@ -405,7 +412,7 @@ def model_dir_tensors(hw: HostWeights) -> tuple[dict, list]:
     if cfg.embed != "tied":
         h = hw.t["head"]
         ts.append(("lm_head.weight",) + ((block_dtype("head"), (V, D), h) if h.dtype == np.uint8
-                                         else (F32, (D, V), h)))
+                                         else (plain(h), (D, V), h)))
     return header, ts
 
 

@@ -134,6 +134,25 @@ JYC_API int jyc_matmul_f32(const float* A, const float* Bt, float* C, int m, int
     return launch_matmul_f32_generic(A, Bt, C, m, n, k, S(stream));
 }
 
+JYC_API int jyc_f16_transpose(const uint16_t* B, uint16_t* Bt, int k, int n, void* stream) {
+    clear_error();
+    if (!B || !Bt) return arg_error("f16_transpose: null pointer");
+    return launch_transpose_h(B, Bt, k, n, 0, 1, S(stream));
+}
+
+JYC_API int jyc_matmul_f16(const float* A, const uint16_t* Bt, float* C, int m, int n, int k,
+                           void* stream) {
+    clear_error();
+    if (!A || !Bt || !C) return arg_error("matmul_f16: null pointer");
+    if (m <= 0 || n <= 0 || k <= 0) return arg_error("matmul_f16: empty shape");
+    if (k % 8 == 0 && m <= 8) {
+        GemvArgs g{};
+        g.x = A; g.ldx = k; g.m = m; g.n = n; g.k = k; g.wh = Bt; g.y = C; g.ldy = n;
+        return launch_gemv(g, W_F16, EPI_STORE, S(stream));
+    }
+    return launch_matmul_f16_generic(A, Bt, C, m, n, k, S(stream));
+}
+
 JYC_API int jyc_rmsnorm(const float* x, float* y, const float* w, int rows, int n, float eps,
                         void* stream) {
     clear_error();

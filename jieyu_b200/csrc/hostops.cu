@@ -99,14 +99,21 @@ int matmul_f32_dev(const float* dA, const float* hB, float* dC, int m, int n, in
     return JYC_OK;
 }
 
+int matmul_f16_dev(const float* dA, const uint16_t* hB, float* dC, int m, int n, int k) {
+    Dev b, bt;
+    TRY(b.up(hB, (size_t)k * n * 2));
+    TRY(bt.alloc((size_t)k * n * 2));
+    TRY(jyc_f16_transpose(b.as<uint16_t>(), bt.as<uint16_t>(), k, n, nullptr));
+    TRY(jyc_matmul_f16(dA, bt.as<uint16_t>(), dC, m, n, k, nullptr));
+    JYC_CUDA(cudaDeviceSynchronize());
+    return JYC_OK;
+}
+
 // matmul_w's dispatch (wmat_kernel.h:9-16) over a device A and C.
 int matmul_w_dev(const jyc_wmat* B, int m, int n, int k, const float* dA, float* dC) {
     if (B->f) return matmul_f32_dev(dA, B->f, dC, m, n, k);
     if (B->q) return matmul_q_dev(dA, B->q, dC, m, n, k, B->qt);
-    if (B->h) {
-        set_error("matmul_w: fp16 weights are not supported by this build");
-        return JYC_ERR_UNSUPPORTED;
-    }
+    if (B->h) return matmul_f16_dev(dA, B->h, dC, m, n, k);
     JYC_CUDA(cudaMemset(dC, 0, (size_t)m * n * 4));  // an empty WMat: C = 0, as the reference
     return JYC_OK;
 }
@@ -135,6 +142,17 @@ JYC_API int jyc_host_matmul_f32(int m, int n, int k, const float* A, const float
     TRY(dc.alloc((size_t)m * n * 4));
     TRY(matmul_f32_dev(da.as<float>(), B, dc.as<float>(), m, n, k));
     return dc.down(C, (size_t)m * n * 4);
+}
+
+JYC_API int jyc_host_matmul_f16(const float* a, const uint16_t* b, float* c, int m, int n, int k) {
+    clear_error();
+    if (!a || !b || !c) return arg_error("matmul_f16: null pointer");
+    if (m <= 0 || n <= 0 || k <= 0) return arg_error("matmul_f16: empty shape");
+    Dev da, dc;
+    TRY(da.up(a, (size_t)m * k * 4));
+    TRY(dc.alloc((size_t)m * n * 4));
+    TRY(matmul_f16_dev(da.as<float>(), b, dc.as<float>(), m, n, k));
+    return dc.down(c, (size_t)m * n * 4);
 }
 
 JYC_API int jyc_host_matmul_w(const jyc_wmat* B, int m, int n, int k, const float* A, float* C) {

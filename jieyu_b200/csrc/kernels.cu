@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a) {
 #pragma unroll
             for (int r = 0; r < RPW; r++) acc[mt][r] = 0.0f;
 
-        constexpr int NV = (WT == W_Q8) ? 1 : 2;  // 16-byte vectors per row and lane-step
+        constexpr int NV = (WT == W_F32) ? 2 : 1;  // 16-byte vectors per row and lane-step
         // weight fetch for lane-step c
         auto fetch = [&](int c, uint4 (&w)[RPW][NV], float (&dsc)[RPW]) {
 #pragma unroll
@@ -89,6 +89,9 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a) {
                 if (WT == W_Q8) {
                     w[r][0] = ldg_stream(a.qs + (size_t)row * k + (size_t)c * 16);
                     dsc[r] = h2f(__ldg(a.d + (size_t)row * (k >> 5) + (c >> 1)));
+                } else if (WT == W_F16) {
+                    w[r][0] = ldg_stream(a.wh + (size_t)row * k + (size_t)c * 8);
+                    dsc[r] = 1.0f;
                 } else {
                     const float* p = a.wt + (size_t)row * k + (size_t)c * 8;
                     w[r][0] = ldg_stream(p);
@@ -112,6 +115,13 @@ __global__ void __launch_bounds__(128) gemv_kernel(GemvArgs a) {
                     u8x4_to_f32(wc[r][0].y, &wf[r][4]);
                     u8x4_to_f32(wc[r][0].z, &wf[r][8]);
                     u8x4_to_f32(wc[r][0].w, &wf[r][12]);
+                } else if (WT == W_F16) {  // exact: every half is a float
+                    const uint32_t hw[4] = {wc[r][0].x, wc[r][0].y, wc[r][0].z, wc[r][0].w};
+#pragma unroll
+                    for (int v = 0; v < 4; v++) {
+                        wf[r][2 * v] = h2f((uint16_t)(hw[v] & 0xffffu));
+                        wf[r][2 * v + 1] = h2f((uint16_t)(hw[v] >> 16));
+                    }
                 } else {
 #pragma unroll
                     for (int v = 0; v < NV; v++) {
@@ -296,7 +306,8 @@ int launch_gemv(const GemvArgs& a, int wtype, int epi, cudaStream_t s) {
         if (a.k % 32) return arg_error("gemv: Q8_0 needs k % 32 == 0");
         return launch_gemv_epi<W_Q8>(a, epi, s);
     }
-    if (a.k % 8) return arg_error("gemv: fp32 path needs k % 8 == 0");
+    if (a.k % 8) return arg_error("gemv: fp32 / fp16 paths need k % 8 == 0");
+    if (wtype == W_F16) return launch_gemv_epi<W_F16>(a, epi, s);
     return launch_gemv_epi<W_F32>(a, epi, s);
 }
 
@@ -727,8 +738,9 @@ int launch_q8_repack(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d,
 }
 
 // B [k][n] -> Bt rows: source column c lands in row row_off + c*row_stride of Bt [.][k].
-__global__ void transpose_kernel(const float* B, float* Bt, int k, int n, int row_off, int row_stride) {
-    __shared__ float tile[32][33];
+template <typename T>
+__global__ void transpose_kernel(const T* B, T* Bt, int k, int n, int row_off, int row_stride) {
+    __shared__ T tile[32][33];
     const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
     for (int j = threadIdx.y; j < 32; j += blockDim.y) {
         const int r = by + j, c = bx + threadIdx.x;
@@ -745,7 +757,28 @@ int launch_transpose(const float* B, float* Bt, int k, int n, int row_off, int r
                      cudaStream_t s) {
     if (k <= 0 || n <= 0) return arg_error("transpose: empty shape");
     dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
-    transpose_kernel<<<grid, block, 0, s>>>(B, Bt, k, n, row_off, row_stride);
+    transpose_kernel<float><<<grid, block, 0, s>>>(B, Bt, k, n, row_off, row_stride);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+int launch_transpose_h(const uint16_t* B, uint16_t* Bt, int k, int n, int row_off, int row_stride,
+                       cudaStream_t s) {
+    if (k <= 0 || n <= 0) return arg_error("transpose: empty shape");
+    dim3 grid((n + 31) / 32, (k + 31) / 32), block(32, 8);
+    transpose_kernel<uint16_t><<<grid, block, 0, s>>>(B, Bt, k, n, row_off, row_stride);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+
+// fp16 -> fp32, exact (wmat::row_to_f32: the embedding of an fp16 model).
+__global__ void h2f_kernel(const uint16_t* h, float* f, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        f[i] = h2f(h[i]);
+}
+int launch_h2f(const uint16_t* h, float* f, size_t n, cudaStream_t s) {
+    if (n == 0) return JYC_OK;
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 16);
+    h2f_kernel<<<blocks, 256, 0, s>>>(h, f, n);
     JYC_LAUNCHED();
     return JYC_OK;
 }
@@ -819,9 +852,12 @@ int launch_argmax(const float* v, int n, unsigned long long* slot, int* out, cud
 }
 
 // ---------------------------------------------------------------------------
-// General fp32 C = A . Bt^T for any shape (op entry point; the model path uses
-// the GEMV kernel). 32x32 tiles, fp32 FMA.
-__global__ void matmul_f32_kernel(const float* A, const float* Bt, float* C, int m, int n, int k) {
+// General C = A . Bt^T for any shape, fp32 or fp16 weights (op entry points;
+// the model path uses the GEMV kernel). 32x32 tiles, fp32 FMA.
+static __device__ __forceinline__ float w_to_f32(float w) { return w; }
+static __device__ __forceinline__ float w_to_f32(uint16_t w) { return h2f(w); }
+template <typename T>
+__global__ void matmul_f32_kernel(const float* A, const T* Bt, float* C, int m, int n, int k) {
     __shared__ float as[32][33], bs[32][33];
     const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
     const int row0 = blockIdx.y * 32, col0 = blockIdx.x * 32;
@@ -831,7 +867,7 @@ __global__ void matmul_f32_kernel(const float* A, const float* Bt, float* C, int
             const int r = row0 + j, p = p0 + tx;
             as[j][tx] = (r < m && p < k) ? A[(size_t)r * k + p] : 0.0f;
             const int c = col0 + j;
-            bs[j][tx] = (c < n && p < k) ? Bt[(size_t)c * k + p] : 0.0f;
+            bs[j][tx] = (c < n && p < k) ? w_to_f32(Bt[(size_t)c * k + p]) : 0.0f;
         }
         __syncthreads();
 #pragma unroll 8
@@ -851,7 +887,14 @@ __global__ void matmul_f32_kernel(const float* A, const float* Bt, float* C, int
 int launch_matmul_f32_generic(const float* A, const float* Bt, float* C, int m, int n, int k,
                               cudaStream_t s) {
     dim3 grid((n + 31) / 32, (m + 31) / 32), block(32, 8);
-    matmul_f32_kernel<<<grid, block, 0, s>>>(A, Bt, C, m, n, k);
+    matmul_f32_kernel<float><<<grid, block, 0, s>>>(A, Bt, C, m, n, k);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+int launch_matmul_f16_generic(const float* A, const uint16_t* Bt, float* C, int m, int n, int k,
+                              cudaStream_t s) {
+    dim3 grid((n + 31) / 32, (m + 31) / 32), block(32, 8);
+    matmul_f32_kernel<uint16_t><<<grid, block, 0, s>>>(A, Bt, C, m, n, k);
     JYC_LAUNCHED();
     return JYC_OK;
 }

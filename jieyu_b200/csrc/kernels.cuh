@@ -5,6 +5,7 @@
 //                        d : n*(k/32) fp16 scales, row-major.
 //                        34 bytes per 32 weights, the same as the reference blocks.
 //   fp32 matrix [n][k]   row-major (the reference's [k][n] transposed once at upload).
+//   fp16 matrix [n][k]   row-major IEEE halves (the reference's [k][n] transposed once).
 //   KV cache (model)     k8/v8 int8 [layer][kv_head][pos][head_dim], ks/vs fp32
 //                        [layer][kv_head][pos]; the op-level entry uses the
 //                        reference's [pos][kv_head][head_dim] through strides.
@@ -13,7 +14,7 @@
 
 namespace jyc {
 
-enum WType { W_Q8 = 0, W_F32 = 1 };
+enum WType { W_Q8 = 0, W_F32 = 1, W_F16 = 2 };
 enum Epi { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
 
 // Step state shared by the kernels of one decode step (device memory).
@@ -57,6 +58,7 @@ struct GemvArgs {
     const uint8_t* qs;     // Q8 weights
     const uint16_t* d;
     const float* wt;       // fp32 weights [n][k]
+    const uint16_t* wh;    // fp16 weights [n][k]
     const float* norm_w;   // optional fused RMSNorm of x (weights [k]); nullptr = off
     float eps;
     float* y;              // output [m][ldy]
@@ -133,6 +135,9 @@ int launch_q8_repack(const void* blocks, int n, int k, uint8_t* qs, uint16_t* d,
                      int row_stride, cudaStream_t s);
 int launch_transpose(const float* B, float* Bt, int k, int n, int row_off, int row_stride,
                      cudaStream_t s);
+int launch_transpose_h(const uint16_t* B, uint16_t* Bt, int k, int n, int row_off, int row_stride, cudaStream_t s);
+int launch_h2f(const uint16_t* h, float* f, size_t n, cudaStream_t s);
+int launch_matmul_f16_generic(const float* A, const uint16_t* Bt, float* C, int m, int n, int k, cudaStream_t s);
 int launch_silu(const float* x, float* y, int n, cudaStream_t s);
 int launch_kv_pack(const float* src, int8_t* dst, float* sc, int heads, int hd, int n,
                    cudaStream_t s);

@@ -39,9 +39,11 @@ struct DevMat {  // one weight matrix on the device, [n][k]
     uint16_t* td = nullptr;
     uint8_t* rexp = nullptr; // Q8: per-row exponent of the largest scale (tensor-core path)
     float* f = nullptr;
+    uint16_t* h = nullptr;   // fp16 [n][k]
     int n = 0, k = 0;
     bool tiled = false;
-    double bytes() const { return f ? 4.0 * n * k : (double)n * k * 34.0 / 32.0; }
+    double bytes() const { return f ? 4.0 * n * k : h ? 2.0 * n * k : (double)n * k * 34.0 / 32.0; }
+    int wtype() const { return f ? W_F32 : h ? W_F16 : W_Q8; }
 };
 
 // Kernel classes of one generic decode step (for per-kernel timing).
@@ -181,10 +183,8 @@ namespace {
 // [row_off + r*row_stride] of `dst` (device layout, n_total rows x k).
 int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int n_total, int row_off,
                 int row_stride, void* staging, size_t staging_bytes, int expect_type) {
-    if (w.h != nullptr && w.f == nullptr && w.q == nullptr) {
-        set_error("fp16 weights are not supported by the B200 path");
-        return JYC_ERR_UNSUPPORTED;
-    }
+    // fp16 weights ([in][out] halves, matmul_f16.h) stay fp16 on the device
+    const bool f16 = w.h != nullptr && w.f == nullptr && w.q == nullptr;
     // K-quant blocks (Q4_K / Q5_K / Q6_K) are dequantised to the reference's
     // fp32 values here and then run on the fp32 path
     const bool kq = w.q != nullptr && w.f == nullptr && kquant_block_bytes(w.qt) != 0;
@@ -193,12 +193,12 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
         set_error("quantised weights must be Q8_0, Q4_K, Q5_K or Q6_K (got type " + std::to_string((int)w.qt) + ")");
         return JYC_ERR_UNSUPPORTED;
     }
-    if (!q8 && !kq && w.f == nullptr) {
+    if (!q8 && !kq && !f16 && w.f == nullptr) {
         set_error("missing weight tensor");
         return JYC_ERR_ARG;
     }
-    if ((q8 ? W_Q8 : W_F32) != expect_type) {
-        set_error("Q8_0 linear weights mixed with fp32 or K-quant ones are not supported");
+    if ((q8 ? W_Q8 : f16 ? W_F16 : W_F32) != expect_type) {
+        set_error("linear weights must all be Q8_0, all fp16, or all fp32 / K-quant");
         return JYC_ERR_UNSUPPORTED;
     }
     if (kq && k % 256) return arg_error("K-quant weights need an input dimension that is a multiple of 256");
@@ -213,18 +213,22 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
                 TRY(m->alloc(&dst.tq, (size_t)n_total * k));
                 TRY(m->alloc(&dst.td, (size_t)n_total * (k / 32)));
             }
+        } else if (f16) {
+            TRY(m->alloc(&dst.h, (size_t)n_total * k));
         } else {
             TRY(m->alloc(&dst.f, (size_t)n_total * k));
         }
     }
-    const size_t bytes = q8   ? (size_t)n * (k / 32) * 34
-                         : kq ? (size_t)n * (k / 256) * kquant_block_bytes(w.qt)
-                              : (size_t)n * k * 4;
+    const size_t bytes = q8    ? (size_t)n * (k / 32) * 34
+                         : kq  ? (size_t)n * (k / 256) * kquant_block_bytes(w.qt)
+                         : f16 ? (size_t)n * k * 2
+                               : (size_t)n * k * 4;
     if (bytes > staging_bytes) {
         set_error("internal: staging buffer too small");
         return JYC_ERR_ARG;
     }
-    JYC_CUDA(cudaMemcpyAsync(staging, w.f ? (const void*)w.f : w.q, bytes, cudaMemcpyHostToDevice, m->stream));
+    const void* src = w.f ? (const void*)w.f : f16 ? (const void*)w.h : w.q;
+    JYC_CUDA(cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, m->stream));
     if (q8) {
         TRY(launch_q8_repack(staging, n, k, dst.qs, dst.d, row_off, row_stride, m->stream));
         if (dst.tiled)
@@ -232,6 +236,8 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
     } else if (kq) {
         TRY(launch_kquant_dequant(static_cast<const uint8_t*>(staging), n, k, w.qt, dst.f, row_off, row_stride,
                                   m->stream));
+    } else if (f16) {
+        TRY(launch_transpose_h(static_cast<const uint16_t*>(staging), dst.h, k, n, row_off, row_stride, m->stream));
     } else
         TRY(launch_transpose(static_cast<const float*>(staging), dst.f, k, n, row_off, row_stride, m->stream));
     // the staging buffer is reused by the next upload: wait for this one
@@ -402,7 +408,11 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     if (m->vocab_off < 0 || (long long)m->vocab_off + m->V > m->Ve)
         return arg_error("model: LM-head rows must be a slice of the embedding's vocabulary");
     m->q_dim = m->H * m->hd; m->kv_dim = m->KV * m->hd; m->nqkv = m->q_dim + 2 * m->kv_dim;
-    m->wtype = (d->layers[0].Wq.q != nullptr && d->layers[0].Wq.qt == JYC_Q8_0) ? W_Q8 : W_F32;  // K-quant: fp32 path
+    // K-quant: the fp32 path; fp16: halves on the device (generic kernels)
+    m->wtype = (d->layers[0].Wq.q != nullptr && d->layers[0].Wq.qt == JYC_Q8_0) ? W_Q8
+               : (d->layers[0].Wq.h != nullptr && d->layers[0].Wq.f == nullptr && d->layers[0].Wq.q == nullptr)
+                   ? W_F16
+                   : W_F32;
     const int kq = m->wtype == W_Q8 ? 32 : 8;
     if (m->D % kq || m->q_dim % kq || m->F % kq)
         return arg_error("model: hidden, heads*head_dim and intermediate must be multiples of " +
@@ -454,7 +464,9 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
                            2.0 * m->D * 4 + (dl.bias ? m->nqkv * 4.0 : 0.0);
     }
     // LM head (Q8 [V][D] blocks, or fp32 [D][V]) and embedding
-    TRY(upload_wmat(m, d->lm_head, m->V, m->D, m->head, m->V, 0, 1, staging, stage, head_q8 ? W_Q8 : W_F32));
+    const bool head_f16 = d->lm_head.h != nullptr && d->lm_head.f == nullptr && d->lm_head.q == nullptr;
+    TRY(upload_wmat(m, d->lm_head, m->V, m->D, m->head, m->V, 0, 1, staging, stage,
+                    head_q8 ? W_Q8 : head_f16 ? W_F16 : W_F32));
     m->weight_bytes += m->head.bytes();
     if (d->embed.f != nullptr) {
         TRY(upload_f32(m, d->embed.f, (size_t)m->Ve * m->D, &m->embed_f));
@@ -477,8 +489,19 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
         TRY(launch_kquant_dequant(static_cast<const uint8_t*>(staging), m->Ve, m->D, d->embed.qt, m->embed_f, 0, 1,
                                   m->stream));
         JYC_CUDA(cudaStreamSynchronize(m->stream));
+    } else if (d->embed.h != nullptr) {
+        // fp16 embedding rows (wmat::row_to_f32, exact): fp32 rows
+        const size_t eb = (size_t)m->Ve * m->D * 2;
+        if (eb > stage) {
+            set_error("internal: staging buffer too small for the embedding");
+            return JYC_ERR_ARG;
+        }
+        TRY(m->alloc(&m->embed_f, (size_t)m->Ve * m->D));
+        JYC_CUDA(cudaMemcpyAsync(staging, d->embed.h, eb, cudaMemcpyHostToDevice, m->stream));
+        TRY(launch_h2f(static_cast<const uint16_t*>(staging), m->embed_f, (size_t)m->Ve * m->D, m->stream));
+        JYC_CUDA(cudaStreamSynchronize(m->stream));
     } else {
-        set_error("embedding must be fp32, Q8_0, Q4_K, Q5_K or Q6_K");
+        set_error("embedding must be fp32, fp16, Q8_0, Q4_K, Q5_K or Q6_K");
         return JYC_ERR_UNSUPPORTED;
     }
     m->weight_bytes += (m->embed_f ? 4.0 * m->D : m->D * 34.0 / 32.0) + 4.0 * m->D;  // row + final norm
@@ -576,7 +599,7 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         // RMSNorm -> fused Q|K|V GEMV (+ bias)
         g.x = m->X; g.ldx = m->D; g.n = m->nqkv; g.k = m->D;
-        g.qs = ly.qkv.qs; g.d = ly.qkv.d; g.wt = ly.qkv.f; g.norm_w = ly.rms1;
+        g.qs = ly.qkv.qs; g.d = ly.qkv.d; g.wt = ly.qkv.f; g.wh = ly.qkv.h; g.norm_w = ly.rms1;
         g.y = m->qkv; g.ldy = m->nqkv; g.bias = ly.bias;
         TRY(launch_gemv(g, m->wtype, ly.bias ? EPI_BIAS : EPI_STORE, s));
         MARK(K_QKV);
@@ -602,14 +625,14 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
         g = GemvArgs{};
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         g.x = m->attn; g.ldx = m->q_dim; g.n = m->D; g.k = m->q_dim;
-        g.qs = ly.o.qs; g.d = ly.o.d; g.wt = ly.o.f; g.y = m->X; g.ldy = m->D;
+        g.qs = ly.o.qs; g.d = ly.o.d; g.wt = ly.o.f; g.wh = ly.o.h; g.y = m->X; g.ldy = m->D;
         TRY(launch_gemv(g, m->wtype, EPI_RESID, s));
         MARK(K_OPROJ);
         // RMSNorm -> gate|up GEMV -> SwiGLU
         g = GemvArgs{};
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         g.x = m->X; g.ldx = m->D; g.n = 2 * m->F; g.k = m->D;
-        g.qs = ly.gateup.qs; g.d = ly.gateup.d; g.wt = ly.gateup.f;
+        g.qs = ly.gateup.qs; g.d = ly.gateup.d; g.wt = ly.gateup.f; g.wh = ly.gateup.h;
         g.norm_w = ly.rms2; g.y = m->h; g.ldy = m->F;
         TRY(launch_gemv(g, m->wtype, EPI_SWIGLU, s));
         MARK(K_GATEUP);
@@ -617,7 +640,7 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
         g = GemvArgs{};
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         g.x = m->h; g.ldx = m->F; g.n = m->D; g.k = m->F;
-        g.qs = ly.down.qs; g.d = ly.down.d; g.wt = ly.down.f; g.y = m->X; g.ldy = m->D;
+        g.qs = ly.down.qs; g.d = ly.down.d; g.wt = ly.down.f; g.wh = ly.down.h; g.y = m->X; g.ldy = m->D;
         TRY(launch_gemv(g, m->wtype, EPI_RESID, s));
         MARK(K_DOWN);
     }
@@ -630,9 +653,9 @@ int run_head(jyc_model* m, int row, cudaStream_t s) {
     GemvArgs g{};
     g.m = 1; g.eps = 1e-5f; g.st = m->st; g.tokens = m->tokens;
     g.x = m->X + (size_t)row * m->D; g.ldx = m->D; g.n = m->V; g.k = m->D;
-    g.qs = m->head.qs; g.d = m->head.d; g.wt = m->head.f; g.norm_w = m->final_norm;
+    g.qs = m->head.qs; g.d = m->head.d; g.wt = m->head.f; g.wh = m->head.h; g.norm_w = m->final_norm;
     g.y = m->logits; g.ldy = m->V;
-    TRY(launch_gemv(g, m->head.f ? W_F32 : W_Q8, EPI_ARGMAX, s));
+    TRY(launch_gemv(g, m->head.wtype(), EPI_ARGMAX, s));
     MARK(K_HEAD);
     return JYC_OK;
 }
@@ -1228,8 +1251,8 @@ JYC_API int jyc_model_profile_decode(jyc_model* m, int n_steps, void* stream, do
         cudaGraphDestroy(graph);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
     }
-    const double wb = m->wtype == W_Q8 ? 34.0 / 32.0 : 4.0;
-    const double hb = m->head.f ? 4.0 : 34.0 / 32.0;
+    const double wb = m->wtype == W_Q8 ? 34.0 / 32.0 : m->wtype == W_F16 ? 2.0 : 4.0;
+    const double hb = m->head.f ? 4.0 : m->head.h ? 2.0 : 34.0 / 32.0;
     bytes[K_EMBED] = m->embed_f ? 4.0 * m->D : m->D * 34.0 / 32.0;
     bytes[K_QKV] = (double)m->nqkv * m->D * wb + 4.0 * m->D;
     bytes[K_ROPEQ] = 4.0 * m->nqkv;

@@ -2,7 +2,7 @@
 
 * ``Config``      — hyper-parameters (the reference's ModelInfo / ModelRefs fields).
 * ``HostWeights`` — host buffers in the reference's own layouts (Q8_0 blocks
-  [out][in/32]x34 B, fp32 [in][out], fp32 norms/biases) plus the
+  [out][in/32]x34 B, fp32 or fp16 [in][out], fp32 norms/biases) plus the
   ``LayerWeights`` / ``jyc_model_desc`` structs that point at them, i.e. what
   ``bind_model`` produces (libs/model_libs/pipeline.h:63-153).
 * ``DeviceModel`` — the uploaded model: ``generate`` mirrors ``generate()``
@@ -34,8 +34,8 @@ class Config:
     inter: int
     vocab: int
     theta: float
-    wtype: str = "q8"          # linear weights: "q8" (Q8_0), "f32", or "kq" (Q4_K / Q5_K / Q6_K blocks)
-    embed: str = "f32"         # "f32", "q8" (separate) or "tied" (Q8_0, = LM head)
+    wtype: str = "q8"          # linear weights: "q8" (Q8_0), "f32", "f16" or "kq" (Q4_K / Q5_K / Q6_K blocks)
+    embed: str = "f32"         # "f32", "f16", "q8" (separate) or "tied" (Q8_0, = LM head)
     qkv_bias: bool = False
     max_seq: int = 512
     prompt_len: int = 32
@@ -176,6 +176,18 @@ class HostWeights:
         return cls(cfg, t, cos, sin)
 
     @classmethod
+    def synthetic_f16(cls, cfg: Config, seed: int = 1234) -> "HostWeights":
+        """The seeded fp32 weights of `synthetic` (fp32 variant of cfg), every
+        linear matrix, the LM head and the embedding rounded to fp16 (IEEE
+        halves, round to nearest even) in the reference's [in][out] layout."""
+        f = cls.synthetic(replace(cfg, wtype="f32", embed="f32"), seed)
+        t = {}
+        for key, a in f.t.items():
+            two_d = key.split(".")[0] in ("q", "k", "v", "o", "gate", "up", "down", "head", "embed")
+            t[key] = a.astype(np.float16).view(np.uint16) if two_d else a
+        return cls(replace(cfg, wtype="f16", embed="f16"), t, f.cos, f.sin)
+
+    @classmethod
     def synthetic_kquant(cls, cfg: Config, seed: int = 1234) -> "HostWeights":
         """Seeded K-quant weights (the formats of the reference's downloads),
         mixed per matrix as Q4_K_M files mix them: Q, O, gate Q4_K; K, up
@@ -292,6 +304,8 @@ class HostWeights:
         a = self.t[key]
         if a.dtype == np.uint8:
             return WMat(None, None, _ptr(a), self.qt.get(key, JYC_Q8_0))
+        if a.dtype == np.uint16:  # IEEE halves, [in][out] (matmul_f16.h)
+            return WMat(None, _ptr(a), None, 0)
         return WMat(_ptr(a), None, None, 0)
 
     def _build_desc(self) -> None:
@@ -329,11 +343,12 @@ class HostWeights:
         """Algorithmic weight bytes one decode token reads (Q8_0: 34 B / 32)."""
         cfg = self.cfg
         D, F = cfg.hidden, cfg.inter
-        per = 34.0 / 32.0 if cfg.wtype == "q8" else 4.0  # "kq": dequantised to fp32 on the device
+        per = {"q8": 34.0 / 32.0, "f16": 2.0}.get(cfg.wtype, 4.0)  # "kq": dequantised to fp32 on the device
         lin = (cfg.q_dim + 2 * cfg.kv_dim) * D + D * cfg.q_dim + 3 * F * D
         b = cfg.layers * (lin * per + 2 * D * 4 + (cfg.q_dim + 2 * cfg.kv_dim) * 4 * cfg.qkv_bias)
         head_q8 = self.t["head"].dtype == np.uint8 and self.qt.get("head", JYC_Q8_0) == JYC_Q8_0
-        b += cfg.vocab * D * (34.0 / 32.0 if head_q8 else 4.0) + 4 * D
+        head_b = 34.0 / 32.0 if head_q8 else 2.0 if self.t["head"].dtype == np.uint16 else 4.0
+        b += cfg.vocab * D * head_b + 4 * D
         emb_key = "head" if cfg.embed == "tied" else "embed"
         emb_q8 = self.t[emb_key].dtype == np.uint8 and self.qt.get(emb_key, JYC_Q8_0) == JYC_Q8_0
         b += D * (34.0 / 32.0 if emb_q8 else 4.0)

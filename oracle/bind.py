@@ -26,6 +26,7 @@ def _sig(lib, prefix: str):
         "matmul_q8": (None, [_P, _P, _P, _I, _I, _I]),
         "matmul_qk": (None, [_P, _P, _P, _I, _I, _I, _I]),
         "matmul_f32": (None, [_I, _I, _I, _P, _P, _P]),
+        "matmul_f16": (None, [_P, _P, _P, _I, _I, _I]),
         "rmsnorm": (None, [_P, _P, _P, _I, _F]),
         "rope_table": (None, [_I, _I, _F, _P, _P]),
         "rope_pos": (None, [_P, _I, _I, _I, _I, _P, _P]),

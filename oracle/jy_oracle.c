@@ -266,6 +266,26 @@ void jyo_matmul_f32(int m, int n, int k, const float* A, const float* B, float* 
     }
 }
 
+/* matmul_f16_avx_fma (matmul_f16.h:19-41): C = 0, then per row i and input
+ * index p in order, every output j += a[i][p] * f32(b[p][j]) as one fused
+ * multiply-add: _mm256_fmadd_ps over the 8-wide column groups (:33-35), and
+ * the scalar n % 8 tail (:37), which the compiler contracts to an FMA inside
+ * that avx2/fma target function (checked bit for bit against the compiled
+ * reference). */
+void jyo_matmul_f16(const float* a, const uint16_t* b, float* c, int m, int n, int k) {
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < m; i++) {
+        float* crow = c + (size_t)i * n;
+        const float* arow = a + (size_t)i * k;
+        for (int j = 0; j < n; j++) crow[j] = 0.0f;
+        for (int p = 0; p < k; p++) {
+            const float va = arow[p];
+            const uint16_t* brow = b + (size_t)p * n;
+            for (int j = 0; j < n; j++) crow[j] = fmaf(va, f16_to_f32(brow[j]), crow[j]);
+        }
+    }
+}
+
 /* rmsnorm x86_classic.txt:1-27: two 8-lane FMA sums (16-wide steps, then one
  * 8-wide step), hsum, scalar tail; y = (x*scale)*w. */
 void jyo_rmsnorm(const float* x, float* y, const float* w, int n, float eps) {
@@ -488,9 +508,11 @@ void jyo_cache_write(void* p, int layer, int npos, const int8_t* k, const float*
     memcpy(c->vs + lay * c->KV, vs, (size_t)npos * c->KV * sizeof(float));
 }
 
-/* matmul_w (wmat_kernel.h:9-16): fp32 [k][n] -> matmul, Q8_0 / K-quant [n][k] -> matmul_q. */
+/* matmul_w (wmat_kernel.h:9-16): fp32 [k][n] -> matmul, fp16 [k][n] -> matmul_f16, Q8_0 / K-quant
+ * [n][k] -> matmul_q. */
 static int matmul_w(const jyc_wmat* w, int m, int n, int k, const float* A, float* Cc) {
     if (w->f) { jyo_matmul_f32(m, n, k, A, w->f, Cc); return 0; }
+    if (w->h && !w->q) { jyo_matmul_f16(A, w->h, Cc, m, n, k); return 0; }
     if (w->q && w->qt == JYC_Q8_0) { jyo_matmul_q8(A, w->q, Cc, m, n, k); return 0; }
     if (w->q && kq_bytes(w->qt)) return jyo_matmul_qk(A, w->q, Cc, m, n, k, w->qt);
     return -1;
@@ -499,6 +521,10 @@ static int matmul_w(const jyc_wmat* w, int m, int n, int k, const float* A, floa
 /* wmat_row (wmat_kernel.h:18-29). */
 static int wmat_row(const jyc_wmat* w, size_t id, int width, float* dst) {
     if (w->f) { memcpy(dst, w->f + id * (size_t)width, (size_t)width * sizeof(float)); return 0; }
+    if (w->h) {  /* wmat::row_to_f32: exact */
+        for (int t = 0; t < width; t++) dst[t] = f16_to_f32(w->h[id * (size_t)width + t]);
+        return 0;
+    }
     if (w->q && w->qt == JYC_Q8_0) {
         const uint8_t* row = (const uint8_t*)w->q + id * (size_t)(width / 32) * 34;
         for (int bl = 0; bl < width / 32; bl++) dequant_q8(row + (size_t)bl * 34, dst + bl * 32);

@@ -25,6 +25,8 @@ void jyo_matmul_q8(const float* a, const void* b, float* c, int m, int n, int k)
 int jyo_matmul_qk(const float* a, const void* b, float* c, int m, int n, int k, int t);
 /* matmul (libs/matmul_libs/matmul.h:7-76), B = [k][n]. */
 void jyo_matmul_f32(int m, int n, int k, const float* A, const float* B, float* C);
+/* matmul_f16_avx_fma (libs/matmul_libs/matmul_f16.h:19-41): B fp16 [k][n]. */
+void jyo_matmul_f16(const float* a, const uint16_t* b, float* c, int m, int n, int k);
 /* rmsnorm (libs/model_libs/rmsnorm/x86/x86_classic.txt:1-27). */
 void jyo_rmsnorm(const float* x, float* y, const float* w, int n, float eps);
 /* RoPETable::init (libs/date_libs/date.h:52-66). */

@@ -112,6 +112,12 @@ void jyref_matmul_f32(int m, int n, int k, const float* A, const float* B, float
     matmul(m, n, k, A, B, C);
 }
 
+void jyref_matmul_f16(const float* a, const uint16_t* b, float* c, int m, int n, int k) {
+    WMat w{};
+    w.h = b;
+    matmul_w(w, m, n, k, a, c);  // the reference's own dispatch picks its f16 kernel
+}
+
 void jyref_rmsnorm(float* x, float* y, const float* w, int n, float eps) {
     rmsnorm(x, y, w, n, eps);
 }

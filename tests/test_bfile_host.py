@@ -39,6 +39,7 @@ def _models():
         "q8_tied_bias": HostWeights.synthetic(TINY_Q8_TIED, seed=5),
         "q8_separate": HostWeights.synthetic(TINY_Q8, seed=6),
         "f32_rect": HostWeights.synthetic(TINY_F32, seed=7),
+        "f16_rect": HostWeights.synthetic_f16(TINY_F32, seed=8),
         "kquant_mixed": kquant_model(),
     }
 
@@ -125,7 +126,7 @@ def test_reference_binds_the_same_bytes(ref, tmp_path, model):
                 if name in hw.qt:
                     want = {0: bfile.Q4K, 1: bfile.Q5K, 2: bfile.Q6K}[hw.qt[name]]
                 else:
-                    want = bfile.Q8_0 if hw.cfg.wtype == "q8" else bfile.F32
+                    want = {"q8": bfile.Q8_0, "f16": bfile.F16}.get(hw.cfg.wtype, bfile.F32)
                 assert dt[12 * l + k] == want
     emb_key = "head" if hw.cfg.embed == "tied" else "embed"
     assert out[12 * L] == off(emb_key)
@@ -215,7 +216,8 @@ def test_binding_errors(ref, tmp_path):
     _write_dir(d, hw, lambda ts: [t for t in ts if t[0] != "model.norm.weight"])
     with pytest.raises(bfile.BFileError, match="model.norm.weight"):
         bfile.load_model_dir(d)
-    # an f16 weight: valid for the reference, not a format this device path runs
+    # one f16 weight among f32 ones: valid for the reference, a mix this device
+    # path does not run (fp16 models decode with all linear weights in fp16)
     d = str(tmp_path / "f16")
     o = "model.layers.0.self_attn.o_proj.weight"
     _write_dir(d, hw, lambda ts: [(n, bfile.F16, s, np.zeros(int(np.prod(s)), np.uint16)) if n == o

@@ -93,3 +93,22 @@ def test_oracle_long_context_matches_reference(oracle, name):
     out, fed = mgl.run(oracle, hw, case["ctx"], None)
     assert fed == case["fed"]
     assert [sha(x) for x in out] == [r["sha"] for r in case["steps"]]
+
+
+def test_oracle_f16_matches_reference(oracle):
+    """fp16 weights (matmul_f16.h:19-41 through matmul_w; tests/golden/f16.json,
+    the reference's own fma path): the oracle's matmul_f16 digests, tail
+    columns included, and the greedy sequence of the configs[0] shape with
+    fp16 linear matrices, LM head and embedding are identical."""
+    import make_golden_f16 as mgf
+    g = golden("f16.json")
+    for m, n, k in mgf.F16_CASES:
+        a, b = mgf.f16_inputs(m, n, k)
+        c = np.empty(m * n, np.float32)
+        oracle.matmul_f16(ptr(a), ptr(b), ptr(c), m, n, k)
+        assert sha(c) == g["ops"][f"f16_{m}_{n}_{k}"], (m, n, k)
+    cfg = CONFIGS["c0"]
+    hw = HostWeights.synthetic_f16(cfg)
+    pr = prompt_ids(cfg)
+    assert list(pr) == g["c0_f16"]["prompt"]
+    assert list(oracle.generate(hw.desc, pr, 64, max_seq=cfg.max_seq)) == g["c0_f16"]["greedy"]
