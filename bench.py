@@ -769,7 +769,9 @@ def run_kquant(args):
     reference's own qmat::matmul_q on one layer's Q4_K matrices (oracle/_ref,
     else the oracle port), all host threads. The line also carries the
     decode tok/s of a configs[2]-shaped model in mixed K-quant formats
-    (model_decode: the model path, weights dequantised to fp32 at upload)."""
+    (model_decode: the model path, the layer matrices read in place as
+    K-quant blocks; beside it the same model with every matrix dequantised to
+    fp32 at upload)."""
     import numpy as np
     import torch
 
@@ -849,13 +851,37 @@ def run_kquant(args):
         e1.record(stream)
         stream.synchronize()
     kms = e0.elapsed_time(e1) / new
-    kbytes = float(khw.weight_bytes_per_token())
-    model_line = {"tok_s": 1e3 / kms, "ms_per_token": kms, "bytes_per_token": kbytes,
-                  "hbm_gbs": kbytes / (kms / 1e3) / 1e9, "hbm_frac": kbytes / (kms / 1e3) / 1e9 / peak,
-                  "note": "Q4_K/Q5_K/Q6_K weights run as fp32 on the generic path (4 B per weight read)"}
+    kbytes = float(lib.jyc_model_weight_bytes_per_token(km.h))
+    assert lib.jyc_device_error(1) == 0
+    km.close()
+    # the same model with every matrix dequantised to fp32 at upload (the
+    # comparison path, JYC_KQ_FP32=1)
+    os.environ["JYC_KQ_FP32"] = "1"
+    try:
+        km = DeviceModel(khw)
+    finally:
+        del os.environ["JYC_KQ_FP32"]
+    with torch.cuda.stream(stream):
+        s = stream.cuda_stream
+        km.prefill_device(kids.data_ptr(), 128, s)
+        km.decode_device(8, s)
+        stream.synchronize()
+        km.rewind(129, s)
+        e0.record(stream)
+        km.decode_device(new, s)
+        e1.record(stream)
+        stream.synchronize()
+    fms = e0.elapsed_time(e1) / new
+    fbytes = float(lib.jyc_model_weight_bytes_per_token(km.h))
     assert lib.jyc_device_error(1) == 0
     km.close()
     del khw
+    model_line = {"tok_s": 1e3 / kms, "ms_per_token": kms, "bytes_per_token": kbytes,
+                  "hbm_gbs": kbytes / (kms / 1e3) / 1e9, "hbm_frac": kbytes / (kms / 1e3) / 1e9 / peak,
+                  "fp32_path": {"tok_s": 1e3 / fms, "ms_per_token": fms, "bytes_per_token": fbytes},
+                  "note": "layer matrices read as K-quant blocks in place by the K-quant matmul, LM head "
+                          "dequantised to fp32 at upload; fp32_path: every matrix dequantised to fp32 "
+                          "(4 B per weight)"}
     clk = clocks.stop()
     # CPU baseline: the reference's matmul_q over one layer's Q4_K matrices
     rng = np.random.default_rng(7)

@@ -289,9 +289,11 @@ typedef struct jyc_model jyc_model;
 
 /* Uploads every weight once (the bind_model point, libs/model_libs/pipeline.h:63-153):
  * Q8_0 blocks are re-laid into the device layout, fp32 [in][out] matrices are
- * transposed, Q4_K / Q5_K / Q6_K blocks (any mix, with fp32 too; input
- * dimensions multiples of 256) are dequantised once to the reference's fp32
- * values and run on the fp32 kernels; fp16 [in][out] matrices (matmul_f16.h)
+ * transposed, Q4_K / Q5_K / Q6_K blocks (input dimensions multiples of 256)
+ * stay as they are and the K-quant matmul reads them in place when every
+ * layer matrix is K-quant (the LM head and embedding are dequantised once to
+ * the reference's fp32 values); K-quant mixed with fp32 matrices is
+ * dequantised once and runs on the fp32 kernels; fp16 [in][out] matrices (matmul_f16.h)
  * are transposed and stay fp16 (2 bytes per weight streamed, converted to fp32
  * exactly in the GEMV; an fp16 embedding becomes fp32 rows); Q/K/V and
  * gate/up are fused. The layer weights are all Q8_0, all fp16, or fp32 and

@@ -256,8 +256,9 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
     """Binds a reference model directory (model.bf + model_info.json) for the
     device path, with the reference's binding rules: per layer the nine
     tensors of load_weights.h:55-68 (norms f32; linear weights all Q8_0, all
-    f16, or any mix of f32 and the K-quants Q4_K / Q5_K / Q6_K, which the
-    device dequantises to fp32 once), optional q/k/v biases,
+    f16, all K-quant (Q4_K / Q5_K / Q6_K, read in place on the device), or a
+    mix of f32 and the K-quants, which the device dequantises to fp32 once),
+    optional q/k/v biases,
     model.embed_tokens.weight (f32, f16, Q8_0 or K-quant), lm_head.weight or
     (block formats only) the embedding as a tied head, model.norm.weight; shapes as bind_model checks
     them (pipeline.h:99-139). max_seq 0 takes max_position_embeddings
@@ -312,8 +313,8 @@ def load_model_dir(path: str, max_seq: int = 0, name: str | None = None) -> Host
             kinds.add(t.dtype)
             if t.dtype in _KQ_CODE:
                 qtypes[f"{key}.{l}"] = _KQ_CODE[t.dtype]
-    # Q8_0 runs on its own kernels and cannot mix; f32 and the K-quants
-    # (dequantised to f32 on the device) mix freely
+    # Q8_0 runs on its own kernels and cannot mix; f32 and the K-quants mix
+    # freely (a mix is dequantised to f32 on the device)
     if Q8_0 in kinds and len(kinds) > 1:
         raise BFileError(f"{path}: Q8_0 linear weights mixed with {sorted(DTYPE_NAMES[k] for k in kinds - {Q8_0})}; "
                          "the device path runs Q8_0 models alone")

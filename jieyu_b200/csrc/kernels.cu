@@ -326,6 +326,35 @@ int launch_add_rows(float* x, const float* p, size_t n, cudaStream_t s) {
 }
 
 // ---------------------------------------------------------------------------
+// Bias rows and the SwiGLU product (the K-quant model path's epilogues, the
+// same arithmetic as the GEMV's EPI_BIAS and EPI_SWIGLU).
+__global__ void bias_rows_kernel(float* y, int ldy, const float* bias, int n, int rows) {
+    const size_t total = (size_t)rows * n;
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(e / n), i = (int)(e - (size_t)r * n);
+        float* p = y + (size_t)r * ldy + i;
+        *p = __fadd_rn(*p, bias[i]);
+    }
+}
+int launch_bias_rows(float* y, int ldy, const float* bias, int n, int rows, cudaStream_t s) {
+    if (n <= 0 || rows <= 0) return JYC_OK;
+    const size_t total = (size_t)rows * n;
+    bias_rows_kernel<<<(int)std::min<size_t>((total + 255) / 256, 148 * 8), 256, 0, s>>>(y, ldy, bias, n, rows);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+__global__ void swiglu_rows_kernel(const float* g, const float* u, float* h, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        h[i] = __fmul_rn(silu_ref(g[i]), u[i]);
+}
+int launch_swiglu_rows(const float* g, const float* u, float* h, size_t n, cudaStream_t s) {
+    if (n == 0) return JYC_OK;
+    swiglu_rows_kernel<<<(int)std::min<size_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(g, u, h, n);
+    JYC_LAUNCHED();
+    return JYC_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Standalone RMSNorm rows (op entry point).
 __global__ void rmsnorm_kernel(const float* x, float* y, const float* w, int n, float eps) {
     __shared__ float red[32];

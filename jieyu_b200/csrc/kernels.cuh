@@ -156,6 +156,12 @@ int launch_set_state(DevState* st, int len, int max_new, int max_len, const int*
 // JYC_Q4K / JYC_Q5K / JYC_Q6K, k % 256 == 0): y[m][n] = x[m][k] . W^T.
 int launch_kquant_matmul(const float* x, int m, int n, int k, const uint8_t* wq, int qtype, float* y,
                          cudaStream_t s);
+int launch_kquant_matmul_ld(const float* x, int ldx, int m, int n, int k, const uint8_t* wq, int qtype, float* y,
+                            int ldy, cudaStream_t s);
+// y[r][i] += bias[i] for rows r < rows (row stride ldy), i < n.
+int launch_bias_rows(float* y, int ldy, const float* bias, int n, int rows, cudaStream_t s);
+// h[i] = silu(g[i]) * u[i] (the reference's silu vector body, ffn.h:7-19).
+int launch_swiglu_rows(const float* g, const float* u, float* h, size_t n, cudaStream_t s);
 // K-quant rows [n][k/256 blocks] -> fp32 rows of `dst` ([.][k]), row r at
 // row_off + r * row_stride, with the reference's dequantised values.
 int launch_kquant_dequant(const uint8_t* blocks, int n, int k, int qtype, float* dst, int row_off, int row_stride,

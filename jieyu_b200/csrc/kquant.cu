@@ -429,6 +429,28 @@ int launch_kquant_matmul(const float* x, int m, int n, int k, const uint8_t* wq,
     return JYC_OK;
 }
 
+// The same with row strides (x rows ldx floats apart, y rows ldy apart): the
+// K-quant model path writes Q, K and V side by side into one q|k|v row.
+int launch_kquant_matmul_ld(const float* x, int ldx, int m, int n, int k, const uint8_t* wq, int qtype, float* y,
+                            int ldy, cudaStream_t s) {
+    if (qtype != JYC_Q4K && qtype != JYC_Q5K && qtype != JYC_Q6K)
+        return arg_error("matmul_qk: qtype must be JYC_Q4K, JYC_Q5K or JYC_Q6K");
+    if (m <= 0 || n <= 0 || k <= 0 || k % 256) return arg_error("matmul_qk: need m, n > 0 and k % 256 == 0");
+    if (((uintptr_t)x & 15) || (ldx & 3) || ((uintptr_t)wq & 3) || ldx < k || ldy < n)
+        return arg_error("matmul_qk: A rows must be 16-byte aligned and the blocks 4-byte aligned");
+    for (int r0 = 0; r0 < m; r0 += kKqMaxRows) {
+        const int mr = std::min(kKqMaxRows, m - r0);
+        const float* xr = x + (size_t)r0 * ldx;
+        float* yr = y + (size_t)r0 * ldy;
+        int r;
+        if (qtype == JYC_Q4K) r = kq_launch_qt<JYC_Q4K>(xr, ldx, mr, n, k, wq, yr, ldy, s);
+        else if (qtype == JYC_Q5K) r = kq_launch_qt<JYC_Q5K>(xr, ldx, mr, n, k, wq, yr, ldy, s);
+        else r = kq_launch_qt<JYC_Q6K>(xr, ldx, mr, n, k, wq, yr, ldy, s);
+        if (r != JYC_OK) return r;
+    }
+    return JYC_OK;
+}
+
 int launch_kquant_dequant(const uint8_t* blocks, int n, int k, int qtype, float* dst, int row_off, int row_stride,
                           cudaStream_t s) {
     if (n <= 0 || k <= 0 || k % 256) return arg_error("K-quant weights need k % 256 == 0");

@@ -40,9 +40,14 @@ struct DevMat {  // one weight matrix on the device, [n][k]
     uint8_t* rexp = nullptr; // Q8: per-row exponent of the largest scale (tensor-core path)
     float* f = nullptr;
     uint16_t* h = nullptr;   // fp16 [n][k]
+    uint8_t* kqb = nullptr;  // K-quant super-blocks as the reference holds them, [n][k/256], read in place
+    int kqt = -1;            // their type (JYC_Q4K / JYC_Q5K / JYC_Q6K)
     int n = 0, k = 0;
     bool tiled = false;
-    double bytes() const { return f ? 4.0 * n * k : h ? 2.0 * n * k : (double)n * k * 34.0 / 32.0; }
+    double bytes() const {
+        return kqb ? (double)n * (k / 256) * kquant_block_bytes(kqt)
+               : f ? 4.0 * n * k : h ? 2.0 * n * k : (double)n * k * 34.0 / 32.0;
+    }
     int wtype() const { return f ? W_F32 : h ? W_F16 : W_Q8; }
 };
 
@@ -76,6 +81,7 @@ struct DevLayer {
     float* rms2 = nullptr;
     float* bias = nullptr;  // fused q|k|v bias, or null
     DevMat qkv, o, gateup, down;
+    DevMat kq[7];           // K-quant models: q, k, v, o, gate, up, down blocks read in place
 };
 
 }  // namespace
@@ -86,6 +92,13 @@ struct jyc_model {
     int vocab_off = 0;   // token id of LM-head row 0 (vocabulary-sharded head)
     int q_dim = 0, kv_dim = 0, nqkv = 0;
     int wtype = W_Q8;
+    // K-quant models whose layer matrices are all K-quant: the blocks stay as
+    // they are on the device and the per-op path reads them in place
+    bool kq_path = false;
+    float* kq_xn = nullptr;  // RMSNorm rows [kMT][D]
+    float* kq_t = nullptr;   // O / down rows before the residual add [kMT][D]
+    float* kq_g = nullptr;   // gate rows [kMT][F]
+    float* kq_u = nullptr;   // up rows [kMT][F]
     bool tiled = false;  // Q8 matrices in the 512-column tiled layout (megakernel models)
     std::vector<DevLayer> layers;
     DevMat head;
@@ -242,6 +255,19 @@ int upload_wmat(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst, int 
         TRY(launch_transpose(static_cast<const float*>(staging), dst.f, k, n, row_off, row_stride, m->stream));
     // the staging buffer is reused by the next upload: wait for this one
     JYC_CUDA(cudaStreamSynchronize(m->stream));
+    return JYC_OK;
+}
+
+// A K-quant matrix kept as the reference holds it ([n][k/256] super-blocks):
+// the in-place path's weights.
+int upload_kq_raw(jyc_model* m, const jyc_wmat& w, int n, int k, DevMat& dst) {
+    if (k % 256) return arg_error("K-quant weights need an input dimension that is a multiple of 256");
+    const size_t bytes = (size_t)n * (k / 256) * kquant_block_bytes(w.qt);
+    TRY(m->alloc(&dst.kqb, bytes));
+    JYC_CUDA(cudaMemcpy(dst.kqb, w.q, bytes, cudaMemcpyHostToDevice));
+    dst.kqt = w.qt;
+    dst.n = n;
+    dst.k = k;
     return JYC_OK;
 }
 
@@ -413,6 +439,17 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
                : (d->layers[0].Wq.h != nullptr && d->layers[0].Wq.f == nullptr && d->layers[0].Wq.q == nullptr)
                    ? W_F16
                    : W_F32;
+    // K-quant models (every layer matrix Q4_K / Q5_K / Q6_K, as the
+    // reference's downloads are) keep their blocks and read them in place;
+    // a mix with fp32 matrices runs every matrix as fp32. JYC_KQ_FP32=1
+    // selects the fp32 path for all (a comparison switch).
+    m->kq_path = m->wtype == W_F32;
+    if (const char* e = std::getenv("JYC_KQ_FP32")) m->kq_path = m->kq_path && std::atoi(e) == 0;
+    for (int l = 0; l < d->num_layers && m->kq_path; l++) {
+        const jyc_layer_weights& w = d->layers[l];
+        for (const jyc_wmat* x : {&w.Wq, &w.Wk, &w.Wv, &w.Wo, &w.W1, &w.W3, &w.W2})
+            if (x->f != nullptr || x->q == nullptr || kquant_block_bytes(x->qt) == 0) m->kq_path = false;
+    }
     const int kq = m->wtype == W_Q8 ? 32 : 8;
     if (m->D % kq || m->q_dim % kq || m->F % kq)
         return arg_error("model: hidden, heads*head_dim and intermediate must be multiples of " +
@@ -446,13 +483,24 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
         TRY(upload_f32(m, w.rms1_weight, m->D, &dl.rms1));
         TRY(upload_f32(m, w.rms2_weight, m->D, &dl.rms2));
         const int wt = m->wtype;
-        TRY(upload_wmat(m, w.Wq, m->q_dim, m->D, dl.qkv, m->nqkv, 0, 1, staging, stage, wt));
-        TRY(upload_wmat(m, w.Wk, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim, 1, staging, stage, wt));
-        TRY(upload_wmat(m, w.Wv, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim + m->kv_dim, 1, staging, stage, wt));
-        TRY(upload_wmat(m, w.Wo, m->D, m->q_dim, dl.o, m->D, 0, 1, staging, stage, wt));
-        TRY(upload_wmat(m, w.W1, m->F, m->D, dl.gateup, 2 * m->F, 0, 2, staging, stage, wt));
-        TRY(upload_wmat(m, w.W3, m->F, m->D, dl.gateup, 2 * m->F, 1, 2, staging, stage, wt));
-        TRY(upload_wmat(m, w.W2, m->D, m->F, dl.down, m->D, 0, 1, staging, stage, wt));
+        if (m->kq_path) {
+            const jyc_wmat* src[7] = {&w.Wq, &w.Wk, &w.Wv, &w.Wo, &w.W1, &w.W3, &w.W2};
+            const int nn[7] = {m->q_dim, m->kv_dim, m->kv_dim, m->D, m->F, m->F, m->D};
+            const int kk[7] = {m->D, m->D, m->D, m->q_dim, m->D, m->D, m->F};
+            for (int i = 0; i < 7; i++) {
+                TRY(upload_kq_raw(m, *src[i], nn[i], kk[i], dl.kq[i]));
+                m->weight_bytes += dl.kq[i].bytes();
+            }
+        } else {
+            TRY(upload_wmat(m, w.Wq, m->q_dim, m->D, dl.qkv, m->nqkv, 0, 1, staging, stage, wt));
+            TRY(upload_wmat(m, w.Wk, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim, 1, staging, stage, wt));
+            TRY(upload_wmat(m, w.Wv, m->kv_dim, m->D, dl.qkv, m->nqkv, m->q_dim + m->kv_dim, 1, staging, stage,
+                            wt));
+            TRY(upload_wmat(m, w.Wo, m->D, m->q_dim, dl.o, m->D, 0, 1, staging, stage, wt));
+            TRY(upload_wmat(m, w.W1, m->F, m->D, dl.gateup, 2 * m->F, 0, 2, staging, stage, wt));
+            TRY(upload_wmat(m, w.W3, m->F, m->D, dl.gateup, 2 * m->F, 1, 2, staging, stage, wt));
+            TRY(upload_wmat(m, w.W2, m->D, m->F, dl.down, m->D, 0, 1, staging, stage, wt));
+        }
         if (w.bq || w.bk || w.bv) {
             std::vector<float> b(m->nqkv, 0.0f);
             if (w.bq) std::memcpy(b.data(), w.bq, m->q_dim * 4);
@@ -535,6 +583,12 @@ int build_model(jyc_model* m, const jyc_model_desc* d) {
     TRY(m->alloc(&m->tmp, (size_t)m->D));
     TRY(m->alloc(&m->q8, arows * m->q_dim));
     TRY(m->alloc(&m->qsc, arows * m->H));
+    if (m->kq_path) {
+        TRY(m->alloc(&m->kq_xn, (size_t)kMT * m->D));
+        TRY(m->alloc(&m->kq_t, (size_t)kMT * m->D));
+        TRY(m->alloc(&m->kq_g, (size_t)kMT * m->F));
+        TRY(m->alloc(&m->kq_u, (size_t)kMT * m->F));
+    }
     if (m->pf_rows) {
         const int kmax = std::max({m->D, m->q_dim, m->F});
         const int nmax = std::max({m->nqkv, m->D, 2 * m->F, m->V});
@@ -595,14 +649,25 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
     MARK(K_EMBED);
     for (int l = 0; l < m->L; l++) {
         const DevLayer& ly = m->layers[l];
-        GemvArgs g{};
-        g.m = rows; g.eps = 1e-5f; g.st = guard;
-        // RMSNorm -> fused Q|K|V GEMV (+ bias)
-        g.x = m->X; g.ldx = m->D; g.n = m->nqkv; g.k = m->D;
-        g.qs = ly.qkv.qs; g.d = ly.qkv.d; g.wt = ly.qkv.f; g.wh = ly.qkv.h; g.norm_w = ly.rms1;
-        g.y = m->qkv; g.ldy = m->nqkv; g.bias = ly.bias;
-        TRY(launch_gemv(g, m->wtype, ly.bias ? EPI_BIAS : EPI_STORE, s));
-        MARK(K_QKV);
+        if (m->kq_path) {  // RMSNorm -> Q, K, V from the K-quant blocks in place (+ bias)
+            TRY(launch_rmsnorm(m->X, m->kq_xn, ly.rms1, rows, m->D, 1e-5f, s));
+            TRY(launch_kquant_matmul_ld(m->kq_xn, m->D, rows, m->q_dim, m->D, ly.kq[0].kqb, ly.kq[0].kqt,
+                                        m->qkv, m->nqkv, s));
+            TRY(launch_kquant_matmul_ld(m->kq_xn, m->D, rows, m->kv_dim, m->D, ly.kq[1].kqb, ly.kq[1].kqt,
+                                        m->qkv + m->q_dim, m->nqkv, s));
+            TRY(launch_kquant_matmul_ld(m->kq_xn, m->D, rows, m->kv_dim, m->D, ly.kq[2].kqb, ly.kq[2].kqt,
+                                        m->qkv + m->q_dim + m->kv_dim, m->nqkv, s));
+            if (ly.bias) TRY(launch_bias_rows(m->qkv, m->nqkv, ly.bias, m->nqkv, rows, s));
+            MARK(K_QKV);
+        } else {  // RMSNorm -> fused Q|K|V GEMV (+ bias)
+            GemvArgs g{};
+            g.m = rows; g.eps = 1e-5f; g.st = guard;
+            g.x = m->X; g.ldx = m->D; g.n = m->nqkv; g.k = m->D;
+            g.qs = ly.qkv.qs; g.d = ly.qkv.d; g.wt = ly.qkv.f; g.wh = ly.qkv.h; g.norm_w = ly.rms1;
+            g.y = m->qkv; g.ldy = m->nqkv; g.bias = ly.bias;
+            TRY(launch_gemv(g, m->wtype, ly.bias ? EPI_BIAS : EPI_STORE, s));
+            MARK(K_QKV);
+        }
         // RoPE(Q,K) + int8 quantisation of Q, K, V; K/V appended to the cache
         RopeQuantArgs rq{};
         rq.q = m->qkv; rq.k = m->qkv + m->q_dim; rq.v = m->qkv + m->q_dim + m->kv_dim;
@@ -621,8 +686,27 @@ int run_layers(jyc_model* m, int rows, PosSrc pos, cudaStream_t s) {
         at.out = m->attn; at.ldo = m->q_dim; at.pos = pos;
         TRY(launch_attention(at, s));
         MARK(K_ATTN);
+        if (m->kq_path) {
+            // O (+ residual), RMSNorm -> gate, up -> SwiGLU, down (+ residual)
+            TRY(launch_kquant_matmul_ld(m->attn, m->q_dim, rows, m->D, m->q_dim, ly.kq[3].kqb, ly.kq[3].kqt,
+                                        m->kq_t, m->D, s));
+            TRY(launch_add_rows(m->X, m->kq_t, (size_t)rows * m->D, s));
+            MARK(K_OPROJ);
+            TRY(launch_rmsnorm(m->X, m->kq_xn, ly.rms2, rows, m->D, 1e-5f, s));
+            TRY(launch_kquant_matmul_ld(m->kq_xn, m->D, rows, m->F, m->D, ly.kq[4].kqb, ly.kq[4].kqt, m->kq_g,
+                                        m->F, s));
+            TRY(launch_kquant_matmul_ld(m->kq_xn, m->D, rows, m->F, m->D, ly.kq[5].kqb, ly.kq[5].kqt, m->kq_u,
+                                        m->F, s));
+            TRY(launch_swiglu_rows(m->kq_g, m->kq_u, m->h, (size_t)rows * m->F, s));
+            MARK(K_GATEUP);
+            TRY(launch_kquant_matmul_ld(m->h, m->F, rows, m->D, m->F, ly.kq[6].kqb, ly.kq[6].kqt, m->kq_t, m->D,
+                                        s));
+            TRY(launch_add_rows(m->X, m->kq_t, (size_t)rows * m->D, s));
+            MARK(K_DOWN);
+            continue;
+        }
         // O projection + residual
-        g = GemvArgs{};
+        GemvArgs g{};
         g.m = rows; g.eps = 1e-5f; g.st = guard;
         g.x = m->attn; g.ldx = m->q_dim; g.n = m->D; g.k = m->q_dim;
         g.qs = ly.o.qs; g.d = ly.o.d; g.wt = ly.o.f; g.wh = ly.o.h; g.y = m->X; g.ldy = m->D;
@@ -1261,6 +1345,19 @@ JYC_API int jyc_model_profile_decode(jyc_model* m, int n_steps, void* stream, do
     bytes[K_GATEUP] = 2.0 * m->F * m->D * wb + 4.0 * m->D;
     bytes[K_DOWN] = (double)m->D * m->F * wb;
     bytes[K_HEAD] = (double)m->V * m->D * hb + 4.0 * m->D;
+    if (m->kq_path) {  // the K-quant blocks each class reads, per layer (types may differ by layer)
+        double q = 0.0, o = 0.0, gu = 0.0, dn = 0.0;
+        for (const DevLayer& ly : m->layers) {
+            q += ly.kq[0].bytes() + ly.kq[1].bytes() + ly.kq[2].bytes();
+            o += ly.kq[3].bytes();
+            gu += ly.kq[4].bytes() + ly.kq[5].bytes();
+            dn += ly.kq[6].bytes();
+        }
+        bytes[K_QKV] = q / m->L + 4.0 * m->D;
+        bytes[K_OPROJ] = o / m->L;
+        bytes[K_GATEUP] = gu / m->L + 4.0 * m->D;
+        bytes[K_DOWN] = dn / m->L;
+    }
     Prof* p = m->prof_marks.get();
     for (int it = 0; it < n_steps; it++) {
         JYC_CUDA(cudaGraphLaunch(m->prof_exec, s));

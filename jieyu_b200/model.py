@@ -343,9 +343,14 @@ class HostWeights:
         """Algorithmic weight bytes one decode token reads (Q8_0: 34 B / 32)."""
         cfg = self.cfg
         D, F = cfg.hidden, cfg.inter
-        per = {"q8": 34.0 / 32.0, "f16": 2.0}.get(cfg.wtype, 4.0)  # "kq": dequantised to fp32 on the device
+        per = {"q8": 34.0 / 32.0, "f16": 2.0}.get(cfg.wtype, 4.0)
         lin = (cfg.q_dim + 2 * cfg.kv_dim) * D + D * cfg.q_dim + 3 * F * D
         b = cfg.layers * (lin * per + 2 * D * 4 + (cfg.q_dim + 2 * cfg.kv_dim) * 4 * cfg.qkv_bias)
+        names = ("q", "k", "v", "o", "gate", "up", "down")
+        if cfg.wtype == "kq" and all(f"{n}.{l}" in self.qt for l in range(cfg.layers) for n in names):
+            # every layer matrix K-quant: the device reads the blocks in place
+            b -= cfg.layers * lin * per
+            b += sum(self.t[f"{n}.{l}"].nbytes for l in range(cfg.layers) for n in names)
         head_q8 = self.t["head"].dtype == np.uint8 and self.qt.get("head", JYC_Q8_0) == JYC_Q8_0
         head_b = 34.0 / 32.0 if head_q8 else 2.0 if self.t["head"].dtype == np.uint16 else 4.0
         b += cfg.vocab * D * head_b + 4 * D
