@@ -289,11 +289,15 @@ def run_c1(args):
         torch.cuda.synchronize()
         barrier()
         e0, e1 = ev(), ev()
+        if args.nvtx:
+            torch.cuda.nvtx.range_push("timed")
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
         stream.synchronize()
+        if args.nvtx:
+            torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         barrier()
         launches = lib.jyc_kernel_launches() - launches0
@@ -520,11 +524,15 @@ def run_headline(args):
         torch.cuda.synchronize()
         barrier()
         e0, e1 = ev(), ev()
+        if args.nvtx:
+            torch.cuda.nvtx.range_push("timed")
         e0.record(stream)
         for _ in range(args.steps):
             step()
         e1.record(stream)
         stream.synchronize()
+        if args.nvtx:
+            torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         barrier()
         launches = lib.jyc_kernel_launches() - launches0
