@@ -18,11 +18,10 @@
 #include <cstdio>
 #include <cstring>
 #include <fstream>
-#include <queue>
 #include <sstream>
 #include <stdexcept>
+#include <set>
 #include <string>
-#include <tuple>
 #include <unordered_map>
 #include <vector>
 
@@ -459,51 +458,55 @@ struct jyt_tokenizer {
         return found;
     }
 
-    // tokenizer.h:483-600: merge the lowest (rank, position) pair first.
+    // Byte-pair merging of one word by the rule of tokenizer.h:483-600: while
+    // two adjacent symbols form a known merge, apply the one of lowest rank,
+    // the leftmost of equal ranks; a merge whose result is not in the
+    // vocabulary never applies. The candidate pairs live in an ordered set
+    // keyed (rank, left position), updated as each merge joins two symbols;
+    // a merge keeps the left position, so position 0 always heads the word.
     void merge_word(std::vector<int>& sym, std::vector<int>& out) const {
         const int n = (int)sym.size();
         if (n < 2 || merge_rank.empty()) {
             out.insert(out.end(), sym.begin(), sym.end());
             return;
         }
-        std::vector<int> prev(n), nxt(n), ver(n, 0);
-        std::vector<char> alive(n, 1);
+        std::vector<int> left(n), right(n);  // neighbours in the live sequence (-1: none)
         for (int i = 0; i < n; ++i) {
-            prev[i] = i - 1;
-            nxt[i] = i + 1 < n ? i + 1 : -1;
+            left[i] = i - 1;
+            right[i] = i + 1 < n ? i + 1 : -1;
         }
-        typedef std::tuple<int, int, int> Item;  // rank, position, version
-        std::priority_queue<Item, std::vector<Item>, std::greater<Item>> heap;
-        auto rank_of = [&](int a, int b) {
-            auto it = merge_rank.find(pair_key(a, b));
-            return it == merge_rank.end() ? -1 : it->second;
+        std::vector<int> in_set(n, -1);  // rank under which the pair starting at i is in `cand`
+        std::set<std::pair<int, int>> cand;
+        auto pair_rank = [&](int p) {
+            const int q = right[p];
+            if (q < 0) return -1;
+            auto it = merge_rank.find(pair_key(sym[p], sym[q]));
+            if (it == merge_rank.end() || merge_result[(size_t)it->second] < 0) return -1;
+            return it->second;
         };
-        auto push = [&](int pos) {
-            if (pos < 0 || pos >= n || nxt[pos] < 0) return;
-            int r = rank_of(sym[pos], sym[nxt[pos]]);
-            if (r >= 0) heap.emplace(r, pos, ver[pos]);
+        auto add = [&](int p) {
+            if (p < 0) return;
+            in_set[p] = pair_rank(p);
+            if (in_set[p] >= 0) cand.emplace(in_set[p], p);
         };
-        for (int i = 0; i + 1 < n; ++i) push(i);
-        while (!heap.empty()) {
-            auto [rank, pos, v] = heap.top();
-            heap.pop();
-            if (!alive[pos] || ver[pos] != v || nxt[pos] < 0) continue;
-            int j = nxt[pos];
-            if (rank_of(sym[pos], sym[j]) != rank) continue;
-            int merged = merge_result[(size_t)rank];
-            if (merged < 0) continue;
-            sym[pos] = merged;
-            int after = nxt[j];
-            alive[j] = 0;
-            nxt[pos] = after;
-            if (after >= 0) prev[after] = pos;
-            ++ver[pos];
-            if (prev[pos] >= 0) ++ver[prev[pos]];
-            push(prev[pos]);
-            push(pos);
+        auto drop = [&](int p) {
+            if (p < 0 || in_set[p] < 0) return;
+            cand.erase({in_set[p], p});
+            in_set[p] = -1;
+        };
+        for (int i = 0; i + 1 < n; ++i) add(i);
+        while (!cand.empty()) {
+            const int r = cand.begin()->first, p = cand.begin()->second, q = right[p];
+            drop(left[p]);
+            drop(p);
+            drop(q);
+            sym[p] = merge_result[(size_t)r];
+            right[p] = right[q];
+            if (right[q] >= 0) left[right[q]] = p;
+            add(left[p]);
+            add(p);
         }
-        for (int i = 0; i >= 0 && i < n; i = nxt[i])
-            if (alive[i]) out.push_back(sym[i]);
+        for (int i = 0; i >= 0; i = right[i]) out.push_back(sym[i]);
     }
 
     std::vector<int> encode(const std::string& data) const {

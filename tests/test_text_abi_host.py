@@ -82,8 +82,15 @@ def test_native_tokenizer_matches_reference(tmp_path):
     vp, mp = _write(str(tmp_path), vocab, merges)
     hr = ref.jyref_tok_load(vp.encode(), mp.encode())
     h = lib.jyt_tok_load(vp.encode(), mp.encode())
+    # long words (no spaces) over the corpus' letters: many merges interact
+    # within one word, ties of equal rank included
+    rng = np.random.default_rng(5)
+    joined = "".join(CORPUS).replace(" ", "").replace("\n", "")
+    letters = sorted(set(joined))
+    long_words = ["".join(rng.choice(letters, size=int(n))) for n in (64, 257, 1000)]
+    long_words += ["abab" * 300, joined[:1500]]
     try:
-        for text in TEXTS:
+        for text in list(TEXTS) + long_words:
             data = text if isinstance(text, bytes) else text.encode()
             out = np.zeros(4 * len(data) + 16, np.int32)
             n = ref.jyref_tok_encode(hr, data, len(data), out.ctypes.data, len(out))
