@@ -271,52 +271,53 @@ class Tokenizer:
         return found, best_at, best_len
 
     def _merge_word(self, symbols: list[int]) -> list[int]:
+        """Byte-pair merging of one word by the rule of tokenizer.h:483-600:
+        while two adjacent symbols form a known merge, apply the one of lowest
+        rank, the leftmost of equal ranks; a merge whose result is not in the
+        vocabulary never applies. Candidates sit in a heap keyed (rank, left
+        position); cur[p] is the rank of the pair now starting at p (-1: none),
+        so an entry is acted on only while it still describes the word. A
+        merge keeps its left position, so position 0 always heads the word."""
         n = len(symbols)
         if n < 2 or not self.merge_rank:
             return list(symbols)
         sym = list(symbols)
-        prev = [i - 1 for i in range(n)]
-        nxt = [i + 1 if i + 1 < n else -1 for i in range(n)]
-        ver = [0] * n
-        alive = [True] * n
-        heap: list[tuple[int, int, int]] = []
+        left = list(range(-1, n - 1))
+        right = list(range(1, n)) + [-1]
+        cur = [-1] * n
+        heap: list[tuple[int, int]] = []
 
-        def push(pos: int) -> None:
-            if pos < 0 or pos >= n or nxt[pos] < 0:
+        def refresh(p: int) -> None:
+            if p < 0:
                 return
-            r = self.merge_rank.get((sym[pos], sym[nxt[pos]]))
-            if r is not None:
-                heapq.heappush(heap, (r, pos, ver[pos]))
+            q, r = right[p], -1
+            if q >= 0:
+                got = self.merge_rank.get((sym[p], sym[q]))
+                if got is not None and self.merge_result[got] >= 0:
+                    r = got
+            cur[p] = r
+            if r >= 0:
+                heapq.heappush(heap, (r, p))
 
         for i in range(n - 1):
-            push(i)
+            refresh(i)
         while heap:
-            rank, pos, v = heapq.heappop(heap)
-            if not alive[pos] or ver[pos] != v or nxt[pos] < 0:
+            r, p = heapq.heappop(heap)
+            if cur[p] != r:
                 continue
-            j = nxt[pos]
-            if self.merge_rank.get((sym[pos], sym[j])) != rank:
-                continue
-            merged = self.merge_result[rank]
-            if merged < 0:
-                continue
-            sym[pos] = merged
-            after = nxt[j]
-            alive[j] = False
-            nxt[pos] = after
-            if after >= 0:
-                prev[after] = pos
-            ver[pos] += 1
-            if prev[pos] >= 0:
-                ver[prev[pos]] += 1
-            push(prev[pos])
-            push(pos)
+            q = right[p]
+            sym[p] = self.merge_result[r]
+            cur[q] = -1
+            right[p] = right[q]
+            if right[q] >= 0:
+                left[right[q]] = p
+            refresh(p)
+            refresh(left[p])
         out = []
         i = 0
-        while 0 <= i < n:
-            if alive[i]:
-                out.append(sym[i])
-            i = nxt[i]
+        while i >= 0:
+            out.append(sym[i])
+            i = right[i]
         return out
 
     def encode(self, text) -> list[int]:

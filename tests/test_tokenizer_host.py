@@ -139,7 +139,12 @@ def test_tokenizer_matches_reference(ref, tmp_path, word_end):
         fuzz = [bytes(rng.integers(0, 256, size=int(rng.integers(1, 40)), dtype=np.uint8)) for _ in range(150)]
         mixed = [b"".join(pool[int(i)][: int(rng.integers(0, 20))] for i in rng.integers(0, len(pool), 4))
                  for _ in range(100)]
-        for data in pool + fuzz + mixed:
+        # long words (no spaces): many merges interact within one word
+        joined = "".join(CORPUS).replace(" ", "").replace("\n", "")
+        letters = sorted(set(joined))
+        long_words = [("".join(rng.choice(letters, size=n))).encode() for n in (64, 257, 1000)]
+        long_words += [b"abab" * 300, joined[:1500].encode()]
+        for data in pool + fuzz + mixed + long_words:
             want = _ref_encode(ref, h, data)
             got = tok.encode(data)
             assert got == want, data
