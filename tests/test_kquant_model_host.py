@@ -21,3 +21,19 @@ def test_kquant_model_oracle_matches_reference():
     assert len(want) == len(prompt) + 12
     assert list(got) == list(want)
     assert len(set(int(x) for x in want[len(prompt):])) > 1  # not a degenerate model
+
+
+def test_kquant_in_place_byte_accounting():
+    """All layer matrices K-quant: the bytes a decode token streams are the
+    blocks' own (read in place), not 4 bytes per weight; the LM head and
+    embedding row stay fp32 (dequantised once at upload)."""
+    hw = kquant_model()
+    cfg = hw.cfg
+    D, F, qd, kvd = cfg.hidden, cfg.inter, cfg.q_dim, cfg.kv_dim
+    names = ("q", "k", "v", "o", "gate", "up", "down")
+    blocks = sum(hw.t[f"{n}.{l}"].nbytes for l in range(cfg.layers) for n in names)
+    bb = {0: 144, 1: 176, 2: 210}
+    dims = {"q": (qd, D), "k": (kvd, D), "v": (kvd, D), "o": (D, qd), "gate": (F, D), "up": (F, D), "down": (D, F)}
+    assert blocks == sum(n * (k // 256) * bb[hw.qt[f"{m}.{l}"]] for l in range(cfg.layers) for m, (n, k) in dims.items())
+    want = blocks + cfg.layers * 2 * D * 4 + cfg.vocab * D * 4 + 4 * D + D * 4
+    assert abs(hw.weight_bytes_per_token() - want) <= 1e-9 * want

@@ -61,3 +61,26 @@ def test_synth_model_equals_host_weights(oracle):
     for f in ("num_layers", "max_seq", "vocab_size", "hidden", "num_heads", "num_kv_heads", "head_dim",
               "intermediate"):
         assert getattr(d, f) == getattr(e, f), f
+
+
+def test_f16_weights_are_the_fp32_ones_rounded():
+    """synthetic_f16: every linear matrix, the LM head and the embedding are the
+    seeded fp32 weights rounded to IEEE halves ([in][out] layout kept), bound
+    through WMat.h; norms stay fp32."""
+    from dataclasses import replace
+    cfg = replace(CONFIGS["c0"], layers=2)
+    f32 = HostWeights.synthetic(replace(cfg, wtype="f32", embed="f32"))
+    f16 = HostWeights.synthetic_f16(cfg)
+    assert f16.cfg.wtype == "f16" and f16.cfg.embed == "f16"
+    for key, a in f16.t.items():
+        if key.split(".")[0] in ("q", "k", "v", "o", "gate", "up", "down", "head", "embed"):
+            assert a.dtype == np.uint16
+            assert np.array_equal(a, f32.t[key].astype(np.float16).view(np.uint16)), key
+        else:
+            assert np.array_equal(a, f32.t[key]), key
+    lw = f16.desc.layers[0]
+    assert lw.Wq.h and not lw.Wq.f and not lw.Wq.q
+    assert f16.desc.lm_head.h and f16.desc.embed.h
+    lin = (cfg.q_dim + 2 * cfg.kv_dim) * cfg.hidden + cfg.hidden * cfg.q_dim + 3 * cfg.inter * cfg.hidden
+    want = cfg.layers * (2.0 * lin + 2 * cfg.hidden * 4) + cfg.vocab * cfg.hidden * 2.0 + 4 * cfg.hidden + cfg.hidden * 4
+    assert f16.weight_bytes_per_token() == want
